@@ -1,0 +1,189 @@
+/*
+ * har_cuda.h — C ABI of the B200-native Q4_K MoE-FFN path (libhar_cuda.so).
+ *
+ * This is the drop-in boundary HAR's Rust runtime binds through a thin FFI
+ * crate (har-cuda).  Every function is extern "C", takes plain pointers and
+ * sizes, and returns an int32 status: 0 = OK, negative = error (see
+ * HAR_CUDA_ERR_*); the message of the last failure on a context is read with
+ * har_cuda_last_error.  No function aborts, panics or falls back to the CPU:
+ * a missing device or kernel is reported as an error status (fail-closed,
+ * as har/crates/har-serve/src/vulkan.rs:18-19 requires of a GPU backend).
+ *
+ * Threading: one context owns one CUDA stream; a context is not
+ * thread-safe (like the reference's &self/RefCell models, moe.rs:47-53) and
+ * must be externally locked if shared.  Device pointers passed in ("_dev")
+ * must belong to the context's device; host pointers ("_host") are
+ * caller-owned and are copied in/out within the call.
+ *
+ * Layouts (identical to GGUF, so `*_exps` tensors upload unchanged):
+ *   Q4_K tensor:  [E][N][K/256] super-blocks of 144 B (f16 d @0, f16 dmin @2,
+ *                 12 B 6-bit scales/mins @4, 128 B nibbles @16),
+ *                 expert e at byte e*N*(K/256)*144
+ *                 (har/crates/har-demo/src/bin/har-native-qwen35moe.rs:664-667).
+ *   Q8_K row:     [K/256] blocks of 292 B (f32 d @0, int8 qs[256] @4,
+ *                 int16 bsums[16] @260).
+ *   activations:  f32 row-major [M][K]; outputs f32 row-major [M][N].
+ */
+#ifndef HAR_CUDA_H
+#define HAR_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define HAR_CUDA_ABI_VERSION 1
+
+/* status codes */
+#define HAR_CUDA_OK 0
+#define HAR_CUDA_ERR_ARG (-1)         /* null pointer / bad enum / bad size */
+#define HAR_CUDA_ERR_GEOMETRY (-2)    /* shape mismatch (K not a multiple of 256, ...) */
+#define HAR_CUDA_ERR_CUDA (-3)        /* a CUDA runtime call failed */
+#define HAR_CUDA_ERR_NCCL (-4)        /* an NCCL call failed */
+#define HAR_CUDA_ERR_TIMEOUT (-5)     /* a bounded wait expired (host or device) */
+#define HAR_CUDA_ERR_NOT_INIT (-6)    /* context / handle not initialised */
+#define HAR_CUDA_ERR_OOM (-7)         /* device allocation failed */
+#define HAR_CUDA_ERR_UNSUPPORTED (-8) /* shape/mode this build does not implement */
+#define HAR_CUDA_ERR_DEVICE (-9)      /* a kernel reported an error word */
+
+/* activation kinds for har_cuda_q4k_gemv */
+#define HAR_CUDA_ACT_F32 0 /* x is f32 [M][K]: HAR's f32-activation arithmetic */
+#define HAR_CUDA_ACT_Q8K 1 /* x is Q8_K [M][K/256][292 B]: integer dot products */
+
+/* flags for har_cuda_moe_ffn */
+#define HAR_CUDA_MOE_ADD_RESIDUAL 0x1u /* y = x + moe(x), as execute_layer_cpu */
+#define HAR_CUDA_MOE_ACT_Q8K 0x2u      /* quantise activations to Q8_K for CUDA-core GEMVs */
+#define HAR_CUDA_MOE_FORCE_GEMV 0x4u   /* every expert on the CUDA-core GEMV path */
+#define HAR_CUDA_MOE_FORCE_TC 0x8u     /* every expert on the tcgen05 tensor-core path */
+
+typedef struct har_cuda_ctx har_cuda_ctx;
+typedef struct har_cuda_weights har_cuda_weights;
+typedef struct har_cuda_moe_layer har_cuda_moe_layer;
+typedef struct har_cuda_ep har_cuda_ep;
+
+/* ---- context ------------------------------------------------------------
+ * Replaces the device/queue pair HAR opens per model
+ * (har/crates/har-vulkan/src/lib.rs:236 Device::open, :1673 Queue::submit_compute). */
+int32_t har_cuda_abi_version(void);
+int32_t har_cuda_ctx_create(int32_t device, har_cuda_ctx **out);
+int32_t har_cuda_ctx_destroy(har_cuda_ctx *ctx);
+/* Copies the last error message (NUL-terminated, truncated to len). */
+int32_t har_cuda_last_error(const har_cuda_ctx *ctx, char *buf, size_t len);
+/* Launch on a caller-owned cudaStream_t (NULL restores the context's own). */
+int32_t har_cuda_ctx_set_stream(har_cuda_ctx *ctx, void *cuda_stream);
+/* Bounded wait for the context's stream (replaces the unbounded
+ * TimelineEvent::wait, har/crates/har-vulkan/src/lib.rs:2168-2175). Also
+ * checks the device error word written by kernels with bounded waits. */
+int32_t har_cuda_synchronize(har_cuda_ctx *ctx, int64_t timeout_ms);
+/* Number of kernels this context has launched (instrumentation). */
+int64_t har_cuda_launch_count(const har_cuda_ctx *ctx);
+
+/* ---- weights ------------------------------------------------------------
+ * Replaces the staging->device-local copy in VulkanQ4KModel::open /
+ * VulkanBatchedModel::open (har/crates/har-serve/src/vulkan.rs:49-119,303-386). */
+int32_t har_cuda_weights_upload_q4k(har_cuda_ctx *ctx, const void *host_bytes, int64_t E,
+                                    int64_t N, int64_t K, har_cuda_weights **out);
+/* Borrow an existing 16-byte-aligned device buffer (not freed by the library). */
+int32_t har_cuda_weights_wrap_q4k(har_cuda_ctx *ctx, const void *dev_bytes, int64_t E,
+                                  int64_t N, int64_t K, har_cuda_weights **out);
+int32_t har_cuda_weights_free(har_cuda_weights *w);
+const void *har_cuda_weights_device_ptr(const har_cuda_weights *w);
+
+/* ---- Q8_K activation quantisation ---------------------------------------
+ * No reference counterpart (the reference only names q8_k_matvec,
+ * har/crates/har-lang-compiler/src/idea_registry.rs:122, and records the
+ * 292 B geometry, benchmarks/local-bench/crates/lb-model/src/lib.rs:88).
+ * x_dev f32 [M][K] -> out_dev [M][K/256][292 B]. */
+int32_t har_cuda_q8k_quantize(har_cuda_ctx *ctx, const float *x_dev, int64_t M, int64_t K,
+                              void *out_dev);
+
+/* ---- Q4_K GEMV ------------------------------------------------------------
+ * y[m][n] = sum_k W_e[n][k] * x[m][k] for m < M.  Replaces Q4KModel::matvec
+ * (har/crates/har-serve/src/q4k.rs:170-188), expert_matvec
+ * (har/crates/har-demo/src/bin/har-native-qwen35moe.rs:626-689) and the
+ * q4k_gemv / q4k_batched_gemv dispatches (har/crates/har-serve/src/vulkan.rs:131-191,402-462).
+ * act_kind HAR_CUDA_ACT_F32: x_dev is f32 [M][K]; HAR_CUDA_ACT_Q8K: Q8_K rows. */
+int32_t har_cuda_q4k_gemv(har_cuda_ctx *ctx, const har_cuda_weights *w, int64_t expert,
+                          const void *x_dev, int32_t act_kind, int64_t M, float *y_dev);
+
+/* ---- router top-k ---------------------------------------------------------
+ * Per token: softmax over all E logits with max subtraction, experts ordered
+ * by probability descending then lower index, first k taken, weights
+ * renormalised by their sum (both sums clamped to >= 1e-9).  Bit-exact with
+ * routed_moe (har/crates/har-demo/src/bin/har-native-qwen35moe.rs:1167-1204).
+ * logits_dev f32 [T][E]; ids_dev int32 [T][k]; weights_dev f32 [T][k]. */
+int32_t har_cuda_route_topk(har_cuda_ctx *ctx, const float *logits_dev, int64_t T, int32_t E,
+                            int32_t k, int32_t *ids_dev, float *weights_dev);
+
+/* ---- expert-major grouping -------------------------------------------------
+ * groups[e] = entries (t*k + slot) routed to e, in position order
+ * (har/crates/har-serve/src/moe.rs:195-202).  counts_dev int32 [E],
+ * offsets_dev int32 [E+1], order_dev int32 [T*k]. */
+int32_t har_cuda_group_by_expert(har_cuda_ctx *ctx, const int32_t *ids_dev, int64_t T,
+                                 int32_t k, int32_t E, int32_t *counts_dev,
+                                 int32_t *offsets_dev, int32_t *order_dev);
+
+/* ---- MoE FFN layer --------------------------------------------------------
+ * A layer = gate/up [E][I][H/256], down [E][H][I/256] Q4_K tensors plus an
+ * optional shared expert (three 1-expert tensors of the same shapes) and an
+ * optional f32 [H] shared-expert gate row (NULL: gate weight 1.0).
+ * Mirrors the tensor set compose_moe_route reads per layer
+ * (har/crates/har-demo/src/bin/har-native-qwen35moe.rs:979-1048). */
+int32_t har_cuda_moe_layer_create(har_cuda_ctx *ctx, const har_cuda_weights *gate,
+                                  const har_cuda_weights *up, const har_cuda_weights *down,
+                                  const har_cuda_weights *sh_gate,
+                                  const har_cuda_weights *sh_up,
+                                  const har_cuda_weights *sh_down,
+                                  const float *sh_gate_inp_dev, har_cuda_moe_layer **out);
+int32_t har_cuda_moe_layer_free(har_cuda_moe_layer *layer);
+
+/* y[t] = sum_s weights[t][s] * down_e(silu(gate_e x_t) * up_e x_t)
+ *        + sigmoid(sh_gate_inp . x_t) * shared(x_t)   [+ x_t with ADD_RESIDUAL],
+ * experts e = ids[t][s] in slot order; device pointers.  Replaces
+ * compose_moe_route / routed_moe's expert loop and MoEModel::forward_batch's
+ * expert-major grouping (har/crates/har-serve/src/moe.rs:182-255). */
+int32_t har_cuda_moe_ffn(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer,
+                         const float *x_dev, int64_t T, int32_t k, const int32_t *ids_dev,
+                         const float *weights_dev, float *y_dev, uint32_t flags);
+/* The same with host buffers: copies x/ids/weights in and y out on the
+ * context's stream and waits (bounded) — the call a BatchStepModel makes. */
+int32_t har_cuda_moe_ffn_host(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer,
+                              const float *x_host, int64_t T, int32_t k,
+                              const int32_t *ids_host, const float *weights_host,
+                              float *y_host, uint32_t flags);
+/* A stack of L layers applied in order (y_l = moe_l(y_{l-1}) [+ residual]),
+ * ids/weights [L][T][k]; x_dev and y_dev may alias.  Attention and norms
+ * between layers are outside this path. */
+int32_t har_cuda_moe_stack(har_cuda_ctx *ctx, const har_cuda_moe_layer *const *layers,
+                           int32_t L, const float *x_dev, int64_t T, int32_t k,
+                           const int32_t *ids_dev, const float *weights_dev, float *y_dev,
+                           uint32_t flags);
+
+/* The stack with host buffers (x [T][H], ids/weights [L][T][k], y [T][H]):
+ * copies in, runs, copies out and waits (bounded). */
+int32_t har_cuda_moe_stack_host(har_cuda_ctx *ctx, const har_cuda_moe_layer *const *layers,
+                                int32_t L, const float *x_host, int64_t T, int32_t k,
+                                const int32_t *ids_host, const float *weights_host,
+                                float *y_host, uint32_t flags);
+
+/* ---- profiling (the role of TimestampQuery, har/crates/har-vulkan/src/lib.rs:2221-2257) ---
+ * Between begin and end every kernel the context launches is bracketed by
+ * CUDA events on its stream; end waits for the stream and returns up to cap
+ * (kernel name, milliseconds) records: names '\n'-separated in `names`. */
+int32_t har_cuda_profile_begin(har_cuda_ctx *ctx);
+int32_t har_cuda_profile_end(har_cuda_ctx *ctx, char *names, size_t names_len, float *ms,
+                             int64_t cap, int64_t *count);
+
+/* ---- synthetic inputs (bench/test generator, not a reference function) ---
+ * Fills dev_bytes with rows x K N(mean,std) values quantised to Q4_K by the
+ * same quantiser as the oracle's haro_q4k_quantize_row, element (r, c) being
+ * normal index (row0 + r)*K + c of `seed`. */
+int32_t har_cuda_gen_q4k(har_cuda_ctx *ctx, void *dev_bytes, int64_t rows, int64_t K,
+                         uint64_t seed, int64_t row0, float mean, float std);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,219 @@
+// gemv_engine.cuh — the CUDA-core Q4_K row-dot engine shared by the GEMV and
+// MoE decode kernels.
+//
+// Work unit: a 64-value "chunk" = 32 bytes of nibbles of one super-block plus
+// that block's 16-byte header (d, dmin, 12 scale bytes).  Chunk c of block b
+// covers values 64c..64c+63: low nibbles are sub-block 2c, high nibbles
+// sub-block 2c+1 (q4k_dot's loop, har/crates/har-demo/src/bin/har-native-qwen3.rs:157-168).
+// A row of K values has C = K/64 chunks; LPR = min(32, C) lanes share a row
+// and each lane owns CPL = ceil(C/32) fixed chunk positions, so its slice of
+// the activations is loaded into registers once and reused for every row the
+// warp visits.  Rows are read with 128-bit loads straight from HBM.
+//
+// Two activation kinds:
+//   ACT_F32 — f32 activations; per sub-block sum_q q*x is accumulated with
+//             FMAs and combined as d1*sum(q*x) - m1*sum(x) (the f32 value
+//             (d1*q - m1)*x of q4k_dot, reassociated; tolerance-checked).
+//   ACT_Q8K — Q8_K activations; per sub-block integer dot products with
+//             __dp4a, combined as (d*dx)*I1 - (dmin*dx)*I2 per chunk.
+#pragma once
+
+#include "har_internal.cuh"
+
+namespace har {
+
+enum : int { ACT_F32 = 0, ACT_Q8K = 1 };
+
+// Shared-memory image of MT tokens' activations for one K.
+//  F32: xs[t][K] f32, sums[t][2*C] f32 (per-sub-block sums of x)
+//  Q8K: qs[t][K] int8, dx[t][K/256] f32, bsum[t][2*C] int (per-sub-block bsums)
+template <int ACT>
+struct ActSmem;
+
+template <>
+struct ActSmem<ACT_F32> {
+  static __host__ __device__ size_t bytes(int MT, int K) {
+    return (size_t)MT * K * 4 + (size_t)MT * (K / 32) * 4;
+  }
+};
+template <>
+struct ActSmem<ACT_Q8K> {
+  static __host__ __device__ size_t bytes(int MT, int K) {
+    return (size_t)MT * K + (size_t)MT * (K / 256) * 4 + (size_t)MT * (K / 32) * 4;
+  }
+};
+
+// Stage f32 activation rows (row pointers may be null for padding tokens).
+__device__ __forceinline__ void stage_f32(uint8_t *smem, const float *const *rows, int MT, int K) {
+  float *xs = reinterpret_cast<float *>(smem);
+  float *sums = xs + (size_t)MT * K;
+  const int nvec = K / 4;
+  for (int i = threadIdx.x; i < MT * nvec; i += blockDim.x) {
+    const int t = i / nvec, v = i - t * nvec;
+    float4 val = rows[t] ? reinterpret_cast<const float4 *>(rows[t])[v] : make_float4(0, 0, 0, 0);
+    reinterpret_cast<float4 *>(xs + (size_t)t * K)[v] = val;
+  }
+  __syncthreads();
+  const int nsub = K / 32;
+  for (int i = threadIdx.x; i < MT * nsub; i += blockDim.x) {
+    const int t = i / nsub, s = i - t * nsub;
+    const float *p = xs + (size_t)t * K + 32 * s;
+    float acc = 0.0f;
+#pragma unroll 8
+    for (int j = 0; j < 32; ++j) acc += p[j];
+    sums[(size_t)t * nsub + s] = acc;
+  }
+  __syncthreads();
+}
+
+// Stage packed Q8_K activation rows (292-byte blocks).
+__device__ __forceinline__ void stage_q8k(uint8_t *smem, const uint8_t *const *rows, int MT, int K) {
+  int8_t *qs = reinterpret_cast<int8_t *>(smem);
+  float *dx = reinterpret_cast<float *>(smem + (size_t)MT * K);
+  int *bsum = reinterpret_cast<int *>(dx + (size_t)MT * (K / 256));
+  const int nb = K / 256;
+  // qs: 64 words per block
+  for (int i = threadIdx.x; i < MT * nb * 64; i += blockDim.x) {
+    const int t = i / (nb * 64), r = i - t * nb * 64, b = r >> 6, w = r & 63;
+    uint32_t v = rows[t] ? reinterpret_cast<const uint32_t *>(rows[t] + (size_t)b * Q8K_BYTES + 4)[w] : 0u;
+    reinterpret_cast<uint32_t *>(qs + (size_t)t * K + 256 * b)[w] = v;
+  }
+  for (int i = threadIdx.x; i < MT * nb; i += blockDim.x) {
+    const int t = i / nb, b = i - t * nb;
+    dx[(size_t)t * nb + b] = rows[t] ? *reinterpret_cast<const float *>(rows[t] + (size_t)b * Q8K_BYTES) : 0.0f;
+  }
+  // per 32-value sub-block: bsums[2s] + bsums[2s+1]
+  for (int i = threadIdx.x; i < MT * nb * 8; i += blockDim.x) {
+    const int t = i / (nb * 8), r = i - t * nb * 8, b = r >> 3, s = r & 7;
+    int v = 0;
+    if (rows[t]) {
+      const int16_t *bs = reinterpret_cast<const int16_t *>(rows[t] + (size_t)b * Q8K_BYTES + 260);
+      v = (int)bs[2 * s] + (int)bs[2 * s + 1];
+    }
+    bsum[(size_t)t * (K / 32) + 8 * b + s] = v;
+  }
+  __syncthreads();
+}
+
+// Per-lane activation registers for one chunk of one token.
+template <int ACT>
+struct LaneAct;
+
+template <>
+struct LaneAct<ACT_F32> {
+  float lo[32], hi[32];
+  float slo, shi;
+  __device__ __forceinline__ void load(const uint8_t *smem, int MT, int K, int t, int chunk) {
+    const float *xs = reinterpret_cast<const float *>(smem) + (size_t)t * K + 64 * chunk;
+    const float *sums = reinterpret_cast<const float *>(smem) + (size_t)MT * K + (size_t)t * (K / 32);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float4 a = reinterpret_cast<const float4 *>(xs)[i];
+      float4 b = reinterpret_cast<const float4 *>(xs + 32)[i];
+      lo[4 * i] = a.x; lo[4 * i + 1] = a.y; lo[4 * i + 2] = a.z; lo[4 * i + 3] = a.w;
+      hi[4 * i] = b.x; hi[4 * i + 1] = b.y; hi[4 * i + 2] = b.z; hi[4 * i + 3] = b.w;
+    }
+    slo = sums[2 * chunk];
+    shi = sums[2 * chunk + 1];
+  }
+};
+
+template <>
+struct LaneAct<ACT_Q8K> {
+  int lo[8], hi[8];
+  int blo, bhi;
+  float dx;
+  __device__ __forceinline__ void load(const uint8_t *smem, int MT, int K, int t, int chunk) {
+    const int8_t *qs = reinterpret_cast<const int8_t *>(smem) + (size_t)t * K + 64 * chunk;
+    const float *dxs = reinterpret_cast<const float *>(smem + (size_t)MT * K);
+    const int *bsum = reinterpret_cast<const int *>(dxs + (size_t)MT * (K / 256));
+    uint4 a0 = reinterpret_cast<const uint4 *>(qs)[0], a1 = reinterpret_cast<const uint4 *>(qs)[1];
+    uint4 b0 = reinterpret_cast<const uint4 *>(qs)[2], b1 = reinterpret_cast<const uint4 *>(qs)[3];
+    lo[0] = a0.x; lo[1] = a0.y; lo[2] = a0.z; lo[3] = a0.w;
+    lo[4] = a1.x; lo[5] = a1.y; lo[6] = a1.z; lo[7] = a1.w;
+    hi[0] = b0.x; hi[1] = b0.y; hi[2] = b0.z; hi[3] = b0.w;
+    hi[4] = b1.x; hi[5] = b1.y; hi[6] = b1.z; hi[7] = b1.w;
+    dx = dxs[(size_t)t * (K / 256) + chunk / 4];
+    blo = bsum[(size_t)t * (K / 32) + 2 * chunk];
+    bhi = bsum[(size_t)t * (K / 32) + 2 * chunk + 1];
+  }
+};
+
+// Raw weight chunk held in registers.
+struct WChunk {
+  uint4 hdr, q0, q1;
+};
+
+__device__ __forceinline__ WChunk load_wchunk(const uint8_t *row, int chunk) {
+  const uint8_t *blk = row + (size_t)(chunk >> 2) * Q4K_BYTES;
+  const int c = chunk & 3;
+  WChunk w;
+  w.hdr = __ldg(reinterpret_cast<const uint4 *>(blk));
+  w.q0 = __ldg(reinterpret_cast<const uint4 *>(blk + 16 + 32 * c));
+  w.q1 = __ldg(reinterpret_cast<const uint4 *>(blk + 32 + 32 * c));
+  return w;
+}
+
+__device__ __forceinline__ float chunk_dot(const WChunk &w, int chunk, const LaneAct<ACT_Q8K> &a) {
+  const uint32_t q[8] = {w.q0.x, w.q0.y, w.q0.z, w.q0.w, w.q1.x, w.q1.y, w.q1.z, w.q1.w};
+  int slo = 0, shi = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    slo = __dp4a((int)(q[i] & 0x0F0F0F0Fu), a.lo[i], slo);
+    shi = __dp4a((int)((q[i] >> 4) & 0x0F0F0F0Fu), a.hi[i], shi);
+  }
+  int sc1, m1, sc2, m2;
+  const int c = chunk & 3;
+  q4k_scale_min(w.hdr.y, w.hdr.z, w.hdr.w, 2 * c, sc1, m1);
+  q4k_scale_min(w.hdr.y, w.hdr.z, w.hdr.w, 2 * c + 1, sc2, m2);
+  const float d = f16_bits_to_f32(w.hdr.x), dmin = f16_bits_to_f32(w.hdr.x >> 16);
+  const int i1 = sc1 * slo + sc2 * shi;
+  const int i2 = m1 * a.blo + m2 * a.bhi;
+  return (d * a.dx) * (float)i1 - (dmin * a.dx) * (float)i2;
+}
+
+__device__ __forceinline__ float chunk_dot(const WChunk &w, int chunk, const LaneAct<ACT_F32> &a) {
+  const uint32_t q[8] = {w.q0.x, w.q0.y, w.q0.z, w.q0.w, w.q1.x, w.q1.y, w.q1.z, w.q1.w};
+  float slo = 0.0f, shi = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      slo = fmaf(u4_to_f32((q[i] >> (8 * j)) & 15u), a.lo[4 * i + j], slo);
+      shi = fmaf(u4_to_f32((q[i] >> (8 * j + 4)) & 15u), a.hi[4 * i + j], shi);
+    }
+  }
+  const ChunkScales s = chunk_scales(w.hdr, chunk & 3);
+  return (s.d1 * slo - s.m1 * a.slo) + (s.d2 * shi - s.m2 * a.shi);
+}
+
+// Lanes per row, chunks per lane and tokens per pass for a given K.
+struct GemvShape {
+  int C;    // chunks per row
+  int LPR;  // lanes per row
+  int CPL;  // chunks per lane
+  int RPW;  // rows per warp iteration (32 / LPR)
+};
+
+__host__ __device__ inline GemvShape gemv_shape(int K) {
+  GemvShape s;
+  s.C = K / 64;
+  if (s.C >= 32) {
+    s.LPR = 32;
+    s.CPL = (s.C + 31) / 32;
+  } else {
+    int l = 1;
+    while (l < s.C) l <<= 1;  // next power of two >= C
+    s.LPR = l;
+    s.CPL = 1;
+  }
+  s.RPW = 32 / s.LPR;
+  return s;
+}
+
+template <int LPR>
+__device__ __forceinline__ float lane_group_sum(float v) {
+  return group_sum<LPR>(v);
+}
+
+}  // namespace har

@@ -1,0 +1,170 @@
+// har_internal.cuh — shared device helpers and host-side handle types of
+// libhar_cuda.so.  Q4_K semantics follow har/crates/har-serve/src/q4k.rs:12-89
+// and har/crates/har-demo/src/bin/har-native-qwen3.rs:116-172 (paths relative
+// to the leoinfer/remora-lab repository).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+#include <vector>
+
+#include "har_cuda.h"
+
+namespace har {
+
+constexpr int QK = 256;           // values per super-block
+constexpr int Q4K_BYTES = 144;    // bytes per Q4_K super-block
+constexpr int Q8K_BYTES = 292;    // bytes per Q8_K block
+constexpr float ROUTER_EPS = 1.0e-9f;
+
+// Device error words (bit flags) written by kernels; read by har_cuda_synchronize.
+constexpr int DEV_ERR_TIMEOUT = 1;
+constexpr int DEV_ERR_BOUNDS = 2;
+
+// ---------------------------------------------------------------------------
+// Q4_K super-block header: 16 bytes = {d|dmin<<16, sc/m bytes 0-3, 4-7, 8-11}
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ float f16_bits_to_f32(uint32_t bits16) {
+  // binary16 -> f32 is exact (subnormals included): the same value as
+  // f16_to_f32 (q4k.rs:22-50) and half_to_f32 (har-native-qwen3.rs:116-136).
+  return __half2float(__ushort_as_half((unsigned short)(bits16 & 0xffffu)));
+}
+
+// 6-bit scale and min of sub-block j (0..7) from the three scale words
+// s0 = bytes 4..7, s1 = bytes 8..11, s2 = bytes 12..15 of the block
+// (scale_min, har-native-qwen3.rs:138-147; scale_at/min_at, q4k.rs:60-74).
+__device__ __forceinline__ void q4k_scale_min(uint32_t s0, uint32_t s1, uint32_t s2, int j,
+                                              int &sc, int &m) {
+  if (j < 4) {
+    sc = (s0 >> (8 * j)) & 63;
+    m = (s1 >> (8 * j)) & 63;
+  } else {
+    const int b = 8 * (j - 4);
+    const uint32_t lo = (s2 >> b) & 0xffu;
+    sc = (lo & 15) | (((s0 >> b) >> 6 & 3) << 4);
+    m = (lo >> 4) | (((s1 >> b) >> 6 & 3) << 4);
+  }
+}
+
+// Dequantised f32 value pair constants of a 64-value chunk c (sub-blocks 2c, 2c+1):
+// value = d1 * q - m1 for the low nibble half, d2 * q - m2 for the high half.
+struct ChunkScales {
+  float d1, m1, d2, m2;  // d*sc, dmin*m  (q4k_dot's d1/min1/d2/min2)
+  int sc1, mn1, sc2, mn2;
+  float d, dmin;
+};
+
+__device__ __forceinline__ ChunkScales chunk_scales(uint4 hdr, int c) {
+  ChunkScales r;
+  r.d = f16_bits_to_f32(hdr.x);
+  r.dmin = f16_bits_to_f32(hdr.x >> 16);
+  q4k_scale_min(hdr.y, hdr.z, hdr.w, 2 * c, r.sc1, r.mn1);
+  q4k_scale_min(hdr.y, hdr.z, hdr.w, 2 * c + 1, r.sc2, r.mn2);
+  r.d1 = r.d * (float)r.sc1;
+  r.m1 = r.dmin * (float)r.mn1;
+  r.d2 = r.d * (float)r.sc2;
+  r.m2 = r.dmin * (float)r.mn2;
+  return r;
+}
+
+// Exact small-integer -> f32 via the mantissa: 2^23 + v reinterpreted, minus 2^23.
+__device__ __forceinline__ float u4_to_f32(uint32_t v) {
+  return __int_as_float(0x4B000000 | v) - 8388608.0f;
+}
+
+__device__ __forceinline__ uint4 ldg_nc_v4(const void *p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+template <int WIDTH>
+__device__ __forceinline__ float group_sum(float v) {
+#pragma unroll
+  for (int o = WIDTH / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+}  // namespace har
+
+// ---------------------------------------------------------------------------
+// Host-side handle types (opaque in the C ABI).
+// ---------------------------------------------------------------------------
+
+struct har_cuda_ctx {
+  int device = 0;
+  cudaStream_t stream = nullptr;      // stream kernels are launched on
+  cudaStream_t own_stream = nullptr;  // the context's own stream
+  int num_sms = 148;
+  std::string last_error;
+  int *d_status = nullptr;            // device error word (bit flags)
+  void *scratch = nullptr;            // grow-only scratch arena
+  size_t scratch_bytes = 0;
+  void *host_pinned = nullptr;        // pinned staging for *_host entry points
+  size_t host_pinned_bytes = 0;
+  void *io_dev = nullptr;             // device staging for *_host entry points
+  size_t io_dev_bytes = 0;
+  int64_t launches = 0;
+  // opt-in per-launch CUDA-event profiling (har_cuda_profile_begin/end)
+  bool prof_on = false;
+  cudaEvent_t prof_pending = nullptr;
+  struct ProfRec {
+    const char *name;
+    cudaEvent_t a, b;
+  };
+  std::vector<ProfRec> prof;
+};
+
+struct har_cuda_weights {
+  const uint8_t *dev = nullptr;
+  bool owned = false;
+  int64_t E = 0, N = 0, K = 0;
+  int64_t row_bytes = 0;  // K/256*144
+  int64_t expert_bytes = 0;
+  int device = 0;
+};
+
+struct har_cuda_moe_layer {
+  const har_cuda_weights *gate = nullptr, *up = nullptr, *down = nullptr;
+  const har_cuda_weights *sh_gate = nullptr, *sh_up = nullptr, *sh_down = nullptr;
+  const float *sh_gate_inp = nullptr;
+  int64_t E = 0, H = 0, I = 0;
+};
+
+namespace har {
+
+// Error helpers shared by the .cu files.
+int32_t set_error(har_cuda_ctx *ctx, int32_t code, const std::string &msg);
+int32_t check_launch(har_cuda_ctx *ctx, const char *what);
+// Call immediately before a kernel launch; check_launch closes the record.
+void prof_begin(har_cuda_ctx *ctx);
+int32_t ensure_scratch(har_cuda_ctx *ctx, size_t bytes);
+
+// Kernel launchers (host functions defined in the kernel .cu files).
+int32_t launch_q8k_quantize(har_cuda_ctx *ctx, const float *x, int64_t M, int64_t K,
+                            uint8_t *out);
+int32_t launch_gemv(har_cuda_ctx *ctx, const har_cuda_weights *w, int64_t expert,
+                    const void *x, int act_kind, int64_t M, float *y);
+int32_t launch_route_topk(har_cuda_ctx *ctx, const float *logits, int64_t T, int E, int k,
+                          int32_t *ids, float *weights);
+int32_t launch_group(har_cuda_ctx *ctx, const int32_t *ids, int64_t T, int k, int E,
+                     int32_t *counts, int32_t *offsets, int32_t *order, int32_t *inv);
+int32_t run_moe_ffn(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const float *x,
+                    int64_t T, int k, const int32_t *ids, const float *weights, float *y,
+                    uint32_t flags);
+int32_t launch_gen_q4k(har_cuda_ctx *ctx, uint8_t *dst, int64_t rows, int64_t K,
+                       uint64_t seed, int64_t row0, float mean, float stdv);
+
+}  // namespace har

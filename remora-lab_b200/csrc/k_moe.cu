@@ -1,0 +1,412 @@
+// k_moe.cu — the expert-FFN executor: compose_moe_route for a batch of
+// tokens, expert-major (har/crates/har-demo/src/bin/har-native-qwen35moe.rs:979-1048
+// for the arithmetic, har/crates/har-serve/src/moe.rs:182-255 for the
+// grouping that reads each routed expert's weights once per step).
+//
+// Pipeline on one stream (all device-side; the host never reads counts):
+//   1. group_kernel: stable counting sort of the T*k (token, slot) entries by
+//      expert; list of non-empty experts.
+//   2. [Q8_K mode] quantise the T token rows once.
+//   3. moe_gate_up_kernel: for each (expert, tile of intermediate rows), the
+//      gate and up GEMV rows for all of the expert's tokens, SwiGLU in
+//      registers: a[slot][i] = silu(gate_i . x) * (up_i . x).
+//   4. [Q8_K mode] quantise the a rows.
+//   5. moe_down_kernel: ybuf[slot][h] = down_h . a[slot] per (expert, tile of
+//      hidden rows).
+//   6. moe_combine_kernel: per token, routed = sum over slots in slot order of
+//      w * down (the reference's `*output += weight * value`), then
+//      + sigmoid(gate_inp . x) * shared, then + x with ADD_RESIDUAL.  The
+//      combine uses separately rounded multiplies and adds like Rust.
+// Slot numbering: routed entries occupy grouped positions [0, n), n = T*k;
+// the shared expert's row for token t is slot n + t.
+#include <algorithm>
+
+#include "gemv_engine.cuh"
+
+namespace har {
+
+size_t group_smem_bytes(int E);
+int32_t launch_group_full(har_cuda_ctx *ctx, const int32_t *ids, int64_t n, int E,
+                          int32_t *counts, int32_t *offsets, int32_t *order, int32_t *inv,
+                          int32_t *ne, int32_t *n_ne);
+
+struct MoeDev {
+  const uint8_t *gate, *up, *down, *sh_gate, *sh_up, *sh_down;
+  int64_t ebytes_gu, ebytes_d;  // bytes per expert
+  int64_t rb_h, rb_i;           // Q4_K row bytes for K = H and K = I
+  int64_t xrow, arow;           // activation row bytes (f32 or Q8_K) for H and I
+  int E, H, I, T, k, n;
+  int has_shared;
+  const int32_t *counts, *offsets, *order, *inv, *ne, *n_ne;
+  const uint8_t *xact;  // x rows (f32) or their Q8_K image
+  float *a;             // [n + T][I] f32
+  const uint8_t *aact;  // a rows (f32, = a) or their Q8_K image
+  float *ybuf;          // [n + T][H] f32
+};
+
+__device__ __forceinline__ float silu_f(float v) { return v / (1.0f + expf(-v)); }
+
+// sigmoid of har-native-qwen35moe.rs:207-214
+__device__ __forceinline__ float sigmoid_f(float v) {
+  if (v >= 0.0f) return 1.0f / (1.0f + expf(-v));
+  const float e = expf(v);
+  return e / (1.0f + e);
+}
+
+// Resolve group gi's expert id, token count and first slot.
+__device__ __forceinline__ void group_info(const MoeDev &p, int gi, int nne, int &g, int &cnt,
+                                           int &base) {
+  if (gi < nne) {
+    g = p.ne[gi];
+    cnt = p.counts[g];
+    base = p.offsets[g];
+  } else {
+    g = p.E;  // shared expert
+    cnt = p.T;
+    base = p.n;
+  }
+}
+
+// Fill the CTA's token table for tokens [tt, tt+MT) of a group.
+template <int MT>
+__device__ __forceinline__ void token_table(const MoeDev &p, int g, int cnt, int base, int tt,
+                                            const uint8_t *act, int64_t arow, bool by_slot,
+                                            const uint8_t **rowp, int *slot) {
+  if (threadIdx.x < MT) {
+    const int idx = tt + threadIdx.x;
+    if (idx < cnt) {
+      int s, tok;
+      if (g == p.E) {
+        tok = idx;
+        s = p.n + idx;
+      } else {
+        tok = p.order[base + idx] / p.k;
+        s = base + idx;
+      }
+      rowp[threadIdx.x] = act + (int64_t)(by_slot ? s : tok) * arow;
+      slot[threadIdx.x] = s;
+    } else {
+      rowp[threadIdx.x] = nullptr;
+      slot[threadIdx.x] = -1;
+    }
+  }
+  __syncthreads();
+}
+
+template <int ACT, int LPR, int CPL, int MT>
+__global__ void __launch_bounds__(256) moe_gate_up_kernel(MoeDev p, int rows_per_tile) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  __shared__ const uint8_t *rowp[MT];
+  __shared__ int slot[MT];
+  constexpr int RPW = 32 / LPR;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int grp = lane / LPR, gl = lane % LPR;
+  const int C = p.H / 64;
+  const int ntg = (p.I + rows_per_tile - 1) / rows_per_tile;
+  const int nne = *p.n_ne;
+  const int total = (nne + p.has_shared) * ntg;
+  for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
+    const int gi = tile / ntg, j = tile - gi * ntg;
+    int g, cnt, base;
+    group_info(p, gi, nne, g, cnt, base);
+    const uint8_t *wg = g == p.E ? p.sh_gate : p.gate + (int64_t)g * p.ebytes_gu;
+    const uint8_t *wu = g == p.E ? p.sh_up : p.up + (int64_t)g * p.ebytes_gu;
+    const int r0 = j * rows_per_tile, r1 = min(p.I, r0 + rows_per_tile);
+    for (int tt = 0; tt < cnt; tt += MT) {
+      token_table<MT>(p, g, cnt, base, tt, p.xact, p.xrow, false, rowp, slot);
+      if (ACT == ACT_F32)
+        stage_f32(smem, reinterpret_cast<const float *const *>(rowp), MT, p.H);
+      else
+        stage_q8k(smem, rowp, MT, p.H);
+      LaneAct<ACT> a[MT][CPL];
+#pragma unroll
+      for (int t = 0; t < MT; ++t)
+#pragma unroll
+        for (int i = 0; i < CPL; ++i) {
+          const int ch = gl + LPR * i;
+          if (ch < C) a[t][i].load(smem, MT, p.H, t, ch);
+        }
+      for (int rb = r0 + warp * RPW; rb < r1; rb += 8 * RPW) {
+        const int r = rb + grp;
+        const bool valid = r < r1;
+        const int rr = valid ? r : rb;
+        const uint8_t *rg = wg + (int64_t)rr * p.rb_h;
+        const uint8_t *ru = wu + (int64_t)rr * p.rb_h;
+        float ag[MT], au[MT];
+#pragma unroll
+        for (int t = 0; t < MT; ++t) ag[t] = au[t] = 0.0f;
+#pragma unroll
+        for (int i = 0; i < CPL; ++i) {
+          const int ch = gl + LPR * i;
+          if (ch < C) {
+            const WChunk w1 = load_wchunk(rg, ch);
+            const WChunk w2 = load_wchunk(ru, ch);
+#pragma unroll
+            for (int t = 0; t < MT; ++t) {
+              ag[t] += chunk_dot(w1, ch, a[t][i]);
+              au[t] += chunk_dot(w2, ch, a[t][i]);
+            }
+          }
+        }
+#pragma unroll
+        for (int t = 0; t < MT; ++t) {
+          ag[t] = lane_group_sum<LPR>(ag[t]);
+          au[t] = lane_group_sum<LPR>(au[t]);
+        }
+        if (valid && gl == 0) {
+#pragma unroll
+          for (int t = 0; t < MT; ++t)
+            if (slot[t] >= 0) p.a[(int64_t)slot[t] * p.I + r] = __fmul_rn(silu_f(ag[t]), au[t]);
+        }
+      }
+      __syncthreads();  // smem and the token table are rewritten next pass
+    }
+  }
+}
+
+template <int ACT, int LPR, int CPL, int MT>
+__global__ void __launch_bounds__(256) moe_down_kernel(MoeDev p, int rows_per_tile) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  __shared__ const uint8_t *rowp[MT];
+  __shared__ int slot[MT];
+  constexpr int RPW = 32 / LPR;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int grp = lane / LPR, gl = lane % LPR;
+  const int C = p.I / 64;
+  const int ntg = (p.H + rows_per_tile - 1) / rows_per_tile;
+  const int nne = *p.n_ne;
+  const int total = (nne + p.has_shared) * ntg;
+  for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
+    const int gi = tile / ntg, j = tile - gi * ntg;
+    int g, cnt, base;
+    group_info(p, gi, nne, g, cnt, base);
+    const uint8_t *wd = g == p.E ? p.sh_down : p.down + (int64_t)g * p.ebytes_d;
+    const int r0 = j * rows_per_tile, r1 = min(p.H, r0 + rows_per_tile);
+    for (int tt = 0; tt < cnt; tt += MT) {
+      token_table<MT>(p, g, cnt, base, tt, p.aact, p.arow, true, rowp, slot);
+      if (ACT == ACT_F32)
+        stage_f32(smem, reinterpret_cast<const float *const *>(rowp), MT, p.I);
+      else
+        stage_q8k(smem, rowp, MT, p.I);
+      LaneAct<ACT> a[MT][CPL];
+#pragma unroll
+      for (int t = 0; t < MT; ++t)
+#pragma unroll
+        for (int i = 0; i < CPL; ++i) {
+          const int ch = gl + LPR * i;
+          if (ch < C) a[t][i].load(smem, MT, p.I, t, ch);
+        }
+      for (int rb = r0 + warp * RPW; rb < r1; rb += 8 * RPW) {
+        const int r = rb + grp;
+        const bool valid = r < r1;
+        const uint8_t *rd = wd + (int64_t)(valid ? r : rb) * p.rb_i;
+        float acc[MT];
+#pragma unroll
+        for (int t = 0; t < MT; ++t) acc[t] = 0.0f;
+#pragma unroll
+        for (int i = 0; i < CPL; ++i) {
+          const int ch = gl + LPR * i;
+          if (ch < C) {
+            const WChunk w = load_wchunk(rd, ch);
+#pragma unroll
+            for (int t = 0; t < MT; ++t) acc[t] += chunk_dot(w, ch, a[t][i]);
+          }
+        }
+#pragma unroll
+        for (int t = 0; t < MT; ++t) acc[t] = lane_group_sum<LPR>(acc[t]);
+        if (valid && gl == 0) {
+#pragma unroll
+          for (int t = 0; t < MT; ++t)
+            if (slot[t] >= 0) p.ybuf[(int64_t)slot[t] * p.H + r] = acc[t];
+        }
+      }
+      __syncthreads();
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256) moe_combine_kernel(MoeDev p, const float *__restrict__ x,
+                                                          const float *__restrict__ weights,
+                                                          const float *__restrict__ sh_gate_inp,
+                                                          float *y, int add_residual) {
+  __shared__ float red[8];
+  const int64_t t = blockIdx.x;
+  const float *xt = x + t * p.H;
+  float g = 1.0f;
+  if (p.has_shared && sh_gate_inp) {
+    float s = 0.0f;
+    for (int h = threadIdx.x; h < p.H; h += blockDim.x) s = fmaf(sh_gate_inp[h], xt[h], s);
+    s = warp_sum(s);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+    __syncthreads();
+    s = 0.0f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) s += red[w];
+    g = sigmoid_f(s);
+  }
+  __syncthreads();  // every read of x[t] by the gate dot precedes the writes below
+  for (int h = threadIdx.x; h < p.H; h += blockDim.x) {
+    float acc = 0.0f;
+    for (int s = 0; s < p.k; ++s) {
+      const int pos = p.inv[t * p.k + s];
+      if (pos >= 0)
+        acc = __fadd_rn(acc, __fmul_rn(weights[t * p.k + s], p.ybuf[(int64_t)pos * p.H + h]));
+    }
+    if (p.has_shared) acc = __fadd_rn(acc, __fmul_rn(g, p.ybuf[(int64_t)(p.n + t) * p.H + h]));
+    if (add_residual) acc = __fadd_rn(xt[h], acc);
+    y[t * p.H + h] = acc;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+
+template <typename K>
+static void set_smem(K kern, size_t smem) {
+  if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+}
+
+// Rows per work tile: 4 warp passes for gate/up, 2 for down.
+static int rows_per_tile_gu(int H) { return 8 * gemv_shape(H).RPW * 4; }
+static int rows_per_tile_d(int I) { return 8 * gemv_shape(I).RPW * 2; }
+
+template <int ACT, int LPR, int CPL, int MT>
+static int32_t launch_gate_up(har_cuda_ctx *ctx, const MoeDev &p, int grid) {
+  const int rows_per_tile = rows_per_tile_gu(p.H);
+  auto kern = moe_gate_up_kernel<ACT, LPR, CPL, MT>;
+  const size_t smem = ActSmem<ACT>::bytes(MT, p.H);
+  set_smem(kern, smem);
+  prof_begin(ctx);
+  kern<<<grid, 256, smem, ctx->stream>>>(p, rows_per_tile);
+  return check_launch(ctx, "moe_gate_up_kernel");
+}
+
+template <int ACT, int LPR, int CPL, int MT>
+static int32_t launch_down(har_cuda_ctx *ctx, const MoeDev &p, int grid) {
+  const int rows_per_tile = rows_per_tile_d(p.I);
+  auto kern = moe_down_kernel<ACT, LPR, CPL, MT>;
+  const size_t smem = ActSmem<ACT>::bytes(MT, p.I);
+  set_smem(kern, smem);
+  prof_begin(ctx);
+  kern<<<grid, 256, smem, ctx->stream>>>(p, rows_per_tile);
+  return check_launch(ctx, "moe_down_kernel");
+}
+
+template <int ACT>
+static int32_t dispatch_gate_up(har_cuda_ctx *ctx, const MoeDev &p, int grid) {
+  const GemvShape s = gemv_shape(p.H);
+  constexpr int M1 = ACT == ACT_Q8K ? 4 : 1;
+  constexpr int M2 = ACT == ACT_Q8K ? 2 : 1;
+  if (s.LPR == 4) return launch_gate_up<ACT, 4, 1, M1>(ctx, p, grid);
+  if (s.LPR == 8) return launch_gate_up<ACT, 8, 1, M1>(ctx, p, grid);
+  if (s.LPR == 16) return launch_gate_up<ACT, 16, 1, M1>(ctx, p, grid);
+  if (s.CPL == 1) return launch_gate_up<ACT, 32, 1, M1>(ctx, p, grid);
+  if (s.CPL == 2) return launch_gate_up<ACT, 32, 2, M2>(ctx, p, grid);
+  return set_error(ctx, HAR_CUDA_ERR_UNSUPPORTED, "moe_ffn: hidden size above 4096");
+}
+
+template <int ACT>
+static int32_t dispatch_down(har_cuda_ctx *ctx, const MoeDev &p, int grid) {
+  const GemvShape s = gemv_shape(p.I);
+  constexpr int M1 = ACT == ACT_Q8K ? 4 : 1;
+  constexpr int M2 = ACT == ACT_Q8K ? 2 : 1;
+  if (s.LPR == 4) return launch_down<ACT, 4, 1, M1>(ctx, p, grid);
+  if (s.LPR == 8) return launch_down<ACT, 8, 1, M1>(ctx, p, grid);
+  if (s.LPR == 16) return launch_down<ACT, 16, 1, M1>(ctx, p, grid);
+  if (s.CPL == 1) return launch_down<ACT, 32, 1, M1>(ctx, p, grid);
+  if (s.CPL == 2) return launch_down<ACT, 32, 2, M2>(ctx, p, grid);
+  return set_error(ctx, HAR_CUDA_ERR_UNSUPPORTED, "moe_ffn: intermediate size above 4096");
+}
+
+static size_t al256(size_t v) { return (v + 255) & ~(size_t)255; }
+
+int32_t run_moe_ffn(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const float *x,
+                    int64_t T, int k, const int32_t *ids, const float *weights, float *y,
+                    uint32_t flags) {
+  if (flags & HAR_CUDA_MOE_FORCE_TC)
+    return set_error(ctx, HAR_CUDA_ERR_UNSUPPORTED, "moe_ffn: tensor-core path not built yet");
+  if (((uintptr_t)x & 15u) || ((uintptr_t)y & 15u))
+    return set_error(ctx, HAR_CUDA_ERR_ARG, "moe_ffn: x and y must be 16-byte aligned");
+  const bool q8 = (flags & HAR_CUDA_MOE_ACT_Q8K) != 0;
+  const int E = (int)layer->E, H = (int)layer->H, I = (int)layer->I;
+  const int64_t n = T * k;
+  const int has_sh = layer->sh_gate ? 1 : 0;
+  const int64_t slots = n + T;
+  const int64_t xq_row = (int64_t)(H / QK) * Q8K_BYTES, aq_row = (int64_t)(I / QK) * Q8K_BYTES;
+  // scratch layout
+  size_t off = 0;
+  auto take = [&](size_t bytes) { size_t o = off; off += al256(bytes); return o; };
+  const size_t o_counts = take(4 * (size_t)E), o_offsets = take(4 * (size_t)(E + 1));
+  const size_t o_order = take(4 * (size_t)n), o_inv = take(4 * (size_t)n);
+  const size_t o_ne = take(4 * (size_t)E), o_nne = take(4);
+  const size_t o_xq = q8 ? take((size_t)(T * xq_row)) : 0;
+  const size_t o_a = take(4 * (size_t)(slots * I));
+  const size_t o_aq = q8 ? take((size_t)(slots * aq_row)) : 0;
+  const size_t o_y = take(4 * (size_t)(slots * H));
+  int32_t st = ensure_scratch(ctx, off);
+  if (st) return st;
+  uint8_t *S = (uint8_t *)ctx->scratch;
+  MoeDev p;
+  p.gate = layer->gate->dev;
+  p.up = layer->up->dev;
+  p.down = layer->down->dev;
+  p.sh_gate = has_sh ? layer->sh_gate->dev : nullptr;
+  p.sh_up = has_sh ? layer->sh_up->dev : nullptr;
+  p.sh_down = has_sh ? layer->sh_down->dev : nullptr;
+  p.ebytes_gu = layer->gate->expert_bytes;
+  p.ebytes_d = layer->down->expert_bytes;
+  p.rb_h = layer->gate->row_bytes;
+  p.rb_i = layer->down->row_bytes;
+  p.E = E;
+  p.H = H;
+  p.I = I;
+  p.T = (int)T;
+  p.k = k;
+  p.n = (int)n;
+  p.has_shared = has_sh;
+  p.counts = (const int32_t *)(S + o_counts);
+  p.offsets = (const int32_t *)(S + o_offsets);
+  p.order = (const int32_t *)(S + o_order);
+  p.inv = (const int32_t *)(S + o_inv);
+  p.ne = (const int32_t *)(S + o_ne);
+  p.n_ne = (const int32_t *)(S + o_nne);
+  p.a = (float *)(S + o_a);
+  p.ybuf = (float *)(S + o_y);
+  if (q8) {
+    p.xact = S + o_xq;
+    p.xrow = xq_row;
+    p.aact = S + o_aq;
+    p.arow = aq_row;
+  } else {
+    p.xact = (const uint8_t *)x;
+    p.xrow = (int64_t)H * 4;
+    p.aact = (const uint8_t *)p.a;
+    p.arow = (int64_t)I * 4;
+  }
+  st = launch_group_full(ctx, ids, n, E, (int32_t *)(S + o_counts), (int32_t *)(S + o_offsets),
+                         (int32_t *)(S + o_order), (int32_t *)(S + o_inv), (int32_t *)(S + o_ne),
+                         (int32_t *)(S + o_nne));
+  if (st) return st;
+  if (q8 && (st = launch_q8k_quantize(ctx, x, T, H, S + o_xq))) return st;
+  const int max_groups = (int)std::min<int64_t>(E, n) + has_sh;
+  const int grid_cap = ctx->num_sms * 4;
+  {
+    const int rpt = rows_per_tile_gu(H), ntg = (I + rpt - 1) / rpt;
+    const int grid = std::max(1, std::min(grid_cap, max_groups * ntg));
+    st = q8 ? dispatch_gate_up<ACT_Q8K>(ctx, p, grid) : dispatch_gate_up<ACT_F32>(ctx, p, grid);
+    if (st) return st;
+  }
+  if (q8 && (st = launch_q8k_quantize(ctx, p.a, n + (has_sh ? T : 0), I, S + o_aq))) return st;
+  {
+    const int rpt = rows_per_tile_d(I), ntg = (H + rpt - 1) / rpt;
+    const int grid = std::max(1, std::min(grid_cap, max_groups * ntg));
+    st = q8 ? dispatch_down<ACT_Q8K>(ctx, p, grid) : dispatch_down<ACT_F32>(ctx, p, grid);
+    if (st) return st;
+  }
+  prof_begin(ctx);
+  moe_combine_kernel<<<(unsigned)T, 256, 0, ctx->stream>>>(
+      p, x, weights, layer->sh_gate_inp, y, (flags & HAR_CUDA_MOE_ADD_RESIDUAL) ? 1 : 0);
+  return check_launch(ctx, "moe_combine_kernel");
+}
+
+}  // namespace har

@@ -1,0 +1,233 @@
+// k_route.cu — router softmax + top-k, and the stable expert-major grouping.
+//
+// route_topk_kernel restates routed_moe's selection
+// (har/crates/har-demo/src/bin/har-native-qwen35moe.rs:1167-1204) with the
+// reference's f32 operation order: max fold, exp(l - max), sequential sum in
+// index order clamped to >= 1e-9, p = e / sum, order by p descending then
+// lower index, take k, renormalise by the sequential sum of the selected p
+// (clamped to >= 1e-9).  exp is the correctly rounded value (f32 result of
+// exp evaluated in double); the reference's f32::exp (glibc expf) differs
+// from it on about 1 in 11,500 inputs, which can move a weight by an ulp but
+// not the selected ids.
+//
+// group_kernel restates MoEModel::forward_batch's grouping
+// (har/crates/har-serve/src/moe.rs:195-202): groups[e] holds the entries
+// (t*k + slot) routed to e in position order.  It is a stable counting sort
+// in one CTA of 16 warps (E <= 2048): each warp owns a contiguous segment of entries,
+// counts per expert with __match_any_sync, a scan turns counts into offsets,
+// and a second pass writes positions.
+#include "har_internal.cuh"
+
+namespace har {
+
+// ---------------------------------------------------------------------------
+// route_topk: one warp per token; the warp's exps live in shared memory.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(128) route_topk_kernel(const float *__restrict__ logits,
+                                                         int64_t T, int E, int k,
+                                                         int32_t *__restrict__ ids,
+                                                         float *__restrict__ weights) {
+  extern __shared__ float rsm[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t t = (int64_t)blockIdx.x * 4 + warp;
+  if (t >= T) return;
+  float *p = rsm + (size_t)warp * E;
+  const float *l = logits + t * E;
+  float mx = -INFINITY;
+  for (int i = lane; i < E; i += 32) mx = fmaxf(mx, l[i]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  for (int i = lane; i < E; i += 32) p[i] = (float)exp((double)__fsub_rn(l[i], mx));
+  __syncwarp();
+  float den = 0.0f;
+  if (lane == 0) {
+    for (int i = 0; i < E; ++i) den = __fadd_rn(den, p[i]);  // exps.iter().sum()
+    den = fmaxf(den, ROUTER_EPS);
+  }
+  den = __shfl_sync(0xffffffffu, den, 0);
+  for (int i = lane; i < E; i += 32) p[i] = __fdiv_rn(p[i], den);
+  __syncwarp();
+  // k rounds of warp arg-max over (p desc, index asc); selected entries are
+  // marked by setting their sign bit (all p >= +0, so -p never wins).
+  int sel_id = 0;
+  float sel_p = 0.0f;
+  for (int s = 0; s < k; ++s) {
+    float bp = -1.0f;
+    int bi = 0x7fffffff;
+    for (int i = lane; i < E; i += 32) {
+      const float v = p[i];
+      if (!(__float_as_uint(v) >> 31) && (v > bp || (v == bp && i < bi))) {
+        bp = v;
+        bi = i;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float op = __shfl_xor_sync(0xffffffffu, bp, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (op > bp || (op == bp && oi < bi)) {
+        bp = op;
+        bi = oi;
+      }
+    }
+    if (lane == s) {
+      sel_id = bi;
+      sel_p = bp;
+    }
+    if (lane == 0) p[bi] = __uint_as_float(__float_as_uint(bp) | 0x80000000u);
+    __syncwarp();
+  }
+  float tot = 0.0f;
+  for (int s = 0; s < k; ++s) tot = __fadd_rn(tot, __shfl_sync(0xffffffffu, sel_p, s));
+  tot = fmaxf(tot, ROUTER_EPS);
+  if (lane < k) {
+    ids[t * k + lane] = sel_id;
+    weights[t * k + lane] = __fdiv_rn(sel_p, tot);
+  }
+}
+
+int32_t launch_route_topk(har_cuda_ctx *ctx, const float *logits, int64_t T, int E, int k,
+                          int32_t *ids, float *weights) {
+  const size_t smem = (size_t)4 * E * sizeof(float);
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(route_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  const int64_t grid = (T + 3) / 4;
+  prof_begin(ctx);
+  route_topk_kernel<<<(unsigned)grid, 128, smem, ctx->stream>>>(logits, T, E, k, ids, weights);
+  return check_launch(ctx, "route_topk_kernel");
+}
+
+// ---------------------------------------------------------------------------
+// group_kernel: stable counting sort of n = T*k entries by expert id.
+// Outputs counts[E], offsets[E+1], order[n] (entry at each grouped position),
+// inv[n] (grouped position of each entry) and, when ne != null, the list of
+// non-empty experts in expert order (ne[0..*n_ne)).  Entries with an
+// out-of-range id set DEV_ERR_BOUNDS in *status and are dropped.
+// ---------------------------------------------------------------------------
+constexpr int GROUP_WARPS = 16;
+
+__global__ void __launch_bounds__(GROUP_WARPS * 32) group_kernel(
+    const int32_t *__restrict__ ids, int n, int E, int32_t *__restrict__ counts,
+    int32_t *__restrict__ offsets, int32_t *__restrict__ order, int32_t *__restrict__ inv,
+    int32_t *__restrict__ ne, int32_t *__restrict__ n_ne, int *status) {
+  extern __shared__ __align__(16) uint8_t gsm[];
+  int32_t *cnt = reinterpret_cast<int32_t *>(gsm);                       // [W][E]
+  int32_t *off = cnt + (size_t)GROUP_WARPS * E;                             // [E+1]
+  __shared__ int32_t warp_tot[GROUP_WARPS + 1];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = threadIdx.x; i < GROUP_WARPS * E; i += blockDim.x) cnt[i] = 0;
+  __syncthreads();
+  const int seg = (n + GROUP_WARPS - 1) / GROUP_WARPS;
+  const int s0 = min(n, warp * seg), s1 = min(n, s0 + seg);
+  const unsigned lt = (1u << lane) - 1u;
+  // pass 1: per-warp counts
+  for (int b = s0; b < s1; b += 32) {
+    const int i = b + lane;
+    int e = -1;
+    if (i < s1) {
+      e = ids[i];
+      if (e < 0 || e >= E) {
+        atomicOr(status, DEV_ERR_BOUNDS);
+        e = -1;
+      }
+    }
+    const unsigned m = __match_any_sync(0xffffffffu, e);
+    if (e >= 0 && (m & lt) == 0) cnt[warp * E + e] += __popc(m);
+    __syncwarp();
+  }
+  __syncthreads();
+  // per-expert totals, then a block-wide exclusive scan in chunks of blockDim
+  for (int base = 0; base < E; base += blockDim.x) {
+    const int e = base + threadIdx.x;
+    int tot = 0;
+    if (e < E) {
+      int run = 0;
+      for (int w = 0; w < GROUP_WARPS; ++w) {
+        const int c = cnt[w * E + e];
+        cnt[w * E + e] = run;  // becomes the warp's base within expert e
+        run += c;
+      }
+      tot = run;
+      counts[e] = tot;
+    }
+    // inclusive warp scan
+    int v = tot;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int u = __shfl_up_sync(0xffffffffu, v, o);
+      if (lane >= o) v += u;
+    }
+    if (lane == 31) warp_tot[warp] = v;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int r = base == 0 ? 0 : off[base];
+      for (int w = 0; w < GROUP_WARPS; ++w) {
+        const int x = warp_tot[w];
+        warp_tot[w] = r;
+        r += x;
+      }
+      warp_tot[GROUP_WARPS] = r;
+    }
+    __syncthreads();
+    if (e < E) off[e] = warp_tot[warp] + v - tot;
+    if (threadIdx.x == 0) off[min(E, base + (int)blockDim.x)] = warp_tot[GROUP_WARPS];
+    __syncthreads();
+  }
+  for (int e = threadIdx.x; e <= E; e += blockDim.x) offsets[e] = off[e];
+  // pass 2: positions
+  for (int b = s0; b < s1; b += 32) {
+    const int i = b + lane;
+    int e = -1;
+    if (i < s1) {
+      e = ids[i];
+      if (e < 0 || e >= E) e = -1;
+    }
+    const unsigned m = __match_any_sync(0xffffffffu, e);
+    int pos = 0;
+    if (e >= 0) pos = off[e] + cnt[warp * E + e] + __popc(m & lt);
+    __syncwarp();
+    if (e >= 0) {
+      order[pos] = i;
+      inv[i] = pos;
+      if ((m & lt) == 0) cnt[warp * E + e] += __popc(m);
+    } else if (i < s1) {
+      inv[i] = -1;
+    }
+    __syncwarp();
+  }
+  // non-empty experts in expert order (warp 0, ballot + popc)
+  if (ne && warp == 0) {
+    int run = 0;
+    for (int base = 0; base < E; base += 32) {
+      const int e = base + lane;
+      const bool nz = e < E && off[e + 1] > off[e];
+      const unsigned bm = __ballot_sync(0xffffffffu, nz);
+      if (nz) ne[run + __popc(bm & lt)] = e;
+      run += __popc(bm);
+    }
+    if (lane == 0) *n_ne = run;
+  }
+}
+
+size_t group_smem_bytes(int E) {
+  return ((size_t)GROUP_WARPS * E + E + 1) * 4;
+}
+
+int32_t launch_group_full(har_cuda_ctx *ctx, const int32_t *ids, int64_t n, int E,
+                          int32_t *counts, int32_t *offsets, int32_t *order, int32_t *inv,
+                          int32_t *ne, int32_t *n_ne) {
+  const size_t smem = group_smem_bytes(E);
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  prof_begin(ctx);
+  group_kernel<<<1, GROUP_WARPS * 32, smem, ctx->stream>>>(ids, (int)n, E, counts, offsets,
+                                                           order, inv, ne, n_ne, ctx->d_status);
+  return check_launch(ctx, "group_kernel");
+}
+
+int32_t launch_group(har_cuda_ctx *ctx, const int32_t *ids, int64_t T, int k, int E,
+                     int32_t *counts, int32_t *offsets, int32_t *order, int32_t *inv) {
+  return launch_group_full(ctx, ids, T * k, E, counts, offsets, order, inv, nullptr, nullptr);
+}
+
+}  // namespace har

@@ -1,0 +1,382 @@
+"""har_cuda — Python host layer over libhar_cuda.so (the C ABI in include/har_cuda.h).
+
+The CUDA library is the product; this module binds it with ctypes and mirrors
+the reference's operator interface for the Q4_K MoE-FFN path (paths relative
+to the leoinfer/remora-lab repository):
+
+* ``CudaQ4KModel.matvec``      <- ``Q4KModel::matvec``            har/crates/har-serve/src/q4k.rs:170-188
+* ``CudaQ4KModel.batch_step``  <- ``BatchStepModel::batch_step``   har/crates/har-serve/src/adapter.rs:28-72
+* ``CudaMoeModel.expert_matvec``     <- ``expert_matvec``         har/crates/har-demo/src/bin/har-native-qwen35moe.rs:626-689
+* ``CudaMoeModel.compose_moe_route`` <- ``compose_moe_route``     har-native-qwen35moe.rs:979-1048
+* ``CudaMoeModel.routed_moe``        <- ``routed_moe``            har-native-qwen35moe.rs:1167-1215
+
+Errors are fail-closed: every non-zero status raises ``HarCudaError`` (the
+reference's GPU adapters panic, har/crates/har-serve/src/vulkan.rs:18-19).
+There is no CPU fallback: importing this module without the built library, or
+creating a context without a B200, raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libhar_cuda.so")
+
+QK_K = 256
+Q4K_BLOCK_BYTES = 144
+Q8K_BLOCK_BYTES = 292
+
+OK = 0
+ERR_ARG, ERR_GEOMETRY, ERR_CUDA, ERR_NCCL, ERR_TIMEOUT = -1, -2, -3, -4, -5
+ERR_NOT_INIT, ERR_OOM, ERR_UNSUPPORTED, ERR_DEVICE = -6, -7, -8, -9
+STATUS_NAMES = {0: "OK", -1: "ARG", -2: "GEOMETRY", -3: "CUDA", -4: "NCCL", -5: "TIMEOUT",
+                -6: "NOT_INIT", -7: "OOM", -8: "UNSUPPORTED", -9: "DEVICE"}
+
+ACT_F32 = 0
+ACT_Q8K = 1
+MOE_ADD_RESIDUAL = 0x1
+MOE_ACT_Q8K = 0x2
+MOE_FORCE_GEMV = 0x4
+MOE_FORCE_TC = 0x8
+
+# Every symbol include/har_cuda.h declares (tests check the library exports them).
+EXPORTS = [
+    "har_cuda_abi_version", "har_cuda_ctx_create", "har_cuda_ctx_destroy", "har_cuda_last_error",
+    "har_cuda_ctx_set_stream", "har_cuda_synchronize", "har_cuda_launch_count",
+    "har_cuda_weights_upload_q4k", "har_cuda_weights_wrap_q4k", "har_cuda_weights_free",
+    "har_cuda_weights_device_ptr", "har_cuda_q8k_quantize", "har_cuda_q4k_gemv",
+    "har_cuda_route_topk", "har_cuda_group_by_expert", "har_cuda_moe_layer_create",
+    "har_cuda_moe_layer_free", "har_cuda_moe_ffn", "har_cuda_moe_ffn_host", "har_cuda_moe_stack",
+    "har_cuda_gen_q4k",
+]
+
+
+class HarCudaError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"har_cuda status {status} ({STATUS_NAMES.get(status, '?')}): {message}")
+        self.status = status
+
+
+_lib = None
+
+
+def load_library() -> C.CDLL:
+    """Load libhar_cuda.so; raises if it has not been built (no fallback)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(f"libhar_cuda.so not built at {LIB_PATH}; run remora-lab_b200/build.py")
+    L = C.CDLL(LIB_PATH)
+    vp, i32, i64, u32, u64 = C.c_void_p, C.c_int32, C.c_int64, C.c_uint32, C.c_uint64
+    pp = C.POINTER(C.c_void_p)
+    sigs = {
+        "har_cuda_abi_version": (i32, []),
+        "har_cuda_ctx_create": (i32, [i32, pp]),
+        "har_cuda_ctx_destroy": (i32, [vp]),
+        "har_cuda_last_error": (i32, [vp, C.c_char_p, C.c_size_t]),
+        "har_cuda_ctx_set_stream": (i32, [vp, vp]),
+        "har_cuda_synchronize": (i32, [vp, i64]),
+        "har_cuda_launch_count": (i64, [vp]),
+        "har_cuda_weights_upload_q4k": (i32, [vp, vp, i64, i64, i64, pp]),
+        "har_cuda_weights_wrap_q4k": (i32, [vp, vp, i64, i64, i64, pp]),
+        "har_cuda_weights_free": (i32, [vp]),
+        "har_cuda_weights_device_ptr": (vp, [vp]),
+        "har_cuda_q8k_quantize": (i32, [vp, vp, i64, i64, vp]),
+        "har_cuda_q4k_gemv": (i32, [vp, vp, i64, vp, i32, i64, vp]),
+        "har_cuda_route_topk": (i32, [vp, vp, i64, i32, i32, vp, vp]),
+        "har_cuda_group_by_expert": (i32, [vp, vp, i64, i32, i32, vp, vp, vp]),
+        "har_cuda_moe_layer_create": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, pp]),
+        "har_cuda_moe_layer_free": (i32, [vp]),
+        "har_cuda_moe_ffn": (i32, [vp, vp, vp, i64, i32, vp, vp, vp, u32]),
+        "har_cuda_moe_ffn_host": (i32, [vp, vp, vp, i64, i32, vp, vp, vp, u32]),
+        "har_cuda_moe_stack": (i32, [vp, vp, i32, vp, i64, i32, vp, vp, vp, u32]),
+        "har_cuda_gen_q4k": (i32, [vp, vp, i64, i64, u64, i64, C.c_float, C.c_float]),
+    }
+    for name, (res, args) in sigs.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = L
+    return L
+
+
+def _dptr(t) -> int:
+    """Device pointer of a torch CUDA tensor (None -> NULL)."""
+    if t is None:
+        return None
+    if not t.is_cuda:
+        raise HarCudaError(ERR_ARG, "expected a CUDA tensor")
+    if not t.is_contiguous():
+        raise HarCudaError(ERR_ARG, "expected a contiguous tensor")
+    return t.data_ptr()
+
+
+def _hptr(a: np.ndarray):
+    return a.ctypes.data_as(C.c_void_p)
+
+
+class Context:
+    """One device + one stream (har/crates/har-vulkan/src/lib.rs:236 Device::open).
+
+    By default kernels run on torch's current stream of the device, so they
+    order with the caller's torch work."""
+
+    def __init__(self, device: int = 0, use_torch_stream: bool = True):
+        self.lib = load_library()
+        h = C.c_void_p()
+        st = self.lib.har_cuda_ctx_create(device, C.byref(h))
+        if st != OK:
+            raise HarCudaError(st, f"ctx_create(device={device}) failed")
+        self.handle = h
+        self.device = device
+        if use_torch_stream:
+            self.bind_torch_stream()
+
+    def bind_torch_stream(self):
+        import torch
+        s = torch.cuda.current_stream(self.device)
+        self.check(self.lib.har_cuda_ctx_set_stream(self.handle, C.c_void_p(s.cuda_stream)))
+
+    def last_error(self) -> str:
+        buf = C.create_string_buffer(1024)
+        self.lib.har_cuda_last_error(self.handle, buf, 1024)
+        return buf.value.decode(errors="replace")
+
+    def check(self, status: int):
+        if status != OK:
+            raise HarCudaError(status, self.last_error())
+
+    def synchronize(self, timeout_ms: int = 60000):
+        self.check(self.lib.har_cuda_synchronize(self.handle, timeout_ms))
+
+    @property
+    def launch_count(self) -> int:
+        return int(self.lib.har_cuda_launch_count(self.handle))
+
+    def close(self):
+        if getattr(self, "handle", None):
+            self.lib.har_cuda_ctx_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # ---- weights --------------------------------------------------------
+    def upload_q4k(self, host_bytes: np.ndarray, E: int, N: int, K: int) -> "Q4KWeights":
+        host_bytes = np.ascontiguousarray(host_bytes, np.uint8)
+        if host_bytes.size != E * N * (K // QK_K) * Q4K_BLOCK_BYTES:
+            raise HarCudaError(ERR_GEOMETRY, "Q4_K byte count does not match E*N*K/256*144")
+        h = C.c_void_p()
+        self.check(self.lib.har_cuda_weights_upload_q4k(self.handle, _hptr(host_bytes), E, N, K,
+                                                        C.byref(h)))
+        return Q4KWeights(self, h, E, N, K)
+
+    def wrap_q4k(self, dev_tensor, E: int, N: int, K: int) -> "Q4KWeights":
+        h = C.c_void_p()
+        self.check(self.lib.har_cuda_weights_wrap_q4k(self.handle, _dptr(dev_tensor), E, N, K,
+                                                      C.byref(h)))
+        w = Q4KWeights(self, h, E, N, K)
+        w.keepalive = dev_tensor
+        return w
+
+    def gen_q4k(self, dev_tensor, rows: int, K: int, seed: int, row0: int = 0,
+                mean: float = 0.0, std: float = 0.02):
+        self.check(self.lib.har_cuda_gen_q4k(self.handle, _dptr(dev_tensor), rows, K, seed, row0,
+                                             mean, std))
+
+    # ---- kernels ----------------------------------------------------------
+    def q8k_quantize(self, x, out):
+        M, K = x.shape
+        self.check(self.lib.har_cuda_q8k_quantize(self.handle, _dptr(x), M, K, _dptr(out)))
+        return out
+
+    def q4k_gemv(self, w: "Q4KWeights", expert: int, x, act_kind: int, M: int, y):
+        self.check(self.lib.har_cuda_q4k_gemv(self.handle, w.handle, expert, _dptr(x), act_kind, M,
+                                              _dptr(y)))
+        return y
+
+    def route_topk(self, logits, k: int, ids, weights):
+        T, E = logits.shape
+        self.check(self.lib.har_cuda_route_topk(self.handle, _dptr(logits), T, E, k, _dptr(ids),
+                                                _dptr(weights)))
+        return ids, weights
+
+    def group_by_expert(self, ids, E: int, counts, offsets, order):
+        T, k = ids.shape
+        self.check(self.lib.har_cuda_group_by_expert(self.handle, _dptr(ids), T, k, E,
+                                                     _dptr(counts), _dptr(offsets), _dptr(order)))
+
+    def moe_layer(self, gate, up, down, shared=None, sh_gate_inp=None) -> "MoeLayer":
+        sg, su, sd = (None, None, None) if shared is None else shared
+        h = C.c_void_p()
+        self.check(self.lib.har_cuda_moe_layer_create(
+            self.handle, gate.handle, up.handle, down.handle,
+            sg.handle if sg else None, su.handle if su else None, sd.handle if sd else None,
+            _dptr(sh_gate_inp), C.byref(h)))
+        return MoeLayer(self, h, (gate, up, down, sg, su, sd, sh_gate_inp))
+
+    def moe_ffn(self, layer: "MoeLayer", x, ids, weights, y, flags: int = 0):
+        T, k = ids.shape
+        self.check(self.lib.har_cuda_moe_ffn(self.handle, layer.handle, _dptr(x), T, k, _dptr(ids),
+                                             _dptr(weights), _dptr(y), flags))
+        return y
+
+    def moe_ffn_host(self, layer: "MoeLayer", x: np.ndarray, ids: np.ndarray,
+                     weights: np.ndarray, flags: int = 0) -> np.ndarray:
+        x = np.ascontiguousarray(x, np.float32)
+        ids = np.ascontiguousarray(ids, np.int32)
+        weights = np.ascontiguousarray(weights, np.float32)
+        T, k = ids.shape
+        y = np.empty_like(x)
+        self.check(self.lib.har_cuda_moe_ffn_host(self.handle, layer.handle, _hptr(x), T, k,
+                                                  _hptr(ids), _hptr(weights), _hptr(y), flags))
+        return y
+
+    def moe_stack(self, layers, x, ids, weights, y, flags: int = 0):
+        L = len(layers)
+        arr = (C.c_void_p * L)(*[l.handle.value for l in layers])
+        _, T, k = ids.shape
+        self.check(self.lib.har_cuda_moe_stack(self.handle, arr, L, _dptr(x), T, k, _dptr(ids),
+                                               _dptr(weights), _dptr(y), flags))
+        return y
+
+
+class Q4KWeights:
+    """A device-resident Q4_K tensor [E][N][K/256] (GGUF `*_exps` layout)."""
+
+    def __init__(self, ctx: Context, handle, E, N, K):
+        self.ctx, self.handle, self.E, self.N, self.K = ctx, handle, E, N, K
+        self.row_bytes = K // QK_K * Q4K_BLOCK_BYTES
+        self.keepalive = None
+
+    @property
+    def nbytes(self) -> int:
+        return self.E * self.N * self.row_bytes
+
+    def free(self):
+        if self.handle:
+            self.ctx.lib.har_cuda_weights_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+class MoeLayer:
+    def __init__(self, ctx: Context, handle, refs):
+        self.ctx, self.handle, self.refs = ctx, handle, refs
+
+    def free(self):
+        if self.handle:
+            self.ctx.lib.har_cuda_moe_layer_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+# ---------------------------------------------------------------------------
+# Reference-interface mirror
+# ---------------------------------------------------------------------------
+
+class CudaQ4KModel:
+    """The serving-seam model of har/crates/har-serve/src/q4k.rs:129-220 with
+    its matvec on the GPU (the role VulkanBatchedModel plays,
+    har/crates/har-serve/src/vulkan.rs:286-493): one GEMV launch per step for
+    the whole batch, weights read once per step."""
+
+    def __init__(self, ctx: Context, blocks: np.ndarray, rows: int, dim: int, embed: np.ndarray,
+                 eos: int, act_kind: int = ACT_F32):
+        import torch
+        if dim % QK_K:
+            raise HarCudaError(ERR_GEOMETRY, "dim must be super-block-aligned")
+        self.ctx, self.rows, self.dim, self.eos, self.act_kind = ctx, rows, dim, eos, act_kind
+        self.w = ctx.upload_q4k(blocks, 1, rows, dim)
+        self.embed = np.ascontiguousarray(embed, np.float32).reshape(-1, dim)
+        self._torch = torch
+
+    def matvec(self, x: np.ndarray) -> np.ndarray:
+        """Q4KModel::matvec for a batch: rows of x [M][dim] -> [M][rows]."""
+        torch = self._torch
+        x = np.ascontiguousarray(x, np.float32).reshape(-1, self.dim)
+        M = x.shape[0]
+        dev = torch.device("cuda", self.ctx.device)
+        xd = torch.from_numpy(x).to(dev)
+        y = torch.empty((M, self.rows), dtype=torch.float32, device=dev)
+        if self.act_kind == ACT_Q8K:
+            xq = torch.empty((M, self.dim // QK_K * Q8K_BLOCK_BYTES), dtype=torch.uint8, device=dev)
+            self.ctx.q8k_quantize(xd, xq)
+            self.ctx.q4k_gemv(self.w, 0, xq, ACT_Q8K, M, y)
+        else:
+            self.ctx.q4k_gemv(self.w, 0, xd, ACT_F32, M, y)
+        return y.cpu().numpy()
+
+    def batch_step(self, inputs):
+        """BatchStepModel::batch_step: x = h + E[t]; logits = W x; next = x."""
+        xs = np.stack([np.asarray(h, np.float32) + self.embed[t] for h, t in inputs])
+        logits = self.matvec(xs)
+        return [(xs[i], logits[i]) for i in range(len(inputs))]
+
+    def initial_hidden(self):
+        return np.zeros(self.dim, np.float32)
+
+    def weight_bytes_per_row(self) -> int:
+        return self.rows * (self.dim // QK_K) * Q4K_BLOCK_BYTES
+
+
+class CudaMoeModel:
+    """Per-layer expert tensors on the device with the reference's expert-FFN
+    entry points (har-native-qwen35moe.rs:626-689, 979-1048, 1167-1215)."""
+
+    def __init__(self, ctx: Context, layers, E: int, H: int, I: int, k: int, flags: int = 0):
+        self.ctx, self.layers, self.E, self.H, self.I, self.k = ctx, layers, E, H, I, k
+        self.flags = flags
+        import torch
+        self._torch = torch
+
+    def _dev(self, a, dtype):
+        torch = self._torch
+        return torch.as_tensor(np.ascontiguousarray(a), dtype=dtype).to(
+            torch.device("cuda", self.ctx.device))
+
+    def expert_matvec(self, w: Q4KWeights, expert: int, x: np.ndarray) -> np.ndarray:
+        torch = self._torch
+        if x.shape[-1] != w.K:
+            raise HarCudaError(ERR_GEOMETRY, f"expert matvec shape mismatch: K={w.K} input={x.shape[-1]}")
+        if not 0 <= expert < w.E:
+            raise HarCudaError(ERR_ARG, f"expert {expert} exceeds model expert count {w.E}")
+        xd = self._dev(x.reshape(1, -1), torch.float32)
+        y = torch.empty((1, w.N), dtype=torch.float32, device=xd.device)
+        self.ctx.q4k_gemv(w, expert, xd, ACT_F32, 1, y)
+        return y.cpu().numpy()[0]
+
+    def compose_moe_route(self, layer: int, x: np.ndarray, experts, weights) -> np.ndarray:
+        if len(experts) != len(weights) or len(experts) != self.k:
+            raise HarCudaError(ERR_GEOMETRY, "route geometry is invalid")
+        y = self.ctx.moe_ffn_host(self.layers[layer], np.asarray(x, np.float32).reshape(1, -1),
+                                  np.asarray(experts, np.int32).reshape(1, -1),
+                                  np.asarray(weights, np.float32).reshape(1, -1), self.flags)
+        return y[0]
+
+    def routed_moe(self, layer: int, x: np.ndarray, router_logits: np.ndarray):
+        """Router top-k on the GPU, then compose_moe_route; returns (out, ids, weights)."""
+        torch = self._torch
+        lg = self._dev(np.asarray(router_logits, np.float32).reshape(1, -1), torch.float32)
+        ids = torch.empty((1, self.k), dtype=torch.int32, device=lg.device)
+        w = torch.empty((1, self.k), dtype=torch.float32, device=lg.device)
+        self.ctx.route_topk(lg, self.k, ids, w)
+        ids_h, w_h = ids.cpu().numpy(), w.cpu().numpy()
+        return self.compose_moe_route(layer, x, ids_h[0], w_h[0]), ids_h[0], w_h[0]

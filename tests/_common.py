@@ -1,0 +1,49 @@
+"""Shared helpers for the parity tests.
+
+Tolerances (the north star's "max relative error 1e-3, f32 accumulation-order
+tolerance", with the denominator the survey recommends so that near-zero
+outputs do not blow it up):
+  rel_max = max|got - ref| / max|ref|
+and the reference's own differential verdict (har/crates/har-execution/src/lib.rs:185-195,285-299):
+  normalized RMS = rms(got - ref) / rms(ref) <= 5e-5, max|got - ref| <= 5e-3.
+"""
+import json
+import os
+
+import numpy as np
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+REL_MAX_TOL = 1e-3
+
+
+def kats():
+    with open(os.path.join(GOLDEN, "reference_kats.json")) as f:
+        return json.load(f)
+
+
+def golden():
+    return np.load(os.path.join(GOLDEN, "oracle_vectors.npz"))
+
+
+def rel_max(got, ref) -> float:
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    return float(np.max(np.abs(got - ref)) / max(np.max(np.abs(ref)), 1e-30))
+
+
+def verdict(got, ref):
+    """(normalized_rms, max_abs) exactly as har-execution's errors() computes them."""
+    got = np.asarray(got, np.float64).ravel()
+    ref = np.asarray(ref, np.float64).ravel()
+    d = got - ref
+    rms = np.sqrt(np.mean(d * d))
+    rref = np.sqrt(np.mean(ref * ref))
+    return float(rms / max(rref, 1e-12)), float(np.max(np.abs(d)))
+
+
+def assert_close(got, ref, rel=REL_MAX_TOL, nrms=5e-5, what=""):
+    r = rel_max(got, ref)
+    n, m = verdict(got, ref)
+    assert r <= rel, f"{what}: max|d|/max|ref| = {r:.3e} > {rel:.1e}"
+    if nrms is not None:
+        assert n <= nrms, f"{what}: normalized RMS {n:.3e} > {nrms:.1e}"
