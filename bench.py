@@ -1,0 +1,490 @@
+#!/usr/bin/env python
+"""bench.py — Q4_K MoE-FFN tokens/s and weight GB/s vs HBM peak on B200.
+
+Default workload ("config 5"): the 48-layer
+Alice-shaped MoE FFN stack, attention omitted — per layer 512 experts (top-10)
++ one shared expert with a sigmoid gate row, hidden 2048, intermediate 512,
+all Q4_K from N(0,0.02); 256 tokens with Zipf(1.1) routing drawn independently
+per layer; residual add between layers (y = x + moe(x), as execute_layer_cpu).
+A step is one pass of the 256 tokens through all 48 layers.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--config 1..5] [--act f32|q8k]
+
+One JSON line on rank 0.  `value` is the device-timed throughput with inputs
+resident in HBM (CUDA graph replay, CUDA events, max over ranks); `e2e` is the
+same metric through the C ABI's host-buffer entry point (host<->device copies
+inside the timed region).  `--impl reference` times the reference's CPU path
+(the oracle's C restatement, all host threads) on a bounded sample.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "remora-lab_b200"))
+
+E, H, I, TOPK = 512, 2048, 512, 10
+EXPERT_BYTES = (2 * I * (H // 256) + H * (I // 256)) * 144  # gate + up + down = 1,769,472 B
+METRIC = "Q4_K MoE-FFN tokens/s (+ weight GB/s vs HBM peak)"
+
+CONFIGS = {
+    1: dict(name="config1: single Q4_K GEMV 4096x4096, batch 1", layers=1, T=1),
+    2: dict(name="config2: one Alice-shaped MoE layer, decode batch 1, uniform top-10", layers=1, T=1),
+    3: dict(name="config3: one MoE layer, 64 concurrent tokens, Zipf(1.1) top-10", layers=1, T=64),
+    4: dict(name="config4: one MoE layer, prefill 4096 tokens, uniform top-10", layers=1, T=4096),
+    5: dict(name="config5: 48-layer Alice-shaped MoE FFN stack, 256 tokens, Zipf(1.1) top-10",
+            layers=48, T=256),
+}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", type=int, choices=sorted(CONFIGS), default=5)
+    ap.add_argument("--act", choices=["f32", "q8k"], default="q8k")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0,
+                    help="target CPU time of the cpu_baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-only", action="store_true",
+                    help="run warm-up + a few steps only (for ncu launch lists)")
+    ap.add_argument("--layers", type=int, default=None,
+                    help="override the layer count (small ncu captures only; the bench "
+                         "line always uses the config's 48)")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# synthetic inputs (seeded; the oracle consumes the same bytes in cpu_baseline)
+# ---------------------------------------------------------------------------
+
+def zipf_routing(seed: int, T: int, n_exp: int, k: int, s: float = 1.1):
+    """Zipf(s) top-k distinct expert ids per token; ranks mapped through a seeded
+    permutation (hot experts spread over expert-parallel shards); weights are
+    a softmax over seeded N(0,1) logits of the k selected."""
+    rng = np.random.default_rng(seed)
+    p = np.arange(1, n_exp + 1, dtype=np.float64) ** (-s)
+    p /= p.sum()
+    perm = rng.permutation(n_exp).astype(np.int32)
+    ids = np.empty((T, k), np.int32)
+    for t in range(T):
+        got = []
+        while len(got) < k:
+            draw = rng.choice(n_exp, size=2 * k, p=p)
+            for d in draw:
+                e = int(perm[d])
+                if e not in got:
+                    got.append(e)
+                    if len(got) == k:
+                        break
+        ids[t] = got
+    lg = rng.standard_normal((T, k))
+    w = np.exp(lg - lg.max(axis=1, keepdims=True))
+    w = (w / w.sum(axis=1, keepdims=True)).astype(np.float32)
+    return ids, w
+
+
+def uniform_routing(seed: int, T: int, n_exp: int, k: int):
+    """Top-k of a softmax over seeded N(0,1) logits (distinct, uniform over experts);
+    weights renormalised over the selected, as routed_moe computes them."""
+    rng = np.random.default_rng(seed)
+    lg = rng.standard_normal((T, n_exp)).astype(np.float32)
+    ids = np.argsort(-lg, axis=1, kind="stable")[:, :k].astype(np.int32)
+    sel = np.take_along_axis(lg, ids, axis=1).astype(np.float64)
+    w = np.exp(sel - sel.max(axis=1, keepdims=True))
+    return ids, (w / w.sum(axis=1, keepdims=True)).astype(np.float32)
+
+
+# ---------------------------------------------------------------------------
+# clocks sampler (nvidia-smi during the timed region)
+# ---------------------------------------------------------------------------
+
+class Clocks:
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.lines = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.device)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for ln in self.proc.stdout:
+            self.lines.append(ln.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# the stack on the device
+# ---------------------------------------------------------------------------
+
+def build_stack(ctx, torch, cfg_id: int, rank: int, n_layers=None):
+    """Weights generated on the device (the library's generator), routing and
+    activations on the host with numpy."""
+    dev = torch.device("cuda", ctx.device)
+    cfg = CONFIGS[cfg_id]
+    L, T = n_layers or cfg["layers"], cfg["T"]
+    layers, keep, dist = [], [], []
+    import har_cuda  # noqa: F401
+    for l in range(L):
+        seed = 1000 + 17 * l
+        t = {}
+        for name, rows, K in (("gate", E * I, H), ("up", E * I, H), ("down", E * H, I),
+                              ("sg", I, H), ("su", I, H), ("sd", H, I)):
+            buf = torch.empty(rows * (K // 256) * 144, dtype=torch.uint8, device=dev)
+            ctx.gen_q4k(buf, rows, K, seed + len(t))
+            t[name] = buf
+        gi = torch.from_numpy(np.random.default_rng(seed).standard_normal(H).astype(np.float32)
+                              * np.float32(0.02)).to(dev)
+        wg = ctx.wrap_q4k(t["gate"], E, I, H)
+        wu = ctx.wrap_q4k(t["up"], E, I, H)
+        wd = ctx.wrap_q4k(t["down"], E, H, I)
+        sh = (ctx.wrap_q4k(t["sg"], 1, I, H), ctx.wrap_q4k(t["su"], 1, I, H),
+              ctx.wrap_q4k(t["sd"], 1, H, I))
+        layers.append(ctx.moe_layer(wg, wu, wd, sh, gi))
+        keep.append((t, gi))
+    rng = np.random.default_rng(77 + rank)
+    x = rng.standard_normal((T, H)).astype(np.float32)
+    ids = np.empty((L, T, TOPK), np.int32)
+    w = np.empty((L, T, TOPK), np.float32)
+    for l in range(L):
+        if cfg_id in (3, 5):
+            ids[l], w[l] = zipf_routing(500 + 31 * l + 1000 * rank, T, E, TOPK)
+        else:
+            ids[l], w[l] = uniform_routing(500 + 31 * l + 1000 * rank, T, E, TOPK)
+        dist.append(len(np.unique(ids[l])))
+    torch.cuda.synchronize()
+    return layers, keep, x, ids, w, dist
+
+
+def cpu_sample(torch, keep, x, ids, w, seconds: float):
+    """The reference's CPU path (oracle restatement of compose_moe_route with
+    expert_matvec's per-call row-chunk threads over all host cores) on the
+    same weights, routing and tokens, one token at a time, layer after layer,
+    for about `seconds` of host time (weight copies to the host not timed).
+    Returns (token-layers per second, token-layers done, seconds, layers, cores)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import haro
+    cores = haro.online_cpus()
+    done, dt, nl = 0, 0.0, 0
+    for layer in range(len(keep)):
+        t, gi = keep[layer]
+        rb = lambda name, rows, K: t[name].cpu().numpy().reshape(rows, K // 256 * 144)  # noqa: E731
+        hg, hu, hd = rb("gate", E * I, H), rb("up", E * I, H), rb("down", E * H, I)
+        sh = (rb("sg", I, H), rb("su", I, H), rb("sd", H, I))
+        gih = gi.cpu().numpy()
+        nl += 1
+        for n in range(x.shape[0]):
+            t0 = time.perf_counter()
+            haro.moe_ffn(hg, hu, hd, sh, gih, E, H, I, x[n:n + 1], ids[layer, n:n + 1],
+                         w[layer, n:n + 1], add_residual=True, threads=0)
+            dt += time.perf_counter() - t0
+            done += 1
+            if dt >= seconds:
+                return done / dt, done, dt, nl, cores
+    return done / dt, done, dt, nl, cores
+
+
+def run_ours(args, torch):
+    import har_cuda
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    ctx = har_cuda.Context(local, use_torch_stream=False)
+    cfg = CONFIGS[args.config]
+    if args.config != 5:
+        raise SystemExit("bench.py times config 5; configs 1-4 are parity-test cases "
+                         "(tests/test_gpu_*.py)")
+    if args.layers and not args.profile_only:
+        raise SystemExit("--layers is only for --profile-only captures")
+    layers, keep, x, ids, w, distinct = build_stack(ctx, torch, args.config, rank, args.layers)
+    L, T = len(layers), cfg["T"]
+    flags = har_cuda.MOE_ADD_RESIDUAL | (har_cuda.MOE_ACT_Q8K if args.act == "q8k" else 0)
+    dev = torch.device("cuda", local)
+    xd = torch.from_numpy(x).to(dev)
+    idd = torch.from_numpy(ids).to(dev)
+    wd = torch.from_numpy(w).to(dev)
+    yd = torch.empty_like(xd)
+    stream = torch.cuda.Stream(dev)
+    ctx.lib.har_cuda_ctx_set_stream(ctx.handle, __import__("ctypes").c_void_p(stream.cuda_stream))
+
+    # eager warm-up (allocates the scratch arena), then capture one step in a graph
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            ctx.moe_stack(layers, xd, idd, wd, yd, flags)
+    ctx.synchronize()
+    torch.cuda.synchronize()
+    n0 = ctx.launch_count
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        ctx.moe_stack(layers, xd, idd, wd, yd, flags)
+    launches_per_step = ctx.launch_count - n0
+    torch.cuda.synchronize()
+
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, args.warmup)):
+            g.replay()
+    torch.cuda.synchronize()
+    if args.profile_only:
+        with torch.cuda.stream(stream):
+            for _ in range(args.steps):
+                g.replay()
+        torch.cuda.synchronize()
+        return None
+
+    clocks = Clocks(local)
+    clocks.start()
+    time.sleep(0.5)  # let the sampler come up before the timed region
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        ev0.record(stream)
+        for _ in range(args.steps):
+            g.replay()
+        ev1.record(stream)
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    if dist:
+        dist.barrier()
+    clk = clocks.stop()
+    if dist:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+
+    # per-kernel durations: one eager step with the library's CUDA-event profiling
+    ctx.profile_begin()
+    with torch.cuda.stream(stream):
+        ctx.moe_stack(layers, xd, idd, wd, yd, flags)
+    prof = ctx.profile_end()
+    kern = {}
+    for name, t_ms in prof:
+        a = kern.setdefault(name, [0, 0.0])
+        a[0] += 1
+        a[1] += t_ms
+    total_k = sum(v[1] for v in kern.values())
+
+    # e2e: the host-buffer C-ABI call (copies inside the timed region)
+    e2e_steps = max(3, min(args.steps, 20))
+    for _ in range(2):
+        ctx.moe_stack_host(layers, x, ids, w, flags)
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        ctx.moe_stack_host(layers, x, ids, w, flags)
+    e2e_ms = (time.perf_counter() - t0) * 1e3 / e2e_steps
+    if dist:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+
+    # algorithmic bytes: each distinct routed expert + the shared expert, once per layer
+    step_bytes = sum((d + 1) * EXPERT_BYTES for d in distinct)
+    gu_bytes = [(d + 1) * 2 * I * (H // 256) * 144 for d in distinct]
+    peaks = load_peaks()
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
+    gu = kern.get("moe_gate_up_kernel", [1, 1.0])
+    achieved = (sum(gu_bytes) / gu[0]) / (gu[1] / gu[0] * 1e-3) / 1e9
+    traffic = load_traffic("moe_gate_up_kernel")
+    out = None
+    if rank == 0:
+        tokens_per_s = world * T / (ms * 1e-3)
+        out = {
+            "metric": METRIC, "value": round(tokens_per_s, 1), "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8 x q4 (dp4a) -> i32, f32 combine" if args.act == "q8k" else "f32",
+            "data": "synthetic: N(0,0.02) weights quantised to Q4_K on device; N(0,1) f32 "
+                    "activations; Zipf(1.1) top-10 routing drawn per layer",
+            "config": {"workload": cfg["name"], "tokens_per_rank": T, "layers": L, "experts": E,
+                       "hidden": H, "intermediate": I, "top_k": TOPK, "shared_expert": True,
+                       "activations": args.act, "parallelism": "replicas" if world > 1 else "single",
+                       "l2": "inputs larger than L2 (%.1f GB of Q4_K weights read per step)"
+                             % (step_bytes / 1e9),
+                       "graph": "one CUDA graph per step"},
+            "weight_gbs": round(step_bytes / (ms * 1e-3) / 1e9, 1),
+            "hbm_frac": round(step_bytes / (ms * 1e-3) / 1e9 / hbm, 4),
+            "roofline": {"bound": "hbm", "kernel": "moe_gate_up_kernel",
+                         "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(achieved / hbm, 4), "peak_source": peak_src,
+                         "traffic": traffic,
+                         "algorithmic_bytes_per_launch": int(sum(gu_bytes) / len(gu_bytes)),
+                         "avg_launch_ms": round(gu[1] / gu[0], 4)},
+            "kernels": {k: {"launches": v[0], "ms": round(v[1], 4),
+                            "share": round(v[1] / total_k, 4)} for k, v in sorted(kern.items())},
+            "e2e": {"value": round(world * T / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
+                    "ms_per_step": round(e2e_ms, 4),
+                    "h2d_bytes_per_step": int(x.nbytes + ids.nbytes + w.nbytes),
+                    "d2h_bytes_per_step": int(x.nbytes)},
+            "clocks": clk,
+            "gpu_launches": int(launches_per_step * args.steps),
+            "distinct_experts_per_layer": {"min": min(distinct), "max": max(distinct),
+                                           "mean": round(sum(distinct) / len(distinct), 1)},
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            tps, n, dt, nl, cores = cpu_sample(torch, keep, x, ids, w, args.cpu_seconds)
+            out["cpu_baseline"] = {
+                "value": round(tps / L, 3), "unit": "tokens/s", "cores": cores, "kind": "port",
+                "sample": f"{n} token-layers of the same stack (layers 0..{nl - 1}, tokens one "
+                          f"at a time, {dt:.1f} s of host time): oracle compose_moe_route with "
+                          f"expert_matvec row threads over {cores} cores; token-layers/s / {L}"}
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return out
+
+
+def run_reference(args):
+    """Reference arm: the reference's CPU path for this workload (the oracle's
+    C restatement of compose_moe_route; HAR's Rust cannot be built here), all
+    host threads, each step a bounded sample of one token through one layer."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return None
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import haro
+    cfg = CONFIGS[args.config]
+    L, T = cfg["layers"], cfg["T"]
+    tok = 2  # tokens per step
+    ids, w = zipf_routing(500, T, E, TOPK)
+    used = sorted(set(ids[:tok].ravel().tolist()))
+    remap = {e: i for i, e in enumerate(used)}
+    Eu = len(used)
+    # weights of the used experts only (the CPU path reads nothing else)
+    hg = np.concatenate([haro.gen_q4k(1000, I, H, row0=e * I) for e in used])
+    hu = np.concatenate([haro.gen_q4k(1001, I, H, row0=e * I) for e in used])
+    hd = np.concatenate([haro.gen_q4k(1002, H, I, row0=e * H) for e in used])
+    sh = (haro.gen_q4k(1003, I, H), haro.gen_q4k(1004, I, H), haro.gen_q4k(1005, H, I))
+    gi = haro.normal_f32(1006, 0, H, 0.0, 0.02)
+    x = np.random.default_rng(77).standard_normal((tok, H)).astype(np.float32)
+    lid = np.vectorize(remap.get)(ids[:tok]).astype(np.int32)
+    cores = haro.online_cpus()
+
+    def step():
+        haro.moe_ffn(hg, hu, hd, sh, gi, Eu, H, I, x, lid, w[:tok], add_residual=True, threads=0)
+
+    for _ in range(max(1, args.warmup)):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = (time.perf_counter() - t0) / args.steps
+    tps = tok / dt / L
+    return {
+        "impl": "reference", "metric": METRIC, "value": round(tps, 3), "unit": "tokens/s",
+        "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: N(0,0.02) Q4_K weights, N(0,1) activations, Zipf(1.1) routing",
+        "config": {"workload": cfg["name"], "layers": L, "experts": E, "hidden": H,
+                   "intermediate": I, "top_k": TOPK, "shared_expert": True},
+        "cpu_baseline": {"value": round(tps, 3), "unit": "tokens/s", "cores": cores,
+                         "kind": "port",
+                         "sample": f"each step: {tok} tokens through one layer (compose_moe_route, "
+                                   f"expert_matvec row threads over {cores} cores); "
+                                   f"tokens/s scaled by 1/{L} layers"},
+        "e2e": {"value": round(tps, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return json.load(f)
+    except (OSError, ValueError):
+        return {}
+
+
+def load_traffic(kernel: str):
+    """DRAM bytes per launch of `kernel` from the committed ncu summary, if any."""
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return d.get(kernel, {}).get("traffic_bytes_per_launch")
+    except (OSError, ValueError):
+        return None
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        out = run_reference(args)
+    else:
+        import torch
+        out = run_ours(args, torch)
+    if out is not None:
+        print(json.dumps(out), flush=True)
+
+
+if __name__ == "__main__":
+    main()

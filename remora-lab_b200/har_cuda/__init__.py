@@ -50,7 +50,8 @@ EXPORTS = [
     "har_cuda_weights_device_ptr", "har_cuda_q8k_quantize", "har_cuda_q4k_gemv",
     "har_cuda_route_topk", "har_cuda_group_by_expert", "har_cuda_moe_layer_create",
     "har_cuda_moe_layer_free", "har_cuda_moe_ffn", "har_cuda_moe_ffn_host", "har_cuda_moe_stack",
-    "har_cuda_gen_q4k",
+    "har_cuda_gen_q4k", "har_cuda_moe_stack_host", "har_cuda_profile_begin",
+    "har_cuda_profile_end",
 ]
 
 
@@ -95,6 +96,9 @@ def load_library() -> C.CDLL:
         "har_cuda_moe_ffn_host": (i32, [vp, vp, vp, i64, i32, vp, vp, vp, u32]),
         "har_cuda_moe_stack": (i32, [vp, vp, i32, vp, i64, i32, vp, vp, vp, u32]),
         "har_cuda_gen_q4k": (i32, [vp, vp, i64, i64, u64, i64, C.c_float, C.c_float]),
+        "har_cuda_moe_stack_host": (i32, [vp, vp, i32, vp, i64, i32, vp, vp, vp, u32]),
+        "har_cuda_profile_begin": (i32, [vp]),
+        "har_cuda_profile_end": (i32, [vp, C.c_char_p, C.c_size_t, vp, i64, C.POINTER(C.c_int64)]),
     }
     for name, (res, args) in sigs.items():
         fn = getattr(L, name)
@@ -238,6 +242,31 @@ class Context:
         self.check(self.lib.har_cuda_moe_ffn_host(self.handle, layer.handle, _hptr(x), T, k,
                                                   _hptr(ids), _hptr(weights), _hptr(y), flags))
         return y
+
+    def moe_stack_host(self, layers, x: np.ndarray, ids: np.ndarray, weights: np.ndarray,
+                       flags: int = 0) -> np.ndarray:
+        x = np.ascontiguousarray(x, np.float32)
+        ids = np.ascontiguousarray(ids, np.int32)
+        weights = np.ascontiguousarray(weights, np.float32)
+        L, T, k = ids.shape
+        arr = (C.c_void_p * L)(*[l.handle.value for l in layers])
+        y = np.empty_like(x)
+        self.check(self.lib.har_cuda_moe_stack_host(self.handle, arr, L, _hptr(x), T, k,
+                                                    _hptr(ids), _hptr(weights), _hptr(y), flags))
+        return y
+
+    def profile_begin(self):
+        self.check(self.lib.har_cuda_profile_begin(self.handle))
+
+    def profile_end(self, cap: int = 1 << 16):
+        """[(kernel name, milliseconds)] for every launch since profile_begin."""
+        names = C.create_string_buffer(cap * 32)
+        ms = np.zeros(cap, np.float32)
+        n = C.c_int64()
+        self.check(self.lib.har_cuda_profile_end(self.handle, names, len(names), _hptr(ms), cap,
+                                                 C.byref(n)))
+        lst = names.value.decode().split("\n")[:n.value]
+        return list(zip(lst, ms[:n.value].tolist()))
 
     def moe_stack(self, layers, x, ids, weights, y, flags: int = 0):
         L = len(layers)
