@@ -153,6 +153,22 @@ int32_t har_cuda_moe_ffn_host(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer
                               const float *x_host, int64_t T, int32_t k,
                               const int32_t *ids_host, const float *weights_host,
                               float *y_host, uint32_t flags);
+/* har_cuda_moe_ffn without any device allocation.  No counterpart in the
+ * reference: it exists for callers that cannot call cudaMalloc — runtimes that
+ * reserve the GPU's memory up front for their own pools, and hot loops that
+ * cannot take the synchronisation an allocation may imply.  Scratch comes from
+ * a static device array of HAR_CUDA_NOALLOC_SCRATCH_BYTES held by every GPU
+ * that loads the library until exit; calls needing more return
+ * HAR_CUDA_ERR_GEOMETRY (about T <= 256 tokens at H = 2048, I = 512, k = 10).
+ * The first call on a device looks up the array's address (make it before any
+ * stream capture).  All calls on a device share the array: calls that overlap
+ * on the GPU race and must be serialised by the caller.  Arguments, results
+ * and error behaviour are those of har_cuda_moe_ffn. */
+#define HAR_CUDA_NOALLOC_SCRATCH_BYTES (32u << 20)
+int32_t har_cuda_moe_ffn_noalloc(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer,
+                                 const float *x_dev, int64_t T, int32_t k,
+                                 const int32_t *ids_dev, const float *weights_dev, float *y_dev,
+                                 uint32_t flags);
 /* A stack of L layers applied in order (y_l = moe_l(y_{l-1}) [+ residual]),
  * ids/weights [L][T][k]; x_dev and y_dev may alias.  Attention and norms
  * between layers are outside this path. */

@@ -455,8 +455,10 @@ int32_t har_cuda_moe_layer_free(har_cuda_moe_layer *layer) {
   return HAR_CUDA_OK;
 }
 
-static int32_t check_moe_args(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, int64_t T,
-                              int32_t k, uint32_t flags) {
+}  // extern "C"
+
+int32_t har::check_moe_args(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, int64_t T,
+                            int32_t k, uint32_t flags) {
   if (!ctx) return HAR_CUDA_ERR_ARG;
   if (!layer) return set_error(ctx, HAR_CUDA_ERR_ARG, "moe_ffn: layer is null");
   if (T < 0 || k <= 0 || k > layer->E)
@@ -468,6 +470,8 @@ static int32_t check_moe_args(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer
   if (flags & ~0xFu) return set_error(ctx, HAR_CUDA_ERR_ARG, "moe_ffn: unknown flag bits");
   return HAR_CUDA_OK;
 }
+
+extern "C" {
 
 int32_t har_cuda_moe_ffn(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer,
                          const float *x_dev, int64_t T, int32_t k, const int32_t *ids_dev,

@@ -164,6 +164,12 @@ int32_t launch_group(har_cuda_ctx *ctx, const int32_t *ids, int64_t T, int k, in
 int32_t run_moe_ffn(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const float *x,
                     int64_t T, int k, const int32_t *ids, const float *weights, float *y,
                     uint32_t flags);
+size_t moe_scratch_bytes(const har_cuda_moe_layer *layer, int64_t T, int k, uint32_t flags);
+int32_t run_moe_ffn_in(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const float *x,
+                       int64_t T, int k, const int32_t *ids, const float *weights, float *y,
+                       uint32_t flags, uint8_t *scratch);
+int32_t check_moe_args(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, int64_t T,
+                       int32_t k, uint32_t flags);
 int32_t launch_gen_q4k(har_cuda_ctx *ctx, uint8_t *dst, int64_t rows, int64_t K,
                        uint64_t seed, int64_t row0, float mean, float stdv);
 

@@ -320,9 +320,49 @@ static int32_t dispatch_down(har_cuda_ctx *ctx, const MoeDev &p, int grid) {
 
 static size_t al256(size_t v) { return (v + 255) & ~(size_t)255; }
 
+// Scratch layout of one moe_ffn call (offsets in bytes, 256-byte aligned).
+struct MoeScratch {
+  size_t o_counts, o_offsets, o_order, o_inv, o_ne, o_nne, o_xq, o_a, o_aq, o_y, total;
+};
+
+static MoeScratch moe_layout(const har_cuda_moe_layer *layer, int64_t T, int k, bool q8) {
+  const int64_t E = layer->E, H = layer->H, I = layer->I;
+  const int64_t n = T * k, slots = n + T;
+  const int64_t xq_row = (H / QK) * Q8K_BYTES, aq_row = (I / QK) * Q8K_BYTES;
+  MoeScratch s;
+  size_t off = 0;
+  auto take = [&](size_t bytes) { size_t o = off; off += al256(bytes); return o; };
+  s.o_counts = take(4 * (size_t)E);
+  s.o_offsets = take(4 * (size_t)(E + 1));
+  s.o_order = take(4 * (size_t)n);
+  s.o_inv = take(4 * (size_t)n);
+  s.o_ne = take(4 * (size_t)E);
+  s.o_nne = take(4);
+  s.o_xq = q8 ? take((size_t)(T * xq_row)) : 0;
+  s.o_a = take(4 * (size_t)(slots * I));
+  s.o_aq = q8 ? take((size_t)(slots * aq_row)) : 0;
+  s.o_y = take(4 * (size_t)(slots * H));
+  s.total = off;
+  return s;
+}
+
+size_t moe_scratch_bytes(const har_cuda_moe_layer *layer, int64_t T, int k, uint32_t flags) {
+  return moe_layout(layer, T, k, (flags & HAR_CUDA_MOE_ACT_Q8K) != 0).total;
+}
+
 int32_t run_moe_ffn(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const float *x,
                     int64_t T, int k, const int32_t *ids, const float *weights, float *y,
                     uint32_t flags) {
+  int32_t st = ensure_scratch(ctx, moe_scratch_bytes(layer, T, k, flags));
+  if (st) return st;
+  return run_moe_ffn_in(ctx, layer, x, T, k, ids, weights, y, flags, (uint8_t *)ctx->scratch);
+}
+
+// The pipeline on a caller-provided scratch region of moe_scratch_bytes()
+// bytes; allocates nothing.  Every scratch word is written before it is read.
+int32_t run_moe_ffn_in(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const float *x,
+                       int64_t T, int k, const int32_t *ids, const float *weights, float *y,
+                       uint32_t flags, uint8_t *S) {
   if (flags & HAR_CUDA_MOE_FORCE_TC)
     return set_error(ctx, HAR_CUDA_ERR_UNSUPPORTED, "moe_ffn: tensor-core path not built yet");
   if (((uintptr_t)x & 15u) || ((uintptr_t)y & 15u))
@@ -331,21 +371,12 @@ int32_t run_moe_ffn(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const fl
   const int E = (int)layer->E, H = (int)layer->H, I = (int)layer->I;
   const int64_t n = T * k;
   const int has_sh = layer->sh_gate ? 1 : 0;
-  const int64_t slots = n + T;
   const int64_t xq_row = (int64_t)(H / QK) * Q8K_BYTES, aq_row = (int64_t)(I / QK) * Q8K_BYTES;
-  // scratch layout
-  size_t off = 0;
-  auto take = [&](size_t bytes) { size_t o = off; off += al256(bytes); return o; };
-  const size_t o_counts = take(4 * (size_t)E), o_offsets = take(4 * (size_t)(E + 1));
-  const size_t o_order = take(4 * (size_t)n), o_inv = take(4 * (size_t)n);
-  const size_t o_ne = take(4 * (size_t)E), o_nne = take(4);
-  const size_t o_xq = q8 ? take((size_t)(T * xq_row)) : 0;
-  const size_t o_a = take(4 * (size_t)(slots * I));
-  const size_t o_aq = q8 ? take((size_t)(slots * aq_row)) : 0;
-  const size_t o_y = take(4 * (size_t)(slots * H));
-  int32_t st = ensure_scratch(ctx, off);
-  if (st) return st;
-  uint8_t *S = (uint8_t *)ctx->scratch;
+  const MoeScratch L = moe_layout(layer, T, k, q8);
+  const size_t o_counts = L.o_counts, o_offsets = L.o_offsets, o_order = L.o_order;
+  const size_t o_inv = L.o_inv, o_ne = L.o_ne, o_nne = L.o_nne, o_xq = L.o_xq, o_a = L.o_a;
+  const size_t o_aq = L.o_aq, o_y = L.o_y;
+  int32_t st;
   MoeDev p;
   p.gate = layer->gate->dev;
   p.up = layer->up->dev;

@@ -51,7 +51,7 @@ EXPORTS = [
     "har_cuda_route_topk", "har_cuda_group_by_expert", "har_cuda_moe_layer_create",
     "har_cuda_moe_layer_free", "har_cuda_moe_ffn", "har_cuda_moe_ffn_host", "har_cuda_moe_stack",
     "har_cuda_gen_q4k", "har_cuda_moe_stack_host", "har_cuda_profile_begin",
-    "har_cuda_profile_end",
+    "har_cuda_profile_end", "har_cuda_moe_ffn_noalloc",
 ]
 
 
@@ -98,6 +98,7 @@ def load_library() -> C.CDLL:
         "har_cuda_gen_q4k": (i32, [vp, vp, i64, i64, u64, i64, C.c_float, C.c_float]),
         "har_cuda_moe_stack_host": (i32, [vp, vp, i32, vp, i64, i32, vp, vp, vp, u32]),
         "har_cuda_profile_begin": (i32, [vp]),
+        "har_cuda_moe_ffn_noalloc": (i32, [vp, vp, vp, i64, i32, vp, vp, vp, u32]),
         "har_cuda_profile_end": (i32, [vp, C.c_char_p, C.c_size_t, vp, i64, C.POINTER(C.c_int64)]),
     }
     for name, (res, args) in sigs.items():
@@ -230,6 +231,14 @@ class Context:
         T, k = ids.shape
         self.check(self.lib.har_cuda_moe_ffn(self.handle, layer.handle, _dptr(x), T, k, _dptr(ids),
                                              _dptr(weights), _dptr(y), flags))
+        return y
+
+    def moe_ffn_noalloc(self, layer: "MoeLayer", x, ids, weights, y, flags: int = 0):
+        """moe_ffn on the library's static device scratch: allocates nothing
+        (for callers that cannot call cudaMalloc; see include/har_cuda.h)."""
+        T, k = ids.shape
+        self.check(self.lib.har_cuda_moe_ffn_noalloc(self.handle, layer.handle, _dptr(x), T, k,
+                                                     _dptr(ids), _dptr(weights), _dptr(y), flags))
         return y
 
     def moe_ffn_host(self, layer: "MoeLayer", x: np.ndarray, ids: np.ndarray,
