@@ -445,6 +445,24 @@ int32_t har_cuda_moe_layer_create(har_cuda_ctx *ctx, const har_cuda_weights *gat
   l->E = E;
   l->H = H;
   l->I = I;
+  // Weight tensor maps for the tensor-core path (H and I multiples of 128).
+  if (H % 128 == 0 && I % 128 == 0) {
+    auto wmap = [&](TmaDesc *m, const har_cuda_weights *w) {
+      return encode_tmap_2d(ctx, m, w->dev, 1, (uint64_t)(w->E * w->N), (uint64_t)w->row_bytes,
+                            (uint64_t)w->row_bytes, 128, Q4K_BYTES, false);
+    };
+    int32_t st = wmap(&l->map_gate, gate);
+    if (!st) st = wmap(&l->map_up, up);
+    if (!st) st = wmap(&l->map_down, down);
+    if (!st && any_sh) st = wmap(&l->map_sh_gate, sh_gate);
+    if (!st && any_sh) st = wmap(&l->map_sh_up, sh_up);
+    if (!st && any_sh) st = wmap(&l->map_sh_down, sh_down);
+    if (st) {
+      delete l;
+      return st;
+    }
+    l->tc_maps = true;
+  }
   *out = l;
   return HAR_CUDA_OK;
 }

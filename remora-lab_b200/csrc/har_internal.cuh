@@ -136,11 +136,20 @@ struct har_cuda_weights {
   int device = 0;
 };
 
+// An encoded TMA tensor map (CUtensorMap: 128 bytes, 64-byte aligned).
+struct alignas(64) TmaDesc {
+  unsigned char bytes[128];
+};
+
 struct har_cuda_moe_layer {
   const har_cuda_weights *gate = nullptr, *up = nullptr, *down = nullptr;
   const har_cuda_weights *sh_gate = nullptr, *sh_up = nullptr, *sh_down = nullptr;
   const float *sh_gate_inp = nullptr;
   int64_t E = 0, H = 0, I = 0;
+  // TMA maps of the weights for the tensor-core path: [E*rows][row_bytes]
+  // bytes, box of 128 rows x one 144-byte super-block (tc_maps: encoded).
+  bool tc_maps = false;
+  TmaDesc map_gate, map_up, map_down, map_sh_gate, map_sh_up, map_sh_down;
 };
 
 namespace har {
@@ -170,6 +179,9 @@ int32_t run_moe_ffn_in(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const
                        uint32_t flags, uint8_t *scratch);
 int32_t check_moe_args(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, int64_t T,
                        int32_t k, uint32_t flags);
+int32_t encode_tmap_2d(har_cuda_ctx *ctx, TmaDesc *out, const void *base, int elem_bytes,
+                       uint64_t rows, uint64_t cols, uint64_t row_stride, uint32_t box_rows,
+                       uint32_t box_cols, bool swizzle128);
 int32_t launch_gen_q4k(har_cuda_ctx *ctx, uint8_t *dst, int64_t rows, int64_t K,
                        uint64_t seed, int64_t row0, float mean, float stdv);
 

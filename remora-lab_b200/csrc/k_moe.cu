@@ -19,16 +19,21 @@
 //      combine uses separately rounded multiplies and adds like Rust.
 // Slot numbering: routed entries occupy grouped positions [0, n), n = T*k;
 // the shared expert's row for token t is slot n + t.
+#include <stdlib.h>
+
 #include <algorithm>
+#include <climits>
 
 #include "gemv_engine.cuh"
+#include "moe_tc.cuh"
 
 namespace har {
 
 size_t group_smem_bytes(int E);
 int32_t launch_group_full(har_cuda_ctx *ctx, const int32_t *ids, int64_t n, int E,
                           int32_t *counts, int32_t *offsets, int32_t *order, int32_t *inv,
-                          int32_t *ne, int32_t *n_ne);
+                          int32_t *ne, int32_t *n_ne, int thr, int nt, int32_t *big,
+                          int32_t *n_big, int32_t *big_tt);
 
 struct MoeDev {
   const uint8_t *gate, *up, *down, *sh_gate, *sh_up, *sh_down;
@@ -36,7 +41,8 @@ struct MoeDev {
   int64_t rb_h, rb_i;           // Q4_K row bytes for K = H and K = I
   int64_t xrow, arow;           // activation row bytes (f32 or Q8_K) for H and I
   int E, H, I, T, k, n;
-  int has_shared;
+  int has_shared;   // the layer has a shared expert (combine adds it)
+  int gemv_shared;  // the shared expert runs on the CUDA-core path
   const int32_t *counts, *offsets, *order, *inv, *ne, *n_ne;
   const uint8_t *xact;  // x rows (f32) or their Q8_K image
   float *a;             // [n + T][I] f32
@@ -104,7 +110,7 @@ __global__ void __launch_bounds__(256) moe_gate_up_kernel(MoeDev p, int rows_per
   const int C = p.H / 64;
   const int ntg = (p.I + rows_per_tile - 1) / rows_per_tile;
   const int nne = *p.n_ne;
-  const int total = (nne + p.has_shared) * ntg;
+  const int total = (nne + p.gemv_shared) * ntg;
   for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
     const int gi = tile / ntg, j = tile - gi * ntg;
     int g, cnt, base;
@@ -175,7 +181,7 @@ __global__ void __launch_bounds__(256) moe_down_kernel(MoeDev p, int rows_per_ti
   const int C = p.I / 64;
   const int ntg = (p.H + rows_per_tile - 1) / rows_per_tile;
   const int nne = *p.n_ne;
-  const int total = (nne + p.has_shared) * ntg;
+  const int total = (nne + p.gemv_shared) * ntg;
   for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
     const int gi = tile / ntg, j = tile - gi * ntg;
     int g, cnt, base;
@@ -322,10 +328,32 @@ static size_t al256(size_t v) { return (v + 255) & ~(size_t)255; }
 
 // Scratch layout of one moe_ffn call (offsets in bytes, 256-byte aligned).
 struct MoeScratch {
-  size_t o_counts, o_offsets, o_order, o_inv, o_ne, o_nne, o_xq, o_a, o_aq, o_y, total;
+  size_t o_counts, o_offsets, o_order, o_inv, o_ne, o_nne, o_xq, o_a, o_aq, o_y;
+  size_t o_big, o_nbig, o_bigtt, o_x16, o_a16, total;
 };
 
-static MoeScratch moe_layout(const har_cuda_moe_layer *layer, int64_t T, int k, bool q8) {
+// Experts with at least this many tokens take the tensor-core path
+// (FORCE_TC: every expert, FORCE_GEMV: none).  HAR_CUDA_TC_MIN_TOKENS in the
+// environment overrides the default for tuning.
+static int tc_threshold(uint32_t flags) {
+  if (flags & HAR_CUDA_MOE_FORCE_TC) return 1;
+  if (flags & HAR_CUDA_MOE_FORCE_GEMV) return INT_MAX;
+  static const int thr = [] {
+    const char *v = getenv("HAR_CUDA_TC_MIN_TOKENS");
+    const int t = v ? atoi(v) : 0;
+    return t > 0 ? t : 16;
+  }();
+  return thr;
+}
+
+// Whether any expert of a call can reach the threshold (a token routes to an
+// expert at most once per slot, the shared expert sees all T tokens).
+static bool tc_possible(int64_t T, int k, uint32_t flags) {
+  return (int64_t)tc_threshold(flags) <= T * k;
+}
+
+static MoeScratch moe_layout(const har_cuda_moe_layer *layer, int64_t T, int k, bool q8,
+                             bool tc) {
   const int64_t E = layer->E, H = layer->H, I = layer->I;
   const int64_t n = T * k, slots = n + T;
   const int64_t xq_row = (H / QK) * Q8K_BYTES, aq_row = (I / QK) * Q8K_BYTES;
@@ -342,12 +370,18 @@ static MoeScratch moe_layout(const har_cuda_moe_layer *layer, int64_t T, int k, 
   s.o_a = take(4 * (size_t)(slots * I));
   s.o_aq = q8 ? take((size_t)(slots * aq_row)) : 0;
   s.o_y = take(4 * (size_t)(slots * H));
+  s.o_big = take(4 * (size_t)(E + 1));
+  s.o_nbig = take(4);
+  s.o_bigtt = take(4 * (size_t)(E + 2));
+  s.o_x16 = tc ? take(2 * (size_t)(slots * H)) : 0;  // token rows in slot order (f16)
+  s.o_a16 = tc ? take(2 * (size_t)(slots * I)) : 0;
   s.total = off;
   return s;
 }
 
 size_t moe_scratch_bytes(const har_cuda_moe_layer *layer, int64_t T, int k, uint32_t flags) {
-  return moe_layout(layer, T, k, (flags & HAR_CUDA_MOE_ACT_Q8K) != 0).total;
+  return moe_layout(layer, T, k, (flags & HAR_CUDA_MOE_ACT_Q8K) != 0, tc_possible(T, k, flags))
+      .total;
 }
 
 int32_t run_moe_ffn(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const float *x,
@@ -363,8 +397,6 @@ int32_t run_moe_ffn(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const fl
 int32_t run_moe_ffn_in(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const float *x,
                        int64_t T, int k, const int32_t *ids, const float *weights, float *y,
                        uint32_t flags, uint8_t *S) {
-  if (flags & HAR_CUDA_MOE_FORCE_TC)
-    return set_error(ctx, HAR_CUDA_ERR_UNSUPPORTED, "moe_ffn: tensor-core path not built yet");
   if (((uintptr_t)x & 15u) || ((uintptr_t)y & 15u))
     return set_error(ctx, HAR_CUDA_ERR_ARG, "moe_ffn: x and y must be 16-byte aligned");
   const bool q8 = (flags & HAR_CUDA_MOE_ACT_Q8K) != 0;
@@ -372,7 +404,13 @@ int32_t run_moe_ffn_in(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const
   const int64_t n = T * k;
   const int has_sh = layer->sh_gate ? 1 : 0;
   const int64_t xq_row = (int64_t)(H / QK) * Q8K_BYTES, aq_row = (int64_t)(I / QK) * Q8K_BYTES;
-  const MoeScratch L = moe_layout(layer, T, k, q8);
+  const bool tc = tc_possible(T, k, flags);
+  const int thr = tc ? tc_threshold(flags) : INT_MAX;
+  const bool shared_tc = has_sh && tc && T >= thr;
+  if (tc && ((H % TC_M) || (I % TC_M) || (H % TC_KS) || (I % TC_KS)))
+    return set_error(ctx, HAR_CUDA_ERR_UNSUPPORTED,
+                     "moe_ffn: the tensor-core path needs H and I multiples of 128");
+  const MoeScratch L = moe_layout(layer, T, k, q8, tc);
   const size_t o_counts = L.o_counts, o_offsets = L.o_offsets, o_order = L.o_order;
   const size_t o_inv = L.o_inv, o_ne = L.o_ne, o_nne = L.o_nne, o_xq = L.o_xq, o_a = L.o_a;
   const size_t o_aq = L.o_aq, o_y = L.o_y;
@@ -395,6 +433,7 @@ int32_t run_moe_ffn_in(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const
   p.k = k;
   p.n = (int)n;
   p.has_shared = has_sh;
+  p.gemv_shared = has_sh && !shared_tc;
   p.counts = (const int32_t *)(S + o_counts);
   p.offsets = (const int32_t *)(S + o_offsets);
   p.order = (const int32_t *)(S + o_order);
@@ -416,8 +455,55 @@ int32_t run_moe_ffn_in(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const
   }
   st = launch_group_full(ctx, ids, n, E, (int32_t *)(S + o_counts), (int32_t *)(S + o_offsets),
                          (int32_t *)(S + o_order), (int32_t *)(S + o_inv), (int32_t *)(S + o_ne),
-                         (int32_t *)(S + o_nne));
+                         (int32_t *)(S + o_nne), thr, TC_NT, (int32_t *)(S + L.o_big),
+                         (int32_t *)(S + L.o_nbig), (int32_t *)(S + L.o_bigtt));
   if (st) return st;
+  // tensor-core path parameters (experts with >= thr tokens)
+  TcParams tp{};
+  TcMaps gmaps{}, dmaps{};
+  if (tc) {
+    tp.E = E;
+    tp.T = (int)T;
+    tp.k = k;
+    tp.n = (int)n;
+    tp.shared_tc = shared_tc ? 1 : 0;
+    tp.counts = p.counts;
+    tp.offsets = p.offsets;
+    tp.big = (const int32_t *)(S + L.o_big);
+    tp.n_big = (const int32_t *)(S + L.o_nbig);
+    tp.big_tt = (const int32_t *)(S + L.o_bigtt);
+    tp.a16 = (__half *)(S + L.o_a16);
+    tp.ybuf = p.ybuf;
+    tp.status = ctx->d_status;
+    if (!layer->tc_maps)
+      return set_error(ctx, HAR_CUDA_ERR_UNSUPPORTED, "moe_ffn: layer has no tensor-core maps");
+    gmaps.a0 = layer->map_gate;
+    gmaps.a1 = layer->map_up;
+    dmaps.a0 = layer->map_down;
+    dmaps.a1 = layer->map_down;
+    if (has_sh) {
+      gmaps.sh0 = layer->map_sh_gate;
+      gmaps.sh1 = layer->map_sh_up;
+      dmaps.sh0 = layer->map_sh_down;
+      dmaps.sh1 = layer->map_sh_down;
+    }
+    // token rows in slot order (f16): the B operands, one 128 x 64 box per K-step
+    const uint64_t slots = (uint64_t)(n + T);
+    for (int bx = 0; bx < 4; ++bx) {
+      if ((st = encode_tmap_2d(ctx, &gmaps.b[bx], S + L.o_x16, 2, slots, (uint64_t)H,
+                               (uint64_t)H * 2, 16u << bx, 64, true)))
+        return st;
+      if ((st = encode_tmap_2d(ctx, &dmaps.b[bx], S + L.o_a16, 2, slots, (uint64_t)I,
+                               (uint64_t)I * 2, 16u << bx, 64, true)))
+        return st;
+    }
+    if ((st = launch_gather_f16(ctx, x, H, p.order, ids, p.counts, thr, (int)n, k, (int)T,
+                                tp.shared_tc, (__half *)(S + L.o_x16))))
+      return st;
+  }
+  // upper bound of tensor-core token tiles: each big expert has >= thr tokens
+  const int64_t max_tc_tt =
+      tc ? std::min<int64_t>(E, n / std::max(thr, 1)) + n / TC_NT + 2 + (shared_tc ? T / TC_NT + 1 : 0) : 0;
   if (q8 && (st = launch_q8k_quantize(ctx, x, T, H, S + o_xq))) return st;
   const int max_groups = (int)std::min<int64_t>(E, n) + has_sh;
   const int grid_cap = ctx->num_sms * 4;
@@ -427,12 +513,28 @@ int32_t run_moe_ffn_in(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const
     st = q8 ? dispatch_gate_up<ACT_Q8K>(ctx, p, grid) : dispatch_gate_up<ACT_F32>(ctx, p, grid);
     if (st) return st;
   }
+  if (tc) {
+    TcParams g = tp;
+    g.rows = I;
+    g.K = H;
+    g.out_ld = I;
+    if ((st = launch_moe_tc(ctx, gmaps, g, 2, (int)std::min<int64_t>(INT_MAX, max_tc_tt * (I / TC_M)))))
+      return st;
+  }
   if (q8 && (st = launch_q8k_quantize(ctx, p.a, n + (has_sh ? T : 0), I, S + o_aq))) return st;
   {
     const int rpt = rows_per_tile_d(I), ntg = (H + rpt - 1) / rpt;
     const int grid = std::max(1, std::min(grid_cap, max_groups * ntg));
     st = q8 ? dispatch_down<ACT_Q8K>(ctx, p, grid) : dispatch_down<ACT_F32>(ctx, p, grid);
     if (st) return st;
+  }
+  if (tc) {
+    TcParams d = tp;
+    d.rows = H;
+    d.K = I;
+    d.out_ld = H;
+    if ((st = launch_moe_tc(ctx, dmaps, d, 1, (int)std::min<int64_t>(INT_MAX, max_tc_tt * (H / TC_M)))))
+      return st;
   }
   prof_begin(ctx);
   moe_combine_kernel<<<(unsigned)T, 256, 0, ctx->stream>>>(

@@ -51,17 +51,27 @@ def test_config2_decode_q8k_matches_q8k_restatement(ctx, alice):
 
 
 def test_config3_zipf_batch_f32_matches_har(ctx, alice):
-    # 64 concurrent tokens, Zipf(1.1) top-10: variable M per expert
+    # 64 concurrent tokens, Zipf(1.1) top-10: variable M per expert.  Every
+    # expert on the f32 CUDA-core path: HAR's engine verdict (nrms <= 5e-5) holds.
+    x = haro.normal_f32(3, 0, 64 * H).reshape(64, H)
+    ids, w = haro.zipf_routing(4, 64, E, K)
+    y = alice.run(ctx, x, ids, w, har_cuda.MOE_FORCE_GEMV)
+    assert_close(y, alice.oracle(x, ids, w), what="config3 f32")
+
+
+def test_config3_zipf_batch_default_paths(ctx, alice):
+    # default threshold: experts with >= 16 tokens run on tcgen05 with f16
+    # operands (max rel 1e-3 holds; RMS bound 1e-3, see test_gpu_tc.py)
     x = haro.normal_f32(3, 0, 64 * H).reshape(64, H)
     ids, w = haro.zipf_routing(4, 64, E, K)
     y = alice.run(ctx, x, ids, w)
-    assert_close(y, alice.oracle(x, ids, w), what="config3 f32")
+    assert_close(y, alice.oracle(x, ids, w), nrms=1e-3, what="config3 default")
 
 
 def test_config3_zipf_batch_q8k(ctx, alice):
     x = haro.normal_f32(3, 0, 64 * H).reshape(64, H)
     ids, w = haro.zipf_routing(4, 64, E, K)
-    y = alice.run(ctx, x, ids, w, har_cuda.MOE_ACT_Q8K)
+    y = alice.run(ctx, x, ids, w, har_cuda.MOE_ACT_Q8K | har_cuda.MOE_FORCE_GEMV)
     assert_close(y, alice.oracle(x, ids, w, act="q8k"), rel=1e-4, nrms=1e-5, what="config3 q8k")
 
 
