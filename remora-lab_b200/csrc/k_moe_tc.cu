@@ -13,18 +13,24 @@
 //            combine kernel applies the routing weights in slot order.
 //
 // One persistent CTA per SM, warp-specialised, every handoff an mbarrier:
-//   TMA warp:     loads raw Q4_K boxes (128 rows x one 144-byte super-block per
-//                 matrix) into a 2-slot raw ring, and 128-byte-swizzled f16
-//                 token tiles (128 rows x 64 values; rows in slot order, so a
-//                 tile is one box) into a 4-slot B ring.
-//   dequant warps: turn each 64-value step of the raw blocks into f16 weights in
-//                 the 128B-swizzled K-major layout the UMMA smem descriptor
-//                 reads (2 A stages), packed-f16 arithmetic, one row per thread.
-//   MMA thread:   4 x tcgen05.mma (K=16) per matrix per step into one of two
-//                 TMEM accumulator buffers; tcgen05.commit frees the A stage and
-//                 the B slot, and signals the epilogue at the end of a tile.
-//   epilogue warps: tcgen05.ld the accumulator while the next tile's MMAs run
-//                 into the other buffer.
+//   TMA threads:  one loads raw Q4_K boxes (128 rows x one 144-byte
+//                 super-block per matrix) into a raw ring in shared memory;
+//                 another loads 128-byte-swizzled f16 token tiles (64 values x
+//                 16/32/64/128 rows: the smallest box covering the tile's
+//                 tokens, which sit in slot order) into a B ring whose 16 KB
+//                 slots hold 128/box-rows K-steps each.
+//   dequant warps: two teams of four take alternate 64-value K-steps, turn
+//                 the raw blocks into f16 weights with packed-f16 arithmetic
+//                 and store them straight into a tensor-memory stage with
+//                 tcgen05.st (warp w owns TMEM lanes 32*(w%4).. = those rows).  Keeping the weight operand
+//                 out of shared memory removes its write and its tensor-core
+//                 read from the shared-memory bandwidth, which otherwise bounds
+//                 this path near 60% of HBM speed.
+//   MMA thread:   4 x tcgen05.mma (K=16, A from TMEM, B from shared memory)
+//                 per matrix per step into the TMEM accumulator;
+//                 tcgen05.commit frees the weight stage and the B slot, and
+//                 signals the epilogue at the end of a tile.
+//   epilogue warps: tcgen05.ld the accumulator, then free it for the next tile.
 // No multicast: every TMA load reads this GPU's memory into this CTA only.
 // Operands are f16 (same tensor rate as bf16, 3 more mantissa bits): each
 // weight is d*(sc*q) with sc*q exact, minus dmin*m rounded to f16, rounded
@@ -37,23 +43,26 @@
 
 namespace har {
 
-// Shared-memory plan.  A stages: f16 weight tiles of one 64-value K-step
-// (the dequantisers may run that many steps ahead of MMA completion); raw
-// ring: one super-block step (4 K-steps) per slot; B ring: 16 KB slots of
-// 128/box-rows K-steps.  Depths use what 227 KB allows for each shape.
+// Shared-memory plan: raw ring (one super-block step = 4 K-steps per slot)
+// and B ring (16 KB slots of 128/box-rows K-steps).  The f16 weight operand
+// does not touch shared memory: it is written to tensor memory.
 template <int NA>
 struct TcSmem {
-  static constexpr int A_STAGES = NA == 2 ? 3 : 4;
-  static constexpr int RAW_SLOTS = NA == 2 ? 2 : 4;
-  static constexpr int B_SLOTS = NA == 2 ? 3 : 4;
+  static constexpr int RAW_SLOTS = NA == 2 ? 4 : 6;
+  static constexpr int B_SLOTS = 4;
   static constexpr int BSL = TC_NT * 128;         // 16 KB (a 128-row box)
-  static constexpr int ASL = NA * TC_M * 128;     // NA x 16 KB
   static constexpr int RAWSL = NA * TC_M * Q4K_BYTES;
   static constexpr int OFF_B = 0;                 // 1024-aligned swizzled buffers first
-  static constexpr int OFF_A = OFF_B + B_SLOTS * BSL;
-  static constexpr int OFF_RAW = OFF_A + A_STAGES * ASL;
+  static constexpr int OFF_RAW = OFF_B + B_SLOTS * BSL;
   static constexpr int BYTES = OFF_RAW + RAW_SLOTS * RAWSL;
 };
+
+// Tensor-memory plan (512 columns x 128 lanes): the accumulator at columns
+// [0, 256) (gate at 0, up at 128; down at 0), then TC_A_STAGES f16 weight
+// stages of NA x 32 columns (one 64-value K-step: row = lane, two f16 per
+// column in K order).
+constexpr int TC_A_STAGES = 4;
+constexpr int TC_A_COL0 = 256;
 
 // Smallest token-tile box (16, 32, 64 or 128 rows) covering n tokens.
 __device__ __forceinline__ int tc_box(int n) { return n <= 16 ? 0 : n <= 32 ? 1 : n <= 64 ? 2 : 3; }
@@ -86,16 +95,15 @@ __device__ __forceinline__ bool tc_tile(const TcParams &p, int tt_global, int &e
   return ntok > 0;
 }
 
-// Dequantise one 32-value half chunk of a raw Q4_K block in shared memory
+// Dequantise one 32-value sub-block of a raw Q4_K block in shared memory
 // (`blk` = the 144-byte block; chunk c of 4; `hi` selects the high nibbles,
-// i.e. the odd sub-block) into pieces 4*hi .. 4*hi+3 of row r of a swizzled
-// atom column.  Packed f16 arithmetic, two values per instruction:
+// i.e. the odd sub-block) into 16 f16x2 words in K order.
+// Packed f16 arithmetic, two values per instruction:
 //   byte-permute each nibble q into the f16 bit pattern 0x64qq = 1024 + q,
 //   hfma2((1024 + q), sc, -1024*sc) = sc*q exactly (an integer <= 945),
 //   hfma2(sc*q, d, -(dmin*m)) = d*sc*q - dmin*m rounded once to f16
 // (d is the block's f16 scale, exact; dmin*m is rounded to f16 first).
-__device__ __forceinline__ void tc_dequant_half(const uint8_t *blk, int c, int hi, uint8_t *atom,
-                                                int r) {
+__device__ __forceinline__ void tc_dequant_sub(const uint8_t *blk, int c, int hi, uint32_t *o) {
   const uint4 hdr = *reinterpret_cast<const uint4 *>(blk);
   const uint4 q0 = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * c);
   const uint4 q1 = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * c);
@@ -108,65 +116,16 @@ __device__ __forceinline__ void tc_dequant_half(const uint8_t *blk, int c, int h
   const __half2 c2 = __half2half2(__float2half_rn(-(dmin * (float)mn)));
   const uint32_t q[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
-  for (int p4 = 0; p4 < 4; ++p4) {  // piece = values 8*p4 .. 8*p4+7 of the sub-block
-    uint32_t out[4];
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const uint32_t w = q[2 * p4 + h];
-      const uint32_t v = hi ? (w >> 4) & 0x0F0F0F0Fu : w & 0x0F0F0F0Fu;
-      const uint32_t p01 = __byte_perm(v, 0x64646464u, 0x5140);  // (1024+q0, 1024+q1)
-      const uint32_t p23 = __byte_perm(v, 0x64646464u, 0x7362);  // (1024+q2, 1024+q3)
-      const __half2 s01 = __hfma2(*reinterpret_cast<const __half2 *>(&p01), sc2, nsc2);
-      const __half2 s23 = __hfma2(*reinterpret_cast<const __half2 *>(&p23), sc2, nsc2);
-      const __half2 w01 = __hfma2(s01, d2, c2);
-      const __half2 w23 = __hfma2(s23, d2, c2);
-      out[2 * h] = *reinterpret_cast<const uint32_t *>(&w01);
-      out[2 * h + 1] = *reinterpret_cast<const uint32_t *>(&w23);
-    }
-    *reinterpret_cast<uint4 *>(atom + tc::sw128_off(r, 4 * hi + p4)) =
-        make_uint4(out[0], out[1], out[2], out[3]);
-  }
-}
-
-// Both halves of a 64-value chunk (one row of one atom column): the header,
-// the 32 nibble bytes and the scale set-up are shared by the two sub-blocks.
-__device__ __forceinline__ void tc_dequant_chunk(const uint8_t *blk, int c, uint8_t *atom, int r) {
-  const uint4 hdr = *reinterpret_cast<const uint4 *>(blk);
-  const uint4 q0 = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * c);
-  const uint4 q1 = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * c);
-  const __half2 d2 = __half2half2(__ushort_as_half((unsigned short)(hdr.x & 0xffffu)));
-  const float dmin = f16_bits_to_f32(hdr.x >> 16);
-  __half2 sc2[2], nsc2[2], c2[2];
-#pragma unroll
-  for (int hi = 0; hi < 2; ++hi) {
-    int sc, mn;
-    q4k_scale_min(hdr.y, hdr.z, hdr.w, 2 * c + hi, sc, mn);
-    sc2[hi] = __half2half2(__int2half_rn(sc));
-    nsc2[hi] = __half2half2(__int2half_rn(-1024 * sc));
-    c2[hi] = __half2half2(__float2half_rn(-(dmin * (float)mn)));
-  }
-  const uint32_t q[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-#pragma unroll
-  for (int hi = 0; hi < 2; ++hi) {
-#pragma unroll
-    for (int p4 = 0; p4 < 4; ++p4) {
-      uint32_t out[4];
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const uint32_t w = q[2 * p4 + h];
-        const uint32_t v = hi ? (w >> 4) & 0x0F0F0F0Fu : w & 0x0F0F0F0Fu;
-        const uint32_t p01 = __byte_perm(v, 0x64646464u, 0x5140);
-        const uint32_t p23 = __byte_perm(v, 0x64646464u, 0x7362);
-        const __half2 s01 = __hfma2(*reinterpret_cast<const __half2 *>(&p01), sc2[hi], nsc2[hi]);
-        const __half2 s23 = __hfma2(*reinterpret_cast<const __half2 *>(&p23), sc2[hi], nsc2[hi]);
-        const __half2 w01 = __hfma2(s01, d2, c2[hi]);
-        const __half2 w23 = __hfma2(s23, d2, c2[hi]);
-        out[2 * h] = *reinterpret_cast<const uint32_t *>(&w01);
-        out[2 * h + 1] = *reinterpret_cast<const uint32_t *>(&w23);
-      }
-      *reinterpret_cast<uint4 *>(atom + tc::sw128_off(r, 4 * hi + p4)) =
-          make_uint4(out[0], out[1], out[2], out[3]);
-    }
+  for (int i = 0; i < 8; ++i) {  // word i holds values 4i .. 4i+3 of the sub-block
+    const uint32_t v = hi ? (q[i] >> 4) & 0x0F0F0F0Fu : q[i] & 0x0F0F0F0Fu;
+    const uint32_t p01 = __byte_perm(v, 0x64646464u, 0x5140);  // (1024+q0, 1024+q1)
+    const uint32_t p23 = __byte_perm(v, 0x64646464u, 0x7362);  // (1024+q2, 1024+q3)
+    const __half2 s01 = __hfma2(*reinterpret_cast<const __half2 *>(&p01), sc2, nsc2);
+    const __half2 s23 = __hfma2(*reinterpret_cast<const __half2 *>(&p23), sc2, nsc2);
+    const __half2 w01 = __hfma2(s01, d2, c2);
+    const __half2 w23 = __hfma2(s23, d2, c2);
+    o[2 * i] = *reinterpret_cast<const uint32_t *>(&w01);
+    o[2 * i + 1] = *reinterpret_cast<const uint32_t *>(&w23);
   }
 }
 
@@ -187,7 +146,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
                                                                const TcParams p) {
   using L = TcSmem<NA>;
   extern __shared__ uint8_t tc_raw[];
-  constexpr int RS = L::RAW_SLOTS, BS = L::B_SLOTS, AS = L::A_STAGES;
+  constexpr int RS = L::RAW_SLOTS, BS = L::B_SLOTS, AS = TC_A_STAGES;
   __shared__ uint64_t bars[2 * RS + 2 * BS + 2 * AS + 4];
   uint64_t *raw_full = bars, *raw_empty = bars + RS, *b_full = bars + 2 * RS, *b_empty = bars + 2 * RS + BS;
   uint64_t *a_full = bars + 2 * RS + 2 * BS, *a_empty = a_full + AS, *acc_full = a_full + 2 * AS;
@@ -208,7 +167,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
       tc::mbar_init(raw_empty + s, TC_DQ_WARPS);
     }
     for (int s = 0; s < AS; ++s) {
-      tc::mbar_init(a_full + s, TC_DQ_WARPS);
+      tc::mbar_init(a_full + s, TC_DQ_WARPS / 2);  // one team fills a stage
       tc::mbar_init(a_empty + s, 1);
     }
     for (int s = 0; s < 2; ++s) {
@@ -294,10 +253,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
         if (!tc_tile(p, tile / RT, e, t0, ntok, base)) continue;
         const uint32_t idesc = tc::idesc_f16(TC_M, (ntok + 15) & ~15);
         const int rows_b = 16 << tc_box(ntok), kpb = 128 / rows_b;
-        const int acc = acc_it & 1;
-        if (!(ok = tc_wait(acc_empty + acc, ((acc_it >> 1) & 1u) ^ 1u, abort_s))) break;
+        const int acc = 0;  // one accumulator buffer; the epilogue frees it
+        if (!(ok = tc_wait(acc_empty + acc, (acc_it & 1u) ^ 1u, abort_s))) break;
         tc::tc_fence_after();
-        const uint32_t dcol = tmem + (uint32_t)(acc * 2 * TC_NT);
+        const uint32_t dcol = tmem;
         for (int ks = 0; ok && ks < KSTEPS; ++ks) {
           const int as = a_it % AS, bs = b_it % BS, sub = ks % kpb;
           if (!(ok = tc_wait(a_full + as, (a_it / AS) & 1u, abort_s))) break;
@@ -305,16 +264,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
             if (!(ok = tc_wait(b_full + bs, (b_it / BS) & 1u, abort_s))) break;
           tc::tc_fence_after();
           const uint32_t bbase = tc::smem_u32(sm + L::OFF_B + bs * L::BSL) + (uint32_t)(sub * rows_b * 128);
-          const uint32_t abase = tc::smem_u32(sm + L::OFF_A + as * L::ASL);
+          const uint32_t acol = tmem + (uint32_t)(TC_A_COL0 + as * NA * 32);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
             const uint64_t bdesc = tc::desc_sw128(bbase + 32u * kk);
 #pragma unroll
-            for (int m = 0; m < NA; ++m) {
-              const uint64_t adesc = tc::desc_sw128(abase + (uint32_t)(m * TC_M * 128) + 32u * kk);
-              tc::mma_f16(dcol + (uint32_t)(m * TC_NT), adesc, bdesc, idesc,
-                          (ks > 0 || kk > 0) ? 1u : 0u);
-            }
+            for (int m = 0; m < NA; ++m)
+              tc::mma_f16_ts(dcol + (uint32_t)(m * TC_NT), acol + (uint32_t)(m * 32 + kk * 8), bdesc,
+                             idesc, (ks > 0 || kk > 0) ? 1u : 0u);
           }
           tc::mma_commit(a_empty + as);
           ++a_it;
@@ -336,12 +293,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
     for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
       int e, t0, ntok, base;
       if (!tc_tile(p, tile / RT, e, t0, ntok, base)) continue;
-      const int acc = acc_it & 1;
-      if (!tc_wait(acc_full + acc, (acc_it >> 1) & 1u, abort_s)) break;
+      const int acc = 0;
+      if (!tc_wait(acc_full + acc, acc_it & 1u, abort_s)) break;
       tc::tc_fence_after();
       const int row = (tile % RT) * TC_M + 32 * g + lane;
       const int64_t slot0 = base + t0;
-      const uint32_t dcol = tmem + (uint32_t)(acc * 2 * TC_NT) + lane_addr;
+      const uint32_t dcol = tmem + lane_addr;
       for (int col = 0; col < ntok; col += 16) {
         uint32_t v0[16];
         tc::tmem_ld16(dcol + (uint32_t)col, v0);
@@ -368,40 +325,44 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
       ++acc_it;
     }
   } else {
-    // ---------------- dequantisers: raw Q4_K -> f16 swizzled A stages ----------------
-    const int dq = tid - TC_WARP_DQ0 * 32;
-    uint32_t raw_it = 0, a_it = 0;
+    // ---------------- dequantisers: raw Q4_K -> f16 weight stages in TMEM ----------------
+    // Two teams of four warps take alternate K-steps, so two weight stages
+    // are filled at once.  Warp w may store only TMEM lanes 32*(w%4)..: it
+    // owns weight rows 32*(w%4)+lane of every matrix of its team's steps.
+    const int g = warp & 3, team = (warp - TC_WARP_DQ0) >> 2;
+    const int r = 32 * g + lane;
+    const uint32_t lane_addr = (uint32_t)(32 * g) << 16;
+    uint32_t gs0 = 0;  // K-steps of earlier tiles (every tile has a multiple of 4)
     bool ok = true;
     for (int tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
       int e, t0, ntok, base;
       if (!tc_tile(p, tile / RT, e, t0, ntok, base)) continue;
-      for (int ks = 0; ok && ks < KSTEPS; ++ks) {
-        const int rs = raw_it % RS, as = a_it % AS;
-        if ((ks & 3) == 0)
-          if (!(ok = tc_wait(raw_full + rs, (raw_it / RS) & 1u, abort_s))) break;
-        if (!(ok = tc_wait(a_empty + as, ((a_it / AS) & 1u) ^ 1u, abort_s))) break;
-        uint8_t *Ast = sm + L::OFF_A + as * L::ASL;
+      for (int ks = team; ok && ks < KSTEPS; ks += 2) {
+        const uint32_t gs = gs0 + ks;               // global K-step = A stage sequence
+        const uint32_t rit = gs >> 2;               // raw slot sequence
+        const int rs = rit % RS, as = gs % AS;
+        if ((ks & 3) == team)                       // this warp's first step of the slot
+          if (!(ok = tc_wait(raw_full + rs, (rit / RS) & 1u, abort_s))) break;
+        if (!(ok = tc_wait(a_empty + as, ((gs / AS) & 1u) ^ 1u, abort_s))) break;
+        tc::tc_fence_after();
         const uint8_t *raw = sm + L::OFF_RAW + rs * L::RAWSL;
-        if (NA * TC_M >= TC_DQ_WARPS * 32) {  // one whole chunk (64 values) per thread
-          for (int u = dq; u < NA * TC_M; u += TC_DQ_WARPS * 32) {
-            const int rr = u % TC_M, m = u / TC_M;
-            tc_dequant_chunk(raw + (m * TC_M + rr) * Q4K_BYTES, ks & 3, Ast + m * (TC_M * 128), rr);
-          }
-        } else {  // half chunks so every dequantiser has work
-          for (int u = dq; u < NA * 2 * TC_M; u += TC_DQ_WARPS * 32) {
-            const int rr = u % TC_M, mh = u / TC_M, m = mh >> 1, hi = mh & 1;
-            tc_dequant_half(raw + (m * TC_M + rr) * Q4K_BYTES, ks & 3, hi, Ast + m * (TC_M * 128), rr);
-          }
+        const uint32_t acol = tmem + lane_addr + (uint32_t)(TC_A_COL0 + as * NA * 32);
+#pragma unroll
+        for (int m = 0; m < NA; ++m) {
+          uint32_t o[32];
+          const uint8_t *blk = raw + (m * TC_M + r) * Q4K_BYTES;
+          tc_dequant_sub(blk, ks & 3, 0, o);
+          tc_dequant_sub(blk, ks & 3, 1, o + 16);
+          tc::tmem_st32(acol + (uint32_t)(m * 32), o);
         }
-        tc::fence_proxy_async_smem();
+        tc::tmem_wait_st();
+        tc::tc_fence_before();
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(a_full + as);
-        ++a_it;
-        if ((ks & 3) == 3) {
+        if ((ks & 3) == 2 + team)                   // this warp's last step of the slot
           if (lane == 0) tc::mbar_arrive(raw_empty + rs);
-          ++raw_it;
-        }
       }
+      gs0 += KSTEPS;
     }
   }
 
