@@ -32,8 +32,8 @@ namespace har {
 size_t group_smem_bytes(int E);
 int32_t launch_group_full(har_cuda_ctx *ctx, const int32_t *ids, int64_t n, int E,
                           int32_t *counts, int32_t *offsets, int32_t *order, int32_t *inv,
-                          int32_t *ne, int32_t *n_ne, int thr, int nt, int32_t *big,
-                          int32_t *n_big, int32_t *big_tt);
+                          int32_t *ne, int32_t *n_ne, int thr, int nt, int2 *tt_info,
+                          int32_t *n_tt);
 
 struct MoeDev {
   const uint8_t *gate, *up, *down, *sh_gate, *sh_up, *sh_down;
@@ -329,7 +329,7 @@ static size_t al256(size_t v) { return (v + 255) & ~(size_t)255; }
 // Scratch layout of one moe_ffn call (offsets in bytes, 256-byte aligned).
 struct MoeScratch {
   size_t o_counts, o_offsets, o_order, o_inv, o_ne, o_nne, o_xq, o_a, o_aq, o_y;
-  size_t o_big, o_nbig, o_bigtt, o_x16, o_a16, total;
+  size_t o_ttinfo, o_ntt, o_x16, o_a16, total;
 };
 
 // Experts with at least this many tokens take the tensor-core path
@@ -370,9 +370,8 @@ static MoeScratch moe_layout(const har_cuda_moe_layer *layer, int64_t T, int k, 
   s.o_a = take(4 * (size_t)(slots * I));
   s.o_aq = q8 ? take((size_t)(slots * aq_row)) : 0;
   s.o_y = take(4 * (size_t)(slots * H));
-  s.o_big = take(4 * (size_t)(E + 1));
-  s.o_nbig = take(4);
-  s.o_bigtt = take(4 * (size_t)(E + 2));
+  s.o_ttinfo = take(8 * (size_t)(std::min<int64_t>(E, n) + n / TC_NT + 1));  // routed token tiles
+  s.o_ntt = take(4);
   s.o_x16 = tc ? take(2 * (size_t)(slots * H)) : 0;  // token rows in slot order (f16)
   s.o_a16 = tc ? take(2 * (size_t)(slots * I)) : 0;
   s.total = off;
@@ -455,8 +454,8 @@ int32_t run_moe_ffn_in(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const
   }
   st = launch_group_full(ctx, ids, n, E, (int32_t *)(S + o_counts), (int32_t *)(S + o_offsets),
                          (int32_t *)(S + o_order), (int32_t *)(S + o_inv), (int32_t *)(S + o_ne),
-                         (int32_t *)(S + o_nne), thr, TC_NT, (int32_t *)(S + L.o_big),
-                         (int32_t *)(S + L.o_nbig), (int32_t *)(S + L.o_bigtt));
+                         (int32_t *)(S + o_nne), thr, TC_NT, (int2 *)(S + L.o_ttinfo),
+                         (int32_t *)(S + L.o_ntt));
   if (st) return st;
   // tensor-core path parameters (experts with >= thr tokens)
   TcParams tp{};
@@ -467,11 +466,8 @@ int32_t run_moe_ffn_in(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const
     tp.k = k;
     tp.n = (int)n;
     tp.shared_tc = shared_tc ? 1 : 0;
-    tp.counts = p.counts;
-    tp.offsets = p.offsets;
-    tp.big = (const int32_t *)(S + L.o_big);
-    tp.n_big = (const int32_t *)(S + L.o_nbig);
-    tp.big_tt = (const int32_t *)(S + L.o_bigtt);
+    tp.tt_info = (const int2 *)(S + L.o_ttinfo);
+    tp.n_tt = (const int32_t *)(S + L.o_ntt);
     tp.a16 = (__half *)(S + L.o_a16);
     tp.ybuf = p.ybuf;
     tp.status = ctx->d_status;
@@ -487,9 +483,10 @@ int32_t run_moe_ffn_in(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const
       dmaps.sh0 = layer->map_sh_down;
       dmaps.sh1 = layer->map_sh_down;
     }
-    // token rows in slot order (f16): the B operands, one 128 x 64 box per K-step
+    // token rows in slot order (f16): the B operands, one box of 16/32/64 rows
+    // x 64 values per K-step
     const uint64_t slots = (uint64_t)(n + T);
-    for (int bx = 0; bx < 4; ++bx) {
+    for (int bx = 0; bx < TC_NBOX; ++bx) {
       if ((st = encode_tmap_2d(ctx, &gmaps.b[bx], S + L.o_x16, 2, slots, (uint64_t)H,
                                (uint64_t)H * 2, 16u << bx, 64, true)))
         return st;

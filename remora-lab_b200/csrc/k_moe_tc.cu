@@ -5,32 +5,39 @@
 // (har/crates/har-demo/src/bin/har-native-qwen35moe.rs:979-1048) per token.
 //
 // Shape: the weights are the MMA's M side ("swap AB"): a tile is 128 weight
-// rows x up to 128 token columns, so a tile of W is dequantised once for up to
-// 128 tokens.  D = W_tile * X^T accumulates in TMEM (f32).
+// rows x up to 64 token columns, so a tile of W is dequantised once for up to
+// 64 tokens.  D = W_tile * X^T accumulates in TMEM (f32).
 //   gate/up: two accumulators (gate rows and up rows of the same 128
 //            intermediate indices); epilogue a = silu(g) * u -> a16[slot][i] (f16).
 //   down:    one accumulator; epilogue ybuf[slot][h] (f32), then the common
 //            combine kernel applies the routing weights in slot order.
 //
+// With few tokens per expert the MMAs are narrow (N = 16..64) and a single
+// issuing warp cannot keep up with HBM: each tcgen05.mma costs the issuer
+// about 100 cycles whatever N is, i.e. ~20 weights per cycle, while one SM's
+// share of HBM bandwidth is ~40 Q4_K weights per cycle.  So two warps issue,
+// each for alternate 64-value K-steps into its own accumulator set, and the
+// epilogue adds the two partial sums.
+//
 // One persistent CTA per SM, warp-specialised, every handoff an mbarrier:
 //   TMA threads:  one loads raw Q4_K boxes (128 rows x one 144-byte
 //                 super-block per matrix) into a raw ring in shared memory;
 //                 another loads 128-byte-swizzled f16 token tiles (64 values x
-//                 16/32/64/128 rows: the smallest box covering the tile's
-//                 tokens, which sit in slot order) into a B ring whose 16 KB
-//                 slots hold 128/box-rows K-steps each.
-//   dequant warps: two teams of four take alternate 64-value K-steps, turn
-//                 the raw blocks into f16 weights with packed-f16 arithmetic
-//                 and store them straight into a tensor-memory stage with
-//                 tcgen05.st (warp w owns TMEM lanes 32*(w%4).. = those rows).  Keeping the weight operand
-//                 out of shared memory removes its write and its tensor-core
-//                 read from the shared-memory bandwidth, which otherwise bounds
-//                 this path near 60% of HBM speed.
-//   MMA thread:   4 x tcgen05.mma (K=16, A from TMEM, B from shared memory)
-//                 per matrix per step into the TMEM accumulator;
-//                 tcgen05.commit frees the weight stage and the B slot, and
-//                 signals the epilogue at the end of a tile.
-//   epilogue warps: tcgen05.ld the accumulator, then free it for the next tile.
+//                 16/32/64 rows: the smallest box covering the tile's tokens,
+//                 which sit in slot order) into a B ring whose 16 KB slots
+//                 hold 128/box-rows K-steps each.
+//   dequant warps: two teams of four, team t taking the K-steps of issuer t,
+//                 turn the raw blocks into f16 weights with packed-f16
+//                 arithmetic and store them straight into the team's two
+//                 tensor-memory stages with tcgen05.st (warp w owns TMEM lanes
+//                 32*(w%4).. = those rows).  Keeping the weight operand out of
+//                 shared memory keeps its write and its tensor-core read off
+//                 the shared-memory bandwidth.
+//   MMA warps:    4 x tcgen05.mma (K=16, A from TMEM, B from shared memory)
+//                 per matrix per K-step; tcgen05.commit frees the weight stage
+//                 and the B slot, and signals the epilogue at the end of a tile.
+//   epilogue warps: tcgen05.ld both partial accumulators, add, apply the
+//                 epilogue, store, then free the accumulator columns.
 // No multicast: every TMA load reads this GPU's memory into this CTA only.
 // Operands are f16 (same tensor rate as bf16, 3 more mantissa bits): each
 // weight is d*(sc*q) with sc*q exact, minus dmin*m rounded to f16, rounded
@@ -50,49 +57,62 @@ template <int NA>
 struct TcSmem {
   static constexpr int RAW_SLOTS = NA == 2 ? 4 : 6;
   static constexpr int B_SLOTS = 4;
-  static constexpr int BSL = TC_NT * 128;         // 16 KB (a 128-row box)
+  static constexpr int BSL = 128 * 128;           // 16 KB: 128 rows of 64 f16
   static constexpr int RAWSL = NA * TC_M * Q4K_BYTES;
   static constexpr int OFF_B = 0;                 // 1024-aligned swizzled buffers first
   static constexpr int OFF_RAW = OFF_B + B_SLOTS * BSL;
   static constexpr int BYTES = OFF_RAW + RAW_SLOTS * RAWSL;
 };
 
-// Tensor-memory plan (512 columns x 128 lanes): the accumulator at columns
-// [0, 256) (gate at 0, up at 128; down at 0), then TC_A_STAGES f16 weight
-// stages of NA x 32 columns (one 64-value K-step: row = lane, two f16 per
-// column in K order).
-constexpr int TC_A_STAGES = 4;
-constexpr int TC_A_COL0 = 256;
+// Tensor-memory plan (512 columns x 128 lanes): accumulators in 64-column
+// quarters at [0, A_COL0), then TC_ISSUERS x 2 f16 weight stages of NA x 32
+// columns (one 64-value K-step: row = lane, two f16 per column in K order).
+// A tile with token box rows_b takes ceil(TC_ISSUERS * NA * rows_b / 64)
+// quarters: issuer i's accumulator of matrix m sits at column
+// (i * NA + m) * rows_b of the tile's first quarter.
+template <int NA>
+struct TcTmem {
+  static constexpr int A_STAGES = 2 * TC_ISSUERS;
+  static constexpr int A_COL0 = TC_TMEM_COLS - A_STAGES * NA * 32;
+  static constexpr int NQ = A_COL0 / 64;
+  static __device__ __forceinline__ int quarters(int rows_b) {
+    return (TC_ISSUERS * NA * rows_b + 63) / 64;
+  }
+};
 
-// Smallest token-tile box (16, 32, 64 or 128 rows) covering n tokens.
-__device__ __forceinline__ int tc_box(int n) { return n <= 16 ? 0 : n <= 32 ? 1 : n <= 64 ? 2 : 3; }
+// Smallest token-tile box (16, 32 or 64 rows) covering n tokens.
+__device__ __forceinline__ int tc_box(int n) { return n <= 16 ? 0 : n <= 32 ? 1 : 2; }
 
-// Map a tile's token-tile index to (expert or E for shared, first token,
-// token count, first slot).  False when the index is past the work.
-__device__ __forceinline__ bool tc_tile(const TcParams &p, int tt_global, int &e, int &t0,
-                                        int &ntok, int &base) {
-  const int nb = *p.n_big;
-  const int routed_tt = p.big_tt[nb];
-  if (tt_global < routed_tt) {
-    int lo = 0, hi = nb - 1;  // last b with big_tt[b] <= tt_global
-    while (lo < hi) {
-      const int mid = (lo + hi + 1) >> 1;
-      if (p.big_tt[mid] <= tt_global) lo = mid; else hi = mid - 1;
-    }
-    e = p.big[lo];
-    const int tt = tt_global - p.big_tt[lo];
-    t0 = tt * TC_NT;
-    ntok = min(TC_NT, p.counts[e] - t0);
-    base = p.offsets[e];
+// Map a token-tile index to (expert, or E for the shared expert; token
+// count; first slot).  Routed tiles come from the grouping kernel's table,
+// the shared expert's tiles follow them.  False when the index is past the work.
+__device__ __forceinline__ bool tc_tile(const TcParams &p, int routed_tt, int ttg, int &e,
+                                        int &ntok, int &slot0) {
+  if (ttg < routed_tt) {
+    const int2 v = p.tt_info[ttg];
+    e = v.x & 0xffff;
+    ntok = v.x >> 16;
+    slot0 = v.y;
     return true;
   }
   if (!p.shared_tc) return false;
-  const int tt = tt_global - routed_tt;
+  const int t0 = (ttg - routed_tt) * TC_NT;
   e = p.E;
-  t0 = tt * TC_NT;
   ntok = min(TC_NT, p.T - t0);
-  base = p.n;
+  slot0 = p.n + t0;
   return ntok > 0;
+}
+
+// Accumulator quarters of the next tile: `qc` is the ring cursor (the MMA
+// warps and the epilogue walk the same tiles, so they agree); a tile that does
+// not fit before the end wraps to quarter 0.  Returns the first quarter.
+template <int NA>
+__device__ __forceinline__ int tc_take_quarters(int &qc, int nq) {
+  if (qc + nq > TcTmem<NA>::NQ) qc = 0;
+  const int q0 = qc;
+  qc += nq;
+  if (qc == TcTmem<NA>::NQ) qc = 0;
+  return q0;
 }
 
 // Dequantise one 32-value sub-block of a raw Q4_K block in shared memory
@@ -139,18 +159,27 @@ __device__ __forceinline__ bool tc_wait(uint64_t *bar, uint32_t parity, volatile
   *abort_s = 1;
   return false;
 }
+// The same for a whole warp: lane 0 polls, the outcome is broadcast, and the
+// warp leaves converged (the warp-wide MMA forms need it so).
+__device__ __forceinline__ bool tc_wait_warp(uint64_t *bar, uint32_t parity, volatile int *abort_s,
+                                             int lane) {
+  bool ok = true;
+  if (lane == 0) ok = tc_wait(bar, parity, abort_s);
+  return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+}
 
 // NA = number of A matrices (2: gate and up with SwiGLU epilogue; 1: down).
 template <int NA>
 __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_constant__ TcMaps maps,
                                                                const TcParams p) {
   using L = TcSmem<NA>;
+  using TM = TcTmem<NA>;
   extern __shared__ uint8_t tc_raw[];
-  constexpr int RS = L::RAW_SLOTS, BS = L::B_SLOTS, AS = TC_A_STAGES;
-  __shared__ uint64_t bars[2 * RS + 2 * BS + 2 * AS + 4];
+  constexpr int RS = L::RAW_SLOTS, BS = L::B_SLOTS, AS = TM::A_STAGES, NQ = TM::NQ;
+  __shared__ uint64_t bars[2 * RS + 2 * BS + 2 * AS + 2 * NQ];
   uint64_t *raw_full = bars, *raw_empty = bars + RS, *b_full = bars + 2 * RS, *b_empty = bars + 2 * RS + BS;
-  uint64_t *a_full = bars + 2 * RS + 2 * BS, *a_empty = a_full + AS, *acc_full = a_full + 2 * AS;
-  uint64_t *acc_empty = acc_full + 2;
+  uint64_t *a_full = bars + 2 * RS + 2 * BS, *a_empty = a_full + AS;
+  uint64_t *acc_full = a_empty + AS, *acc_empty = acc_full + NQ;
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
   volatile int *abort_s = &abort_flag;
@@ -167,16 +196,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
       tc::mbar_init(raw_empty + s, TC_DQ_WARPS);
     }
     for (int s = 0; s < AS; ++s) {
-      tc::mbar_init(a_full + s, TC_DQ_WARPS / 2);  // one team fills a stage
+      tc::mbar_init(a_full + s, TC_DQ_WARPS / TC_ISSUERS);  // one team fills a stage
       tc::mbar_init(a_empty + s, 1);
     }
-    for (int s = 0; s < 2; ++s) {
-      tc::mbar_init(acc_full + s, 1);
-      tc::mbar_init(acc_empty + s, 4);
+    for (int q = 0; q < NQ; ++q) {
+      tc::mbar_init(acc_full + q, TC_ISSUERS);
+      tc::mbar_init(acc_empty + q, 4);
     }
     for (int s = 0; s < BS; ++s) {
       tc::mbar_init(b_full + s, 1);
-      tc::mbar_init(b_empty + s, 1);
+      tc::mbar_init(b_empty + s, TC_ISSUERS);
     }
     tc::fence_mbar_init();
     abort_flag = 0;
@@ -192,8 +221,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
 
   const int RT = p.rows / TC_M;
   const int KSTEPS = p.K / 64, KSB = p.K / 256;
-  const int nb = *p.n_big;
-  const int total_tt = p.big_tt[nb] + (p.shared_tc ? (p.T + TC_NT - 1) / TC_NT : 0);
+  const int routed_tt = *p.n_tt;
+  const int total_tt = routed_tt + (p.shared_tc ? (p.T + TC_NT - 1) / TC_NT : 0);
   const int total = total_tt * RT;
 
   if (warp == TC_WARP_TMA) {
@@ -202,8 +231,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
       uint32_t raw_it = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
-        int e, t0, ntok, base;
-        if (!tc_tile(p, tile / RT, e, t0, ntok, base)) continue;
+        int e, ntok, slot0;
+        if (!tc_tile(p, routed_tt, tile / RT, e, ntok, slot0)) continue;
         const int r0 = (tile % RT) * TC_M;
         const bool sh = e == p.E;
         const void *m0 = sh ? (const void *)&maps.sh0 : (const void *)&maps.a0;
@@ -226,127 +255,137 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
       uint32_t b_it = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
-        int e, t0, ntok, base;
-        if (!tc_tile(p, tile / RT, e, t0, ntok, base)) continue;
+        int e, ntok, slot0;
+        if (!tc_tile(p, routed_tt, tile / RT, e, ntok, slot0)) continue;
         const int bx = tc_box(ntok);
         const void *bm = &maps.b[bx];
         const int rows_b = 16 << bx, kpb = 128 / rows_b;  // K-steps per B slot
         const uint32_t sub_bytes = (uint32_t)rows_b * 128u;
-        const int yb = base + t0;
-        for (int ks = 0; ok && ks < KSTEPS; ks += kpb) {
-          const int bs = b_it % BS;
+        for (int s0 = 0; ok && s0 < KSTEPS; s0 += kpb) {
+          const int bs = b_it % BS, nsub = min(kpb, KSTEPS - s0);
           if (!(ok = tc_wait(b_empty + bs, ((b_it / BS) & 1u) ^ 1u, abort_s))) break;
-          tc::mbar_expect_tx(b_full + bs, sub_bytes * (uint32_t)kpb);
-          for (int j = 0; j < kpb; ++j)
-            tc::tma_load_2d(sm + L::OFF_B + bs * L::BSL + j * sub_bytes, bm, (ks + j) * 64, yb, b_full + bs);
+          tc::mbar_expect_tx(b_full + bs, sub_bytes * (uint32_t)nsub);
+          for (int j = 0; j < nsub; ++j)
+            tc::tma_load_2d(sm + L::OFF_B + bs * L::BSL + j * sub_bytes, bm, (s0 + j) * 64, slot0, b_full + bs);
           ++b_it;
         }
       }
     }
-  } else if (warp == TC_WARP_MMA) {
-    // ---------------- MMA issuer ----------------
-    if (lane == 0) {
-      uint32_t a_it = 0, b_it = 0, acc_it = 0;
-      bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
-        int e, t0, ntok, base;
-        if (!tc_tile(p, tile / RT, e, t0, ntok, base)) continue;
-        const uint32_t idesc = tc::idesc_f16(TC_M, (ntok + 15) & ~15);
-        const int rows_b = 16 << tc_box(ntok), kpb = 128 / rows_b;
-        const int acc = 0;  // one accumulator buffer; the epilogue frees it
-        if (!(ok = tc_wait(acc_empty + acc, (acc_it & 1u) ^ 1u, abort_s))) break;
+  } else if (warp == TC_WARP_MMA0 || warp == TC_WARP_MMA1) {
+    // ---------------- MMA issuers (whole warp, one elected lane issues) ----------------
+    const int is = warp == TC_WARP_MMA0 ? 0 : 1;  // this warp takes K-steps ks % 2 == is
+    uint32_t j = 0, b_it = 0, par = 0;  // par bit q: parity of quarter q's uses
+    int qc = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
+      int e, ntok, slot0;
+      if (!tc_tile(p, routed_tt, tile / RT, e, ntok, slot0)) continue;
+      const int rows_b = 16 << tc_box(ntok), kpb = 128 / rows_b, nq = TM::quarters(rows_b);
+      const int q0 = tc_take_quarters<NA>(qc, nq);
+      for (int u = 0; ok && u < nq; ++u)
+        ok = tc_wait_warp(acc_empty + q0 + u, ((par >> (q0 + u)) & 1u) ^ 1u, abort_s, lane);
+      if (!ok) break;
+      tc::tc_fence_after();
+      const uint32_t idesc = tc::idesc_f16(TC_M, (ntok + 15) & ~15);
+      const uint32_t dcol = tmem + (uint32_t)(q0 * 64 + is * NA * rows_b);
+      for (int ks = is; ks < KSTEPS; ks += 2, ++j) {
+        const int st = is * 2 + (int)(j & 1u);
+        if (!(ok = tc_wait_warp(a_full + st, (j >> 1) & 1u, abort_s, lane))) break;
+        const int s0 = ks - ks % kpb, send = min(s0 + kpb, KSTEPS), bs = b_it % BS;
+        if (ks == s0 + is)
+          if (!(ok = tc_wait_warp(b_full + bs, (b_it / BS) & 1u, abort_s, lane))) break;
         tc::tc_fence_after();
-        const uint32_t dcol = tmem;
-        for (int ks = 0; ok && ks < KSTEPS; ++ks) {
-          const int as = a_it % AS, bs = b_it % BS, sub = ks % kpb;
-          if (!(ok = tc_wait(a_full + as, (a_it / AS) & 1u, abort_s))) break;
-          if (sub == 0)
-            if (!(ok = tc_wait(b_full + bs, (b_it / BS) & 1u, abort_s))) break;
-          tc::tc_fence_after();
-          const uint32_t bbase = tc::smem_u32(sm + L::OFF_B + bs * L::BSL) + (uint32_t)(sub * rows_b * 128);
-          const uint32_t acol = tmem + (uint32_t)(TC_A_COL0 + as * NA * 32);
+        const uint64_t bdesc0 =
+            tc::desc_sw128(tc::smem_u32(sm + L::OFF_B + bs * L::BSL) + (uint32_t)((ks - s0) * rows_b * 128));
+        const uint32_t acol = tmem + (uint32_t)(TM::A_COL0 + st * NA * 32);
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint64_t bdesc = tc::desc_sw128(bbase + 32u * kk);
+        for (int kk = 0; kk < 4; ++kk) {
 #pragma unroll
-            for (int m = 0; m < NA; ++m)
-              tc::mma_f16_ts(dcol + (uint32_t)(m * TC_NT), acol + (uint32_t)(m * 32 + kk * 8), bdesc,
-                             idesc, (ks > 0 || kk > 0) ? 1u : 0u);
-          }
-          tc::mma_commit(a_empty + as);
-          ++a_it;
-          if (sub == kpb - 1) {
-            tc::mma_commit(b_empty + bs);
-            ++b_it;
-          }
+          for (int m = 0; m < NA; ++m)
+            tc::mma_f16_ts_w(dcol + (uint32_t)(m * rows_b), acol + (uint32_t)(m * 32 + kk * 8),
+                             bdesc0 + (uint64_t)(2 * kk), idesc, (ks >= 2 || kk > 0) ? 1u : 0u);
         }
-        if (!ok) break;
-        tc::mma_commit(acc_full + acc);
-        ++acc_it;
+        tc::mma_commit_w(a_empty + st);
+        if (ks == send - 2 + is) {
+          tc::mma_commit_w(b_empty + bs);
+          ++b_it;
+        }
       }
+      if (!ok) break;
+      for (int u = 0; u < nq; ++u) tc::mma_commit_w(acc_full + q0 + u);
+      par ^= ((1u << nq) - 1u) << q0;
     }
   } else if (warp < TC_WARP_DQ0) {
     // ---------------- epilogue: TMEM -> global ----------------
     const int g = warp & 3;  // TMEM lane group this warp may access
     const uint32_t lane_addr = (uint32_t)(32 * g) << 16;
-    uint32_t acc_it = 0;
-    for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
-      int e, t0, ntok, base;
-      if (!tc_tile(p, tile / RT, e, t0, ntok, base)) continue;
-      const int acc = 0;
-      if (!tc_wait(acc_full + acc, acc_it & 1u, abort_s)) break;
+    uint32_t par = 0;
+    int qc = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
+      int e, ntok, slot0;
+      if (!tc_tile(p, routed_tt, tile / RT, e, ntok, slot0)) continue;
+      const int rows_b = 16 << tc_box(ntok), nq = TM::quarters(rows_b);
+      const int q0 = tc_take_quarters<NA>(qc, nq);
+      for (int u = 0; ok && u < nq; ++u)
+        ok = tc_wait_warp(acc_full + q0 + u, (par >> (q0 + u)) & 1u, abort_s, lane);
+      if (!ok) break;
       tc::tc_fence_after();
       const int row = (tile % RT) * TC_M + 32 * g + lane;
-      const int64_t slot0 = base + t0;
-      const uint32_t dcol = tmem + lane_addr;
+      const uint32_t dcol = tmem + lane_addr + (uint32_t)(q0 * 64);
       for (int col = 0; col < ntok; col += 16) {
-        uint32_t v0[16];
-        tc::tmem_ld16(dcol + (uint32_t)col, v0);
+        uint32_t g0[16], g1[16];
+        tc::tmem_ld16(dcol + (uint32_t)col, g0);                         // issuer 0, matrix 0
+        tc::tmem_ld16(dcol + (uint32_t)(NA * rows_b + col), g1);          // issuer 1, matrix 0
         if (NA == 2) {
-          uint32_t v1[16];
-          tc::tmem_ld16(dcol + (uint32_t)(TC_NT + col), v1);
+          uint32_t u0[16], u1[16];
+          tc::tmem_ld16(dcol + (uint32_t)(rows_b + col), u0);             // issuer 0, matrix 1
+          tc::tmem_ld16(dcol + (uint32_t)(3 * rows_b + col), u1);         // issuer 1, matrix 1
           tc::tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 16; ++j)
-            if (col + j < ntok) {
-              const float av = __fmul_rn(tc_silu(__uint_as_float(v0[j])), __uint_as_float(v1[j]));
-              p.a16[(slot0 + col + j) * p.out_ld + row] = __float2half_rn(av);
+          for (int c = 0; c < 16; ++c)
+            if (col + c < ntok) {
+              const float gv = __uint_as_float(g0[c]) + __uint_as_float(g1[c]);
+              const float uv = __uint_as_float(u0[c]) + __uint_as_float(u1[c]);
+              p.a16[((int64_t)slot0 + col + c) * p.out_ld + row] = __float2half_rn(__fmul_rn(tc_silu(gv), uv));
             }
         } else {
           tc::tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 16; ++j)
-            if (col + j < ntok) p.ybuf[(slot0 + col + j) * p.out_ld + row] = __uint_as_float(v0[j]);
+          for (int c = 0; c < 16; ++c)
+            if (col + c < ntok)
+              p.ybuf[((int64_t)slot0 + col + c) * p.out_ld + row] = __uint_as_float(g0[c]) + __uint_as_float(g1[c]);
         }
       }
       tc::tc_fence_before();
       __syncwarp();
-      if (lane == 0) tc::mbar_arrive(acc_empty + acc);
-      ++acc_it;
+      if (lane == 0)
+        for (int u = 0; u < nq; ++u) tc::mbar_arrive(acc_empty + q0 + u);
+      par ^= ((1u << nq) - 1u) << q0;
     }
   } else {
     // ---------------- dequantisers: raw Q4_K -> f16 weight stages in TMEM ----------------
-    // Two teams of four warps take alternate K-steps, so two weight stages
-    // are filled at once.  Warp w may store only TMEM lanes 32*(w%4)..: it
+    // Team t (four warps) takes the K-steps of issuer t, filling that issuer's
+    // two stages in turn.  Warp w may store only TMEM lanes 32*(w%4)..: it
     // owns weight rows 32*(w%4)+lane of every matrix of its team's steps.
     const int g = warp & 3, team = (warp - TC_WARP_DQ0) >> 2;
     const int r = 32 * g + lane;
     const uint32_t lane_addr = (uint32_t)(32 * g) << 16;
-    uint32_t gs0 = 0;  // K-steps of earlier tiles (every tile has a multiple of 4)
+    uint32_t j = 0, gs0 = 0;  // team K-steps so far; K-steps of earlier tiles
     bool ok = true;
     for (int tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
-      int e, t0, ntok, base;
-      if (!tc_tile(p, tile / RT, e, t0, ntok, base)) continue;
-      for (int ks = team; ok && ks < KSTEPS; ks += 2) {
-        const uint32_t gs = gs0 + ks;               // global K-step = A stage sequence
-        const uint32_t rit = gs >> 2;               // raw slot sequence
-        const int rs = rit % RS, as = gs % AS;
+      int e, ntok, slot0;
+      if (!tc_tile(p, routed_tt, tile / RT, e, ntok, slot0)) continue;
+      for (int ks = team; ks < KSTEPS; ks += 2, ++j) {
+        const uint32_t gs = gs0 + ks;               // global K-step
+        const uint32_t rit = gs >> 2;               // raw slot sequence (4 K-steps a slot)
+        const int rs = rit % RS, st = team * 2 + (int)(j & 1u);
         if ((ks & 3) == team)                       // this warp's first step of the slot
-          if (!(ok = tc_wait(raw_full + rs, (rit / RS) & 1u, abort_s))) break;
-        if (!(ok = tc_wait(a_empty + as, ((gs / AS) & 1u) ^ 1u, abort_s))) break;
+          if (!(ok = tc_wait_warp(raw_full + rs, (rit / RS) & 1u, abort_s, lane))) break;
+        if (!(ok = tc_wait_warp(a_empty + st, ((j >> 1) & 1u) ^ 1u, abort_s, lane))) break;
         tc::tc_fence_after();
         const uint8_t *raw = sm + L::OFF_RAW + rs * L::RAWSL;
-        const uint32_t acol = tmem + lane_addr + (uint32_t)(TC_A_COL0 + as * NA * 32);
+        const uint32_t acol = tmem + lane_addr + (uint32_t)(TM::A_COL0 + st * NA * 32);
 #pragma unroll
         for (int m = 0; m < NA; ++m) {
           uint32_t o[32];
@@ -358,7 +397,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
         tc::tmem_wait_st();
         tc::tc_fence_before();
         __syncwarp();
-        if (lane == 0) tc::mbar_arrive(a_full + as);
+        if (lane == 0) tc::mbar_arrive(a_full + st);
         if ((ks & 3) == 2 + team)                   // this warp's last step of the slot
           if (lane == 0) tc::mbar_arrive(raw_empty + rs);
       }

@@ -101,8 +101,9 @@ int32_t launch_route_topk(har_cuda_ctx *ctx, const float *logits, int64_t T, int
 // group_kernel: stable counting sort of n = T*k entries by expert id.
 // Outputs counts[E], offsets[E+1], order[n] (entry at each grouped position),
 // inv[n] (grouped position of each entry) and, when ne != null, the list of
-// non-empty experts in expert order (ne[0..*n_ne)).  Entries with an
-// out-of-range id set DEV_ERR_BOUNDS in *status and are dropped.
+// non-empty experts in expert order (ne[0..*n_ne)) below `thr` tokens, and
+// the token tiles of the experts at or above it (see the tail below).
+// Entries with an out-of-range id set DEV_ERR_BOUNDS in *status and are dropped.
 // ---------------------------------------------------------------------------
 constexpr int GROUP_WARPS = 16;
 
@@ -110,8 +111,7 @@ __global__ void __launch_bounds__(GROUP_WARPS * 32) group_kernel(
     const int32_t *__restrict__ ids, int n, int E, int32_t *__restrict__ counts,
     int32_t *__restrict__ offsets, int32_t *__restrict__ order, int32_t *__restrict__ inv,
     int32_t *__restrict__ ne, int32_t *__restrict__ n_ne, int thr, int nt,
-    int32_t *__restrict__ big, int32_t *__restrict__ n_big, int32_t *__restrict__ big_tt,
-    int *status) {
+    int2 *__restrict__ tt_info, int32_t *__restrict__ n_tt, int *status) {
   extern __shared__ __align__(16) uint8_t gsm[];
   int32_t *cnt = reinterpret_cast<int32_t *>(gsm);                       // [W][E]
   int32_t *off = cnt + (size_t)GROUP_WARPS * E;                             // [E+1]
@@ -198,18 +198,18 @@ __global__ void __launch_bounds__(GROUP_WARPS * 32) group_kernel(
     __syncwarp();
   }
   // Non-empty experts in expert order (warp 0, ballot + popc), split by token
-  // count: ne[] those below `thr` (CUDA-core path), big[] those at or above it
-  // (tensor-core path) with big_tt[] the prefix of their ceil(count/nt) token
-  // tiles (big_tt[n_big] = total).
+  // count: ne[] those below `thr` (CUDA-core path); those at or above it
+  // (tensor-core path) are cut into ceil(count/nt) token tiles, listed in
+  // expert order as tt_info[j] = {expert | tokens << 16, first slot}, with the
+  // number of tiles in *n_tt.
   if (ne && warp == 0) {
-    int run = 0, run_b = 0, run_tt = 0;
+    int run = 0, run_tt = 0;
     for (int base = 0; base < E; base += 32) {
       const int e = base + lane;
       const int c = e < E ? off[e + 1] - off[e] : 0;
       const bool small = c > 0 && c < thr;
       const bool bg = c > 0 && c >= thr;
       const unsigned bm = __ballot_sync(0xffffffffu, small);
-      const unsigned bb = __ballot_sync(0xffffffffu, bg);
       if (small) ne[run + __popc(bm & lt)] = e;
       const int tt = bg ? (c + nt - 1) / nt : 0;
       int incl = tt;
@@ -218,19 +218,14 @@ __global__ void __launch_bounds__(GROUP_WARPS * 32) group_kernel(
         const int u = __shfl_up_sync(0xffffffffu, incl, o);
         if (lane >= o) incl += u;
       }
-      if (bg) {
-        const int idx = run_b + __popc(bb & lt);
-        big[idx] = e;
-        big_tt[idx] = run_tt + incl - tt;
-      }
+      for (int j = 0; j < tt; ++j)
+        tt_info[run_tt + incl - tt + j] = make_int2(e | (min(nt, c - j * nt) << 16), off[e] + j * nt);
       run += __popc(bm);
-      run_b += __popc(bb);
       run_tt += __shfl_sync(0xffffffffu, incl, 31);
     }
     if (lane == 0) {
       *n_ne = run;
-      *n_big = run_b;
-      big_tt[run_b] = run_tt;
+      *n_tt = run_tt;
     }
   }
 }
@@ -241,22 +236,22 @@ size_t group_smem_bytes(int E) {
 
 int32_t launch_group_full(har_cuda_ctx *ctx, const int32_t *ids, int64_t n, int E,
                           int32_t *counts, int32_t *offsets, int32_t *order, int32_t *inv,
-                          int32_t *ne, int32_t *n_ne, int thr, int nt, int32_t *big,
-                          int32_t *n_big, int32_t *big_tt) {
+                          int32_t *ne, int32_t *n_ne, int thr, int nt, int2 *tt_info,
+                          int32_t *n_tt) {
   const size_t smem = group_smem_bytes(E);
   if (smem > 48 * 1024)
     cudaFuncSetAttribute(group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   prof_begin(ctx);
   group_kernel<<<1, GROUP_WARPS * 32, smem, ctx->stream>>>(ids, (int)n, E, counts, offsets,
-                                                           order, inv, ne, n_ne, thr, nt, big,
-                                                           n_big, big_tt, ctx->d_status);
+                                                           order, inv, ne, n_ne, thr, nt,
+                                                           tt_info, n_tt, ctx->d_status);
   return check_launch(ctx, "group_kernel");
 }
 
 int32_t launch_group(har_cuda_ctx *ctx, const int32_t *ids, int64_t T, int k, int E,
                      int32_t *counts, int32_t *offsets, int32_t *order, int32_t *inv) {
   return launch_group_full(ctx, ids, T * k, E, counts, offsets, order, inv, nullptr, nullptr, 0,
-                           1, nullptr, nullptr, nullptr);
+                           1, nullptr, nullptr);
 }
 
 }  // namespace har
