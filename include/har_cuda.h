@@ -54,7 +54,8 @@ extern "C" {
 
 /* flags for har_cuda_moe_ffn */
 #define HAR_CUDA_MOE_ADD_RESIDUAL 0x1u /* y = x + moe(x), as execute_layer_cpu */
-#define HAR_CUDA_MOE_ACT_Q8K 0x2u      /* quantise activations to Q8_K for CUDA-core GEMVs */
+#define HAR_CUDA_MOE_ACT_Q8K 0x2u      /* quantise activations to Q8_K: every expert on the
+                                          CUDA-core GEMVs (integer dots); not with FORCE_TC */
 #define HAR_CUDA_MOE_FORCE_GEMV 0x4u   /* every expert on the CUDA-core GEMV path */
 #define HAR_CUDA_MOE_FORCE_TC 0x8u     /* every expert on the tcgen05 tensor-core path */
 
@@ -73,6 +74,11 @@ int32_t har_cuda_ctx_destroy(har_cuda_ctx *ctx);
 int32_t har_cuda_last_error(const har_cuda_ctx *ctx, char *buf, size_t len);
 /* Launch on a caller-owned cudaStream_t (NULL restores the context's own). */
 int32_t har_cuda_ctx_set_stream(har_cuda_ctx *ctx, void *cuda_stream);
+/* Experts with at least `min_tokens` tokens in a moe_ffn call run on the
+ * tensor-core (tcgen05) kernels, the rest on the CUDA-core GEMV kernels;
+ * 0 restores the default (1: every expert, when the layer's shapes allow).
+ * A tuning knob of this library; the reference has no counterpart. */
+int32_t har_cuda_ctx_set_tc_min_tokens(har_cuda_ctx *ctx, int32_t min_tokens);
 /* Bounded wait for the context's stream (replaces the unbounded
  * TimelineEvent::wait, har/crates/har-vulkan/src/lib.rs:2168-2175). Also
  * checks the device error word written by kernels with bounded waits. */
@@ -159,7 +165,8 @@ int32_t har_cuda_moe_ffn_host(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer
  * cannot take the synchronisation an allocation may imply.  Scratch comes from
  * a static device array of HAR_CUDA_NOALLOC_SCRATCH_BYTES held by every GPU
  * that loads the library until exit; calls needing more return
- * HAR_CUDA_ERR_GEOMETRY (about T <= 256 tokens at H = 2048, I = 512, k = 10).
+ * HAR_CUDA_ERR_GEOMETRY (T <= 198 tokens at E = 512, H = 2048, I = 512, k = 10
+ * with f32 activations, 188 with HAR_CUDA_MOE_ACT_Q8K).
  * The first call on a device looks up the array's address (make it before any
  * stream capture).  All calls on a device share the array: calls that overlap
  * on the GPU race and must be serialised by the caller.  Arguments, results

@@ -194,6 +194,13 @@ int32_t har_cuda_ctx_set_stream(har_cuda_ctx *ctx, void *cuda_stream) {
   return HAR_CUDA_OK;
 }
 
+int32_t har_cuda_ctx_set_tc_min_tokens(har_cuda_ctx *ctx, int32_t min_tokens) {
+  if (!ctx) return HAR_CUDA_ERR_ARG;
+  if (min_tokens < 0) return har::set_error(ctx, HAR_CUDA_ERR_ARG, "set_tc_min_tokens: negative");
+  ctx->tc_min_tokens = min_tokens;
+  return HAR_CUDA_OK;
+}
+
 int64_t har_cuda_launch_count(const har_cuda_ctx *ctx) { return ctx ? ctx->launches : -1; }
 
 int32_t har_cuda_profile_begin(har_cuda_ctx *ctx) {
@@ -485,6 +492,9 @@ int32_t har::check_moe_args(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, 
     return set_error(ctx, HAR_CUDA_ERR_GEOMETRY, "moe_ffn: E <= 2048 and T*k <= 2^24");
   if ((flags & HAR_CUDA_MOE_FORCE_GEMV) && (flags & HAR_CUDA_MOE_FORCE_TC))
     return set_error(ctx, HAR_CUDA_ERR_ARG, "moe_ffn: FORCE_GEMV and FORCE_TC are exclusive");
+  if ((flags & HAR_CUDA_MOE_ACT_Q8K) && (flags & HAR_CUDA_MOE_FORCE_TC))
+    return set_error(ctx, HAR_CUDA_ERR_UNSUPPORTED,
+                     "moe_ffn: the tensor-core path has no Q8_K activation mode");
   if (flags & ~0xFu) return set_error(ctx, HAR_CUDA_ERR_ARG, "moe_ffn: unknown flag bits");
   return HAR_CUDA_OK;
 }

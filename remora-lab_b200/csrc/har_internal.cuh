@@ -117,6 +117,7 @@ struct har_cuda_ctx {
   void *io_dev = nullptr;             // device staging for *_host entry points
   size_t io_dev_bytes = 0;
   int64_t launches = 0;
+  int tc_min_tokens = 0;              // tensor-core threshold override (0 = default)
   // opt-in per-launch CUDA-event profiling (har_cuda_profile_begin/end)
   bool prof_on = false;
   cudaEvent_t prof_pending = nullptr;
@@ -173,7 +174,8 @@ int32_t launch_group(har_cuda_ctx *ctx, const int32_t *ids, int64_t T, int k, in
 int32_t run_moe_ffn(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const float *x,
                     int64_t T, int k, const int32_t *ids, const float *weights, float *y,
                     uint32_t flags);
-size_t moe_scratch_bytes(const har_cuda_moe_layer *layer, int64_t T, int k, uint32_t flags);
+size_t moe_scratch_bytes(const har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, int64_t T, int k,
+                         uint32_t flags);
 int32_t run_moe_ffn_in(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const float *x,
                        int64_t T, int k, const int32_t *ids, const float *weights, float *y,
                        uint32_t flags, uint8_t *scratch);

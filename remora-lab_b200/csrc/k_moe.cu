@@ -33,7 +33,7 @@ size_t group_smem_bytes(int E);
 int32_t launch_group_full(har_cuda_ctx *ctx, const int32_t *ids, int64_t n, int E,
                           int32_t *counts, int32_t *offsets, int32_t *order, int32_t *inv,
                           int32_t *ne, int32_t *n_ne, int thr, int nt, int2 *tt_info,
-                          int32_t *n_tt);
+                          int32_t *n_tt, int shared_T);
 
 struct MoeDev {
   const uint8_t *gate, *up, *down, *sh_gate, *sh_up, *sh_down;
@@ -333,23 +333,41 @@ struct MoeScratch {
 };
 
 // Experts with at least this many tokens take the tensor-core path
-// (FORCE_TC: every expert, FORCE_GEMV: none).  HAR_CUDA_TC_MIN_TOKENS in the
-// environment overrides the default for tuning.
-static int tc_threshold(uint32_t flags) {
+// (FORCE_TC: every expert, FORCE_GEMV: none).  The default, 1, sends every
+// expert there: measured on the config-5 stack (Zipf top-10 over 512 experts,
+// most experts with 1..16 tokens), the tensor-core kernels beat the CUDA-core
+// GEMV kernels even for single-token experts.  har_cuda_ctx_set_tc_min_tokens
+// overrides it per context, HAR_CUDA_TC_MIN_TOKENS in the environment per process.
+static int tc_threshold(const har_cuda_ctx *ctx, uint32_t flags) {
   if (flags & HAR_CUDA_MOE_FORCE_TC) return 1;
   if (flags & HAR_CUDA_MOE_FORCE_GEMV) return INT_MAX;
+  if (ctx->tc_min_tokens > 0) return ctx->tc_min_tokens;
   static const int thr = [] {
     const char *v = getenv("HAR_CUDA_TC_MIN_TOKENS");
     const int t = v ? atoi(v) : 0;
-    return t > 0 ? t : 16;
+    return t > 0 ? t : 1;
   }();
   return thr;
 }
 
-// Whether any expert of a call can reach the threshold (a token routes to an
-// expert at most once per slot, the shared expert sees all T tokens).
-static bool tc_possible(int64_t T, int k, uint32_t flags) {
-  return (int64_t)tc_threshold(flags) <= T * k;
+// Whether the layer's shapes fit the tensor-core kernels (H and I multiples
+// of 128, TMA maps encoded at layer creation).
+static bool tc_shapes_ok(const har_cuda_moe_layer *layer) {
+  return layer->tc_maps && layer->H % TC_M == 0 && layer->I % TC_M == 0 &&
+         layer->H % TC_KS == 0 && layer->I % TC_KS == 0;
+}
+
+// Whether any expert of a call can take the tensor-core path: f32 activation
+// semantics (Q8_K calls stay on the GEMV kernels, whose integer dots are the
+// Q8_K semantics), the shapes fit, and the threshold is reachable (a token
+// routes to an expert at most once, the shared expert sees all T tokens).
+// Layers whose shapes do not fit run every expert on the GEMV kernels unless
+// FORCE_TC asks for tensor cores.
+static bool tc_possible(const har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, int64_t T, int k,
+                        uint32_t flags) {
+  if (flags & HAR_CUDA_MOE_ACT_Q8K) return false;
+  if (!tc_shapes_ok(layer) && !(flags & HAR_CUDA_MOE_FORCE_TC)) return false;
+  return (int64_t)tc_threshold(ctx, flags) <= T * k;
 }
 
 static MoeScratch moe_layout(const har_cuda_moe_layer *layer, int64_t T, int k, bool q8,
@@ -370,23 +388,26 @@ static MoeScratch moe_layout(const har_cuda_moe_layer *layer, int64_t T, int k, 
   s.o_a = take(4 * (size_t)(slots * I));
   s.o_aq = q8 ? take((size_t)(slots * aq_row)) : 0;
   s.o_y = take(4 * (size_t)(slots * H));
-  s.o_ttinfo = take(8 * (size_t)(std::min<int64_t>(E, n) + n / TC_NT + 1));  // routed token tiles
+  // token tiles: routed (<= one partial tile per expert) then the shared expert's
+  s.o_ttinfo = take(8 * (size_t)(std::min<int64_t>(E, n) + n / TC_NT + T / TC_NT + 2));
   s.o_ntt = take(4);
-  s.o_x16 = tc ? take(2 * (size_t)(slots * H)) : 0;  // token rows in slot order (f16)
-  s.o_a16 = tc ? take(2 * (size_t)(slots * I)) : 0;
+  s.o_x16 = tc ? take(4 * (size_t)(slots * H)) : 0;  // token rows in slot order (f16 hi/lo)
+  s.o_a16 = tc ? take(4 * (size_t)(slots * I)) : 0;
   s.total = off;
   return s;
 }
 
-size_t moe_scratch_bytes(const har_cuda_moe_layer *layer, int64_t T, int k, uint32_t flags) {
-  return moe_layout(layer, T, k, (flags & HAR_CUDA_MOE_ACT_Q8K) != 0, tc_possible(T, k, flags))
+size_t moe_scratch_bytes(const har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, int64_t T, int k,
+                         uint32_t flags) {
+  return moe_layout(layer, T, k, (flags & HAR_CUDA_MOE_ACT_Q8K) != 0,
+                    tc_possible(ctx, layer, T, k, flags))
       .total;
 }
 
 int32_t run_moe_ffn(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const float *x,
                     int64_t T, int k, const int32_t *ids, const float *weights, float *y,
                     uint32_t flags) {
-  int32_t st = ensure_scratch(ctx, moe_scratch_bytes(layer, T, k, flags));
+  int32_t st = ensure_scratch(ctx, moe_scratch_bytes(ctx, layer, T, k, flags));
   if (st) return st;
   return run_moe_ffn_in(ctx, layer, x, T, k, ids, weights, y, flags, (uint8_t *)ctx->scratch);
 }
@@ -403,8 +424,8 @@ int32_t run_moe_ffn_in(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const
   const int64_t n = T * k;
   const int has_sh = layer->sh_gate ? 1 : 0;
   const int64_t xq_row = (int64_t)(H / QK) * Q8K_BYTES, aq_row = (int64_t)(I / QK) * Q8K_BYTES;
-  const bool tc = tc_possible(T, k, flags);
-  const int thr = tc ? tc_threshold(flags) : INT_MAX;
+  const bool tc = tc_possible(ctx, layer, T, k, flags);
+  const int thr = tc ? tc_threshold(ctx, flags) : INT_MAX;
   const bool shared_tc = has_sh && tc && T >= thr;
   if (tc && ((H % TC_M) || (I % TC_M) || (H % TC_KS) || (I % TC_KS)))
     return set_error(ctx, HAR_CUDA_ERR_UNSUPPORTED,
@@ -455,7 +476,7 @@ int32_t run_moe_ffn_in(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const
   st = launch_group_full(ctx, ids, n, E, (int32_t *)(S + o_counts), (int32_t *)(S + o_offsets),
                          (int32_t *)(S + o_order), (int32_t *)(S + o_inv), (int32_t *)(S + o_ne),
                          (int32_t *)(S + o_nne), thr, TC_NT, (int2 *)(S + L.o_ttinfo),
-                         (int32_t *)(S + L.o_ntt));
+                         (int32_t *)(S + L.o_ntt), shared_tc ? (int)T : 0);
   if (st) return st;
   // tensor-core path parameters (experts with >= thr tokens)
   TcParams tp{};
@@ -483,19 +504,19 @@ int32_t run_moe_ffn_in(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const
       dmaps.sh0 = layer->map_sh_down;
       dmaps.sh1 = layer->map_sh_down;
     }
-    // token rows in slot order (f16): the B operands, one box of 16/32/64 rows
-    // x 64 values per K-step
-    const uint64_t slots = (uint64_t)(n + T);
+    // token rows in slot order (f16 hi/lo row pairs): the B operands, one box
+    // of 32/64 rows x 64 values per K-step
+    const uint64_t rows2 = 2 * (uint64_t)(n + T);
     for (int bx = 0; bx < TC_NBOX; ++bx) {
-      if ((st = encode_tmap_2d(ctx, &gmaps.b[bx], S + L.o_x16, 2, slots, (uint64_t)H,
-                               (uint64_t)H * 2, 16u << bx, 64, true)))
+      if ((st = encode_tmap_2d(ctx, &gmaps.b[bx], S + L.o_x16, 2, rows2, (uint64_t)H,
+                               (uint64_t)H * 2, 32u << bx, 64, true)))
         return st;
-      if ((st = encode_tmap_2d(ctx, &dmaps.b[bx], S + L.o_a16, 2, slots, (uint64_t)I,
-                               (uint64_t)I * 2, 16u << bx, 64, true)))
+      if ((st = encode_tmap_2d(ctx, &dmaps.b[bx], S + L.o_a16, 2, rows2, (uint64_t)I,
+                               (uint64_t)I * 2, 32u << bx, 64, true)))
         return st;
     }
-    if ((st = launch_gather_f16(ctx, x, H, p.order, ids, p.counts, thr, (int)n, k, (int)T,
-                                tp.shared_tc, (__half *)(S + L.o_x16))))
+    if ((st = launch_gather_f16(ctx, x, H, p.order, ids, p.counts, p.offsets + E, thr, (int)n, k,
+                                (int)T, tp.shared_tc, (__half *)(S + L.o_x16))))
       return st;
   }
   // upper bound of tensor-core token tiles: each big expert has >= thr tokens

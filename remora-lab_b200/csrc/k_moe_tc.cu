@@ -5,43 +5,52 @@
 // (har/crates/har-demo/src/bin/har-native-qwen35moe.rs:979-1048) per token.
 //
 // Shape: the weights are the MMA's M side ("swap AB"): a tile is 128 weight
-// rows x up to 64 token columns, so a tile of W is dequantised once for up to
-// 64 tokens.  D = W_tile * X^T accumulates in TMEM (f32).
+// rows x up to 32 tokens, so a tile of W is dequantised once for up to 32
+// tokens.  Each token is two B rows, the f16 value and the f16 remainder
+// (hi = f16(x), lo = f16(x - hi)), so activations reach the tensor cores with
+// ~22 significant bits and only the weights are rounded to f16; the epilogue
+// adds the two accumulator columns.  D = W_tile * X^T accumulates in TMEM (f32).
 //   gate/up: two accumulators (gate rows and up rows of the same 128
-//            intermediate indices); epilogue a = silu(g) * u -> a16[slot][i] (f16).
+//            intermediate indices); epilogue a = silu(g) * u -> a16 (hi/lo f16
+//            rows of the slot, the down GEMM's B operand).
 //   down:    one accumulator; epilogue ybuf[slot][h] (f32), then the common
 //            combine kernel applies the routing weights in slot order.
 //
-// With few tokens per expert the MMAs are narrow (N = 16..64) and a single
-// issuing warp cannot keep up with HBM: each tcgen05.mma costs the issuer
-// about 100 cycles whatever N is, i.e. ~20 weights per cycle, while one SM's
-// share of HBM bandwidth is ~40 Q4_K weights per cycle.  So two warps issue,
-// each for alternate 64-value K-steps into its own accumulator set, and the
-// epilogue adds the two partial sums.
+// With few tokens per expert the MMAs are narrow (N = 32..64) and issue
+// rate matters: one SM's share of HBM bandwidth is ~40 Q4_K weights per cycle,
+// and a K-step (NA x 4 MMAs of 128 x 16 weights) must issue in ~400 cycles.
+// The issuing warp stays warp-uniform, elects its lane once and issues a
+// K-step's MMAs from one asm block (~40 cycles per MMA, measured).
 //
 // One persistent CTA per SM, warp-specialised, every handoff an mbarrier:
 //   TMA threads:  one loads raw Q4_K boxes (128 rows x one 144-byte
 //                 super-block per matrix) into a raw ring in shared memory;
 //                 another loads 128-byte-swizzled f16 token tiles (64 values x
-//                 16/32/64 rows: the smallest box covering the tile's tokens,
+//                 32/64 rows: the smallest box covering the tile's hi/lo rows,
 //                 which sit in slot order) into a B ring whose 16 KB slots
 //                 hold 128/box-rows K-steps each.
-//   dequant warps: two teams of four, team t taking the K-steps of issuer t,
-//                 turn the raw blocks into f16 weights with packed-f16
-//                 arithmetic and store them straight into the team's two
-//                 tensor-memory stages with tcgen05.st (warp w owns TMEM lanes
+//   dequant warps: four teams of four, team t taking the K-steps ks = t
+//                 (mod 4), turn the raw blocks into f16 weights with packed-f16
+//                 arithmetic and store them straight into the team's
+//                 tensor-memory stage with tcgen05.st (warp w owns TMEM lanes
 //                 32*(w%4).. = those rows).  Keeping the weight operand out of
 //                 shared memory keeps its write and its tensor-core read off
-//                 the shared-memory bandwidth.
-//   MMA warps:    4 x tcgen05.mma (K=16, A from TMEM, B from shared memory)
+//                 the shared-memory bandwidth.  The dequantisation is most of
+//                 the kernel's instruction stream, hence the 16 warps.
+//   MMA warp:     4 x tcgen05.mma (K=16, A from TMEM, B from shared memory)
 //                 per matrix per K-step; tcgen05.commit frees the weight stage
 //                 and the B slot, and signals the epilogue at the end of a tile.
-//   epilogue warps: tcgen05.ld both partial accumulators, add, apply the
-//                 epilogue, store, then free the accumulator columns.
+//   epilogue warps: tcgen05.ld the accumulator (hi and lo columns of each
+//                 token), add, apply the epilogue, store, then free the
+//                 accumulator columns.
 // No multicast: every TMA load reads this GPU's memory into this CTA only.
 // Operands are f16 (same tensor rate as bf16, 3 more mantissa bits): each
-// weight is d*(sc*q) with sc*q exact, minus dmin*m rounded to f16, rounded
-// once more to f16; each activation is rounded once to f16; accumulation is f32.
+// weight is rounded once to f16 from d*sc*(q - 8) (exact) plus a centred
+// per-sub-block offset rounded to f16; activations are hi/lo f16 pairs;
+// accumulation is f32.
+// K order: inside every group of four K values both operands hold positions
+// (0, 2, 1, 3) -- the order in which nibble pairs come out of a 32-bit word
+// with one mask each -- which leaves every dot product unchanged.
 #include <algorithm>
 
 #include "gemv_engine.cuh"
@@ -65,43 +74,23 @@ struct TcSmem {
 };
 
 // Tensor-memory plan (512 columns x 128 lanes): accumulators in 64-column
-// quarters at [0, A_COL0), then TC_ISSUERS x 2 f16 weight stages of NA x 32
-// columns (one 64-value K-step: row = lane, two f16 per column in K order).
-// A tile with token box rows_b takes ceil(TC_ISSUERS * NA * rows_b / 64)
-// quarters: issuer i's accumulator of matrix m sits at column
-// (i * NA + m) * rows_b of the tile's first quarter.
+// quarters at [0, A_COL0), then one f16 weight stage per dequant team, NA x 32
+// columns each (one 64-value K-step: row = lane, two f16 per column).
+// A tile whose token box has bw B rows (2 per token) takes
+// ceil(NA * bw / 64) quarters: matrix m's accumulator sits at column m * bw
+// of the tile's first quarter.
 template <int NA>
 struct TcTmem {
-  static constexpr int A_STAGES = 2 * TC_ISSUERS;
+  static constexpr int A_STAGES = TC_DQ_TEAMS;
   static constexpr int A_COL0 = TC_TMEM_COLS - A_STAGES * NA * 32;
   static constexpr int NQ = A_COL0 / 64;
-  static __device__ __forceinline__ int quarters(int rows_b) {
-    return (TC_ISSUERS * NA * rows_b + 63) / 64;
+  static __device__ __forceinline__ int quarters(int bw) {
+    return (NA * bw + 63) / 64;
   }
 };
 
-// Smallest token-tile box (16, 32 or 64 rows) covering n tokens.
-__device__ __forceinline__ int tc_box(int n) { return n <= 16 ? 0 : n <= 32 ? 1 : 2; }
-
-// Map a token-tile index to (expert, or E for the shared expert; token
-// count; first slot).  Routed tiles come from the grouping kernel's table,
-// the shared expert's tiles follow them.  False when the index is past the work.
-__device__ __forceinline__ bool tc_tile(const TcParams &p, int routed_tt, int ttg, int &e,
-                                        int &ntok, int &slot0) {
-  if (ttg < routed_tt) {
-    const int2 v = p.tt_info[ttg];
-    e = v.x & 0xffff;
-    ntok = v.x >> 16;
-    slot0 = v.y;
-    return true;
-  }
-  if (!p.shared_tc) return false;
-  const int t0 = (ttg - routed_tt) * TC_NT;
-  e = p.E;
-  ntok = min(TC_NT, p.T - t0);
-  slot0 = p.n + t0;
-  return ntok > 0;
-}
+// Smallest token-tile box covering n tokens: 0 = 32 B rows (16 tokens), 1 = 64.
+__device__ __forceinline__ int tc_box(int n) { return n <= 16 ? 0 : 1; }
 
 // Accumulator quarters of the next tile: `qc` is the ring cursor (the MMA
 // warps and the epilogue walk the same tiles, so they agree); a tile that does
@@ -115,38 +104,60 @@ __device__ __forceinline__ int tc_take_quarters(int &qc, int nq) {
   return q0;
 }
 
-// Dequantise one 32-value sub-block of a raw Q4_K block in shared memory
-// (`blk` = the 144-byte block; chunk c of 4; `hi` selects the high nibbles,
-// i.e. the odd sub-block) into 16 f16x2 words in K order.
+// Dequantise one 64-value K-step (chunk c of 4) of a raw Q4_K block in
+// shared memory (`blk` = the 144-byte block of this lane's row) into 32 f16x2
+// words: o[0..16) the low-nibble sub-block 2c, o[16..32) the high-nibble
+// sub-block 2c+1, each word-pair holding values (4i, 4i+2), (4i+1, 4i+3).
+//
+// Each weight is computed centred, w = d*sc*(q - 8) + (8*d*sc - dmin*m):
+// the offset c = 8*d*sc - dmin*m sits near the middle of the sub-block's
+// range, so rounding it to f16 costs little.  (Rounding the raw offset
+// -dmin*m instead, as large as the weights, puts one shared error on all 32
+// weights of a sub-block and about doubles the error of a dot product.)
 // Packed f16 arithmetic, two values per instruction:
-//   byte-permute each nibble q into the f16 bit pattern 0x64qq = 1024 + q,
-//   hfma2((1024 + q), sc, -1024*sc) = sc*q exactly (an integer <= 945),
-//   hfma2(sc*q, d, -(dmin*m)) = d*sc*q - dmin*m rounded once to f16
-// (d is the block's f16 scale, exact; dmin*m is rounded to f16 first).
-__device__ __forceinline__ void tc_dequant_sub(const uint8_t *blk, int c, int hi, uint32_t *o) {
+//   a mask and a shift put two nibbles in mantissa bits 4..7 under the
+//   exponent of 64: (v & 0x00F000F0) | 0x54005400 = (64 + q0, 64 + q2);
+//   hfma2(64 + q, sc, -72 sc) = sc*(q - 8) exactly (|.| <= 504, and 72*sc has
+//   at most 10 significant bits);
+//   hfma2(sc*(q - 8), d, c) = the weight rounded once to f16 (d is the block's
+//   f16 scale, exact; c is rounded to f16 from f32).
+__device__ __forceinline__ void tc_dequant_step(const uint8_t *blk, int c, uint32_t (&o)[32]) {
   const uint4 hdr = *reinterpret_cast<const uint4 *>(blk);
-  const uint4 q0 = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * c);
-  const uint4 q1 = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * c);
-  int sc, mn;
-  q4k_scale_min(hdr.y, hdr.z, hdr.w, 2 * c + hi, sc, mn);
+  const uint4 qa = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * c);
+  const uint4 qb = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * c);
+  int sc0, m0, sc1, m1;
+  q4k_scale_min(hdr.y, hdr.z, hdr.w, 2 * c, sc0, m0);
+  q4k_scale_min(hdr.y, hdr.z, hdr.w, 2 * c + 1, sc1, m1);
   const __half2 d2 = __half2half2(__ushort_as_half((unsigned short)(hdr.x & 0xffffu)));
-  const __half2 sc2 = __half2half2(__int2half_rn(sc));
-  const __half2 nsc2 = __half2half2(__int2half_rn(-1024 * sc));
-  const float dmin = f16_bits_to_f32(hdr.x >> 16);
-  const __half2 c2 = __half2half2(__float2half_rn(-(dmin * (float)mn)));
-  const uint32_t q[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+  const float d = f16_bits_to_f32(hdr.x & 0xffffu), dmin = f16_bits_to_f32(hdr.x >> 16);
+  const __half2 s_lo = __half2half2(__int2half_rn(sc0));
+  const __half2 n_lo = __half2half2(__int2half_rn(-72 * sc0));
+  const __half2 c_lo = __half2half2(__float2half_rn(8.0f * d * (float)sc0 - dmin * (float)m0));
+  const __half2 s_hi = __half2half2(__int2half_rn(sc1));
+  const __half2 n_hi = __half2half2(__int2half_rn(-72 * sc1));
+  const __half2 c_hi = __half2half2(__float2half_rn(8.0f * d * (float)sc1 - dmin * (float)m1));
+  const uint32_t q[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {  // word i holds values 4i .. 4i+3 of the sub-block
-    const uint32_t v = hi ? (q[i] >> 4) & 0x0F0F0F0Fu : q[i] & 0x0F0F0F0Fu;
-    const uint32_t p01 = __byte_perm(v, 0x64646464u, 0x5140);  // (1024+q0, 1024+q1)
-    const uint32_t p23 = __byte_perm(v, 0x64646464u, 0x7362);  // (1024+q2, 1024+q3)
-    const __half2 s01 = __hfma2(*reinterpret_cast<const __half2 *>(&p01), sc2, nsc2);
-    const __half2 s23 = __hfma2(*reinterpret_cast<const __half2 *>(&p23), sc2, nsc2);
-    const __half2 w01 = __hfma2(s01, d2, c2);
-    const __half2 w23 = __hfma2(s23, d2, c2);
-    o[2 * i] = *reinterpret_cast<const uint32_t *>(&w01);
-    o[2 * i + 1] = *reinterpret_cast<const uint32_t *>(&w23);
+  for (int i = 0; i < 8; ++i) {  // word i: bytes 4i .. 4i+3 of the chunk
+    const uint32_t w = q[i];
+    const uint32_t pa = ((w << 4) & 0x00F000F0u) | 0x54005400u;  // low nibbles of bytes 0, 2
+    const uint32_t pb = ((w >> 4) & 0x00F000F0u) | 0x54005400u;  // low nibbles of bytes 1, 3
+    const uint32_t pc = (w & 0x00F000F0u) | 0x54005400u;         // high nibbles of bytes 0, 2
+    const uint32_t pd = ((w >> 8) & 0x00F000F0u) | 0x54005400u;  // high nibbles of bytes 1, 3
+    const __half2 a = __hfma2(__hfma2(*reinterpret_cast<const __half2 *>(&pa), s_lo, n_lo), d2, c_lo);
+    const __half2 b = __hfma2(__hfma2(*reinterpret_cast<const __half2 *>(&pb), s_lo, n_lo), d2, c_lo);
+    const __half2 e = __hfma2(__hfma2(*reinterpret_cast<const __half2 *>(&pc), s_hi, n_hi), d2, c_hi);
+    const __half2 f = __hfma2(__hfma2(*reinterpret_cast<const __half2 *>(&pd), s_hi, n_hi), d2, c_hi);
+    o[2 * i] = *reinterpret_cast<const uint32_t *>(&a);
+    o[2 * i + 1] = *reinterpret_cast<const uint32_t *>(&b);
+    o[16 + 2 * i] = *reinterpret_cast<const uint32_t *>(&e);
+    o[16 + 2 * i + 1] = *reinterpret_cast<const uint32_t *>(&f);
   }
+}
+
+// Position of K index k in the (0, 2, 1, 3)-per-group order of the operands.
+__host__ __device__ __forceinline__ int tc_kperm(int k) {
+  return (k & ~3) | ((k & 1) << 1) | ((k >> 1) & 1);
 }
 
 __device__ __forceinline__ float tc_silu(float v) { return v / (1.0f + expf(-v)); }
@@ -159,10 +170,12 @@ __device__ __forceinline__ bool tc_wait(uint64_t *bar, uint32_t parity, volatile
   *abort_s = 1;
   return false;
 }
-// The same for a whole warp: lane 0 polls, the outcome is broadcast, and the
-// warp leaves converged (the warp-wide MMA forms need it so).
+// The same for a whole warp, which leaves converged (the warp-wide tcgen05
+// forms need it so): one warp-wide test first, then lane 0 polls and the
+// outcome is broadcast.
 __device__ __forceinline__ bool tc_wait_warp(uint64_t *bar, uint32_t parity, volatile int *abort_s,
                                              int lane) {
+  if (__all_sync(0xffffffffu, tc::mbar_try_wait(bar, parity))) return true;
   bool ok = true;
   if (lane == 0) ok = tc_wait(bar, parity, abort_s);
   return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
@@ -196,16 +209,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
       tc::mbar_init(raw_empty + s, TC_DQ_WARPS);
     }
     for (int s = 0; s < AS; ++s) {
-      tc::mbar_init(a_full + s, TC_DQ_WARPS / TC_ISSUERS);  // one team fills a stage
+      tc::mbar_init(a_full + s, TC_DQ_WARPS / TC_DQ_TEAMS);  // one team fills a stage
       tc::mbar_init(a_empty + s, 1);
     }
     for (int q = 0; q < NQ; ++q) {
-      tc::mbar_init(acc_full + q, TC_ISSUERS);
+      tc::mbar_init(acc_full + q, 1);
       tc::mbar_init(acc_empty + q, 4);
     }
     for (int s = 0; s < BS; ++s) {
       tc::mbar_init(b_full + s, 1);
-      tc::mbar_init(b_empty + s, TC_ISSUERS);
+      tc::mbar_init(b_empty + s, 1);
     }
     tc::fence_mbar_init();
     abort_flag = 0;
@@ -221,18 +234,21 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
 
   const int RT = p.rows / TC_M;
   const int KSTEPS = p.K / 64, KSB = p.K / 256;
-  const int routed_tt = *p.n_tt;
-  const int total_tt = routed_tt + (p.shared_tc ? (p.T + TC_NT - 1) / TC_NT : 0);
-  const int total = total_tt * RT;
+  // Tiles: token tile (tile / RT) x weight-row tile (tile % RT), walked with a
+  // stride of gridDim.x.  Each role loads the table entry of its next tile one
+  // tile ahead, unconditionally (clamped index), so the load stays in flight.
+  const int total = *p.n_tt * RT;
 
   if (warp == TC_WARP_TMA) {
     // ---------------- producer: raw weight boxes ----------------
     if (lane == 0) {
       uint32_t raw_it = 0;
       bool ok = true;
+      int2 nxt = p.tt_info[min((int)blockIdx.x, max(total - 1, 0)) / RT];
       for (int tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
-        int e, ntok, slot0;
-        if (!tc_tile(p, routed_tt, tile / RT, e, ntok, slot0)) continue;
+        const int2 cur = nxt;  // the next tile's entry is loaded one tile ahead
+        nxt = p.tt_info[min(tile + (int)gridDim.x, total - 1) / RT];
+        const int e = cur.x & 0xffff;
         const int r0 = (tile % RT) * TC_M;
         const bool sh = e == p.E;
         const void *m0 = sh ? (const void *)&maps.sh0 : (const void *)&maps.a0;
@@ -254,66 +270,71 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
     if (lane == 0) {
       uint32_t b_it = 0;
       bool ok = true;
+      int2 nxt = p.tt_info[min((int)blockIdx.x, max(total - 1, 0)) / RT];
       for (int tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
-        int e, ntok, slot0;
-        if (!tc_tile(p, routed_tt, tile / RT, e, ntok, slot0)) continue;
+        const int2 cur = nxt;  // the next tile's entry is loaded one tile ahead
+        nxt = p.tt_info[min(tile + (int)gridDim.x, total - 1) / RT];
+        const int ntok = cur.x >> 16, slot0 = cur.y;
         const int bx = tc_box(ntok);
         const void *bm = &maps.b[bx];
-        const int rows_b = 16 << bx, kpb = 128 / rows_b;  // K-steps per B slot
-        const uint32_t sub_bytes = (uint32_t)rows_b * 128u;
+        const int bw = 32 << bx, kpb = 128 / bw;  // B rows of the tile; K-steps per B slot
+        const uint32_t sub_bytes = (uint32_t)bw * 128u;
         for (int s0 = 0; ok && s0 < KSTEPS; s0 += kpb) {
           const int bs = b_it % BS, nsub = min(kpb, KSTEPS - s0);
           if (!(ok = tc_wait(b_empty + bs, ((b_it / BS) & 1u) ^ 1u, abort_s))) break;
           tc::mbar_expect_tx(b_full + bs, sub_bytes * (uint32_t)nsub);
           for (int j = 0; j < nsub; ++j)
-            tc::tma_load_2d(sm + L::OFF_B + bs * L::BSL + j * sub_bytes, bm, (s0 + j) * 64, slot0, b_full + bs);
+            tc::tma_load_2d(sm + L::OFF_B + bs * L::BSL + j * sub_bytes, bm, (s0 + j) * 64, 2 * slot0,
+                            b_full + bs);
           ++b_it;
         }
       }
     }
-  } else if (warp == TC_WARP_MMA0 || warp == TC_WARP_MMA1) {
-    // ---------------- MMA issuers (whole warp, one elected lane issues) ----------------
-    const int is = warp == TC_WARP_MMA0 ? 0 : 1;  // this warp takes K-steps ks % 2 == is
-    uint32_t j = 0, b_it = 0, par = 0;  // par bit q: parity of quarter q's uses
+  } else if (warp == TC_WARP_MMA) {
+    // ---------------- MMA issuer (whole warp, one elected lane issues) ----------------
+    // K-step ks of a tile sits in weight stage ks % 4 (every tile has a
+    // multiple of 4 K-steps), whose u-th fill is global K-step 4u + stage.
+    const uint32_t lead = tc::elect_one();
+    const uint32_t b_base = tc::smem_u32(sm + L::OFF_B);
+    const uint32_t a_base = tmem + (uint32_t)TM::A_COL0;
+    uint32_t gs0 = 0, b_it = 0, par = 0;  // par bit q: parity of quarter q's uses
     int qc = 0;
     bool ok = true;
+    int2 nxt = p.tt_info[min((int)blockIdx.x, max(total - 1, 0)) / RT];
     for (int tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
-      int e, ntok, slot0;
-      if (!tc_tile(p, routed_tt, tile / RT, e, ntok, slot0)) continue;
-      const int rows_b = 16 << tc_box(ntok), kpb = 128 / rows_b, nq = TM::quarters(rows_b);
+      const int2 cur = nxt;  // the next tile's entry is loaded one tile ahead
+      nxt = p.tt_info[min(tile + (int)gridDim.x, total - 1) / RT];
+      const int ntok = cur.x >> 16;
+      const int bw = 32 << tc_box(ntok), kpb = 128 / bw, nq = TM::quarters(bw);
       const int q0 = tc_take_quarters<NA>(qc, nq);
       for (int u = 0; ok && u < nq; ++u)
         ok = tc_wait_warp(acc_empty + q0 + u, ((par >> (q0 + u)) & 1u) ^ 1u, abort_s, lane);
       if (!ok) break;
       tc::tc_fence_after();
-      const uint32_t idesc = tc::idesc_f16(TC_M, (ntok + 15) & ~15);
-      const uint32_t dcol = tmem + (uint32_t)(q0 * 64 + is * NA * rows_b);
-      for (int ks = is; ks < KSTEPS; ks += 2, ++j) {
-        const int st = is * 2 + (int)(j & 1u);
-        if (!(ok = tc_wait_warp(a_full + st, (j >> 1) & 1u, abort_s, lane))) break;
-        const int s0 = ks - ks % kpb, send = min(s0 + kpb, KSTEPS), bs = b_it % BS;
-        if (ks == s0 + is)
-          if (!(ok = tc_wait_warp(b_full + bs, (b_it / BS) & 1u, abort_s, lane))) break;
-        tc::tc_fence_after();
-        const uint64_t bdesc0 =
-            tc::desc_sw128(tc::smem_u32(sm + L::OFF_B + bs * L::BSL) + (uint32_t)((ks - s0) * rows_b * 128));
-        const uint32_t acol = tmem + (uint32_t)(TM::A_COL0 + st * NA * 32);
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-#pragma unroll
-          for (int m = 0; m < NA; ++m)
-            tc::mma_f16_ts_w(dcol + (uint32_t)(m * rows_b), acol + (uint32_t)(m * 32 + kk * 8),
-                             bdesc0 + (uint64_t)(2 * kk), idesc, (ks >= 2 || kk > 0) ? 1u : 0u);
+      const uint32_t idesc = tc::idesc_f16(TC_M, (2 * ntok + 15) & ~15);
+      const uint32_t dcol = tmem + (uint32_t)(q0 * 64);
+      const uint32_t sub_desc = (uint32_t)(bw * 128) >> 4;  // one K-step of B, descriptor units
+      for (int s0 = 0; ok && s0 < KSTEPS; s0 += kpb) {  // the tile's B slots
+        const int bs = b_it % BS, send = min(kpb, KSTEPS - s0);
+        if (!(ok = tc_wait_warp(b_full + bs, (b_it / BS) & 1u, abort_s, lane))) break;
+        const uint64_t bslot = tc::desc_sw128(b_base + (uint32_t)(bs * L::BSL));
+        for (int sub = 0; sub < send; ++sub) {
+          const int ks = s0 + sub, st = ks & 3;
+          if (!(ok = tc_wait_warp(a_full + st, ((gs0 + (uint32_t)ks) >> 2) & 1u, abort_s, lane))) break;
+          tc::tc_fence_after();
+          const uint64_t bdesc = bslot + (uint64_t)(sub * sub_desc);
+          const uint32_t acol = a_base + (uint32_t)(st * NA * 32);
+          tc::mma_kstep_ts<NA>(lead, dcol, (uint32_t)bw, acol, bdesc, idesc, ks > 0 ? 1u : 0u);
+          tc::mma_commit_w(lead, a_empty + st);
         }
-        tc::mma_commit_w(a_empty + st);
-        if (ks == send - 2 + is) {
-          tc::mma_commit_w(b_empty + bs);
-          ++b_it;
-        }
+        if (!ok) break;
+        tc::mma_commit_w(lead, b_empty + bs);
+        ++b_it;
       }
       if (!ok) break;
-      for (int u = 0; u < nq; ++u) tc::mma_commit_w(acc_full + q0 + u);
+      for (int u = 0; u < nq; ++u) tc::mma_commit_w(lead, acc_full + q0 + u);
       par ^= ((1u << nq) - 1u) << q0;
+      gs0 += (uint32_t)KSTEPS;
     }
   } else if (warp < TC_WARP_DQ0) {
     // ---------------- epilogue: TMEM -> global ----------------
@@ -322,10 +343,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
     uint32_t par = 0;
     int qc = 0;
     bool ok = true;
+    int2 nxt = p.tt_info[min((int)blockIdx.x, max(total - 1, 0)) / RT];
     for (int tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
-      int e, ntok, slot0;
-      if (!tc_tile(p, routed_tt, tile / RT, e, ntok, slot0)) continue;
-      const int rows_b = 16 << tc_box(ntok), nq = TM::quarters(rows_b);
+      const int2 cur = nxt;  // the next tile's entry is loaded one tile ahead
+      nxt = p.tt_info[min(tile + (int)gridDim.x, total - 1) / RT];
+      const int ntok = cur.x >> 16, slot0 = cur.y;
+      const int bw = 32 << tc_box(ntok), nq = TM::quarters(bw);
       const int q0 = tc_take_quarters<NA>(qc, nq);
       for (int u = 0; ok && u < nq; ++u)
         ok = tc_wait_warp(acc_full + q0 + u, (par >> (q0 + u)) & 1u, abort_s, lane);
@@ -333,28 +356,34 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
       tc::tc_fence_after();
       const int row = (tile % RT) * TC_M + 32 * g + lane;
       const uint32_t dcol = tmem + lane_addr + (uint32_t)(q0 * 64);
-      for (int col = 0; col < ntok; col += 16) {
-        uint32_t g0[16], g1[16];
-        tc::tmem_ld16(dcol + (uint32_t)col, g0);                         // issuer 0, matrix 0
-        tc::tmem_ld16(dcol + (uint32_t)(NA * rows_b + col), g1);          // issuer 1, matrix 0
+      const int prow = tc_kperm(row);  // a16 feeds the down GEMM's K axis
+      // column 2t holds token t's hi part, 2t+1 its lo part; 16 columns = 8 tokens
+      for (int col = 0; col < 2 * ntok; col += 16) {
+        const int t0 = col >> 1;
+        uint32_t v[16];
+        tc::tmem_ld16(dcol + (uint32_t)col, v);                          // matrix 0
+        tc::tmem_wait_ld();
+        float gv[8];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) gv[c] = __uint_as_float(v[2 * c]) + __uint_as_float(v[2 * c + 1]);
         if (NA == 2) {
-          uint32_t u0[16], u1[16];
-          tc::tmem_ld16(dcol + (uint32_t)(rows_b + col), u0);             // issuer 0, matrix 1
-          tc::tmem_ld16(dcol + (uint32_t)(3 * rows_b + col), u1);         // issuer 1, matrix 1
+          tc::tmem_ld16(dcol + (uint32_t)(bw + col), v);                 // matrix 1
           tc::tmem_wait_ld();
 #pragma unroll
-          for (int c = 0; c < 16; ++c)
-            if (col + c < ntok) {
-              const float gv = __uint_as_float(g0[c]) + __uint_as_float(g1[c]);
-              const float uv = __uint_as_float(u0[c]) + __uint_as_float(u1[c]);
-              p.a16[((int64_t)slot0 + col + c) * p.out_ld + row] = __float2half_rn(__fmul_rn(tc_silu(gv), uv));
+          for (int c = 0; c < 8; ++c)
+            if (t0 + c < ntok) {
+              const float uv = __uint_as_float(v[2 * c]) + __uint_as_float(v[2 * c + 1]);
+              const float av = __fmul_rn(tc_silu(gv[c]), uv);
+              const __half hi = __float2half_rn(av);
+              const __half lo = __float2half_rn(av - __half2float(hi));
+              __half *dst = p.a16 + 2 * ((int64_t)slot0 + t0 + c) * p.out_ld + prow;
+              dst[0] = hi;
+              dst[p.out_ld] = lo;
             }
         } else {
-          tc::tmem_wait_ld();
 #pragma unroll
-          for (int c = 0; c < 16; ++c)
-            if (col + c < ntok)
-              p.ybuf[((int64_t)slot0 + col + c) * p.out_ld + row] = __uint_as_float(g0[c]) + __uint_as_float(g1[c]);
+          for (int c = 0; c < 8; ++c)
+            if (t0 + c < ntok) p.ybuf[((int64_t)slot0 + t0 + c) * p.out_ld + row] = gv[c];
         }
       }
       tc::tc_fence_before();
@@ -365,43 +394,37 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
     }
   } else {
     // ---------------- dequantisers: raw Q4_K -> f16 weight stages in TMEM ----------------
-    // Team t (four warps) takes the K-steps of issuer t, filling that issuer's
-    // two stages in turn.  Warp w may store only TMEM lanes 32*(w%4)..: it
-    // owns weight rows 32*(w%4)+lane of every matrix of its team's steps.
+    // Team t (four warps) takes the K-steps ks = t (mod 4) -- one of the four
+    // K-steps of every raw slot -- and fills weight stage t with them.  Warp
+    // w may store only TMEM lanes 32*(w%4)..: it owns weight rows
+    // 32*(w%4)+lane of every matrix.
     const int g = warp & 3, team = (warp - TC_WARP_DQ0) >> 2;
     const int r = 32 * g + lane;
     const uint32_t lane_addr = (uint32_t)(32 * g) << 16;
-    uint32_t j = 0, gs0 = 0;  // team K-steps so far; K-steps of earlier tiles
+    const uint32_t acol = tmem + lane_addr + (uint32_t)(TM::A_COL0 + team * NA * 32);
+    uint32_t u = 0, rit = 0;  // team K-steps so far; raw slots so far
     bool ok = true;
     for (int tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
-      int e, ntok, slot0;
-      if (!tc_tile(p, routed_tt, tile / RT, e, ntok, slot0)) continue;
-      for (int ks = team; ks < KSTEPS; ks += 2, ++j) {
-        const uint32_t gs = gs0 + ks;               // global K-step
-        const uint32_t rit = gs >> 2;               // raw slot sequence (4 K-steps a slot)
-        const int rs = rit % RS, st = team * 2 + (int)(j & 1u);
-        if ((ks & 3) == team)                       // this warp's first step of the slot
-          if (!(ok = tc_wait_warp(raw_full + rs, (rit / RS) & 1u, abort_s, lane))) break;
-        if (!(ok = tc_wait_warp(a_empty + st, ((j >> 1) & 1u) ^ 1u, abort_s, lane))) break;
+      for (int ks = team; ks < KSTEPS; ks += TC_DQ_TEAMS, ++u, ++rit) {
+        const int rs = rit % RS;
+        if (!(ok = tc_wait_warp(raw_full + rs, (rit / RS) & 1u, abort_s, lane))) break;
+        if (!(ok = tc_wait_warp(a_empty + team, (u & 1u) ^ 1u, abort_s, lane))) break;
         tc::tc_fence_after();
         const uint8_t *raw = sm + L::OFF_RAW + rs * L::RAWSL;
-        const uint32_t acol = tmem + lane_addr + (uint32_t)(TM::A_COL0 + st * NA * 32);
 #pragma unroll
-        for (int m = 0; m < NA; ++m) {
+        for (int m = 0; m < NA; ++m) {  // team t holds chunk t of the super-block
           uint32_t o[32];
-          const uint8_t *blk = raw + (m * TC_M + r) * Q4K_BYTES;
-          tc_dequant_sub(blk, ks & 3, 0, o);
-          tc_dequant_sub(blk, ks & 3, 1, o + 16);
+          tc_dequant_step(raw + (m * TC_M + r) * Q4K_BYTES, team, o);
           tc::tmem_st32(acol + (uint32_t)(m * 32), o);
         }
         tc::tmem_wait_st();
         tc::tc_fence_before();
         __syncwarp();
-        if (lane == 0) tc::mbar_arrive(a_full + st);
-        if ((ks & 3) == 2 + team)                   // this warp's last step of the slot
-          if (lane == 0) tc::mbar_arrive(raw_empty + rs);
+        if (lane == 0) {
+          tc::mbar_arrive(a_full + team);
+          tc::mbar_arrive(raw_empty + rs);
+        }
       }
-      gs0 += KSTEPS;
     }
   }
 
@@ -417,19 +440,24 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
   if (warp == 0) tc::tmem_dealloc(tmem, TC_TMEM_COLS);
 }
 
-// xg[slot][H] = f16(x[token of slot]) for every slot whose expert runs on the
-// tensor-core path: routed slot s holds entry order[s] (token order[s] / k,
+// xg[2 slot] = hi = f16(x[token of slot]) and xg[2 slot + 1] = f16(x - hi),
+// K order (0, 2, 1, 3) inside each group of four (the weight operand's order),
+// for every slot whose expert runs on the tensor-core path: routed slot s holds entry order[s] (token order[s] / k,
 // expert ids[order[s]]); slot n + t is the shared expert's row of token t.
 // One CTA per slot; slots of CUDA-core experts are skipped.
 __global__ void __launch_bounds__(256) gather_f16_kernel(const float *__restrict__ x, int H,
                                                          const int32_t *__restrict__ order,
                                                          const int32_t *__restrict__ ids,
                                                          const int32_t *__restrict__ counts,
+                                                         const int32_t *__restrict__ n_valid,
                                                          int thr, int n, int k, int shared_tc,
                                                          __half *__restrict__ xg) {
   const int slot = blockIdx.x;
   int tok;
   if (slot < n) {
+    // grouped positions past the valid entries (those with an out-of-range
+    // expert id are dropped by the grouping) hold no entry
+    if (slot >= *n_valid) return;
     const int entry = order[slot];
     if (counts[ids[entry]] < thr) return;
     tok = entry / k;
@@ -438,19 +466,23 @@ __global__ void __launch_bounds__(256) gather_f16_kernel(const float *__restrict
     tok = slot - n;
   }
   const float4 *src = reinterpret_cast<const float4 *>(x + (int64_t)tok * H);
-  uint2 *dst = reinterpret_cast<uint2 *>(xg + (int64_t)slot * H);
+  uint2 *dhi = reinterpret_cast<uint2 *>(xg + 2 * (int64_t)slot * H);
+  uint2 *dlo = dhi + H / 4;
   for (int i = threadIdx.x; i < H / 4; i += blockDim.x) {
-    const float4 v = src[i];
-    const __half2 a = __floats2half2_rn(v.x, v.y), b = __floats2half2_rn(v.z, v.w);
-    dst[i] = make_uint2(*reinterpret_cast<const uint32_t *>(&a), *reinterpret_cast<const uint32_t *>(&b));
+    const float4 v = src[i];  // K order (0, 2, 1, 3) inside each group of four
+    const __half2 a = __floats2half2_rn(v.x, v.z), b = __floats2half2_rn(v.y, v.w);
+    const float2 fa = __half22float2(a), fb = __half22float2(b);
+    const __half2 la = __floats2half2_rn(v.x - fa.x, v.z - fa.y), lb = __floats2half2_rn(v.y - fb.x, v.w - fb.y);
+    dhi[i] = make_uint2(*reinterpret_cast<const uint32_t *>(&a), *reinterpret_cast<const uint32_t *>(&b));
+    dlo[i] = make_uint2(*reinterpret_cast<const uint32_t *>(&la), *reinterpret_cast<const uint32_t *>(&lb));
   }
 }
 
 int32_t launch_gather_f16(har_cuda_ctx *ctx, const float *x, int H, const int32_t *order,
-                          const int32_t *ids, const int32_t *counts, int thr, int n, int k,
-                          int T, int shared_tc, __half *xg) {
+                          const int32_t *ids, const int32_t *counts, const int32_t *n_valid,
+                          int thr, int n, int k, int T, int shared_tc, __half *xg) {
   prof_begin(ctx);
-  gather_f16_kernel<<<n + T, 256, 0, ctx->stream>>>(x, H, order, ids, counts, thr, n, k,
+  gather_f16_kernel<<<n + T, 256, 0, ctx->stream>>>(x, H, order, ids, counts, n_valid, thr, n, k,
                                                     shared_tc, xg);
   return check_launch(ctx, "gather_f16_kernel");
 }

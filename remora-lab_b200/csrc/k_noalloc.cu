@@ -66,7 +66,7 @@ extern "C" int32_t har_cuda_moe_ffn_noalloc(har_cuda_ctx *ctx, const har_cuda_mo
   if (T == 0) return HAR_CUDA_OK;
   if (!x_dev || !ids_dev || !weights_dev || !y_dev)
     return set_error(ctx, HAR_CUDA_ERR_ARG, "moe_ffn_noalloc: null pointer");
-  const size_t need = moe_scratch_bytes(layer, T, k, flags);
+  const size_t need = moe_scratch_bytes(ctx, layer, T, k, flags);
   if (need > (size_t)HAR_CUDA_NOALLOC_SCRATCH_BYTES)
     return set_error(ctx, HAR_CUDA_ERR_GEOMETRY,
                      "moe_ffn_noalloc: this call needs " + std::to_string(need) +

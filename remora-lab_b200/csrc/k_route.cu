@@ -111,7 +111,7 @@ __global__ void __launch_bounds__(GROUP_WARPS * 32) group_kernel(
     const int32_t *__restrict__ ids, int n, int E, int32_t *__restrict__ counts,
     int32_t *__restrict__ offsets, int32_t *__restrict__ order, int32_t *__restrict__ inv,
     int32_t *__restrict__ ne, int32_t *__restrict__ n_ne, int thr, int nt,
-    int2 *__restrict__ tt_info, int32_t *__restrict__ n_tt, int *status) {
+    int2 *__restrict__ tt_info, int32_t *__restrict__ n_tt, int shared_T, int *status) {
   extern __shared__ __align__(16) uint8_t gsm[];
   int32_t *cnt = reinterpret_cast<int32_t *>(gsm);                       // [W][E]
   int32_t *off = cnt + (size_t)GROUP_WARPS * E;                             // [E+1]
@@ -200,8 +200,9 @@ __global__ void __launch_bounds__(GROUP_WARPS * 32) group_kernel(
   // Non-empty experts in expert order (warp 0, ballot + popc), split by token
   // count: ne[] those below `thr` (CUDA-core path); those at or above it
   // (tensor-core path) are cut into ceil(count/nt) token tiles, listed in
-  // expert order as tt_info[j] = {expert | tokens << 16, first slot}, with the
-  // number of tiles in *n_tt.
+  // expert order as tt_info[j] = {expert | tokens << 16, first slot}.  When
+  // shared_T > 0 the shared expert (index E, slots n .. n + shared_T) follows
+  // with ceil(shared_T/nt) tiles.  *n_tt = the number of tiles.
   if (ne && warp == 0) {
     int run = 0, run_tt = 0;
     for (int base = 0; base < E; base += 32) {
@@ -223,9 +224,11 @@ __global__ void __launch_bounds__(GROUP_WARPS * 32) group_kernel(
       run += __popc(bm);
       run_tt += __shfl_sync(0xffffffffu, incl, 31);
     }
+    for (int t0 = lane * nt; t0 < shared_T; t0 += 32 * nt)
+      tt_info[run_tt + t0 / nt] = make_int2(E | (min(nt, shared_T - t0) << 16), n + t0);
     if (lane == 0) {
       *n_ne = run;
-      *n_tt = run_tt;
+      *n_tt = run_tt + (shared_T + nt - 1) / nt;
     }
   }
 }
@@ -237,21 +240,21 @@ size_t group_smem_bytes(int E) {
 int32_t launch_group_full(har_cuda_ctx *ctx, const int32_t *ids, int64_t n, int E,
                           int32_t *counts, int32_t *offsets, int32_t *order, int32_t *inv,
                           int32_t *ne, int32_t *n_ne, int thr, int nt, int2 *tt_info,
-                          int32_t *n_tt) {
+                          int32_t *n_tt, int shared_T) {
   const size_t smem = group_smem_bytes(E);
   if (smem > 48 * 1024)
     cudaFuncSetAttribute(group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   prof_begin(ctx);
   group_kernel<<<1, GROUP_WARPS * 32, smem, ctx->stream>>>(ids, (int)n, E, counts, offsets,
                                                            order, inv, ne, n_ne, thr, nt,
-                                                           tt_info, n_tt, ctx->d_status);
+                                                           tt_info, n_tt, shared_T, ctx->d_status);
   return check_launch(ctx, "group_kernel");
 }
 
 int32_t launch_group(har_cuda_ctx *ctx, const int32_t *ids, int64_t T, int k, int E,
                      int32_t *counts, int32_t *offsets, int32_t *order, int32_t *inv) {
   return launch_group_full(ctx, ids, T * k, E, counts, offsets, order, inv, nullptr, nullptr, 0,
-                           1, nullptr, nullptr);
+                           1, nullptr, nullptr, 0);
 }
 
 }  // namespace har

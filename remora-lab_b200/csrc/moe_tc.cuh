@@ -9,21 +9,20 @@
 namespace har {
 
 constexpr int TC_M = 128;   // weight rows per tile (MMA M)
-constexpr int TC_NT = 64;   // token columns per tile (MMA N, max)
-constexpr int TC_NBOX = 3;  // token-tile boxes of 16, 32 and 64 rows
+constexpr int TC_NT = 32;   // tokens per tile (two MMA N columns each: hi and lo)
+constexpr int TC_NBOX = 2;  // token-tile boxes of 32 and 64 rows (16 and 32 tokens)
 constexpr int TC_KS = 128;  // H and I must be multiples of this
 constexpr uint32_t TC_WAIT_LIMIT = 1u << 22;  // polls before a wait is declared stuck
 
 // Warp roles of the tensor-core kernel.
 constexpr int TC_WARP_TMA = 0;    // one thread: TMA loads of raw weight boxes
-constexpr int TC_WARP_MMA0 = 1;   // MMA issuer of the even K-steps
+constexpr int TC_WARP_MMA = 1;    // the MMA issuer (whole warp, one elected lane issues)
 constexpr int TC_WARP_BTMA = 2;   // one thread: TMA loads of token tiles
 constexpr int TC_WARP_EPI0 = 3;   // warps 3..6: TMEM -> global epilogue (one per lane group)
-constexpr int TC_WARP_DQ0 = 7;    // warps 7..14: dequantise raw Q4_K into f16 weight stages
-constexpr int TC_DQ_WARPS = 8;
-constexpr int TC_WARP_MMA1 = 15;  // MMA issuer of the odd K-steps
-constexpr int TC_ISSUERS = 2;
-constexpr int TC_WARPS = 16;
+constexpr int TC_WARP_DQ0 = 7;    // warps 7..22: dequantise raw Q4_K into f16 weight stages
+constexpr int TC_DQ_TEAMS = 4;    // four warps each; team t fills weight stage t
+constexpr int TC_DQ_WARPS = 4 * TC_DQ_TEAMS;
+constexpr int TC_WARPS = TC_WARP_DQ0 + TC_DQ_WARPS;
 constexpr int TC_THREADS = 32 * TC_WARPS;
 constexpr int TC_TMEM_COLS = 512;  // accumulators, then the f16 weight stages
 
@@ -32,9 +31,9 @@ struct TcParams {
   int K;           // reduction length (H for gate/up, I for down)
   int E, T, k, n;
   int shared_tc;   // the shared expert runs on this path
-  const int2 *tt_info;    // routed token tiles: {expert | tokens << 16, first slot}
-  const int32_t *n_tt;    // number of routed token tiles
-  __half *a16;     // gate/up output [slots][I]
+  const int2 *tt_info;    // token tiles: {expert (E = shared) | tokens << 16, first slot}
+  const int32_t *n_tt;    // number of token tiles
+  __half *a16;     // gate/up output [2 * slots][I]: f16 hi/lo row pairs
   float *ybuf;     // down output [slots][H]
   int out_ld;      // row length of the output (I or H)
   int *status;
@@ -42,18 +41,21 @@ struct TcParams {
 
 // TMA maps of one launch: the A matrices (routed [E*rows][row_bytes] and the
 // shared expert's [rows][row_bytes], 128 x 144-byte boxes) and the B operand
-// ([slots][K] f16 in slot order, 64-value boxes of 16/32/64 rows, 128-byte
-// swizzle: a tile loads the smallest box that covers its tokens).
+// ([2 * slots][K] f16: slot s is rows 2s (hi) and 2s+1 (lo), 64-value boxes
+// of 32/64 rows, 128-byte swizzle: a tile loads the smallest box that covers
+// its tokens).
 struct TcMaps {
   TmaDesc a0, a1, sh0, sh1;
-  TmaDesc b[TC_NBOX];  // token-tile boxes of 16, 32 and 64 rows
+  TmaDesc b[TC_NBOX];  // token-tile boxes of 32 and 64 rows (16 and 32 tokens)
 };
 
 int32_t launch_moe_tc(har_cuda_ctx *ctx, const TcMaps &maps, const TcParams &p, int na,
                       int max_tiles);
-// xg[slot][H] = f16(x[token of slot]) for the slots of experts on the tensor-core path.
+// xg[2 slot], xg[2 slot + 1] = f16 hi/lo of x[token of slot] for the slots of
+// experts on the tensor-core path.
+// n_valid = the number of grouped entries (offsets[E]); later routed slots are empty.
 int32_t launch_gather_f16(har_cuda_ctx *ctx, const float *x, int H, const int32_t *order,
-                          const int32_t *ids, const int32_t *counts, int thr, int n, int k,
-                          int T, int shared_tc, __half *xg);
+                          const int32_t *ids, const int32_t *counts, const int32_t *n_valid,
+                          int thr, int n, int k, int T, int shared_tc, __half *xg);
 
 }  // namespace har

@@ -191,26 +191,93 @@ __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
-// Warp-wide forms: the whole (converged) warp executes them and one lane,
-// chosen by elect.sync, issues.  Keeping the issuing loop warp-uniform lets
-// the operands stay in uniform registers; a loop run by a single thread
-// issues several times more slowly.
-__device__ __forceinline__ void mma_f16_ts_w(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc,
-                                             uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred e, p;\n\t"
-      "elect.sync _|e, 0xffffffff;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-__device__ __forceinline__ void mma_commit_w(uint64_t *bar) {
+// Warp-wide forms: the whole (converged) warp executes them and the lane
+// picked once by elect_one() (`lead` != 0) issues.  Keeping the issuing loop
+// warp-uniform lets the operands stay in uniform registers; a loop run by a
+// single thread, or an elect.sync per MMA, issues several times more slowly.
+__device__ __forceinline__ uint32_t elect_one() {
+  uint32_t p;
   asm volatile(
       "{\n\t.reg .pred e;\n\t"
       "elect.sync _|e, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, e;\n\t}"
+      : "=r"(p));
+  return p;
+}
+__device__ __forceinline__ void mma_f16_ts_w(uint32_t lead, uint32_t d_tmem, uint32_t a_tmem,
+                                             uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred e, p;\n\t"
+      "setp.ne.b32 e, %5, 0;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(lead)
+      : "memory");
+}
+// The MMAs of one 64-value K-step (4 x K=16) for NA = 1 or 2 matrices, from
+// one asm block: matrix m accumulates at column d + m*bw and reads its weights
+// from TMEM columns a + m*32 + kk*8; B advances 32 bytes (2 descriptor units)
+// per K=16 slice.  The first slice overwrites when acc0 == 0.
+template <int NA>
+__device__ __forceinline__ void mma_kstep_ts(uint32_t lead, uint32_t d, uint32_t bw, uint32_t a,
+                                             uint64_t b, uint32_t idesc, uint32_t acc0) {
+  if (NA == 2) {
+    asm volatile(
+        "{\n\t.reg .pred e, p, t;\n\t.reg .b32 d1, a1, a2, a3, a4, a5, a6, a7;\n\t"
+        ".reg .b64 b1, b2, b3;\n\t"
+        "setp.ne.b32 e, %0, 0;\n\t"
+        "setp.ne.b32 p, %6, 0;\n\t"
+        "setp.eq.b32 t, %0, %0;\n\t"
+        "add.u32 d1, %1, %2;\n\t"
+        "add.u32 a1, %3, 32;\n\t"
+        "add.u32 a2, %3, 8;\n\t"
+        "add.u32 a3, %3, 40;\n\t"
+        "add.u32 a4, %3, 16;\n\t"
+        "add.u32 a5, %3, 48;\n\t"
+        "add.u32 a6, %3, 24;\n\t"
+        "add.u32 a7, %3, 56;\n\t"
+        "add.u64 b1, %4, 2;\n\t"
+        "add.u64 b2, %4, 4;\n\t"
+        "add.u64 b3, %4, 6;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%1], [%3], %4, %5, p;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [d1], [a1], %4, %5, p;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%1], [a2], b1, %5, t;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [d1], [a3], b1, %5, t;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%1], [a4], b2, %5, t;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [d1], [a5], b2, %5, t;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%1], [a6], b3, %5, t;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [d1], [a7], b3, %5, t;\n\t}" ::"r"(lead),
+        "r"(d), "r"(bw), "r"(a), "l"(b), "r"(idesc), "r"(acc0)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred e, p, t;\n\t.reg .b32 a1, a2, a3;\n\t.reg .b64 b1, b2, b3;\n\t"
+        "setp.ne.b32 e, %0, 0;\n\t"
+        "setp.ne.b32 p, %5, 0;\n\t"
+        "setp.eq.b32 t, %0, %0;\n\t"
+        "add.u32 a1, %2, 8;\n\t"
+        "add.u32 a2, %2, 16;\n\t"
+        "add.u32 a3, %2, 24;\n\t"
+        "add.u64 b1, %3, 2;\n\t"
+        "add.u64 b2, %3, 4;\n\t"
+        "add.u64 b3, %3, 6;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%1], [%2], %3, %4, p;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%1], [a1], b1, %4, t;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%1], [a2], b2, %4, t;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%1], [a3], b3, %4, t;\n\t}" ::"r"(lead),
+        "r"(d), "r"(a), "l"(b), "r"(idesc), "r"(acc0)
+        : "memory");
+    (void)bw;
+  }
+}
+
+__device__ __forceinline__ void mma_commit_w(uint32_t lead, uint64_t *bar) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "setp.ne.b32 e, %1, 0;\n\t"
       "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(
-          smem_u32(bar))
+          smem_u32(bar)),
+      "r"(lead)
       : "memory");
 }
 

@@ -51,7 +51,7 @@ EXPORTS = [
     "har_cuda_route_topk", "har_cuda_group_by_expert", "har_cuda_moe_layer_create",
     "har_cuda_moe_layer_free", "har_cuda_moe_ffn", "har_cuda_moe_ffn_host", "har_cuda_moe_stack",
     "har_cuda_gen_q4k", "har_cuda_moe_stack_host", "har_cuda_profile_begin",
-    "har_cuda_profile_end", "har_cuda_moe_ffn_noalloc",
+    "har_cuda_profile_end", "har_cuda_moe_ffn_noalloc", "har_cuda_ctx_set_tc_min_tokens",
 ]
 
 
@@ -80,6 +80,7 @@ def load_library() -> C.CDLL:
         "har_cuda_ctx_destroy": (i32, [vp]),
         "har_cuda_last_error": (i32, [vp, C.c_char_p, C.c_size_t]),
         "har_cuda_ctx_set_stream": (i32, [vp, vp]),
+        "har_cuda_ctx_set_tc_min_tokens": (i32, [vp, i32]),
         "har_cuda_synchronize": (i32, [vp, i64]),
         "har_cuda_launch_count": (i64, [vp]),
         "har_cuda_weights_upload_q4k": (i32, [vp, vp, i64, i64, i64, pp]),
@@ -145,6 +146,10 @@ class Context:
         import torch
         s = torch.cuda.current_stream(self.device)
         self.check(self.lib.har_cuda_ctx_set_stream(self.handle, C.c_void_p(s.cuda_stream)))
+
+    def set_tc_min_tokens(self, n: int):
+        """Experts with >= n tokens take the tensor-core kernels (0 = default)."""
+        self.check(self.lib.har_cuda_ctx_set_tc_min_tokens(self.handle, n))
 
     def last_error(self) -> str:
         buf = C.create_string_buffer(1024)

@@ -14,6 +14,13 @@ import numpy as np
 
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 REL_MAX_TOL = 1e-3
+# HAR's differential verdict (har-execution/src/lib.rs:185-195): the f32
+# CUDA-core GEMV path meets it.
+VERDICT_NRMS = 5e-5
+# RMS bound of the tensor-core path, where each dequantised weight is rounded
+# once to f16 (activations go in as hi/lo f16 pairs): about 4e-4 measured on
+# the Alice layer; the max-relative bound REL_MAX_TOL is the north star's.
+TC_NRMS = 6e-4
 
 
 def kats():
@@ -41,7 +48,7 @@ def verdict(got, ref):
     return float(rms / max(rref, 1e-12)), float(np.max(np.abs(d)))
 
 
-def assert_close(got, ref, rel=REL_MAX_TOL, nrms=5e-5, what=""):
+def assert_close(got, ref, rel=REL_MAX_TOL, nrms=VERDICT_NRMS, what=""):
     r = rel_max(got, ref)
     n, m = verdict(got, ref)
     assert r <= rel, f"{what}: max|d|/max|ref| = {r:.3e} > {rel:.1e}"

@@ -1,9 +1,9 @@
 """GPU parity of the tensor-core (tcgen05) expert path against the oracle's
 restatement of compose_moe_route (har-native-qwen35moe.rs:979-1048).
 
-Operands are f16 on this path (each dequantised weight and each activation is
-rounded once to f16, accumulation in f32), so besides the north star's
-max|d|/max|ref| <= 1e-3 the RMS bound is 1e-3 instead of the 5e-5 that the
+Each dequantised weight is rounded once to f16 on this path (activations go
+in as hi/lo f16 pairs, accumulation is f32), so besides the north star's
+max|d|/max|ref| <= 1e-3 the RMS bound is 6e-4 instead of the 5e-5 that the
 f32 CUDA-core path meets."""
 import numpy as np
 import pytest
@@ -14,10 +14,9 @@ torch = pytest.importorskip("torch")
 
 import haro  # noqa: E402
 import har_cuda  # noqa: E402
-from _common import assert_close  # noqa: E402
+from _common import TC_NRMS, assert_close  # noqa: E402
 from gpu_util import Layer  # noqa: E402
 
-TC_NRMS = 1e-3
 FORCE_TC = har_cuda.MOE_FORCE_TC
 
 
@@ -47,14 +46,19 @@ def test_tc_zipf_batch(ctx, small):
     ids, w = haro.zipf_routing(4, 64, 64, 10)
     ref = small.oracle(x, ids, w)
     assert_close(small.run(ctx, x, ids, w, FORCE_TC), ref, nrms=TC_NRMS, what="tc forced")
-    # default threshold: hot experts on tcgen05, the tail on the CUDA-core GEMV
-    assert_close(small.run(ctx, x, ids, w), ref, nrms=TC_NRMS, what="mixed")
-    assert_close(small.run(ctx, x, ids, w, har_cuda.MOE_ACT_Q8K),
-                 small.oracle(x, ids, w), rel=3e-2, nrms=None, what="mixed q8k")
+    # hot experts on tcgen05, the tail on the CUDA-core GEMV
+    ctx.set_tc_min_tokens(8)
+    try:
+        assert_close(small.run(ctx, x, ids, w), ref, nrms=TC_NRMS, what="mixed")
+        # Q8_K activations keep every expert on the GEMV kernels
+        assert_close(small.run(ctx, x, ids, w, har_cuda.MOE_ACT_Q8K),
+                     small.oracle(x, ids, w, act="q8k"), rel=1e-4, nrms=1e-5, what="q8k")
+    finally:
+        ctx.set_tc_min_tokens(0)
 
 
 def test_tc_prefill_tiles(ctx, small):
-    # more than 128 tokens on one expert: several token tiles, shared expert on tcgen05
+    # hundreds of tokens on one expert: several 32-token tiles, shared expert on tcgen05
     T = 300
     x = haro.normal_f32(5, 0, T * 2048).reshape(T, 2048)
     ids, w = haro.route_topk(haro.normal_f32(6, 0, T * 64).reshape(T, 64), 10)
