@@ -58,6 +58,8 @@ extern "C" {
                                           CUDA-core GEMVs (integer dots); not with FORCE_TC */
 #define HAR_CUDA_MOE_FORCE_GEMV 0x4u   /* every expert on the CUDA-core GEMV path */
 #define HAR_CUDA_MOE_FORCE_TC 0x8u     /* every expert on the tcgen05 tensor-core path */
+#define HAR_CUDA_MOE_EMPTY_SLOTS 0x10u /* expert id -1 marks an empty slot (no contribution);
+                                          used by the expert-parallel exchange */
 
 typedef struct har_cuda_ctx har_cuda_ctx;
 typedef struct har_cuda_weights har_cuda_weights;
@@ -190,6 +192,38 @@ int32_t har_cuda_moe_stack_host(har_cuda_ctx *ctx, const har_cuda_moe_layer *con
                                 int32_t L, const float *x_host, int64_t T, int32_t k,
                                 const int32_t *ids_host, const float *weights_host,
                                 float *y_host, uint32_t flags);
+
+/* ---- expert parallelism over the GPUs of one box (NCCL over NVLink) ----------------------
+ * No counterpart in the reference, which runs every expert on one CPU
+ * (compose_moe_route, har-native-qwen35moe.rs:979-1048): this is the router-to-
+ * expert dispatch of a sharded deployment.  Rank r of G holds the routed experts
+ * [r*E/G, (r+1)*E/G) of every layer as a `local` layer (no shared expert) and the
+ * shared expert as a one-expert `shared` layer (replicated on every rank), plus
+ * the shared expert's gate row.  Per layer: token rows go to the ranks holding
+ * their experts (one grouped NCCL send/recv round), each rank runs its experts,
+ * partial sums come back (a second round), and the tokens' rank adds residual,
+ * shared expert and partial sums.  Results equal har_cuda_moe_ffn on the
+ * unsharded layer up to f32 summation order.  All ranks call collectively with
+ * the same T, k and flags (ADD_RESIDUAL, ACT_Q8K, FORCE_*). */
+/* An NCCL unique id (rank 0 creates it; the caller broadcasts the bytes). */
+int32_t har_cuda_ep_unique_id(uint8_t *out, size_t len);
+/* Collective: every rank of `world` joins the communicator on ctx's device. */
+int32_t har_cuda_ep_create(har_cuda_ctx *ctx, const uint8_t *unique_id, size_t len, int32_t world,
+                           int32_t rank, har_cuda_ep **out);
+int32_t har_cuda_ep_free(har_cuda_ep *ep);
+/* One layer; ids are global expert ids [T][k] of this rank's T tokens. */
+int32_t har_cuda_ep_moe_ffn(har_cuda_ctx *ctx, har_cuda_ep *ep, const har_cuda_moe_layer *local,
+                            const har_cuda_moe_layer *shared, const float *gate_inp_dev,
+                            const float *x_dev, int64_t T, int32_t k, const int32_t *ids_dev,
+                            const float *weights_dev, float *y_dev, uint32_t flags);
+/* L layers in order (ids/weights [L][T][k]); shared_layers and gate_inp_devs may
+ * be null; x_dev and y_dev may alias. */
+int32_t har_cuda_ep_moe_stack(har_cuda_ctx *ctx, har_cuda_ep *ep,
+                              const har_cuda_moe_layer *const *local_layers,
+                              const har_cuda_moe_layer *const *shared_layers,
+                              const float *const *gate_inp_devs, int32_t L, const float *x_dev,
+                              int64_t T, int32_t k, const int32_t *ids_dev,
+                              const float *weights_dev, float *y_dev, uint32_t flags);
 
 /* ---- profiling (the role of TimestampQuery, har/crates/har-vulkan/src/lib.rs:2221-2257) ---
  * Between begin and end every kernel the context launches is bracketed by

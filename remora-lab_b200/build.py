@@ -58,8 +58,8 @@ def build(verbose: bool = False, force: bool = False) -> str:
     if failed:
         raise RuntimeError("nvcc failed")
     tmp = OUT + ".tmp"
-    subprocess.run([NVCC, *ARCH, "-shared", "-o", tmp, *objs, "-lcudart_static", "-lrt",
-                    "-lpthread", "-ldl"], check=True)
+    subprocess.run([NVCC, *ARCH, "-shared", "-o", tmp, *objs, "-lcudart_static", "-lnccl",
+                    "-lrt", "-lpthread", "-ldl"], check=True)
     os.replace(tmp, OUT)
     return OUT
 

@@ -495,7 +495,7 @@ int32_t har::check_moe_args(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, 
   if ((flags & HAR_CUDA_MOE_ACT_Q8K) && (flags & HAR_CUDA_MOE_FORCE_TC))
     return set_error(ctx, HAR_CUDA_ERR_UNSUPPORTED,
                      "moe_ffn: the tensor-core path has no Q8_K activation mode");
-  if (flags & ~0xFu) return set_error(ctx, HAR_CUDA_ERR_ARG, "moe_ffn: unknown flag bits");
+  if (flags & ~0x1Fu) return set_error(ctx, HAR_CUDA_ERR_ARG, "moe_ffn: unknown flag bits");
   return HAR_CUDA_OK;
 }
 

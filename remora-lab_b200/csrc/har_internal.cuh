@@ -84,6 +84,13 @@ __device__ __forceinline__ uint4 ldg_nc_v4(const void *p) {
   return r;
 }
 
+// sigmoid of har-native-qwen35moe.rs:207-214
+__device__ __forceinline__ float sigmoid_f(float v) {
+  if (v >= 0.0f) return 1.0f / (1.0f + expf(-v));
+  const float e = expf(v);
+  return e / (1.0f + e);
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -33,7 +33,7 @@ size_t group_smem_bytes(int E);
 int32_t launch_group_full(har_cuda_ctx *ctx, const int32_t *ids, int64_t n, int E,
                           int32_t *counts, int32_t *offsets, int32_t *order, int32_t *inv,
                           int32_t *ne, int32_t *n_ne, int thr, int nt, int2 *tt_info,
-                          int32_t *n_tt, int shared_T);
+                          int32_t *n_tt, int shared_T, int allow_empty);
 
 struct MoeDev {
   const uint8_t *gate, *up, *down, *sh_gate, *sh_up, *sh_down;
@@ -52,12 +52,6 @@ struct MoeDev {
 
 __device__ __forceinline__ float silu_f(float v) { return v / (1.0f + expf(-v)); }
 
-// sigmoid of har-native-qwen35moe.rs:207-214
-__device__ __forceinline__ float sigmoid_f(float v) {
-  if (v >= 0.0f) return 1.0f / (1.0f + expf(-v));
-  const float e = expf(v);
-  return e / (1.0f + e);
-}
 
 // Resolve group gi's expert id, token count and first slot.
 __device__ __forceinline__ void group_info(const MoeDev &p, int gi, int nne, int &g, int &cnt,
@@ -476,7 +470,8 @@ int32_t run_moe_ffn_in(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const
   st = launch_group_full(ctx, ids, n, E, (int32_t *)(S + o_counts), (int32_t *)(S + o_offsets),
                          (int32_t *)(S + o_order), (int32_t *)(S + o_inv), (int32_t *)(S + o_ne),
                          (int32_t *)(S + o_nne), thr, TC_NT, (int2 *)(S + L.o_ttinfo),
-                         (int32_t *)(S + L.o_ntt), shared_tc ? (int)T : 0);
+                         (int32_t *)(S + L.o_ntt), shared_tc ? (int)T : 0,
+                         (flags & HAR_CUDA_MOE_EMPTY_SLOTS) ? 1 : 0);
   if (st) return st;
   // tensor-core path parameters (experts with >= thr tokens)
   TcParams tp{};

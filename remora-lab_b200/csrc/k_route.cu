@@ -103,7 +103,8 @@ int32_t launch_route_topk(har_cuda_ctx *ctx, const float *logits, int64_t T, int
 // inv[n] (grouped position of each entry) and, when ne != null, the list of
 // non-empty experts in expert order (ne[0..*n_ne)) below `thr` tokens, and
 // the token tiles of the experts at or above it (see the tail below).
-// Entries with an out-of-range id set DEV_ERR_BOUNDS in *status and are dropped.
+// Entries with an out-of-range id set DEV_ERR_BOUNDS in *status and are dropped;
+// with allow_empty, id -1 marks an empty slot and is dropped silently.
 // ---------------------------------------------------------------------------
 constexpr int GROUP_WARPS = 16;
 
@@ -111,7 +112,8 @@ __global__ void __launch_bounds__(GROUP_WARPS * 32) group_kernel(
     const int32_t *__restrict__ ids, int n, int E, int32_t *__restrict__ counts,
     int32_t *__restrict__ offsets, int32_t *__restrict__ order, int32_t *__restrict__ inv,
     int32_t *__restrict__ ne, int32_t *__restrict__ n_ne, int thr, int nt,
-    int2 *__restrict__ tt_info, int32_t *__restrict__ n_tt, int shared_T, int *status) {
+    int2 *__restrict__ tt_info, int32_t *__restrict__ n_tt, int shared_T, int allow_empty,
+    int *status) {
   extern __shared__ __align__(16) uint8_t gsm[];
   int32_t *cnt = reinterpret_cast<int32_t *>(gsm);                       // [W][E]
   int32_t *off = cnt + (size_t)GROUP_WARPS * E;                             // [E+1]
@@ -129,7 +131,7 @@ __global__ void __launch_bounds__(GROUP_WARPS * 32) group_kernel(
     if (i < s1) {
       e = ids[i];
       if (e < 0 || e >= E) {
-        atomicOr(status, DEV_ERR_BOUNDS);
+        if (!(allow_empty && e == -1)) atomicOr(status, DEV_ERR_BOUNDS);
         e = -1;
       }
     }
@@ -240,21 +242,22 @@ size_t group_smem_bytes(int E) {
 int32_t launch_group_full(har_cuda_ctx *ctx, const int32_t *ids, int64_t n, int E,
                           int32_t *counts, int32_t *offsets, int32_t *order, int32_t *inv,
                           int32_t *ne, int32_t *n_ne, int thr, int nt, int2 *tt_info,
-                          int32_t *n_tt, int shared_T) {
+                          int32_t *n_tt, int shared_T, int allow_empty) {
   const size_t smem = group_smem_bytes(E);
   if (smem > 48 * 1024)
     cudaFuncSetAttribute(group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   prof_begin(ctx);
   group_kernel<<<1, GROUP_WARPS * 32, smem, ctx->stream>>>(ids, (int)n, E, counts, offsets,
                                                            order, inv, ne, n_ne, thr, nt,
-                                                           tt_info, n_tt, shared_T, ctx->d_status);
+                                                           tt_info, n_tt, shared_T, allow_empty,
+                                                           ctx->d_status);
   return check_launch(ctx, "group_kernel");
 }
 
 int32_t launch_group(har_cuda_ctx *ctx, const int32_t *ids, int64_t T, int k, int E,
                      int32_t *counts, int32_t *offsets, int32_t *order, int32_t *inv) {
   return launch_group_full(ctx, ids, T * k, E, counts, offsets, order, inv, nullptr, nullptr, 0,
-                           1, nullptr, nullptr, 0);
+                           1, nullptr, nullptr, 0, 0);
 }
 
 }  // namespace har

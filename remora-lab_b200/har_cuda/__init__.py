@@ -52,6 +52,8 @@ EXPORTS = [
     "har_cuda_moe_layer_free", "har_cuda_moe_ffn", "har_cuda_moe_ffn_host", "har_cuda_moe_stack",
     "har_cuda_gen_q4k", "har_cuda_moe_stack_host", "har_cuda_profile_begin",
     "har_cuda_profile_end", "har_cuda_moe_ffn_noalloc", "har_cuda_ctx_set_tc_min_tokens",
+    "har_cuda_ep_unique_id", "har_cuda_ep_create", "har_cuda_ep_free", "har_cuda_ep_moe_ffn",
+    "har_cuda_ep_moe_stack",
 ]
 
 
@@ -81,6 +83,11 @@ def load_library() -> C.CDLL:
         "har_cuda_last_error": (i32, [vp, C.c_char_p, C.c_size_t]),
         "har_cuda_ctx_set_stream": (i32, [vp, vp]),
         "har_cuda_ctx_set_tc_min_tokens": (i32, [vp, i32]),
+        "har_cuda_ep_unique_id": (i32, [vp, C.c_size_t]),
+        "har_cuda_ep_create": (i32, [vp, vp, C.c_size_t, i32, i32, pp]),
+        "har_cuda_ep_free": (i32, [vp]),
+        "har_cuda_ep_moe_ffn": (i32, [vp, vp, vp, vp, vp, vp, i64, i32, vp, vp, vp, u32]),
+        "har_cuda_ep_moe_stack": (i32, [vp, vp, vp, vp, vp, i32, vp, i64, i32, vp, vp, vp, u32]),
         "har_cuda_synchronize": (i32, [vp, i64]),
         "har_cuda_launch_count": (i64, [vp]),
         "har_cuda_weights_upload_q4k": (i32, [vp, vp, i64, i64, i64, pp]),
@@ -289,6 +296,66 @@ class Context:
         self.check(self.lib.har_cuda_moe_stack(self.handle, arr, L, _dptr(x), T, k, _dptr(ids),
                                                _dptr(weights), _dptr(y), flags))
         return y
+
+    # ---- expert parallelism -------------------------------------------------
+    def ep_create(self, unique_id: bytes, world: int, rank: int) -> "EpComm":
+        """Collective over `world` ranks: join the NCCL communicator on this device."""
+        buf = (C.c_uint8 * len(unique_id)).from_buffer_copy(unique_id)
+        h = C.c_void_p()
+        self.check(self.lib.har_cuda_ep_create(self.handle, buf, len(unique_id), world, rank,
+                                               C.byref(h)))
+        return EpComm(self, h, world, rank)
+
+    def ep_moe_ffn(self, ep: "EpComm", local: "MoeLayer", shared, gate_inp, x, ids, weights, y,
+                   flags: int = 0):
+        T, k = ids.shape
+        self.check(self.lib.har_cuda_ep_moe_ffn(
+            self.handle, ep.handle, local.handle, shared.handle if shared else None,
+            _dptr(gate_inp), _dptr(x), T, k, _dptr(ids), _dptr(weights), _dptr(y), flags))
+        return y
+
+    def ep_moe_stack(self, ep: "EpComm", locals_, shareds, gate_inps, x, ids, weights, y,
+                     flags: int = 0):
+        L = len(locals_)
+        la = (C.c_void_p * L)(*[l.handle.value for l in locals_])
+        sa = (C.c_void_p * L)(*[s.handle.value for s in shareds]) if shareds else None
+        ga = (C.c_void_p * L)(*[_dptr(g) for g in gate_inps]) if gate_inps else None
+        _, T, k = ids.shape
+        self.check(self.lib.har_cuda_ep_moe_stack(
+            self.handle, ep.handle, la, sa, ga, L, _dptr(x), T, k, _dptr(ids), _dptr(weights),
+            _dptr(y), flags))
+        return y
+
+
+def ep_unique_id() -> bytes:
+    """An NCCL unique id for har_cuda_ep_create (made on one rank, sent to all)."""
+    lib = load_library()
+    buf = (C.c_uint8 * 128)()
+    st = lib.har_cuda_ep_unique_id(buf, 128)
+    if st != 0:
+        raise HarCudaError(st, "ncclGetUniqueId failed")
+    return bytes(buf)
+
+
+def expert_range(E: int, world: int, rank: int):
+    """Routed experts [lo, hi) held by `rank` of `world` (E divisible by world)."""
+    if world < 1 or not 0 <= rank < world or E % world:
+        raise ValueError(f"cannot shard {E} experts over {world} ranks (rank {rank})")
+    el = E // world
+    return rank * el, (rank + 1) * el
+
+
+class EpComm:
+    """An expert-parallel NCCL communicator (one per rank and context); free it
+    explicitly, on every rank, after the last collective call."""
+
+    def __init__(self, ctx: "Context", handle, world: int, rank: int):
+        self.ctx, self.handle, self.world, self.rank = ctx, handle, world, rank
+
+    def free(self):
+        if self.handle:
+            self.ctx.lib.har_cuda_ep_free(self.handle)
+            self.handle = None
 
 
 class Q4KWeights:
