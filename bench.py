@@ -6,7 +6,10 @@ Alice-shaped MoE FFN stack, attention omitted — per layer 512 experts (top-10)
 + one shared expert with a sigmoid gate row, hidden 2048, intermediate 512,
 all Q4_K from N(0,0.02); 256 tokens with Zipf(1.1) routing drawn independently
 per layer; residual add between layers (y = x + moe(x), as execute_layer_cpu).
-A step is one pass of the 256 tokens through all 48 layers.
+A step is one pass of the 256 tokens through all 48 layers.  With N GPUs
+(torchrun) each rank has its own 256 tokens and holds 512/N experts of every
+layer (expert parallelism: token rows go to the experts' GPUs and partial sums
+come back over NCCL); the job's tokens grow with N ("scaling": "weak").
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                   [--config 1..5] [--act f32|q8k]
@@ -212,6 +215,59 @@ def build_stack(ctx, torch, cfg_id: int, rank: int, n_layers=None):
     return layers, keep, x, ids, w, dist
 
 
+def routing(cfg_id: int, rank: int, L: int, T: int):
+    """The per-layer routing of `rank`'s T tokens ([L][T][k] ids and weights)."""
+    ids = np.empty((L, T, TOPK), np.int32)
+    w = np.empty((L, T, TOPK), np.float32)
+    for l in range(L):
+        gen = zipf_routing if cfg_id in (3, 5) else uniform_routing
+        ids[l], w[l] = gen(500 + 31 * l + 1000 * rank, T, E, TOPK)
+    return ids, w
+
+
+def build_ep_stack(ctx, torch, cfg_id: int, rank: int, world: int):
+    """Rank `rank`'s share of the stack for expert parallelism: its routed
+    experts [lo, hi) of every layer (the same bytes as the unsharded stack:
+    the generator is seeded per tensor and indexed by row), the shared expert
+    as a one-expert layer, and the gate row; its own T tokens and routing.
+    distinct[l] counts the experts of layer l that any rank's tokens reach
+    (the weights read per layer over the whole job, shared experts apart)."""
+    import har_cuda
+    dev = torch.device("cuda", ctx.device)
+    cfg = CONFIGS[cfg_id]
+    L, T = cfg["layers"], cfg["T"]
+    lo, hi = har_cuda.expert_range(E, world, rank)
+    El = hi - lo
+    locals_, shareds, gates, keep = [], [], [], []
+    for l in range(L):
+        seed = 1000 + 17 * l
+        t = {}
+        for j, (name, rows, K, row0) in enumerate((
+                ("gate", El * I, H, lo * I), ("up", El * I, H, lo * I), ("down", El * H, I, lo * H),
+                ("sg", I, H, 0), ("su", I, H, 0), ("sd", H, I, 0))):
+            buf = torch.empty(rows * (K // 256) * 144, dtype=torch.uint8, device=dev)
+            ctx.gen_q4k(buf, rows, K, seed + j, row0)
+            t[name] = buf
+        gi = torch.from_numpy(np.random.default_rng(seed).standard_normal(H).astype(np.float32)
+                              * np.float32(0.02)).to(dev)
+        locals_.append(ctx.moe_layer(ctx.wrap_q4k(t["gate"], El, I, H),
+                                     ctx.wrap_q4k(t["up"], El, I, H),
+                                     ctx.wrap_q4k(t["down"], El, H, I)))
+        shareds.append(ctx.moe_layer(ctx.wrap_q4k(t["sg"], 1, I, H), ctx.wrap_q4k(t["su"], 1, I, H),
+                                     ctx.wrap_q4k(t["sd"], 1, H, I)))
+        gates.append(gi)
+        keep.append((t, gi))
+    x = np.random.default_rng(77 + rank).standard_normal((T, H)).astype(np.float32)
+    ids, w = routing(cfg_id, rank, L, T)
+    all_ids = [routing(cfg_id, r, L, T)[0] for r in range(world)]
+    distinct = [len(np.unique(np.concatenate([a[l].ravel() for a in all_ids]))) for l in range(L)]
+    local_distinct = [int(np.sum((np.unique(np.concatenate([a[l].ravel() for a in all_ids])) >= lo)
+                                 & (np.unique(np.concatenate([a[l].ravel() for a in all_ids])) < hi)))
+                      for l in range(L)]
+    torch.cuda.synchronize()
+    return locals_, shareds, gates, keep, x, ids, w, distinct, local_distinct
+
+
 def cpu_sample(torch, keep, x, ids, w, seconds: float):
     """The reference's CPU path (oracle restatement of compose_moe_route with
     expert_matvec's per-call row-chunk threads over all host cores) on the
@@ -260,8 +316,20 @@ def run_ours(args, torch):
                          "(tests/test_gpu_*.py)")
     if args.layers and not args.profile_only:
         raise SystemExit("--layers is only for --profile-only captures")
-    layers, keep, x, ids, w, distinct = build_stack(ctx, torch, args.config, rank, args.layers)
-    L, T = len(layers), cfg["T"]
+    ep = None
+    if world > 1:
+        # expert parallelism: this rank's expert shard, NCCL dispatch/combine
+        locals_, shareds, gates, keep, x, ids, w, distinct, local_distinct = build_ep_stack(
+            ctx, torch, args.config, rank, world)
+        box = [har_cuda.ep_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(box, src=0)
+        ep = ctx.ep_create(box[0], world, rank)
+        L = len(locals_)
+    else:
+        layers, keep, x, ids, w, distinct = build_stack(ctx, torch, args.config, rank, args.layers)
+        local_distinct = distinct
+        L = len(layers)
+    T = cfg["T"]
     flags = har_cuda.MOE_ADD_RESIDUAL | (har_cuda.MOE_ACT_Q8K if args.act == "q8k" else 0)
     dev = torch.device("cuda", local)
     xd = torch.from_numpy(x).to(dev)
@@ -271,16 +339,22 @@ def run_ours(args, torch):
     stream = torch.cuda.Stream(dev)
     ctx.lib.har_cuda_ctx_set_stream(ctx.handle, __import__("ctypes").c_void_p(stream.cuda_stream))
 
+    def step(xin, idin, win, yout):
+        if ep is not None:
+            ctx.ep_moe_stack(ep, locals_, shareds, gates, xin, idin, win, yout, flags)
+        else:
+            ctx.moe_stack(layers, xin, idin, win, yout, flags)
+
     # eager warm-up (allocates the scratch arena), then capture one step in a graph
     with torch.cuda.stream(stream):
         for _ in range(2):
-            ctx.moe_stack(layers, xd, idd, wd, yd, flags)
+            step(xd, idd, wd, yd)
     ctx.synchronize()
     torch.cuda.synchronize()
     n0 = ctx.launch_count
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g, stream=stream):
-        ctx.moe_stack(layers, xd, idd, wd, yd, flags)
+        step(xd, idd, wd, yd)
     launches_per_step = ctx.launch_count - n0
     torch.cuda.synchronize()
 
@@ -321,7 +395,7 @@ def run_ours(args, torch):
     # per-kernel durations: one eager step with the library's CUDA-event profiling
     ctx.profile_begin()
     with torch.cuda.stream(stream):
-        ctx.moe_stack(layers, xd, idd, wd, yd, flags)
+        step(xd, idd, wd, yd)
     prof = ctx.profile_end()
     kern = {}
     for name, t_ms in prof:
@@ -330,24 +404,46 @@ def run_ours(args, torch):
         a[1] += t_ms
     total_k = sum(v[1] for v in kern.values())
 
-    # e2e: the host-buffer C-ABI call (copies inside the timed region)
+    # e2e: host buffers in and out, copies inside the timed region (one GPU:
+    # the host-buffer C-ABI call; expert parallel: pinned copies around the
+    # public ep_moe_stack call)
     e2e_steps = max(3, min(args.steps, 20))
+    if ep is None:
+        def e2e_step():
+            ctx.moe_stack_host(layers, x, ids, w, flags)
+    else:
+        xh = torch.from_numpy(x).pin_memory()
+        ih = torch.from_numpy(ids).pin_memory()
+        wh = torch.from_numpy(w).pin_memory()
+        yh = torch.empty_like(xh).pin_memory()
+
+        def e2e_step():
+            with torch.cuda.stream(stream):
+                xd.copy_(xh, non_blocking=True)
+                idd.copy_(ih, non_blocking=True)
+                wd.copy_(wh, non_blocking=True)
+                step(xd, idd, wd, yd)
+                yh.copy_(yd, non_blocking=True)
+            stream.synchronize()
+            ctx.synchronize()
     for _ in range(2):
-        ctx.moe_stack_host(layers, x, ids, w, flags)
+        e2e_step()
     if dist:
         dist.barrier()
     t0 = time.perf_counter()
     for _ in range(e2e_steps):
-        ctx.moe_stack_host(layers, x, ids, w, flags)
+        e2e_step()
     e2e_ms = (time.perf_counter() - t0) * 1e3 / e2e_steps
     if dist:
         t = torch.tensor([e2e_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
 
-    # algorithmic bytes: each distinct routed expert + the shared expert, once per layer
-    step_bytes = sum((d + 1) * EXPERT_BYTES for d in distinct)
-    gu_bytes = [(d + 1) * 2 * I * (H // 256) * 144 for d in distinct]
+    # algorithmic bytes: each distinct routed expert once per layer over the
+    # job, plus the shared expert once per rank; the roofline kernel's bytes are
+    # this rank's (its reached local experts and the shared expert)
+    step_bytes = sum((d + world) * EXPERT_BYTES for d in distinct)
+    gu_bytes = [(d + 1) * 2 * I * (H // 256) * 144 for d in local_distinct]
     peaks = load_peaks()
     hbm = peaks.get("hbm_gbs", 6650.0)
     peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
@@ -355,7 +451,8 @@ def run_ours(args, torch):
     # tensor-core path at the default threshold); the GEMV kernel otherwise
     rk = "moe_tc_gate_up_kernel" if "moe_tc_gate_up_kernel" in kern else "moe_gate_up_kernel"
     gu = kern.get(rk, [1, 1.0])
-    achieved = (sum(gu_bytes) / gu[0]) / (gu[1] / gu[0] * 1e-3) / 1e9
+    # all launches of the kernel in one step: bytes they move / time they take
+    achieved = sum(gu_bytes) / (gu[1] * 1e-3) / 1e9
     traffic = load_traffic(rk)
     out = None
     if rank == 0:
@@ -372,18 +469,20 @@ def run_ours(args, torch):
                     "activations; Zipf(1.1) top-10 routing drawn per layer",
             "config": {"workload": cfg["name"], "tokens_per_rank": T, "layers": L, "experts": E,
                        "hidden": H, "intermediate": I, "top_k": TOPK, "shared_expert": True,
-                       "activations": args.act, "parallelism": "replicas" if world > 1 else "single",
+                       "activations": args.act,
+                       "parallelism": f"ep{world}: {E // world} experts per rank" if world > 1
+                       else "single",
                        "l2": "inputs larger than L2 (%.1f GB of Q4_K weights read per step)"
                              % (step_bytes / 1e9),
                        "graph": "one CUDA graph per step"},
             "weight_gbs": round(step_bytes / (ms * 1e-3) / 1e9, 1),
-            "hbm_frac": round(step_bytes / (ms * 1e-3) / 1e9 / hbm, 4),
+            "hbm_frac": round(step_bytes / (ms * 1e-3) / 1e9 / hbm / world, 4),
             "roofline": {"bound": "hbm", "kernel": rk,
                          "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(achieved / hbm, 4), "peak_source": peak_src,
                          "traffic": traffic,
-                         "algorithmic_bytes_per_launch": int(sum(gu_bytes) / len(gu_bytes)),
-                         "avg_launch_ms": round(gu[1] / gu[0], 4)},
+                         "algorithmic_bytes_per_step": int(sum(gu_bytes)),
+                         "kernel_ms_per_step": round(gu[1], 4), "launches_per_step": gu[0]},
             "kernels": {k: {"launches": v[0], "ms": round(v[1], 4),
                             "share": round(v[1] / total_k, 4)} for k, v in sorted(kern.items())},
             "e2e": {"value": round(world * T / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
@@ -404,6 +503,10 @@ def run_ours(args, torch):
                           f"expert_matvec row threads over {cores} cores; token-layers/s / {L}"}
     if dist:
         dist.barrier()
+        del g  # the graph holds NCCL work: release it before the communicators
+        torch.cuda.synchronize()
+        if ep is not None:
+            ep.free()
         dist.destroy_process_group()
     return out
 
@@ -484,11 +587,22 @@ def load_traffic(kernel: str):
 
 def main():
     args = parse()
-    if args.impl == "reference":
-        out = run_reference(args)
-    else:
-        import torch
-        out = run_ours(args, torch)
+    # Only the JSON line goes to stdout: libraries that print at start-up
+    # (NCCL's version banner, for one) write to file descriptor 1 directly, so
+    # it points at stderr until the result is ready.
+    sys.stdout.flush()
+    saved = os.dup(1)
+    os.dup2(2, 1)
+    try:
+        if args.impl == "reference":
+            out = run_reference(args)
+        else:
+            import torch
+            out = run_ours(args, torch)
+    finally:
+        sys.stdout.flush()
+        os.dup2(saved, 1)
+        os.close(saved)
     if out is not None:
         print(json.dumps(out), flush=True)
 
