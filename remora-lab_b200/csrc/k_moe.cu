@@ -229,7 +229,10 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(MoeDev p, const float 
                                                           const float *__restrict__ weights,
                                                           const float *__restrict__ sh_gate_inp,
                                                           float *y, int add_residual) {
+  constexpr int SLOTS = 32;  // slots of the token cached in shared memory
   __shared__ float red[8];
+  __shared__ int spos[SLOTS];
+  __shared__ float sw[SLOTS];
   const int64_t t = blockIdx.x;
   const float *xt = x + t * p.H;
   float g = 1.0f;
@@ -243,17 +246,44 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(MoeDev p, const float 
     for (int w = 0; w < (int)(blockDim.x >> 5); ++w) s += red[w];
     g = sigmoid_f(s);
   }
+  for (int s = threadIdx.x; s < p.k && s < SLOTS; s += blockDim.x) {
+    spos[s] = p.inv[t * p.k + s];
+    sw[s] = weights[t * p.k + s];
+  }
   __syncthreads();  // every read of x[t] by the gate dot precedes the writes below
-  for (int h = threadIdx.x; h < p.H; h += blockDim.x) {
-    float acc = 0.0f;
+  // four consecutive h per thread (float4); per element the same operation
+  // order as the reference: slots in order, then the shared expert, then x
+  const float4 *xt4 = reinterpret_cast<const float4 *>(xt);
+  const float4 *yb4 = reinterpret_cast<const float4 *>(p.ybuf);
+  float4 *y4 = reinterpret_cast<float4 *>(y + t * p.H);
+  const int H4 = p.H / 4;
+  for (int h = threadIdx.x; h < H4; h += blockDim.x) {
+    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     for (int s = 0; s < p.k; ++s) {
-      const int pos = p.inv[t * p.k + s];
-      if (pos >= 0)
-        acc = __fadd_rn(acc, __fmul_rn(weights[t * p.k + s], p.ybuf[(int64_t)pos * p.H + h]));
+      const int pos = s < SLOTS ? spos[s] : p.inv[t * p.k + s];
+      if (pos < 0) continue;
+      const float wv = s < SLOTS ? sw[s] : weights[t * p.k + s];
+      const float4 v = yb4[(int64_t)pos * H4 + h];
+      acc.x = __fadd_rn(acc.x, __fmul_rn(wv, v.x));
+      acc.y = __fadd_rn(acc.y, __fmul_rn(wv, v.y));
+      acc.z = __fadd_rn(acc.z, __fmul_rn(wv, v.z));
+      acc.w = __fadd_rn(acc.w, __fmul_rn(wv, v.w));
     }
-    if (p.has_shared) acc = __fadd_rn(acc, __fmul_rn(g, p.ybuf[(int64_t)(p.n + t) * p.H + h]));
-    if (add_residual) acc = __fadd_rn(xt[h], acc);
-    y[t * p.H + h] = acc;
+    if (p.has_shared) {
+      const float4 v = yb4[(int64_t)(p.n + t) * H4 + h];
+      acc.x = __fadd_rn(acc.x, __fmul_rn(g, v.x));
+      acc.y = __fadd_rn(acc.y, __fmul_rn(g, v.y));
+      acc.z = __fadd_rn(acc.z, __fmul_rn(g, v.z));
+      acc.w = __fadd_rn(acc.w, __fmul_rn(g, v.w));
+    }
+    if (add_residual) {
+      const float4 xv = xt4[h];
+      acc.x = __fadd_rn(xv.x, acc.x);
+      acc.y = __fadd_rn(xv.y, acc.y);
+      acc.z = __fadd_rn(xv.z, acc.z);
+      acc.w = __fadd_rn(xv.w, acc.w);
+    }
+    y4[h] = acc;
   }
 }
 
@@ -520,7 +550,10 @@ int32_t run_moe_ffn_in(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const
   if (q8 && (st = launch_q8k_quantize(ctx, x, T, H, S + o_xq))) return st;
   const int max_groups = (int)std::min<int64_t>(E, n) + has_sh;
   const int grid_cap = ctx->num_sms * 4;
-  {
+  // the CUDA-core kernels have work unless every non-empty expert (threshold 1)
+  // and the shared expert take the tensor-core path
+  const bool gemv_work = !tc || thr > 1 || (has_sh && !shared_tc);
+  if (gemv_work) {
     const int rpt = rows_per_tile_gu(H), ntg = (I + rpt - 1) / rpt;
     const int grid = std::max(1, std::min(grid_cap, max_groups * ntg));
     st = q8 ? dispatch_gate_up<ACT_Q8K>(ctx, p, grid) : dispatch_gate_up<ACT_F32>(ctx, p, grid);
@@ -535,7 +568,7 @@ int32_t run_moe_ffn_in(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const
       return st;
   }
   if (q8 && (st = launch_q8k_quantize(ctx, p.a, n + (has_sh ? T : 0), I, S + o_aq))) return st;
-  {
+  if (gemv_work) {
     const int rpt = rows_per_tile_d(I), ntg = (H + rpt - 1) / rpt;
     const int grid = std::max(1, std::min(grid_cap, max_groups * ntg));
     st = q8 ? dispatch_down<ACT_Q8K>(ctx, p, grid) : dispatch_down<ACT_F32>(ctx, p, grid);
