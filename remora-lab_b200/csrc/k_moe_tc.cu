@@ -164,9 +164,15 @@ __device__ __forceinline__ float tc_silu(float v) { return v / (1.0f + expf(-v))
 
 // Bounded wait shared by the roles: false (and the CTA-wide abort flag set)
 // when the barrier phase did not complete within TC_WAIT_LIMIT polls.
-__device__ __forceinline__ bool tc_wait(uint64_t *bar, uint32_t parity, volatile int *abort_s) {
+// Waiters with sleep_ns > 0 sleep between polls (up to sleep_ns): the
+// producers and the epilogue, off the critical path; the MMA issuer and the
+// dequantisers spin.
+__device__ __forceinline__ bool tc_wait(uint64_t *bar, uint32_t parity, volatile int *abort_s,
+                                        uint32_t sleep_ns = 0) {
   if (*abort_s) return false;
-  if (tc::mbar_wait(bar, parity, TC_WAIT_LIMIT)) return true;
+  if (sleep_ns ? tc::mbar_wait_lazy(bar, parity, TC_WAIT_LIMIT, sleep_ns)
+               : tc::mbar_wait(bar, parity, TC_WAIT_LIMIT))
+    return true;
   *abort_s = 1;
   return false;
 }
@@ -174,10 +180,10 @@ __device__ __forceinline__ bool tc_wait(uint64_t *bar, uint32_t parity, volatile
 // forms need it so): one warp-wide test first, then lane 0 polls and the
 // outcome is broadcast.
 __device__ __forceinline__ bool tc_wait_warp(uint64_t *bar, uint32_t parity, volatile int *abort_s,
-                                             int lane) {
+                                             int lane, uint32_t sleep_ns = 0) {
   if (__all_sync(0xffffffffu, tc::mbar_try_wait(bar, parity))) return true;
   bool ok = true;
-  if (lane == 0) ok = tc_wait(bar, parity, abort_s);
+  if (lane == 0) ok = tc_wait(bar, parity, abort_s, sleep_ns);
   return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
 }
 
@@ -256,7 +262,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
         const int ya = sh ? r0 : e * p.rows + r0;
         for (int s = 0; ok && s < KSB; ++s) {
           const int rs = raw_it % RS;
-          if (!(ok = tc_wait(raw_empty + rs, ((raw_it / RS) & 1u) ^ 1u, abort_s))) break;
+          if (!(ok = tc_wait(raw_empty + rs, ((raw_it / RS) & 1u) ^ 1u, abort_s, 256))) break;
           tc::mbar_expect_tx(raw_full + rs, (uint32_t)L::RAWSL);
           uint8_t *dst = sm + L::OFF_RAW + rs * L::RAWSL;
           tc::tma_load_2d(dst, m0, s * Q4K_BYTES, ya, raw_full + rs);
@@ -281,7 +287,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
         const uint32_t sub_bytes = (uint32_t)bw * 128u;
         for (int s0 = 0; ok && s0 < KSTEPS; s0 += kpb) {
           const int bs = b_it % BS, nsub = min(kpb, KSTEPS - s0);
-          if (!(ok = tc_wait(b_empty + bs, ((b_it / BS) & 1u) ^ 1u, abort_s))) break;
+          if (!(ok = tc_wait(b_empty + bs, ((b_it / BS) & 1u) ^ 1u, abort_s, 256))) break;
           tc::mbar_expect_tx(b_full + bs, sub_bytes * (uint32_t)nsub);
           for (int j = 0; j < nsub; ++j)
             tc::tma_load_2d(sm + L::OFF_B + bs * L::BSL + j * sub_bytes, bm, (s0 + j) * 64, 2 * slot0,
@@ -351,7 +357,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
       const int bw = 32 << tc_box(ntok), nq = TM::quarters(bw);
       const int q0 = tc_take_quarters<NA>(qc, nq);
       for (int u = 0; ok && u < nq; ++u)
-        ok = tc_wait_warp(acc_full + q0 + u, (par >> (q0 + u)) & 1u, abort_s, lane);
+        ok = tc_wait_warp(acc_full + q0 + u, (par >> (q0 + u)) & 1u, abort_s, lane, 256);
       if (!ok) break;
       tc::tc_fence_after();
       const int row = (tile % RT) * TC_M + 32 * g + lane;

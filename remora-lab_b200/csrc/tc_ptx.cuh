@@ -43,6 +43,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32
     if (mbar_try_wait(bar, parity)) return true;
   return false;
 }
+// The same with a short sleep between polls (32 ns doubling up to cap_ns),
+// for waiters that can afford the delay: a spinning warp takes issue slots
+// from the warps that do the work.  At most limit polls, ~limit * cap_ns.
+__device__ __forceinline__ bool mbar_wait_lazy(uint64_t *bar, uint32_t parity, uint32_t limit,
+                                               uint32_t cap_ns) {
+  uint32_t ns = 32;
+  for (uint32_t i = 0; i < limit; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    __nanosleep(ns);
+    if (ns < cap_ns) ns <<= 1;
+  }
+  return false;
+}
 
 __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
