@@ -298,12 +298,21 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
     }
   } else if (warp == TC_WARP_MMA) {
     // ---------------- MMA issuer (whole warp, one elected lane issues) ----------------
-    // K-step ks of a tile sits in weight stage ks % 4 (every tile has a
-    // multiple of 4 K-steps), whose u-th fill is global K-step 4u + stage.
+    // Global K-step gs (over this CTA's tiles) sits in weight stage gs % 4
+    // (every tile has a multiple of 4 K-steps); its fill completes phase
+    // gs / 4 of a_full[gs % 4], and B slot use b_it completes phase b_it / BS
+    // of b_full[b_it % BS].  The issuer is the critical path: while its MMAs
+    // are queued the tensor core runs, and every instruction between two
+    // K-steps' MMAs leaves it idle.  So the barrier of the next K-step (and
+    // of the next B slot) is tested without blocking before the current
+    // MMAs are issued, and the blocking wait runs only when that test failed.
+    // A stage (slot) cannot complete its next phase before this warp commits
+    // the current one, so an early positive test stays valid.
     const uint32_t lead = tc::elect_one();
     const uint32_t b_base = tc::smem_u32(sm + L::OFF_B);
     const uint32_t a_base = tmem + (uint32_t)TM::A_COL0;
-    uint32_t gs0 = 0, b_it = 0, par = 0;  // par bit q: parity of quarter q's uses
+    uint32_t gs = 0, b_it = 0, par = 0;  // par bit q: parity of quarter q's uses
+    uint32_t a_rdy = tc::mbar_test_wait(a_full, 0), b_rdy = tc::mbar_test_wait(b_full, 0);
     int qc = 0;
     bool ok = true;
     int2 nxt = p.tt_info[min((int)blockIdx.x, max(total - 1, 0)) / RT];
@@ -320,17 +329,22 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
       const uint32_t idesc = tc::idesc_f16(TC_M, (2 * ntok + 15) & ~15);
       const uint32_t dcol = tmem + (uint32_t)(q0 * 64);
       const uint32_t sub_desc = (uint32_t)(bw * 128) >> 4;  // one K-step of B, descriptor units
-      for (int s0 = 0; ok && s0 < KSTEPS; s0 += kpb) {  // the tile's B slots
-        const int bs = b_it % BS, send = min(kpb, KSTEPS - s0);
-        if (!(ok = tc_wait_warp(b_full + bs, (b_it / BS) & 1u, abort_s, lane))) break;
+      for (int s0 = 0; ok && s0 < KSTEPS; s0 += kpb) {  // the tile's B slots (kpb divides KSTEPS)
+        const int bs = (int)(b_it % BS);
+        if (!__all_sync(0xffffffffu, b_rdy != 0) &&
+            !(ok = tc_wait_warp(b_full + bs, (b_it / BS) & 1u, abort_s, lane)))
+          break;
         const uint64_t bslot = tc::desc_sw128(b_base + (uint32_t)(bs * L::BSL));
-        for (int sub = 0; sub < send; ++sub) {
-          const int ks = s0 + sub, st = ks & 3;
-          if (!(ok = tc_wait_warp(a_full + st, ((gs0 + (uint32_t)ks) >> 2) & 1u, abort_s, lane))) break;
+        b_rdy = tc::mbar_test_wait(b_full + (b_it + 1u) % BS, ((b_it + 1u) / BS) & 1u);
+        for (int sub = 0; sub < kpb; ++sub, ++gs) {
+          const int st = (int)(gs & 3u);
+          if (!__all_sync(0xffffffffu, a_rdy != 0) &&
+              !(ok = tc_wait_warp(a_full + st, (gs >> 2) & 1u, abort_s, lane)))
+            break;
           tc::tc_fence_after();
-          const uint64_t bdesc = bslot + (uint64_t)(sub * sub_desc);
-          const uint32_t acol = a_base + (uint32_t)(st * NA * 32);
-          tc::mma_kstep_ts<NA>(lead, dcol, (uint32_t)bw, acol, bdesc, idesc, ks > 0 ? 1u : 0u);
+          a_rdy = tc::mbar_test_wait(a_full + ((gs + 1u) & 3u), ((gs + 1u) >> 2) & 1u);
+          tc::mma_kstep_ts<NA>(lead, dcol, (uint32_t)bw, a_base + (uint32_t)(st * NA * 32),
+                               bslot + (uint64_t)(sub * sub_desc), idesc, (s0 | sub) != 0 ? 1u : 0u);
           tc::mma_commit_w(lead, a_empty + st);
         }
         if (!ok) break;
@@ -340,7 +354,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
       if (!ok) break;
       for (int u = 0; u < nq; ++u) tc::mma_commit_w(lead, acc_full + q0 + u);
       par ^= ((1u << nq) - 1u) << q0;
-      gs0 += (uint32_t)KSTEPS;
     }
   } else if (warp < TC_WARP_DQ0) {
     // ---------------- epilogue: TMEM -> global ----------------
