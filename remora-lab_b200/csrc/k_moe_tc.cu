@@ -187,6 +187,63 @@ __device__ __forceinline__ bool tc_wait_warp(uint64_t *bar, uint32_t parity, vol
   return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
 }
 
+// MMA issuer state carried across tiles.
+struct TcIssuer {
+  uint32_t lead, b_base, a_base, af, ae;  // af / ae: shared addresses of a_full[0] / a_empty[0]
+  uint64_t *a_full, *b_full, *b_empty;
+  uint32_t ph;     // phase of the current group of four stages
+  uint32_t b_it;   // B slot uses so far
+  uint32_t a_rdy;  // non-blocking test of the next K-step's stage
+  uint32_t b_rdy;  // ... and of the next B slot
+};
+
+// K-step J (0..3) of a group: stage J, B K-step J % KPB of the current slot
+// (a new slot opens when J % KPB == 0).  False when a bounded wait gave up.
+template <int NA, int BW, typename L, int J>
+__device__ __forceinline__ bool tc_issue_kstep(TcIssuer &is, uint32_t dcol, uint32_t idesc, bool first,
+                                               uint64_t &bslot, int &bs, volatile int *abort_s, int lane) {
+  constexpr int KPB = 128 / BW, BS = L::B_SLOTS;
+  constexpr uint32_t SUB = BW * 128 / 16;  // one K-step of B, descriptor units
+  if (J % KPB == 0) {
+    bs = (int)(is.b_it % BS);
+    if (!__all_sync(0xffffffffu, is.b_rdy != 0) &&
+        !tc_wait_warp(is.b_full + bs, (is.b_it / BS) & 1u, abort_s, lane))
+      return false;
+    bslot = tc::desc_sw128(is.b_base + (uint32_t)(bs * L::BSL));
+    is.b_rdy = tc::mbar_test_wait(is.b_full + (is.b_it + 1u) % BS, ((is.b_it + 1u) / BS) & 1u);
+  }
+  if (!__all_sync(0xffffffffu, is.a_rdy != 0) && !tc_wait_warp(is.a_full + J, is.ph, abort_s, lane))
+    return false;
+  tc::tc_fence_after();
+  is.a_rdy = tc::mbar_test_wait_at<((J + 1) & 3) * 8>(is.af, J == 3 ? is.ph ^ 1u : is.ph);
+  tc::mma_kstep_ts_imm<NA, BW>(is.lead, dcol, is.a_base + (uint32_t)(J * NA * 32),
+                               bslot + (uint64_t)((J % KPB) * SUB), idesc, first ? 0u : 1u);
+  tc::mma_commit_at<J * 8>(is.lead, is.ae);
+  if (J % KPB == KPB - 1) {
+    tc::mma_commit_w(is.lead, is.b_empty + bs);
+    ++is.b_it;
+  }
+  return true;
+}
+
+// The MMAs of one tile: K-steps in groups of four, one per weight stage; B
+// slots of 128 / BW K-steps.  False when a bounded wait gave up.
+template <int NA, int BW, typename L>
+__device__ __forceinline__ bool tc_issue_tile(TcIssuer &is, uint32_t dcol, uint32_t idesc, int ksteps,
+                                              volatile int *abort_s, int lane) {
+  uint64_t bslot = 0;
+  int bs = 0;
+  for (int g = 0; g < ksteps; g += 4) {
+    if (!tc_issue_kstep<NA, BW, L, 0>(is, dcol, idesc, g == 0, bslot, bs, abort_s, lane) ||
+        !tc_issue_kstep<NA, BW, L, 1>(is, dcol, idesc, false, bslot, bs, abort_s, lane) ||
+        !tc_issue_kstep<NA, BW, L, 2>(is, dcol, idesc, false, bslot, bs, abort_s, lane) ||
+        !tc_issue_kstep<NA, BW, L, 3>(is, dcol, idesc, false, bslot, bs, abort_s, lane))
+      return false;
+    is.ph ^= 1u;
+  }
+  return true;
+}
+
 // NA = number of A matrices (2: gate and up with SwiGLU epilogue; 1: down).
 template <int NA>
 __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_constant__ TcMaps maps,
@@ -301,18 +358,30 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
     // Global K-step gs (over this CTA's tiles) sits in weight stage gs % 4
     // (every tile has a multiple of 4 K-steps); its fill completes phase
     // gs / 4 of a_full[gs % 4], and B slot use b_it completes phase b_it / BS
-    // of b_full[b_it % BS].  The issuer is the critical path: while its MMAs
-    // are queued the tensor core runs, and every instruction between two
-    // K-steps' MMAs leaves it idle.  So the barrier of the next K-step (and
-    // of the next B slot) is tested without blocking before the current
-    // MMAs are issued, and the blocking wait runs only when that test failed.
-    // A stage (slot) cannot complete its next phase before this warp commits
-    // the current one, so an early positive test stays valid.
+    // of b_full[b_it % BS].  The issuer is the critical path: a single warp
+    // whose every instruction between two K-steps' MMAs leaves the tensor
+    // pipe idle.  So the K-steps of a tile run as groups of four unrolled
+    // over the stages (stage, barrier and column offsets are immediates), and
+    // the barrier of the next K-step (and of the next B slot) is tested
+    // without blocking before the current MMAs are issued; the blocking wait
+    // runs only when that test failed.  A stage (slot) cannot complete its
+    // next phase before this warp commits the current one, so an early
+    // positive test stays valid.
     const uint32_t lead = tc::elect_one();
-    const uint32_t b_base = tc::smem_u32(sm + L::OFF_B);
-    const uint32_t a_base = tmem + (uint32_t)TM::A_COL0;
-    uint32_t gs = 0, b_it = 0, par = 0;  // par bit q: parity of quarter q's uses
-    uint32_t a_rdy = tc::mbar_test_wait(a_full, 0), b_rdy = tc::mbar_test_wait(b_full, 0);
+    TcIssuer is;
+    is.lead = lead;
+    is.b_base = tc::smem_u32(sm + L::OFF_B);
+    is.a_base = tmem + (uint32_t)TM::A_COL0;
+    is.af = tc::smem_u32(a_full);
+    is.ae = tc::smem_u32(a_empty);
+    is.b_full = b_full;
+    is.b_empty = b_empty;
+    is.a_full = a_full;
+    is.ph = 0;
+    is.b_it = 0;
+    is.a_rdy = tc::mbar_test_wait(a_full, 0);
+    is.b_rdy = tc::mbar_test_wait(b_full, 0);
+    uint32_t par = 0;  // par bit q: parity of quarter q's uses
     int qc = 0;
     bool ok = true;
     int2 nxt = p.tt_info[min((int)blockIdx.x, max(total - 1, 0)) / RT];
@@ -320,7 +389,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
       const int2 cur = nxt;  // the next tile's entry is loaded one tile ahead
       nxt = p.tt_info[min(tile + (int)gridDim.x, total - 1) / RT];
       const int ntok = cur.x >> 16;
-      const int bw = 32 << tc_box(ntok), kpb = 128 / bw, nq = TM::quarters(bw);
+      const int bw = 32 << tc_box(ntok), nq = TM::quarters(bw);
       const int q0 = tc_take_quarters<NA>(qc, nq);
       for (int u = 0; ok && u < nq; ++u)
         ok = tc_wait_warp(acc_empty + q0 + u, ((par >> (q0 + u)) & 1u) ^ 1u, abort_s, lane);
@@ -328,29 +397,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
       tc::tc_fence_after();
       const uint32_t idesc = tc::idesc_f16(TC_M, (2 * ntok + 15) & ~15);
       const uint32_t dcol = tmem + (uint32_t)(q0 * 64);
-      const uint32_t sub_desc = (uint32_t)(bw * 128) >> 4;  // one K-step of B, descriptor units
-      for (int s0 = 0; ok && s0 < KSTEPS; s0 += kpb) {  // the tile's B slots (kpb divides KSTEPS)
-        const int bs = (int)(b_it % BS);
-        if (!__all_sync(0xffffffffu, b_rdy != 0) &&
-            !(ok = tc_wait_warp(b_full + bs, (b_it / BS) & 1u, abort_s, lane)))
-          break;
-        const uint64_t bslot = tc::desc_sw128(b_base + (uint32_t)(bs * L::BSL));
-        b_rdy = tc::mbar_test_wait(b_full + (b_it + 1u) % BS, ((b_it + 1u) / BS) & 1u);
-        for (int sub = 0; sub < kpb; ++sub, ++gs) {
-          const int st = (int)(gs & 3u);
-          if (!__all_sync(0xffffffffu, a_rdy != 0) &&
-              !(ok = tc_wait_warp(a_full + st, (gs >> 2) & 1u, abort_s, lane)))
-            break;
-          tc::tc_fence_after();
-          a_rdy = tc::mbar_test_wait(a_full + ((gs + 1u) & 3u), ((gs + 1u) >> 2) & 1u);
-          tc::mma_kstep_ts<NA>(lead, dcol, (uint32_t)bw, a_base + (uint32_t)(st * NA * 32),
-                               bslot + (uint64_t)(sub * sub_desc), idesc, (s0 | sub) != 0 ? 1u : 0u);
-          tc::mma_commit_w(lead, a_empty + st);
-        }
-        if (!ok) break;
-        tc::mma_commit_w(lead, b_empty + bs);
-        ++b_it;
-      }
+      ok = bw == 32 ? tc_issue_tile<NA, 32, L>(is, dcol, idesc, KSTEPS, abort_s, lane)
+                    : tc_issue_tile<NA, 64, L>(is, dcol, idesc, KSTEPS, abort_s, lane);
       if (!ok) break;
       for (int u = 0; u < nq; ++u) tc::mma_commit_w(lead, acc_full + q0 + u);
       par ^= ((1u << nq) - 1u) << q0;

@@ -49,6 +49,19 @@ __device__ __forceinline__ uint32_t mbar_test_wait(uint64_t *bar, uint32_t parit
       : "memory");
   return ok;
 }
+// The same test at shared address bar + OFF (bytes).
+template <int OFF>
+__device__ __forceinline__ uint32_t mbar_test_wait_at(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1+%3], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "n"(OFF)
+      : "memory");
+  return ok;
+}
 // Bounded wait: false after `limit` polls (the caller records an error word).
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32_t limit) {
   for (uint32_t i = 0; i < limit; ++i)
@@ -294,6 +307,62 @@ __device__ __forceinline__ void mma_kstep_ts(uint32_t lead, uint32_t d, uint32_t
         : "memory");
     (void)bw;
   }
+}
+
+// mma_kstep_ts with every column offset an immediate (TMEM addresses take
+// [reg+imm]): matrix m accumulates at column d + m*BW and reads weight
+// columns a + m*32 + 8*kk for K=16 slice kk; B advances 2 descriptor units
+// per slice.  Fewer instructions between two K-steps' MMAs keep the tensor
+// pipe fed: a single issuing warp runs them back to back.
+template <int NA, int BW>
+__device__ __forceinline__ void mma_kstep_ts_imm(uint32_t lead, uint32_t d, uint32_t a, uint64_t b,
+                                                 uint32_t idesc, uint32_t acc0) {
+  if (NA == 2) {
+    asm volatile(
+        "{\n\t.reg .pred e, p, t;\n\t.reg .b64 b1, b2, b3;\n\t"
+        "setp.ne.b32 e, %0, 0;\n\t"
+        "setp.ne.b32 p, %5, 0;\n\t"
+        "setp.eq.b32 t, %0, %0;\n\t"
+        "add.u64 b1, %3, 2;\n\t"
+        "add.u64 b2, %3, 4;\n\t"
+        "add.u64 b3, %3, 6;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%1], [%2], %3, %4, p;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%1+%6], [%2+32], %3, %4, p;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%1], [%2+8], b1, %4, t;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%1+%6], [%2+40], b1, %4, t;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%1], [%2+16], b2, %4, t;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%1+%6], [%2+48], b2, %4, t;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%1], [%2+24], b3, %4, t;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%1+%6], [%2+56], b3, %4, t;\n\t}" ::"r"(lead),
+        "r"(d), "r"(a), "l"(b), "r"(idesc), "r"(acc0), "n"(BW)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred e, p, t;\n\t.reg .b64 b1, b2, b3;\n\t"
+        "setp.ne.b32 e, %0, 0;\n\t"
+        "setp.ne.b32 p, %5, 0;\n\t"
+        "setp.eq.b32 t, %0, %0;\n\t"
+        "add.u64 b1, %3, 2;\n\t"
+        "add.u64 b2, %3, 4;\n\t"
+        "add.u64 b3, %3, 6;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%1], [%2], %3, %4, p;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%1], [%2+8], b1, %4, t;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%1], [%2+16], b2, %4, t;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%1], [%2+24], b3, %4, t;\n\t}" ::"r"(lead),
+        "r"(d), "r"(a), "l"(b), "r"(idesc), "r"(acc0), "n"(BW)
+        : "memory");
+  }
+}
+
+// Commit to the mbarrier at shared address bar + OFF (bytes).
+template <int OFF>
+__device__ __forceinline__ void mma_commit_at(uint32_t lead, uint32_t bar) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "setp.ne.b32 e, %1, 0;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0+%2];\n\t}" ::"r"(bar),
+      "r"(lead), "n"(OFF)
+      : "memory");
 }
 
 __device__ __forceinline__ void mma_commit_w(uint32_t lead, uint64_t *bar) {
