@@ -225,12 +225,17 @@ __global__ void __launch_bounds__(256) moe_down_kernel(MoeDev p, int rows_per_ti
   }
 }
 
-__global__ void __launch_bounds__(256) moe_combine_kernel(MoeDev p, const float *__restrict__ x,
-                                                          const float *__restrict__ weights,
-                                                          const float *__restrict__ sh_gate_inp,
-                                                          float *y, int add_residual) {
+// One block per (token, chunk of COMB_T float4 columns): more blocks than
+// tokens keep enough loads in flight, and each thread loads the rows of up
+// to eight slots before it adds them -- in slot order, as the reference does.
+constexpr int COMB_T = 128;
+
+__global__ void __launch_bounds__(COMB_T) moe_combine_kernel(MoeDev p, const float *__restrict__ x,
+                                                             const float *__restrict__ weights,
+                                                             const float *__restrict__ sh_gate_inp,
+                                                             float *y, int add_residual) {
   constexpr int SLOTS = 32;  // slots of the token cached in shared memory
-  __shared__ float red[8];
+  __shared__ float red[COMB_T / 32];
   __shared__ int spos[SLOTS];
   __shared__ float sw[SLOTS];
   const int64_t t = blockIdx.x;
@@ -253,38 +258,51 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(MoeDev p, const float 
   __syncthreads();  // every read of x[t] by the gate dot precedes the writes below
   // four consecutive h per thread (float4); per element the same operation
   // order as the reference: slots in order, then the shared expert, then x
-  const float4 *xt4 = reinterpret_cast<const float4 *>(xt);
-  const float4 *yb4 = reinterpret_cast<const float4 *>(p.ybuf);
-  float4 *y4 = reinterpret_cast<float4 *>(y + t * p.H);
   const int H4 = p.H / 4;
-  for (int h = threadIdx.x; h < H4; h += blockDim.x) {
-    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    for (int s = 0; s < p.k; ++s) {
-      const int pos = s < SLOTS ? spos[s] : p.inv[t * p.k + s];
-      if (pos < 0) continue;
-      const float wv = s < SLOTS ? sw[s] : weights[t * p.k + s];
-      const float4 v = yb4[(int64_t)pos * H4 + h];
-      acc.x = __fadd_rn(acc.x, __fmul_rn(wv, v.x));
-      acc.y = __fadd_rn(acc.y, __fmul_rn(wv, v.y));
-      acc.z = __fadd_rn(acc.z, __fmul_rn(wv, v.z));
-      acc.w = __fadd_rn(acc.w, __fmul_rn(wv, v.w));
+  const int h = blockIdx.y * COMB_T + threadIdx.x;
+  if (h >= H4) return;
+  const float4 *yb4 = reinterpret_cast<const float4 *>(p.ybuf);
+  float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  for (int s0 = 0; s0 < p.k; s0 += 8) {
+    float4 v[8];
+    float wv[8];
+    unsigned used = 0;  // bit j: slot s0 + j holds a row
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {  // the loads first: up to eight in flight
+      const int s = s0 + j;
+      int pos = -1;
+      wv[j] = 0.0f;
+      if (s < p.k) {
+        pos = s < SLOTS ? spos[s] : p.inv[t * p.k + s];
+        wv[j] = s < SLOTS ? sw[s] : weights[t * p.k + s];
+      }
+      v[j] = pos >= 0 ? yb4[(int64_t)pos * H4 + h] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      used |= (pos >= 0 ? 1u : 0u) << j;
     }
-    if (p.has_shared) {
-      const float4 v = yb4[(int64_t)(p.n + t) * H4 + h];
-      acc.x = __fadd_rn(acc.x, __fmul_rn(g, v.x));
-      acc.y = __fadd_rn(acc.y, __fmul_rn(g, v.y));
-      acc.z = __fadd_rn(acc.z, __fmul_rn(g, v.z));
-      acc.w = __fadd_rn(acc.w, __fmul_rn(g, v.w));
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (!((used >> j) & 1u)) continue;
+      acc.x = __fadd_rn(acc.x, __fmul_rn(wv[j], v[j].x));
+      acc.y = __fadd_rn(acc.y, __fmul_rn(wv[j], v[j].y));
+      acc.z = __fadd_rn(acc.z, __fmul_rn(wv[j], v[j].z));
+      acc.w = __fadd_rn(acc.w, __fmul_rn(wv[j], v[j].w));
     }
-    if (add_residual) {
-      const float4 xv = xt4[h];
-      acc.x = __fadd_rn(xv.x, acc.x);
-      acc.y = __fadd_rn(xv.y, acc.y);
-      acc.z = __fadd_rn(xv.z, acc.z);
-      acc.w = __fadd_rn(xv.w, acc.w);
-    }
-    y4[h] = acc;
   }
+  if (p.has_shared) {
+    const float4 v = yb4[(int64_t)(p.n + t) * H4 + h];
+    acc.x = __fadd_rn(acc.x, __fmul_rn(g, v.x));
+    acc.y = __fadd_rn(acc.y, __fmul_rn(g, v.y));
+    acc.z = __fadd_rn(acc.z, __fmul_rn(g, v.z));
+    acc.w = __fadd_rn(acc.w, __fmul_rn(g, v.w));
+  }
+  if (add_residual) {
+    const float4 xv = reinterpret_cast<const float4 *>(xt)[h];
+    acc.x = __fadd_rn(xv.x, acc.x);
+    acc.y = __fadd_rn(xv.y, acc.y);
+    acc.z = __fadd_rn(xv.z, acc.z);
+    acc.w = __fadd_rn(xv.w, acc.w);
+  }
+  reinterpret_cast<float4 *>(y + t * p.H)[h] = acc;
 }
 
 // ---------------------------------------------------------------------------
@@ -583,7 +601,7 @@ int32_t run_moe_ffn_in(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const
       return st;
   }
   prof_begin(ctx);
-  moe_combine_kernel<<<(unsigned)T, 256, 0, ctx->stream>>>(
+  moe_combine_kernel<<<dim3((unsigned)T, (unsigned)((H / 4 + COMB_T - 1) / COMB_T)), COMB_T, 0, ctx->stream>>>(
       p, x, weights, layer->sh_gate_inp, y, (flags & HAR_CUDA_MOE_ADD_RESIDUAL) ? 1 : 0);
   return check_launch(ctx, "moe_combine_kernel");
 }

@@ -512,14 +512,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
 // for every slot whose expert runs on the tensor-core path: routed slot s holds entry order[s] (token order[s] / k,
 // expert ids[order[s]]); slot n + t is the shared expert's row of token t.
 // One CTA per slot; slots of CUDA-core experts are skipped.
-__global__ void __launch_bounds__(256) gather_f16_kernel(const float *__restrict__ x, int H,
-                                                         const int32_t *__restrict__ order,
-                                                         const int32_t *__restrict__ ids,
-                                                         const int32_t *__restrict__ counts,
-                                                         const int32_t *__restrict__ n_valid,
-                                                         int thr, int n, int k, int shared_tc,
-                                                         __half *__restrict__ xg) {
-  const int slot = blockIdx.x;
+// One warp per slot, GATHER_WARPS slots per block: the slot's index chain
+// (order -> ids -> counts) of several slots is in flight at once.
+constexpr int GATHER_WARPS = 8;
+
+__global__ void __launch_bounds__(GATHER_WARPS * 32) gather_f16_kernel(
+    const float *__restrict__ x, int H, const int32_t *__restrict__ order,
+    const int32_t *__restrict__ ids, const int32_t *__restrict__ counts,
+    const int32_t *__restrict__ n_valid, int thr, int n, int k, int T, int shared_tc,
+    __half *__restrict__ xg) {
+  const int slot = blockIdx.x * GATHER_WARPS + (int)(threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (slot >= n + T) return;
   int tok;
   if (slot < n) {
     // grouped positions past the valid entries (those with an out-of-range
@@ -535,7 +538,8 @@ __global__ void __launch_bounds__(256) gather_f16_kernel(const float *__restrict
   const float4 *src = reinterpret_cast<const float4 *>(x + (int64_t)tok * H);
   uint2 *dhi = reinterpret_cast<uint2 *>(xg + 2 * (int64_t)slot * H);
   uint2 *dlo = dhi + H / 4;
-  for (int i = threadIdx.x; i < H / 4; i += blockDim.x) {
+#pragma unroll 4
+  for (int i = lane; i < H / 4; i += 32) {
     const float4 v = src[i];  // K order (0, 2, 1, 3) inside each group of four
     const __half2 a = __floats2half2_rn(v.x, v.z), b = __floats2half2_rn(v.y, v.w);
     const float2 fa = __half22float2(a), fb = __half22float2(b);
@@ -549,8 +553,9 @@ int32_t launch_gather_f16(har_cuda_ctx *ctx, const float *x, int H, const int32_
                           const int32_t *ids, const int32_t *counts, const int32_t *n_valid,
                           int thr, int n, int k, int T, int shared_tc, __half *xg) {
   prof_begin(ctx);
-  gather_f16_kernel<<<n + T, 256, 0, ctx->stream>>>(x, H, order, ids, counts, n_valid, thr, n, k,
-                                                    shared_tc, xg);
+  const unsigned grid = (unsigned)((n + T + GATHER_WARPS - 1) / GATHER_WARPS);
+  gather_f16_kernel<<<grid, GATHER_WARPS * 32, 0, ctx->stream>>>(x, H, order, ids, counts, n_valid, thr,
+                                                                n, k, T, shared_tc, xg);
   return check_launch(ctx, "gather_f16_kernel");
 }
 
