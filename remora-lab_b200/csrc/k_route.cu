@@ -124,20 +124,28 @@ __global__ void __launch_bounds__(GROUP_WARPS * 32) group_kernel(
   const int seg = (n + GROUP_WARPS - 1) / GROUP_WARPS;
   const int s0 = min(n, warp * seg), s1 = min(n, s0 + seg);
   const unsigned lt = (1u << lane) - 1u;
-  // pass 1: per-warp counts
-  for (int b = s0; b < s1; b += 32) {
-    const int i = b + lane;
-    int e = -1;
-    if (i < s1) {
-      e = ids[i];
-      if (e < 0 || e >= E) {
+  // pass 1: per-warp counts.  Ids are loaded GB chunks of 32 at a time before
+  // the warp-synchronous updates, so one load latency covers 32 * GB entries.
+  constexpr int GB = 8;
+  for (int b0 = s0; b0 < s1; b0 += 32 * GB) {
+    int ev[GB];
+#pragma unroll
+    for (int j = 0; j < GB; ++j) {
+      const int i = b0 + 32 * j + lane;
+      ev[j] = i < s1 ? ids[i] : -1;
+    }
+#pragma unroll
+    for (int j = 0; j < GB; ++j) {
+      const int i = b0 + 32 * j + lane;
+      int e = ev[j];
+      if (i < s1 && (e < 0 || e >= E)) {
         if (!(allow_empty && e == -1)) atomicOr(status, DEV_ERR_BOUNDS);
         e = -1;
       }
+      const unsigned m = __match_any_sync(0xffffffffu, e);
+      if (e >= 0 && (m & lt) == 0) cnt[warp * E + e] += __popc(m);
+      __syncwarp();
     }
-    const unsigned m = __match_any_sync(0xffffffffu, e);
-    if (e >= 0 && (m & lt) == 0) cnt[warp * E + e] += __popc(m);
-    __syncwarp();
   }
   __syncthreads();
   // per-expert totals, then a block-wide exclusive scan in chunks of blockDim
@@ -178,43 +186,93 @@ __global__ void __launch_bounds__(GROUP_WARPS * 32) group_kernel(
     __syncthreads();
   }
   for (int e = threadIdx.x; e <= E; e += blockDim.x) offsets[e] = off[e];
-  // pass 2: positions
-  for (int b = s0; b < s1; b += 32) {
-    const int i = b + lane;
-    int e = -1;
-    if (i < s1) {
-      e = ids[i];
+  // pass 2: positions (ids loaded in batches as in pass 1)
+  for (int b0 = s0; b0 < s1; b0 += 32 * GB) {
+    int ev[GB];
+#pragma unroll
+    for (int j = 0; j < GB; ++j) {
+      const int i = b0 + 32 * j + lane;
+      ev[j] = i < s1 ? ids[i] : -1;
+    }
+#pragma unroll
+    for (int j = 0; j < GB; ++j) {
+      const int i = b0 + 32 * j + lane;
+      int e = ev[j];
       if (e < 0 || e >= E) e = -1;
+      const unsigned m = __match_any_sync(0xffffffffu, e);
+      int pos = 0;
+      if (e >= 0) pos = off[e] + cnt[warp * E + e] + __popc(m & lt);
+      __syncwarp();
+      if (e >= 0) {
+        order[pos] = i;
+        inv[i] = pos;
+        if ((m & lt) == 0) cnt[warp * E + e] += __popc(m);
+      } else if (i < s1) {
+        inv[i] = -1;
+      }
+      __syncwarp();
     }
-    const unsigned m = __match_any_sync(0xffffffffu, e);
-    int pos = 0;
-    if (e >= 0) pos = off[e] + cnt[warp * E + e] + __popc(m & lt);
-    __syncwarp();
-    if (e >= 0) {
-      order[pos] = i;
-      inv[i] = pos;
-      if ((m & lt) == 0) cnt[warp * E + e] += __popc(m);
-    } else if (i < s1) {
-      inv[i] = -1;
-    }
-    __syncwarp();
   }
-  // Non-empty experts in expert order (warp 0, ballot + popc), split by token
-  // count: ne[] those below `thr` (CUDA-core path); those at or above it
-  // (tensor-core path) are cut into ceil(count/nt) token tiles, listed in
-  // expert order as tt_info[j] = {expert | tokens << 16, first slot}.  When
-  // shared_T > 0 the shared expert (index E, slots n .. n + shared_T) follows
-  // with ceil(shared_T/nt) tiles.  *n_tt = the number of tiles.
-  if (ne && warp == 0) {
-    int run = 0, run_tt = 0;
-    for (int base = 0; base < E; base += 32) {
-      const int e = base + lane;
-      const int c = e < E ? off[e + 1] - off[e] : 0;
-      const bool small = c > 0 && c < thr;
-      const bool bg = c > 0 && c >= thr;
+  // Non-empty experts in expert order, split by token count: ne[] those
+  // below `thr` (CUDA-core path); those at or above it (tensor-core path) are
+  // cut into ceil(count/nt) token tiles, listed in expert order as
+  // tt_info[j] = {expert | tokens << 16, first slot}.  When shared_T > 0 the
+  // shared expert (index E, slots n .. n + shared_T) follows with
+  // ceil(shared_T/nt) tiles.  *n_ne / *n_tt = the list lengths.  Each warp
+  // takes chunks of 32 experts; a scan of the chunks' totals (kept in the
+  // per-warp counters, free after pass 2) gives each chunk its offsets.
+  if (ne) {
+    const int nch = (E + 31) / 32;
+    int32_t *ch_small = cnt, *ch_tt = cnt + nch;
+    __syncthreads();  // pass 2 is done with cnt
+    for (int c = warp; c < nch; c += GROUP_WARPS) {
+      const int e = c * 32 + lane;
+      const int ce = e < E ? off[e + 1] - off[e] : 0;
+      const bool small = ce > 0 && ce < thr;
+      const int tt = ce > 0 && ce >= thr ? (ce + nt - 1) / nt : 0;
+      const int ns = __popc(__ballot_sync(0xffffffffu, small));
+      const int ntt = __reduce_add_sync(0xffffffffu, (unsigned)tt);
+      if (lane == 0) {
+        ch_small[c] = ns;
+        ch_tt[c] = ntt;
+      }
+    }
+    __syncthreads();
+    if (warp == 0) {  // exclusive scans over the chunks
+      int rs = 0, rt = 0;
+      for (int base = 0; base < nch; base += 32) {
+        const int c = base + lane;
+        const int a = c < nch ? ch_small[c] : 0, b = c < nch ? ch_tt[c] : 0;
+        int ia = a, ib = b;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int ua = __shfl_up_sync(0xffffffffu, ia, o), ub = __shfl_up_sync(0xffffffffu, ib, o);
+          if (lane >= o) {
+            ia += ua;
+            ib += ub;
+          }
+        }
+        if (c < nch) {
+          ch_small[c] = rs + ia - a;
+          ch_tt[c] = rt + ib - b;
+        }
+        rs += __shfl_sync(0xffffffffu, ia, 31);
+        rt += __shfl_sync(0xffffffffu, ib, 31);
+      }
+      if (lane == 0) {
+        *n_ne = rs;
+        *n_tt = rt + (shared_T + nt - 1) / nt;
+        warp_tot[0] = rt;  // first tile of the shared expert
+      }
+    }
+    __syncthreads();
+    for (int c = warp; c < nch; c += GROUP_WARPS) {
+      const int e = c * 32 + lane;
+      const int ce = e < E ? off[e + 1] - off[e] : 0;
+      const bool small = ce > 0 && ce < thr;
+      const int tt = ce > 0 && ce >= thr ? (ce + nt - 1) / nt : 0;
       const unsigned bm = __ballot_sync(0xffffffffu, small);
-      if (small) ne[run + __popc(bm & lt)] = e;
-      const int tt = bg ? (c + nt - 1) / nt : 0;
+      if (small) ne[ch_small[c] + __popc(bm & lt)] = e;
       int incl = tt;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
@@ -222,16 +280,11 @@ __global__ void __launch_bounds__(GROUP_WARPS * 32) group_kernel(
         if (lane >= o) incl += u;
       }
       for (int j = 0; j < tt; ++j)
-        tt_info[run_tt + incl - tt + j] = make_int2(e | (min(nt, c - j * nt) << 16), off[e] + j * nt);
-      run += __popc(bm);
-      run_tt += __shfl_sync(0xffffffffu, incl, 31);
+        tt_info[ch_tt[c] + incl - tt + j] = make_int2(e | (min(nt, ce - j * nt) << 16), off[e] + j * nt);
     }
-    for (int t0 = lane * nt; t0 < shared_T; t0 += 32 * nt)
+    const int run_tt = warp_tot[0];
+    for (int t0 = (int)threadIdx.x * nt; t0 < shared_T; t0 += (int)blockDim.x * nt)
       tt_info[run_tt + t0 / nt] = make_int2(E | (min(nt, shared_T - t0) << 16), n + t0);
-    if (lane == 0) {
-      *n_ne = run;
-      *n_tt = run_tt + (shared_T + nt - 1) / nt;
-    }
   }
 }
 
