@@ -74,15 +74,18 @@ struct TcSmem {
 };
 
 // Tensor-memory plan (512 columns x 128 lanes): accumulators in 64-column
-// quarters at [0, A_COL0), then one f16 weight stage per dequant team, NA x 32
-// columns each (one 64-value K-step: row = lane, two f16 per column).
+// quarters at [0, A_COL0), then one f16 weight stage per dequant team of SW
+// columns (row = lane, two f16 per column): NA x 32 (one 64-value K-step of
+// each matrix), or with DBL (one matrix, NA = 1) 64 columns holding two
+// consecutive K-steps, so a stage feeds 8 MMAs either way.
 // A tile whose token box has bw B rows (2 per token) takes
 // ceil(NA * bw / 64) quarters: matrix m's accumulator sits at column m * bw
 // of the tile's first quarter.
-template <int NA>
+template <int NA, bool DBL>
 struct TcTmem {
   static constexpr int A_STAGES = TC_DQ_TEAMS;
-  static constexpr int A_COL0 = TC_TMEM_COLS - A_STAGES * NA * 32;
+  static constexpr int SW = DBL ? 64 : NA * 32;
+  static constexpr int A_COL0 = TC_TMEM_COLS - A_STAGES * SW;
   static constexpr int NQ = A_COL0 / 64;
   static __device__ __forceinline__ int quarters(int bw) {
     return (NA * bw + 63) / 64;
@@ -95,12 +98,12 @@ __device__ __forceinline__ int tc_box(int n) { return n <= 16 ? 0 : 1; }
 // Accumulator quarters of the next tile: `qc` is the ring cursor (the MMA
 // warps and the epilogue walk the same tiles, so they agree); a tile that does
 // not fit before the end wraps to quarter 0.  Returns the first quarter.
-template <int NA>
+template <typename TM>
 __device__ __forceinline__ int tc_take_quarters(int &qc, int nq) {
-  if (qc + nq > TcTmem<NA>::NQ) qc = 0;
+  if (qc + nq > TM::NQ) qc = 0;
   const int q0 = qc;
   qc += nq;
-  if (qc == TcTmem<NA>::NQ) qc = 0;
+  if (qc == TM::NQ) qc = 0;
   return q0;
 }
 
@@ -197,13 +200,16 @@ struct TcIssuer {
   uint32_t b_rdy;  // ... and of the next B slot
 };
 
-// K-step J (0..3) of a group: stage J, B K-step J % KPB of the current slot
-// (a new slot opens when J % KPB == 0).  False when a bounded wait gave up.
-template <int NA, int BW, typename L, int J>
+// Step J (0..3) of a group: weight stage J.  A step is one 64-value K-step
+// of each matrix, or with DBL two consecutive K-steps of the one matrix; B
+// slots hold 128 / BW K-steps, i.e. KPB steps, and a new slot opens when
+// J % KPB == 0.  False when a bounded wait gave up.
+template <int NA, bool DBL, int BW, typename L, int J>
 __device__ __forceinline__ bool tc_issue_kstep(TcIssuer &is, uint32_t dcol, uint32_t idesc, bool first,
                                                uint64_t &bslot, int &bs, volatile int *abort_s, int lane) {
-  constexpr int KPB = 128 / BW, BS = L::B_SLOTS;
+  constexpr int KPB = DBL ? 64 / BW : 128 / BW, BS = L::B_SLOTS;
   constexpr uint32_t SUB = BW * 128 / 16;  // one K-step of B, descriptor units
+  constexpr int SW = TcTmem<NA, DBL>::SW;
   if (J % KPB == 0) {
     bs = (int)(is.b_it % BS);
     if (!__all_sync(0xffffffffu, is.b_rdy != 0) &&
@@ -216,8 +222,12 @@ __device__ __forceinline__ bool tc_issue_kstep(TcIssuer &is, uint32_t dcol, uint
     return false;
   tc::tc_fence_after();
   is.a_rdy = tc::mbar_test_wait_at<((J + 1) & 3) * 8>(is.af, J == 3 ? is.ph ^ 1u : is.ph);
-  tc::mma_kstep_ts_imm<NA, BW>(is.lead, dcol, is.a_base + (uint32_t)(J * NA * 32),
-                               bslot + (uint64_t)((J % KPB) * SUB), idesc, first ? 0u : 1u);
+  if (DBL)
+    tc::mma_kstep2_ts_imm<SUB>(is.lead, dcol, is.a_base + (uint32_t)(J * SW),
+                               bslot + (uint64_t)((J % KPB) * 2 * SUB), idesc, first ? 0u : 1u);
+  else
+    tc::mma_kstep_ts_imm<NA, BW>(is.lead, dcol, is.a_base + (uint32_t)(J * SW),
+                                 bslot + (uint64_t)((J % KPB) * SUB), idesc, first ? 0u : 1u);
   tc::mma_commit_at<J * 8>(is.lead, is.ae);
   if (J % KPB == KPB - 1) {
     tc::mma_commit_w(is.lead, is.b_empty + bs);
@@ -226,18 +236,18 @@ __device__ __forceinline__ bool tc_issue_kstep(TcIssuer &is, uint32_t dcol, uint
   return true;
 }
 
-// The MMAs of one tile: K-steps in groups of four, one per weight stage; B
-// slots of 128 / BW K-steps.  False when a bounded wait gave up.
-template <int NA, int BW, typename L>
-__device__ __forceinline__ bool tc_issue_tile(TcIssuer &is, uint32_t dcol, uint32_t idesc, int ksteps,
+// The MMAs of one tile: `steps` steps in groups of four, one per weight
+// stage.  False when a bounded wait gave up.
+template <int NA, bool DBL, int BW, typename L>
+__device__ __forceinline__ bool tc_issue_tile(TcIssuer &is, uint32_t dcol, uint32_t idesc, int steps,
                                               volatile int *abort_s, int lane) {
   uint64_t bslot = 0;
   int bs = 0;
-  for (int g = 0; g < ksteps; g += 4) {
-    if (!tc_issue_kstep<NA, BW, L, 0>(is, dcol, idesc, g == 0, bslot, bs, abort_s, lane) ||
-        !tc_issue_kstep<NA, BW, L, 1>(is, dcol, idesc, false, bslot, bs, abort_s, lane) ||
-        !tc_issue_kstep<NA, BW, L, 2>(is, dcol, idesc, false, bslot, bs, abort_s, lane) ||
-        !tc_issue_kstep<NA, BW, L, 3>(is, dcol, idesc, false, bslot, bs, abort_s, lane))
+  for (int g = 0; g < steps; g += 4) {
+    if (!tc_issue_kstep<NA, DBL, BW, L, 0>(is, dcol, idesc, g == 0, bslot, bs, abort_s, lane) ||
+        !tc_issue_kstep<NA, DBL, BW, L, 1>(is, dcol, idesc, false, bslot, bs, abort_s, lane) ||
+        !tc_issue_kstep<NA, DBL, BW, L, 2>(is, dcol, idesc, false, bslot, bs, abort_s, lane) ||
+        !tc_issue_kstep<NA, DBL, BW, L, 3>(is, dcol, idesc, false, bslot, bs, abort_s, lane))
       return false;
     is.ph ^= 1u;
   }
@@ -245,11 +255,13 @@ __device__ __forceinline__ bool tc_issue_tile(TcIssuer &is, uint32_t dcol, uint3
 }
 
 // NA = number of A matrices (2: gate and up with SwiGLU epilogue; 1: down).
-template <int NA>
+// DBL (NA = 1, K a multiple of 512): a weight stage holds two K-steps.
+template <int NA, bool DBL>
 __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_constant__ TcMaps maps,
                                                                const TcParams p) {
   using L = TcSmem<NA>;
-  using TM = TcTmem<NA>;
+  using TM = TcTmem<NA, DBL>;
+  static_assert(!DBL || NA == 1, "two-K-step stages are for the one-matrix GEMM");
   extern __shared__ uint8_t tc_raw[];
   constexpr int RS = L::RAW_SLOTS, BS = L::B_SLOTS, AS = TM::A_STAGES, NQ = TM::NQ;
   __shared__ uint64_t bars[2 * RS + 2 * BS + 2 * AS + 2 * NQ];
@@ -269,7 +281,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
   if (tid == 32) {
     for (int s = 0; s < RS; ++s) {
       tc::mbar_init(raw_full + s, 1);
-      tc::mbar_init(raw_empty + s, TC_DQ_WARPS);
+      tc::mbar_init(raw_empty + s, DBL ? TC_DQ_WARPS / 2 : TC_DQ_WARPS);  // the warps that read the slot
     }
     for (int s = 0; s < AS; ++s) {
       tc::mbar_init(a_full + s, TC_DQ_WARPS / TC_DQ_TEAMS);  // one team fills a stage
@@ -390,15 +402,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
       nxt = p.tt_info[min(tile + (int)gridDim.x, total - 1) / RT];
       const int ntok = cur.x >> 16;
       const int bw = 32 << tc_box(ntok), nq = TM::quarters(bw);
-      const int q0 = tc_take_quarters<NA>(qc, nq);
+      const int q0 = tc_take_quarters<TM>(qc, nq);
       for (int u = 0; ok && u < nq; ++u)
         ok = tc_wait_warp(acc_empty + q0 + u, ((par >> (q0 + u)) & 1u) ^ 1u, abort_s, lane);
       if (!ok) break;
       tc::tc_fence_after();
       const uint32_t idesc = tc::idesc_f16(TC_M, (2 * ntok + 15) & ~15);
       const uint32_t dcol = tmem + (uint32_t)(q0 * 64);
-      ok = bw == 32 ? tc_issue_tile<NA, 32, L>(is, dcol, idesc, KSTEPS, abort_s, lane)
-                    : tc_issue_tile<NA, 64, L>(is, dcol, idesc, KSTEPS, abort_s, lane);
+      const int steps = DBL ? KSTEPS / 2 : KSTEPS;
+      ok = bw == 32 ? tc_issue_tile<NA, DBL, 32, L>(is, dcol, idesc, steps, abort_s, lane)
+                    : tc_issue_tile<NA, DBL, 64, L>(is, dcol, idesc, steps, abort_s, lane);
       if (!ok) break;
       for (int u = 0; u < nq; ++u) tc::mma_commit_w(lead, acc_full + q0 + u);
       par ^= ((1u << nq) - 1u) << q0;
@@ -416,7 +429,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
       nxt = p.tt_info[min(tile + (int)gridDim.x, total - 1) / RT];
       const int ntok = cur.x >> 16, slot0 = cur.y;
       const int bw = 32 << tc_box(ntok), nq = TM::quarters(bw);
-      const int q0 = tc_take_quarters<NA>(qc, nq);
+      const int q0 = tc_take_quarters<TM>(qc, nq);
       for (int u = 0; ok && u < nq; ++u)
         ok = tc_wait_warp(acc_full + q0 + u, (par >> (q0 + u)) & 1u, abort_s, lane, 256);
       if (!ok) break;
@@ -461,28 +474,42 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
     }
   } else {
     // ---------------- dequantisers: raw Q4_K -> f16 weight stages in TMEM ----------------
-    // Team t (four warps) takes the K-steps ks = t (mod 4) -- one of the four
-    // K-steps of every raw slot -- and fills weight stage t with them.  Warp
-    // w may store only TMEM lanes 32*(w%4)..: it owns weight rows
-    // 32*(w%4)+lane of every matrix.
+    // Team t (four warps) takes the steps t (mod 4) and fills weight stage t
+    // with them.  Without DBL a step is chunk t of every raw slot (one of its
+    // four K-steps) for each matrix; with DBL it is the chunk pair 2(t&1),
+    // 2(t&1)+1 of every second raw slot (slot 2u + t/2 for the team's u-th
+    // step), so each slot is released by the two teams that use it.  Warp w
+    // may store only TMEM lanes 32*(w%4)..: it owns weight rows 32*(w%4)+lane
+    // of every matrix.
     const int g = warp & 3, team = (warp - TC_WARP_DQ0) >> 2;
     const int r = 32 * g + lane;
     const uint32_t lane_addr = (uint32_t)(32 * g) << 16;
-    const uint32_t acol = tmem + lane_addr + (uint32_t)(TM::A_COL0 + team * NA * 32);
-    uint32_t u = 0, rit = 0;  // team K-steps so far; raw slots so far
+    const uint32_t acol = tmem + lane_addr + (uint32_t)(TM::A_COL0 + team * TM::SW);
+    const int steps = DBL ? KSTEPS / 2 : KSTEPS;
+    uint32_t u = 0;  // this team's steps so far
     bool ok = true;
     for (int tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
-      for (int ks = team; ks < KSTEPS; ks += TC_DQ_TEAMS, ++u, ++rit) {
-        const int rs = rit % RS;
-        if (!(ok = tc_wait_warp(raw_full + rs, (rit / RS) & 1u, abort_s, lane))) break;
+      for (int ks = team; ks < steps; ks += TC_DQ_TEAMS, ++u) {
+        const uint32_t slot = DBL ? 2u * u + (uint32_t)(team >> 1) : u;
+        const int rs = (int)(slot % RS);
+        if (!(ok = tc_wait_warp(raw_full + rs, (slot / RS) & 1u, abort_s, lane))) break;
         if (!(ok = tc_wait_warp(a_empty + team, (u & 1u) ^ 1u, abort_s, lane))) break;
         tc::tc_fence_after();
         const uint8_t *raw = sm + L::OFF_RAW + rs * L::RAWSL;
+        if (DBL) {
 #pragma unroll
-        for (int m = 0; m < NA; ++m) {  // team t holds chunk t of the super-block
-          uint32_t o[32];
-          tc_dequant_step(raw + (m * TC_M + r) * Q4K_BYTES, team, o);
-          tc::tmem_st32(acol + (uint32_t)(m * 32), o);
+          for (int h = 0; h < 2; ++h) {  // K-steps 2(t&1) + h of the super-block
+            uint32_t o[32];
+            tc_dequant_step(raw + r * Q4K_BYTES, 2 * (team & 1) + h, o);
+            tc::tmem_st32(acol + (uint32_t)(h * 32), o);
+          }
+        } else {
+#pragma unroll
+          for (int m = 0; m < NA; ++m) {  // team t holds chunk t of the super-block
+            uint32_t o[32];
+            tc_dequant_step(raw + (m * TC_M + r) * Q4K_BYTES, team, o);
+            tc::tmem_st32(acol + (uint32_t)(m * 32), o);
+          }
         }
         tc::tmem_wait_st();
         tc::tc_fence_before();
@@ -564,15 +591,17 @@ int32_t launch_moe_tc(har_cuda_ctx *ctx, const TcMaps &maps, const TcParams &p, 
   const int grid = std::max(1, std::min(ctx->num_sms, max_tiles));
   if (na == 2) {
     const size_t smem = (size_t)TcSmem<2>::BYTES + 1024;
-    cudaFuncSetAttribute(moe_tc_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(moe_tc_kernel<2, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     prof_begin(ctx);
-    moe_tc_kernel<2><<<grid, TC_THREADS, smem, ctx->stream>>>(maps, p);
+    moe_tc_kernel<2, false><<<grid, TC_THREADS, smem, ctx->stream>>>(maps, p);
     return check_launch(ctx, "moe_tc_gate_up_kernel");
   }
   const size_t smem = (size_t)TcSmem<1>::BYTES + 1024;
-  cudaFuncSetAttribute(moe_tc_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  // two K-steps per weight stage when a tile's K-steps come in groups of 8
+  auto kern = p.K % 512 == 0 ? moe_tc_kernel<1, true> : moe_tc_kernel<1, false>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   prof_begin(ctx);
-  moe_tc_kernel<1><<<grid, TC_THREADS, smem, ctx->stream>>>(maps, p);
+  kern<<<grid, TC_THREADS, smem, ctx->stream>>>(maps, p);
   return check_launch(ctx, "moe_tc_down_kernel");
 }
 
