@@ -256,12 +256,16 @@ __device__ __forceinline__ bool tc_issue_tile(TcIssuer &is, uint32_t dcol, uint3
 
 // NA = number of A matrices (2: gate and up with SwiGLU epilogue; 1: down).
 // DBL (NA = 1, K a multiple of 512): a weight stage holds two K-steps.
-template <int NA, bool DBL>
+// PAIR (NA = 2): the down GEMM with its two "matrices" the row blocks
+// [r0, r0 + 128) and [r0 + 128, r0 + 256) of one weight tensor; a tile covers
+// 256 output rows, and the epilogue writes both accumulators to ybuf.
+template <int NA, bool DBL, bool PAIR>
 __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_constant__ TcMaps maps,
                                                                const TcParams p) {
   using L = TcSmem<NA>;
   using TM = TcTmem<NA, DBL>;
   static_assert(!DBL || NA == 1, "two-K-step stages are for the one-matrix GEMM");
+  static_assert(!PAIR || NA == 2, "row-block pairs run on the two-matrix path");
   extern __shared__ uint8_t tc_raw[];
   constexpr int RS = L::RAW_SLOTS, BS = L::B_SLOTS, AS = TM::A_STAGES, NQ = TM::NQ;
   __shared__ uint64_t bars[2 * RS + 2 * BS + 2 * AS + 2 * NQ];
@@ -307,7 +311,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
   tc::tc_fence_after();
   const uint32_t tmem = tmem_base;
 
-  const int RT = p.rows / TC_M;
+  const int RT = p.rows / (PAIR ? 2 * TC_M : TC_M);
   const int KSTEPS = p.K / 64, KSB = p.K / 256;
   // Tiles: token tile (tile / RT) x weight-row tile (tile % RT), walked with a
   // stride of gridDim.x.  Each role loads the table entry of its next tile one
@@ -324,18 +328,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
         const int2 cur = nxt;  // the next tile's entry is loaded one tile ahead
         nxt = p.tt_info[min(tile + (int)gridDim.x, total - 1) / RT];
         const int e = cur.x & 0xffff;
-        const int r0 = (tile % RT) * TC_M;
+        const int r0 = (tile % RT) * (PAIR ? 2 * TC_M : TC_M);
         const bool sh = e == p.E;
         const void *m0 = sh ? (const void *)&maps.sh0 : (const void *)&maps.a0;
-        const void *m1 = sh ? (const void *)&maps.sh1 : (const void *)&maps.a1;
+        const void *m1 = PAIR ? m0 : sh ? (const void *)&maps.sh1 : (const void *)&maps.a1;
         const int ya = sh ? r0 : e * p.rows + r0;
+        const int ya1 = PAIR ? ya + TC_M : ya;  // matrix 1's rows
         for (int s = 0; ok && s < KSB; ++s) {
           const int rs = raw_it % RS;
           if (!(ok = tc_wait(raw_empty + rs, ((raw_it / RS) & 1u) ^ 1u, abort_s, 256))) break;
           tc::mbar_expect_tx(raw_full + rs, (uint32_t)L::RAWSL);
           uint8_t *dst = sm + L::OFF_RAW + rs * L::RAWSL;
           tc::tma_load_2d(dst, m0, s * Q4K_BYTES, ya, raw_full + rs);
-          if (NA == 2) tc::tma_load_2d(dst + TC_M * Q4K_BYTES, m1, s * Q4K_BYTES, ya, raw_full + rs);
+          if (NA == 2) tc::tma_load_2d(dst + TC_M * Q4K_BYTES, m1, s * Q4K_BYTES, ya1, raw_full + rs);
           ++raw_it;
         }
       }
@@ -434,7 +439,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
         ok = tc_wait_warp(acc_full + q0 + u, (par >> (q0 + u)) & 1u, abort_s, lane, 256);
       if (!ok) break;
       tc::tc_fence_after();
-      const int row = (tile % RT) * TC_M + 32 * g + lane;
+      const int row = (tile % RT) * (PAIR ? 2 * TC_M : TC_M) + 32 * g + lane;
       const uint32_t dcol = tmem + lane_addr + (uint32_t)(q0 * 64);
       const int prow = tc_kperm(row);  // a16 feeds the down GEMM's K axis
       // column 2t holds token t's hi part, 2t+1 its lo part; 16 columns = 8 tokens
@@ -446,7 +451,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
         float gv[8];
 #pragma unroll
         for (int c = 0; c < 8; ++c) gv[c] = __uint_as_float(v[2 * c]) + __uint_as_float(v[2 * c + 1]);
-        if (NA == 2) {
+        if (PAIR) {
+          tc::tmem_ld16(dcol + (uint32_t)(bw + col), v);                 // rows + 128
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            if (t0 + c < ntok) {
+              float *dst = p.ybuf + ((int64_t)slot0 + t0 + c) * p.out_ld + row;
+              dst[0] = gv[c];
+              dst[TC_M] = __uint_as_float(v[2 * c]) + __uint_as_float(v[2 * c + 1]);
+            }
+        } else if (NA == 2) {
           tc::tmem_ld16(dcol + (uint32_t)(bw + col), v);                 // matrix 1
           tc::tmem_wait_ld();
 #pragma unroll
@@ -591,14 +606,24 @@ int32_t launch_moe_tc(har_cuda_ctx *ctx, const TcMaps &maps, const TcParams &p, 
   const int grid = std::max(1, std::min(ctx->num_sms, max_tiles));
   if (na == 2) {
     const size_t smem = (size_t)TcSmem<2>::BYTES + 1024;
-    cudaFuncSetAttribute(moe_tc_kernel<2, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(moe_tc_kernel<2, false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)smem);
     prof_begin(ctx);
-    moe_tc_kernel<2, false><<<grid, TC_THREADS, smem, ctx->stream>>>(maps, p);
+    moe_tc_kernel<2, false, false><<<grid, TC_THREADS, smem, ctx->stream>>>(maps, p);
     return check_launch(ctx, "moe_tc_gate_up_kernel");
+  }
+  if (p.rows % (2 * TC_M) == 0) {
+    // the down GEMM as 256-row tiles: two 128-row blocks share each token tile
+    const size_t smem = (size_t)TcSmem<2>::BYTES + 1024;
+    cudaFuncSetAttribute(moe_tc_kernel<2, false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)smem);
+    prof_begin(ctx);
+    moe_tc_kernel<2, false, true><<<grid, TC_THREADS, smem, ctx->stream>>>(maps, p);
+    return check_launch(ctx, "moe_tc_down_kernel");
   }
   const size_t smem = (size_t)TcSmem<1>::BYTES + 1024;
   // two K-steps per weight stage when a tile's K-steps come in groups of 8
-  auto kern = p.K % 512 == 0 ? moe_tc_kernel<1, true> : moe_tc_kernel<1, false>;
+  auto kern = p.K % 512 == 0 ? moe_tc_kernel<1, true, false> : moe_tc_kernel<1, false, false>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   prof_begin(ctx);
   kern<<<grid, TC_THREADS, smem, ctx->stream>>>(maps, p);
