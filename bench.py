@@ -565,6 +565,105 @@ def run_reference(args):
     }
 
 
+GEMV_N, GEMV_K = 131072, 4096  # one decode GEMV of LM-head size: 302 MB of Q4_K (L2 is 126 MB)
+GEMV_N_SMALL = 65536            # half the rows, reported beside: the fixed cost per launch shows
+
+
+def run_gemv_roofline(args, torch):
+    """Config 1's kernel, the batch-1 Q4_K GEMV (har_cuda_q4k_gemv), measured as
+    a decode roofline: y = W x with W a 131072 x 4096 Q4_K matrix (302 MB, the
+    size of an LM-head GEMV) and x one f32 row quantised to Q8_K (config 1's
+    activations), alternating between two such matrices so the working set is
+    far larger than L2.  The value is weight bytes streamed per second; f32
+    activations and the 65536-row matrix are reported beside it.  One JSON
+    line; not the driver's bench line (config 5)."""
+    import har_cuda
+
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    ctx = har_cuda.Context(local, use_torch_stream=False)
+    stream = torch.cuda.Stream(dev)
+    ctx.lib.har_cuda_ctx_set_stream(ctx.handle, __import__("ctypes").c_void_p(stream.cuda_stream))
+    N, K = GEMV_N, GEMV_K
+    wbytes = N * (K // 256) * 144
+    mats, keep = [], []
+    for i in range(2):
+        t = torch.empty(wbytes, dtype=torch.uint8, device=dev)
+        ctx.gen_q4k(t, N, K, 9100 + i)
+        keep.append(t)
+        mats.append(ctx.wrap_q4k(t, 1, N, K))
+    # the same bytes seen as two matrices of half the rows each
+    small = [ctx.wrap_q4k(t, 2, GEMV_N_SMALL, K) for t in keep]
+    x = torch.from_numpy(np.random.default_rng(9200).standard_normal((1, K)).astype(np.float32)).to(dev)
+    xq = torch.empty((K // 256) * 292, dtype=torch.uint8, device=dev)
+    y = torch.empty((1, N), dtype=torch.float32, device=dev)
+    per = 8  # GEMVs per graph, alternating matrices
+    peaks = load_peaks()
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    res = {}
+    for act, kind, sm in (("q8k", har_cuda.ACT_Q8K, False), ("f32", har_cuda.ACT_F32, False),
+                          ("q8k_small", har_cuda.ACT_Q8K, True)):
+        with torch.cuda.stream(stream):
+            ctx.q8k_quantize(x, xq)
+        src = xq if kind == har_cuda.ACT_Q8K else x
+        nb = wbytes // 2 if sm else wbytes
+
+        def gemvs():
+            for j in range(per):
+                if sm:  # four distinct half-size matrices in turn
+                    ctx.q4k_gemv(small[j % 2], (j // 2) % 2, src, kind, 1, y)
+                else:
+                    ctx.q4k_gemv(mats[j % 2], 0, src, kind, 1, y)
+
+        with torch.cuda.stream(stream):
+            gemvs()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            gemvs()
+        with torch.cuda.stream(stream):
+            for _ in range(max(3, args.warmup)):
+                g.replay()
+        torch.cuda.synchronize()
+        clocks = Clocks(local)
+        clocks.start()
+        time.sleep(0.5)
+        ev0 = torch.cuda.Event(enable_timing=True)
+        ev1 = torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            ev0.record(stream)
+            for _ in range(args.steps):
+                g.replay()
+            ev1.record(stream)
+        torch.cuda.synchronize()
+        clk = clocks.stop()
+        ms = ev0.elapsed_time(ev1) / (args.steps * per)
+        gbs = nb / (ms * 1e-3) / 1e9
+        res[act] = {"ms_per_gemv": round(ms, 5), "weight_gbs": round(gbs, 1), "frac": round(gbs / hbm, 4),
+                    "clocks": clk}
+    q = res["q8k"]
+    return {
+        "metric": "Q4_K decode GEMV weight GB/s (batch 1)", "value": q["weight_gbs"], "unit": "GB/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": q["ms_per_gemv"],
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8 x q4 (dp4a) -> i32, f32 scales", "data": "synthetic: N(0,0.02) weights "
+        "quantised to Q4_K on device; one N(0,1) f32 row quantised to Q8_K",
+        "config": {"workload": f"config1 kernel as a decode roofline: {N} x {K} Q4_K GEMV, batch 1",
+                   "rows": N, "K": K, "batch": 1, "per_graph": per,
+                   "l2": "two 302 MB matrices alternate (604 MB working set > 126 MB L2)"},
+        "roofline": {"bound": "hbm", "kernel": "q4k_gemv_kernel", "achieved": q["weight_gbs"],
+                     "peak": hbm, "unit": "GB/s", "frac": q["frac"],
+                     "peak_source": "measured" if "hbm_gbs" in peaks else "fallback",
+                     "algorithmic_bytes_per_launch": wbytes},
+        "f32_activations": {"weight_gbs": res["f32"]["weight_gbs"], "frac": res["f32"]["frac"],
+                            "ms_per_gemv": res["f32"]["ms_per_gemv"]},
+        "rows_65536": {"weight_gbs": res["q8k_small"]["weight_gbs"], "frac": res["q8k_small"]["frac"],
+                       "ms_per_gemv": res["q8k_small"]["ms_per_gemv"]},
+        "clocks": q["clocks"],
+    }
+
+
 def load_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -596,6 +695,9 @@ def main():
     try:
         if args.impl == "reference":
             out = run_reference(args)
+        elif args.config == 1:
+            import torch
+            out = run_gemv_roofline(args, torch)
         else:
             import torch
             out = run_ours(args, torch)

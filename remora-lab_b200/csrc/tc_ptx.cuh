@@ -102,6 +102,17 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const void *tmap, int x, 
       "l"(tmap), "r"(x), "r"(y), "r"(smem_u32(bar))
       : "memory");
 }
+// Untiled bulk copy of `bytes` contiguous bytes global -> this CTA's shared
+// memory, completing `bytes` of transaction on `bar`.  Both addresses 16-byte
+// aligned, bytes a multiple of 16.  No multicast.
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
 __device__ __forceinline__ void tma_prefetch_desc(const void *tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }

@@ -210,3 +210,22 @@ def test_gemv_argument_errors(ctx):
     with pytest.raises(har_cuda.HarCudaError) as e:
         ctx.wrap_q4k(wd, 1, 8, 300)                      # K not a multiple of 256
     assert e.value.status == har_cuda.ERR_GEOMETRY
+
+
+@pytest.mark.parametrize("K", [512, 4096])
+@pytest.mark.parametrize("act", [har_cuda.ACT_F32, har_cuda.ACT_Q8K])
+def test_gemv_decode_stream(ctx, K, act):
+    # batch 1 streams the weights through a shared-memory ring; 12,000 rows give
+    # each CTA more stages than ring slots.  Equals the oracle, and equals bit for
+    # bit the register-resident kernel's row for the same token (M = 2 call).
+    N = 12000
+    wd, wh = gen_tensor(ctx, N, K, 4242 + K)
+    x = haro.normal_f32(31, 0, 2 * K).reshape(2, K)
+    y1 = gemv(ctx, wd, N, K, x[:1], act)
+    y2 = gemv(ctx, wd, N, K, x, act)
+    assert np.array_equal(y1[0], y2[0])
+    if act == har_cuda.ACT_F32:
+        assert_close(y1[0], haro.q4k_matvec(wh, N, K, x[0]), what=f"stream f32 K={K}")
+    else:
+        ref = haro.q4k_gemv_q8k(wh, N, K, haro.q8k_quantize(x[:1])[0])
+        assert_close(y1[0], ref, rel=1e-5, nrms=1e-6, what=f"stream q8k K={K}")
