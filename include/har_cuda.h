@@ -187,7 +187,9 @@ int32_t har_cuda_moe_stack(har_cuda_ctx *ctx, const har_cuda_moe_layer *const *l
                            uint32_t flags);
 
 /* The stack with host buffers (x [T][H], ids/weights [L][T][k], y [T][H]):
- * copies in, runs, copies out and waits (bounded). */
+ * copies in, runs, copies out and waits (bounded).  A call repeated with the
+ * same layers, shapes, flags and stream replays a CUDA graph of its device work
+ * (captured on the second such call); the inputs are read afresh every call. */
 int32_t har_cuda_moe_stack_host(har_cuda_ctx *ctx, const har_cuda_moe_layer *const *layers,
                                 int32_t L, const float *x_host, int64_t T, int32_t k,
                                 const int32_t *ids_host, const float *weights_host,

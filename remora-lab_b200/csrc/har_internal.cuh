@@ -125,6 +125,20 @@ struct har_cuda_ctx {
   size_t io_dev_bytes = 0;
   int64_t launches = 0;
   int tc_min_tokens = 0;              // tensor-core threshold override (0 = default)
+  uint64_t epoch = 0;                 // bumped whenever scratch or staging is reallocated
+  // CUDA graph of the last repeated har_cuda_moe_stack_host call (copies in,
+  // the stack, copy out), replayed while the call's key is unchanged
+  struct HostGraph {
+    std::vector<const void *> layers;
+    int64_t T = 0;
+    int32_t k = 0;
+    uint32_t flags = 0;
+    int tc_min = 0;
+    uint64_t epoch = 0;
+    cudaStream_t stream = nullptr;
+    int seen = 0;  // consecutive calls with this key
+    cudaGraphExec_t exec = nullptr;
+  } host_graph;
   // opt-in per-launch CUDA-event profiling (har_cuda_profile_begin/end)
   bool prof_on = false;
   cudaEvent_t prof_pending = nullptr;
