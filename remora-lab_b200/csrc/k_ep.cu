@@ -36,6 +36,10 @@ struct har_cuda_ep {
   ncclComm_t comm = nullptr;
   void *buf = nullptr;  // exchange buffers, grown on demand
   size_t bytes = 0;
+  // the exchanges run on their own stream, joined to the caller's by events,
+  // so the shared expert computes while the dispatch moves rows
+  cudaStream_t cs = nullptr;
+  cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};  // plan, dispatch, local, return
 };
 
 namespace har {
@@ -166,9 +170,9 @@ int32_t ep_all_to_all(har_cuda_ctx *ctx, har_cuda_ep *ep, const void *send, void
                       ncclDataType_t type, size_t esize) {
   for (int d = 0; d < ep->world; ++d) {
     ncclResult_t r = ncclSend((const uint8_t *)send + (size_t)d * n * esize, n, type, d, ep->comm,
-                              ctx->stream);
+                              ep->cs);
     if (r != ncclSuccess) return nccl_error(ctx, "ncclSend", r);
-    r = ncclRecv((uint8_t *)recv + (size_t)d * n * esize, n, type, d, ep->comm, ctx->stream);
+    r = ncclRecv((uint8_t *)recv + (size_t)d * n * esize, n, type, d, ep->comm, ep->cs);
     if (r != ncclSuccess) return nccl_error(ctx, "ncclRecv", r);
   }
   return HAR_CUDA_OK;
@@ -191,12 +195,22 @@ int32_t ep_layer(har_cuda_ctx *ctx, har_cuda_ep *ep, const har_cuda_moe_layer *l
   int32_t *ids0 = (int32_t *)(B + L.ids0);
   const uint32_t mode =
       flags & (HAR_CUDA_MOE_ACT_Q8K | HAR_CUDA_MOE_FORCE_GEMV | HAR_CUDA_MOE_FORCE_TC);
+  // Compute runs on ctx->stream, the exchanges on ep->cs; events order them:
+  // plan -> dispatch -> local experts -> return -> combine, with the shared
+  // expert (it needs only this rank's x) computing while the dispatch moves
+  // rows.  The same order holds under CUDA-graph capture (fork and join).
+  auto join = [&](cudaStream_t from, cudaStream_t to, cudaEvent_t e) -> int32_t {
+    if (cudaEventRecord(e, from) != cudaSuccess || cudaStreamWaitEvent(to, e, 0) != cudaSuccess)
+      return set_error(ctx, HAR_CUDA_ERR_CUDA, "ep: stream ordering failed");
+    return HAR_CUDA_OK;
+  };
   // 1. plan
   prof_begin(ctx);
   ep_plan_kernel<<<(unsigned)(G * T), 128, 0, ctx->stream>>>(x, (int)H, ids, w, (int)T, k, E, El,
                                                             sx, sids, sw, ctx->d_status);
   if ((st = check_launch(ctx, "ep_plan_kernel"))) return st;
-  // 2. dispatch
+  if ((st = join(ctx->stream, ep->cs, ep->ev[0]))) return st;
+  // 2. dispatch (exchange stream)
   ncclResult_t r = ncclGroupStart();
   if (r != ncclSuccess) return nccl_error(ctx, "ncclGroupStart", r);
   st = ep_all_to_all(ctx, ep, sx, rx, (size_t)T * H, ncclFloat32, 4);
@@ -205,18 +219,7 @@ int32_t ep_layer(har_cuda_ctx *ctx, har_cuda_ep *ep, const har_cuda_moe_layer *l
   r = ncclGroupEnd();
   if (st) return st;
   if (r != ncclSuccess) return nccl_error(ctx, "ncclGroupEnd", r);
-  // 3. the rank's experts on the received rows: partial sums per row
-  if ((st = run_moe_ffn(ctx, local, rx, (int64_t)G * T, k, rids, rw, part,
-                        mode | HAR_CUDA_MOE_EMPTY_SLOTS)))
-    return st;
-  // 4. return the partial sums
-  r = ncclGroupStart();
-  if (r != ncclSuccess) return nccl_error(ctx, "ncclGroupStart", r);
-  st = ep_all_to_all(ctx, ep, part, back, (size_t)T * H, ncclFloat32, 4);
-  r = ncclGroupEnd();
-  if (st) return st;
-  if (r != ncclSuccess) return nccl_error(ctx, "ncclGroupEnd", r);
-  // 5. shared expert on the rank's tokens, then the combine
+  // 3. the shared expert on the rank's tokens, meanwhile
   if (shared) {
     prof_begin(ctx);
     ep_gate_kernel<<<(unsigned)T, 256, 0, ctx->stream>>>(x, (int)H, gate_inp, g, ids0);
@@ -225,6 +228,21 @@ int32_t ep_layer(har_cuda_ctx *ctx, har_cuda_ep *ep, const har_cuda_moe_layer *l
   } else if (cudaMemsetAsync(ysh, 0, 4 * (size_t)T * H, ctx->stream) != cudaSuccess) {
     return set_error(ctx, HAR_CUDA_ERR_CUDA, "ep: memset failed");
   }
+  // 4. the rank's experts on the received rows: partial sums per row
+  if ((st = join(ep->cs, ctx->stream, ep->ev[1]))) return st;
+  if ((st = run_moe_ffn(ctx, local, rx, (int64_t)G * T, k, rids, rw, part,
+                        mode | HAR_CUDA_MOE_EMPTY_SLOTS)))
+    return st;
+  if ((st = join(ctx->stream, ep->cs, ep->ev[2]))) return st;
+  // 5. return the partial sums (exchange stream)
+  r = ncclGroupStart();
+  if (r != ncclSuccess) return nccl_error(ctx, "ncclGroupStart", r);
+  st = ep_all_to_all(ctx, ep, part, back, (size_t)T * H, ncclFloat32, 4);
+  r = ncclGroupEnd();
+  if (st) return st;
+  if (r != ncclSuccess) return nccl_error(ctx, "ncclGroupEnd", r);
+  if ((st = join(ep->cs, ctx->stream, ep->ev[3]))) return st;
+  // 6. residual + shared + partials in rank order
   prof_begin(ctx);
   ep_combine_kernel<<<(unsigned)T, 256, 0, ctx->stream>>>(
       x, (int)H, (int)T, G, ysh, back, (flags & HAR_CUDA_MOE_ADD_RESIDUAL) ? 1 : 0, y);
@@ -287,9 +305,17 @@ int32_t har_cuda_ep_create(har_cuda_ctx *ctx, const uint8_t *unique_id, size_t l
   ep->world = world;
   ep->rank = rank;
   ep->device = ctx->device;
+  bool ok = cudaStreamCreateWithFlags(&ep->cs, cudaStreamNonBlocking) == cudaSuccess;
+  for (int i = 0; i < 4 && ok; ++i)
+    ok = cudaEventCreateWithFlags(&ep->ev[i], cudaEventDisableTiming) == cudaSuccess;
+  if (!ok) {
+    har_cuda_ep_free(ep);
+    return set_error(ctx, HAR_CUDA_ERR_CUDA, "ep_create: stream or event creation failed");
+  }
   ncclResult_t r = ncclCommInitRank(&ep->comm, world, id, rank);
   if (r != ncclSuccess) {
-    delete ep;
+    ep->comm = nullptr;
+    har_cuda_ep_free(ep);
     return nccl_error(ctx, "ncclCommInitRank", r);
   }
   *out = ep;
@@ -304,6 +330,12 @@ int32_t har_cuda_ep_free(har_cuda_ep *ep) {
     cudaFree(ep->buf);
   }
   if (ep->comm) ncclCommDestroy(ep->comm);
+  for (int i = 0; i < 4; ++i)
+    if (ep->ev[i]) cudaEventDestroy(ep->ev[i]);
+  if (ep->cs) {
+    cudaStreamSynchronize(ep->cs);
+    cudaStreamDestroy(ep->cs);
+  }
   delete ep;
   return HAR_CUDA_OK;
 }
