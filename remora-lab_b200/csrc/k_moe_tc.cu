@@ -74,17 +74,15 @@ struct TcSmem {
 };
 
 // Tensor-memory plan (512 columns x 128 lanes): accumulators in 64-column
-// quarters at [0, A_COL0), then one f16 weight stage per dequant team of SW
-// columns (row = lane, two f16 per column): NA x 32 (one 64-value K-step of
-// each matrix), or with DBL (one matrix, NA = 1) 64 columns holding two
-// consecutive K-steps, so a stage feeds 8 MMAs either way.
-// A tile whose token box has bw B rows (2 per token) takes
+// quarters at [0, A_COL0), then one f16 weight stage per dequant team of
+// SW = NA x 32 columns (one 64-value K-step of each matrix: row = lane, two
+// f16 per column).  A tile whose token box has bw B rows (2 per token) takes
 // ceil(NA * bw / 64) quarters: matrix m's accumulator sits at column m * bw
 // of the tile's first quarter.
-template <int NA, bool DBL>
+template <int NA>
 struct TcTmem {
   static constexpr int A_STAGES = TC_DQ_TEAMS;
-  static constexpr int SW = DBL ? 64 : NA * 32;
+  static constexpr int SW = NA * 32;
   static constexpr int A_COL0 = TC_TMEM_COLS - A_STAGES * SW;
   static constexpr int NQ = A_COL0 / 64;
   static __device__ __forceinline__ int quarters(int bw) {
@@ -200,16 +198,15 @@ struct TcIssuer {
   uint32_t b_rdy;  // ... and of the next B slot
 };
 
-// Step J (0..3) of a group: weight stage J.  A step is one 64-value K-step
-// of each matrix, or with DBL two consecutive K-steps of the one matrix; B
-// slots hold 128 / BW K-steps, i.e. KPB steps, and a new slot opens when
-// J % KPB == 0.  False when a bounded wait gave up.
-template <int NA, bool DBL, int BW, typename L, int J>
+// K-step J (0..3) of a group: weight stage J; B slots hold KPB = 128 / BW
+// K-steps and a new slot opens when J % KPB == 0.  False when a bounded wait
+// gave up.
+template <int NA, int BW, typename L, int J>
 __device__ __forceinline__ bool tc_issue_kstep(TcIssuer &is, uint32_t dcol, uint32_t idesc, bool first,
                                                uint64_t &bslot, int &bs, volatile int *abort_s, int lane) {
-  constexpr int KPB = DBL ? 64 / BW : 128 / BW, BS = L::B_SLOTS;
+  constexpr int KPB = 128 / BW, BS = L::B_SLOTS;
   constexpr uint32_t SUB = BW * 128 / 16;  // one K-step of B, descriptor units
-  constexpr int SW = TcTmem<NA, DBL>::SW;
+  constexpr int SW = TcTmem<NA>::SW;
   if (J % KPB == 0) {
     bs = (int)(is.b_it % BS);
     if (!__all_sync(0xffffffffu, is.b_rdy != 0) &&
@@ -222,12 +219,8 @@ __device__ __forceinline__ bool tc_issue_kstep(TcIssuer &is, uint32_t dcol, uint
     return false;
   tc::tc_fence_after();
   is.a_rdy = tc::mbar_test_wait_at<((J + 1) & 3) * 8>(is.af, J == 3 ? is.ph ^ 1u : is.ph);
-  if (DBL)
-    tc::mma_kstep2_ts_imm<SUB>(is.lead, dcol, is.a_base + (uint32_t)(J * SW),
-                               bslot + (uint64_t)((J % KPB) * 2 * SUB), idesc, first ? 0u : 1u);
-  else
-    tc::mma_kstep_ts_imm<NA, BW>(is.lead, dcol, is.a_base + (uint32_t)(J * SW),
-                                 bslot + (uint64_t)((J % KPB) * SUB), idesc, first ? 0u : 1u);
+  tc::mma_kstep_ts_imm<NA, BW>(is.lead, dcol, is.a_base + (uint32_t)(J * SW),
+                               bslot + (uint64_t)((J % KPB) * SUB), idesc, first ? 0u : 1u);
   tc::mma_commit_at<J * 8>(is.lead, is.ae);
   if (J % KPB == KPB - 1) {
     tc::mma_commit_w(is.lead, is.b_empty + bs);
@@ -236,35 +229,34 @@ __device__ __forceinline__ bool tc_issue_kstep(TcIssuer &is, uint32_t dcol, uint
   return true;
 }
 
-// The MMAs of one tile: `steps` steps in groups of four, one per weight
-// stage.  False when a bounded wait gave up.
-template <int NA, bool DBL, int BW, typename L>
-__device__ __forceinline__ bool tc_issue_tile(TcIssuer &is, uint32_t dcol, uint32_t idesc, int steps,
+// The MMAs of one tile: its K-steps in groups of four, one per weight stage.
+// False when a bounded wait gave up.
+template <int NA, int BW, typename L>
+__device__ __forceinline__ bool tc_issue_tile(TcIssuer &is, uint32_t dcol, uint32_t idesc, int ksteps,
                                               volatile int *abort_s, int lane) {
   uint64_t bslot = 0;
   int bs = 0;
-  for (int g = 0; g < steps; g += 4) {
-    if (!tc_issue_kstep<NA, DBL, BW, L, 0>(is, dcol, idesc, g == 0, bslot, bs, abort_s, lane) ||
-        !tc_issue_kstep<NA, DBL, BW, L, 1>(is, dcol, idesc, false, bslot, bs, abort_s, lane) ||
-        !tc_issue_kstep<NA, DBL, BW, L, 2>(is, dcol, idesc, false, bslot, bs, abort_s, lane) ||
-        !tc_issue_kstep<NA, DBL, BW, L, 3>(is, dcol, idesc, false, bslot, bs, abort_s, lane))
+  for (int g = 0; g < ksteps; g += 4) {
+    if (!tc_issue_kstep<NA, BW, L, 0>(is, dcol, idesc, g == 0, bslot, bs, abort_s, lane) ||
+        !tc_issue_kstep<NA, BW, L, 1>(is, dcol, idesc, false, bslot, bs, abort_s, lane) ||
+        !tc_issue_kstep<NA, BW, L, 2>(is, dcol, idesc, false, bslot, bs, abort_s, lane) ||
+        !tc_issue_kstep<NA, BW, L, 3>(is, dcol, idesc, false, bslot, bs, abort_s, lane))
       return false;
     is.ph ^= 1u;
   }
   return true;
 }
 
-// NA = number of A matrices (2: gate and up with SwiGLU epilogue; 1: down).
-// DBL (NA = 1, K a multiple of 512): a weight stage holds two K-steps.
+// NA = number of A matrices (2: gate and up with SwiGLU epilogue; 1: one
+// matrix, the fallback for a down GEMM whose H is not a multiple of 256).
 // PAIR (NA = 2): the down GEMM with its two "matrices" the row blocks
 // [r0, r0 + 128) and [r0 + 128, r0 + 256) of one weight tensor; a tile covers
 // 256 output rows, and the epilogue writes both accumulators to ybuf.
-template <int NA, bool DBL, bool PAIR>
+template <int NA, bool PAIR>
 __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_constant__ TcMaps maps,
                                                                const TcParams p) {
   using L = TcSmem<NA>;
-  using TM = TcTmem<NA, DBL>;
-  static_assert(!DBL || NA == 1, "two-K-step stages are for the one-matrix GEMM");
+  using TM = TcTmem<NA>;
   static_assert(!PAIR || NA == 2, "row-block pairs run on the two-matrix path");
   extern __shared__ uint8_t tc_raw[];
   constexpr int RS = L::RAW_SLOTS, BS = L::B_SLOTS, AS = TM::A_STAGES, NQ = TM::NQ;
@@ -285,7 +277,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
   if (tid == 32) {
     for (int s = 0; s < RS; ++s) {
       tc::mbar_init(raw_full + s, 1);
-      tc::mbar_init(raw_empty + s, DBL ? TC_DQ_WARPS / 2 : TC_DQ_WARPS);  // the warps that read the slot
+      tc::mbar_init(raw_empty + s, TC_DQ_WARPS);
     }
     for (int s = 0; s < AS; ++s) {
       tc::mbar_init(a_full + s, TC_DQ_WARPS / TC_DQ_TEAMS);  // one team fills a stage
@@ -414,9 +406,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
       tc::tc_fence_after();
       const uint32_t idesc = tc::idesc_f16(TC_M, (2 * ntok + 15) & ~15);
       const uint32_t dcol = tmem + (uint32_t)(q0 * 64);
-      const int steps = DBL ? KSTEPS / 2 : KSTEPS;
-      ok = bw == 32 ? tc_issue_tile<NA, DBL, 32, L>(is, dcol, idesc, steps, abort_s, lane)
-                    : tc_issue_tile<NA, DBL, 64, L>(is, dcol, idesc, steps, abort_s, lane);
+      ok = bw == 32 ? tc_issue_tile<NA, 32, L>(is, dcol, idesc, KSTEPS, abort_s, lane)
+                    : tc_issue_tile<NA, 64, L>(is, dcol, idesc, KSTEPS, abort_s, lane);
       if (!ok) break;
       for (int u = 0; u < nq; ++u) tc::mma_commit_w(lead, acc_full + q0 + u);
       par ^= ((1u << nq) - 1u) << q0;
@@ -489,42 +480,28 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
     }
   } else {
     // ---------------- dequantisers: raw Q4_K -> f16 weight stages in TMEM ----------------
-    // Team t (four warps) takes the steps t (mod 4) and fills weight stage t
-    // with them.  Without DBL a step is chunk t of every raw slot (one of its
-    // four K-steps) for each matrix; with DBL it is the chunk pair 2(t&1),
-    // 2(t&1)+1 of every second raw slot (slot 2u + t/2 for the team's u-th
-    // step), so each slot is released by the two teams that use it.  Warp w
-    // may store only TMEM lanes 32*(w%4)..: it owns weight rows 32*(w%4)+lane
-    // of every matrix.
+    // Team t (four warps) takes the K-steps ks = t (mod 4) -- one of the four
+    // K-steps of every raw slot -- and fills weight stage t with them.  Warp
+    // w may store only TMEM lanes 32*(w%4)..: it owns weight rows
+    // 32*(w%4)+lane of every matrix.
     const int g = warp & 3, team = (warp - TC_WARP_DQ0) >> 2;
     const int r = 32 * g + lane;
     const uint32_t lane_addr = (uint32_t)(32 * g) << 16;
     const uint32_t acol = tmem + lane_addr + (uint32_t)(TM::A_COL0 + team * TM::SW);
-    const int steps = DBL ? KSTEPS / 2 : KSTEPS;
-    uint32_t u = 0;  // this team's steps so far
+    uint32_t u = 0;  // this team's K-steps so far (and raw slots: one K-step each)
     bool ok = true;
     for (int tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
-      for (int ks = team; ks < steps; ks += TC_DQ_TEAMS, ++u) {
-        const uint32_t slot = DBL ? 2u * u + (uint32_t)(team >> 1) : u;
-        const int rs = (int)(slot % RS);
-        if (!(ok = tc_wait_warp(raw_full + rs, (slot / RS) & 1u, abort_s, lane))) break;
+      for (int ks = team; ks < KSTEPS; ks += TC_DQ_TEAMS, ++u) {
+        const int rs = (int)(u % RS);
+        if (!(ok = tc_wait_warp(raw_full + rs, (u / RS) & 1u, abort_s, lane))) break;
         if (!(ok = tc_wait_warp(a_empty + team, (u & 1u) ^ 1u, abort_s, lane))) break;
         tc::tc_fence_after();
         const uint8_t *raw = sm + L::OFF_RAW + rs * L::RAWSL;
-        if (DBL) {
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {  // K-steps 2(t&1) + h of the super-block
-            uint32_t o[32];
-            tc_dequant_step(raw + r * Q4K_BYTES, 2 * (team & 1) + h, o);
-            tc::tmem_st32(acol + (uint32_t)(h * 32), o);
-          }
-        } else {
-#pragma unroll
-          for (int m = 0; m < NA; ++m) {  // team t holds chunk t of the super-block
-            uint32_t o[32];
-            tc_dequant_step(raw + (m * TC_M + r) * Q4K_BYTES, team, o);
-            tc::tmem_st32(acol + (uint32_t)(m * 32), o);
-          }
+        for (int m = 0; m < NA; ++m) {  // team t holds chunk t of the super-block
+          uint32_t o[32];
+          tc_dequant_step(raw + (m * TC_M + r) * Q4K_BYTES, team, o);
+          tc::tmem_st32(acol + (uint32_t)(m * 32), o);
         }
         tc::tmem_wait_st();
         tc::tc_fence_before();
@@ -606,27 +583,23 @@ int32_t launch_moe_tc(har_cuda_ctx *ctx, const TcMaps &maps, const TcParams &p, 
   const int grid = std::max(1, std::min(ctx->num_sms, max_tiles));
   if (na == 2) {
     const size_t smem = (size_t)TcSmem<2>::BYTES + 1024;
-    cudaFuncSetAttribute(moe_tc_kernel<2, false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)smem);
+    cudaFuncSetAttribute(moe_tc_kernel<2, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     prof_begin(ctx);
-    moe_tc_kernel<2, false, false><<<grid, TC_THREADS, smem, ctx->stream>>>(maps, p);
+    moe_tc_kernel<2, false><<<grid, TC_THREADS, smem, ctx->stream>>>(maps, p);
     return check_launch(ctx, "moe_tc_gate_up_kernel");
   }
   if (p.rows % (2 * TC_M) == 0) {
     // the down GEMM as 256-row tiles: two 128-row blocks share each token tile
     const size_t smem = (size_t)TcSmem<2>::BYTES + 1024;
-    cudaFuncSetAttribute(moe_tc_kernel<2, false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)smem);
+    cudaFuncSetAttribute(moe_tc_kernel<2, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     prof_begin(ctx);
-    moe_tc_kernel<2, false, true><<<grid, TC_THREADS, smem, ctx->stream>>>(maps, p);
+    moe_tc_kernel<2, true><<<grid, TC_THREADS, smem, ctx->stream>>>(maps, p);
     return check_launch(ctx, "moe_tc_down_kernel");
   }
   const size_t smem = (size_t)TcSmem<1>::BYTES + 1024;
-  // two K-steps per weight stage when a tile's K-steps come in groups of 8
-  auto kern = p.K % 512 == 0 ? moe_tc_kernel<1, true, false> : moe_tc_kernel<1, false, false>;
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaFuncSetAttribute(moe_tc_kernel<1, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   prof_begin(ctx);
-  kern<<<grid, TC_THREADS, smem, ctx->stream>>>(maps, p);
+  moe_tc_kernel<1, false><<<grid, TC_THREADS, smem, ctx->stream>>>(maps, p);
   return check_launch(ctx, "moe_tc_down_kernel");
 }
 

@@ -365,37 +365,6 @@ __device__ __forceinline__ void mma_kstep_ts_imm(uint32_t lead, uint32_t d, uint
   }
 }
 
-// Two consecutive 64-value K-steps of one matrix into one accumulator: weight
-// columns a + 8*kk for the 8 K=16 slices (the stage holds K-step 0 in columns
-// 0..31 and K-step 1 in 32..63); B advances 2 descriptor units per slice and
-// SUB units (one K-step of the token box) between the two K-steps.
-template <int SUB>
-__device__ __forceinline__ void mma_kstep2_ts_imm(uint32_t lead, uint32_t d, uint32_t a, uint64_t b,
-                                                  uint32_t idesc, uint32_t acc0) {
-  asm volatile(
-      "{\n\t.reg .pred e, p, t;\n\t.reg .b64 b1, b2, b3, b4, b5, b6, b7;\n\t"
-      "setp.ne.b32 e, %0, 0;\n\t"
-      "setp.ne.b32 p, %5, 0;\n\t"
-      "setp.eq.b32 t, %0, %0;\n\t"
-      "add.u64 b1, %3, 2;\n\t"
-      "add.u64 b2, %3, 4;\n\t"
-      "add.u64 b3, %3, 6;\n\t"
-      "add.u64 b4, %3, %6;\n\t"
-      "add.u64 b5, b4, 2;\n\t"
-      "add.u64 b6, b4, 4;\n\t"
-      "add.u64 b7, b4, 6;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%1], [%2], %3, %4, p;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%1], [%2+8], b1, %4, t;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%1], [%2+16], b2, %4, t;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%1], [%2+24], b3, %4, t;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%1], [%2+32], b4, %4, t;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%1], [%2+40], b5, %4, t;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%1], [%2+48], b6, %4, t;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%1], [%2+56], b7, %4, t;\n\t}" ::"r"(lead),
-      "r"(d), "r"(a), "l"(b), "r"(idesc), "r"(acc0), "n"(SUB)
-      : "memory");
-}
-
 // Commit to the mbarrier at shared address bar + OFF (bytes).
 template <int OFF>
 __device__ __forceinline__ void mma_commit_at(uint32_t lead, uint32_t bar) {

@@ -86,8 +86,8 @@ def test_tc_other_shapes(ctx):
 
 @pytest.mark.parametrize("I", [768, 1024])
 def test_tc_down_stage_layouts(ctx, I):
-    # the down GEMM packs two K-steps per weight stage when I is a multiple of
-    # 512 (I = 1024) and one otherwise (I = 768): both against the oracle
+    # the down GEMM's K (= I) at 12 and 16 K-steps per tile, on the 256-row
+    # paired tiles, against the oracle
     lay = Layer(ctx, 8, 1024, I, seed=31 + I, shared=True)
     x = haro.normal_f32(12, 0, 24 * 1024).reshape(24, 1024)
     ids, w = haro.zipf_routing(13, 24, 8, 3)
