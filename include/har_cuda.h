@@ -125,6 +125,23 @@ int32_t har_cuda_q4k_gemv(har_cuda_ctx *ctx, const har_cuda_weights *w, int64_t 
 int32_t har_cuda_route_topk(har_cuda_ctx *ctx, const float *logits_dev, int64_t T, int32_t E,
                             int32_t k, int32_t *ids_dev, float *weights_dev);
 
+/* ---- router GEMV ------------------------------------------------------------
+ * logits[t][e] = sum_h gate_inp[e][h] * x[t][h] for the f32 router matrix
+ * ffn_gate_inp [E][H]: one f32 accumulator per (token, expert), h ascending,
+ * each product rounded before it is added — bit-exact with routed_moe's
+ * self.matvec(ffn_gate_inp) (har/crates/har-demo/src/bin/har-native-qwen35moe.rs:1168-1172),
+ * whose F32 row dot is dot_f32_row (:154-163).
+ * gate_inp_dev f32 [E][H]; x_dev f32 [T][H]; logits_dev f32 [T][E]. */
+int32_t har_cuda_router_logits(har_cuda_ctx *ctx, const float *gate_inp_dev, int32_t E,
+                               int64_t H, const float *x_dev, int64_t T, float *logits_dev);
+/* routed_moe's whole selection on the device: the router GEMV above, then
+ * har_cuda_route_topk's softmax + top-k (har-native-qwen35moe.rs:1167-1204).
+ * The logits live in the context's scratch arena.  ids_dev int32 [T][k],
+ * weights_dev f32 [T][k] (the RouteRecord's experts and weights). */
+int32_t har_cuda_route(har_cuda_ctx *ctx, const float *gate_inp_dev, int32_t E, int64_t H,
+                       const float *x_dev, int64_t T, int32_t k, int32_t *ids_dev,
+                       float *weights_dev);
+
 /* ---- expert-major grouping -------------------------------------------------
  * groups[e] = entries (t*k + slot) routed to e, in position order
  * (har/crates/har-serve/src/moe.rs:195-202).  counts_dev int32 [E],
@@ -155,6 +172,13 @@ int32_t har_cuda_moe_layer_free(har_cuda_moe_layer *layer);
 int32_t har_cuda_moe_ffn(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer,
                          const float *x_dev, int64_t T, int32_t k, const int32_t *ids_dev,
                          const float *weights_dev, float *y_dev, uint32_t flags);
+/* routed_moe (har/crates/har-demo/src/bin/har-native-qwen35moe.rs:1167-1215)
+ * on the device: har_cuda_route with the layer's E and H (gate_inp_dev f32
+ * [E][H], the layer's ffn_gate_inp), writing the route record to ids_dev
+ * [T][k] / weights_dev [T][k], then har_cuda_moe_ffn on that routing. */
+int32_t har_cuda_routed_moe(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer,
+                            const float *gate_inp_dev, const float *x_dev, int64_t T, int32_t k,
+                            int32_t *ids_dev, float *weights_dev, float *y_dev, uint32_t flags);
 /* The same with host buffers: copies x/ids/weights in and y out on the
  * context's stream and waits (bounded) — the call a BatchStepModel makes. */
 int32_t har_cuda_moe_ffn_host(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer,

@@ -227,6 +227,15 @@ float haro_dot_f32_row(const float *row, const float *input, int64_t k) {
     return sum;
 }
 
+/* har/crates/har-demo/src/bin/har-native-qwen35moe.rs:1168-1172: routed_moe's
+ * router logits, self.matvec(ffn_gate_inp) on an F32 tensor [E][H]; each row
+ * is dot_f32_row (:154-163).  The worker split of matvec (:583-624) only
+ * decides which thread computes a row, not the row's value. */
+void haro_router_logits(const float *gate_inp, int64_t E, int64_t H, const float *x,
+                        float *logits) {
+    for (int64_t e = 0; e < E; ++e) logits[e] = haro_dot_f32_row(gate_inp + e * H, x, H);
+}
+
 /* ------------------------------------------------------------------------ */
 /* a6: expert_matvec with per-call worker threads                            */
 /* ------------------------------------------------------------------------ */

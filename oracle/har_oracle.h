@@ -70,6 +70,11 @@ float haro_dot_quant_row(const uint8_t *row, const float *x, int64_t k);
 /* har/crates/har-demo/src/bin/har-native-qwen35moe.rs:154-163 */
 float haro_dot_f32_row(const float *row, const float *x, int64_t k);
 
+/* har/crates/har-demo/src/bin/har-native-qwen35moe.rs:1168-1172 with :154-163:
+ * logits[e] = dot_f32_row(gate_inp[e], x) for the f32 router [E][H]. */
+void haro_router_logits(const float *gate_inp, int64_t E, int64_t H, const float *x,
+                        float *logits);
+
 /* ---- a6: expert matvec --------------------------------------------------- */
 /* har/crates/har-demo/src/bin/har-native-qwen35moe.rs:626-689: tensor of
  * [E][N][K/256] super-blocks, expert e at e*N*row_bytes; rows split into

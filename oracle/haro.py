@@ -57,6 +57,7 @@ def lib():
         "haro_silu": (C.c_float, [C.c_float]),
         "haro_sigmoid": (C.c_float, [C.c_float]),
         "haro_route_topk": (None, [_f32p, C.c_int, C.c_int, _i32p, _f32p]),
+        "haro_router_logits": (None, [_f32p, _i64, _i64, _f32p, _f32p]),
         "haro_group_by_expert": (None, [_i64, C.c_int, C.c_int, _i32p, _i32p, _i32p, _i32p]),
         "haro_q8k_quantize": (None, [_f32p, _i64, _u8p]),
         "haro_q8k_dot_row": (C.c_float, [_u8p, _u8p, _i64]),
@@ -166,6 +167,21 @@ def route_topk(logits: np.ndarray, k: int, exp_mode: int = 0):
         w[t] = w_row
     lib().haro_set_exp_mode(0)
     return ids, w
+
+
+def router_logits(gate_inp: np.ndarray, x: np.ndarray) -> np.ndarray:
+    """routed_moe's self.matvec(ffn_gate_inp) on an F32 router
+    (har/crates/har-demo/src/bin/har-native-qwen35moe.rs:1168-1172, :154-163),
+    per token row of x [T][H]; gate_inp [E][H]."""
+    gate_inp = np.ascontiguousarray(gate_inp, np.float32)
+    x = np.ascontiguousarray(x, np.float32)
+    E, H = gate_inp.shape
+    out = np.empty((x.shape[0], E), np.float32)
+    for t in range(x.shape[0]):
+        row = np.empty(E, np.float32)
+        lib().haro_router_logits(gate_inp, E, H, np.ascontiguousarray(x[t]), row)
+        out[t] = row
+    return out
 
 
 def group_by_expert(ids: np.ndarray, E: int):

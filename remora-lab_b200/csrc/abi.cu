@@ -401,6 +401,38 @@ int32_t har_cuda_route_topk(har_cuda_ctx *ctx, const float *logits_dev, int64_t 
   return launch_route_topk(ctx, logits_dev, T, E, k, ids_dev, weights_dev);
 }
 
+int32_t har_cuda_router_logits(har_cuda_ctx *ctx, const float *gate_inp_dev, int32_t E,
+                               int64_t H, const float *x_dev, int64_t T, float *logits_dev) {
+  if (!ctx) return HAR_CUDA_ERR_ARG;
+  if (!gate_inp_dev || !x_dev || !logits_dev)
+    return set_error(ctx, HAR_CUDA_ERR_ARG, "router_logits: null pointer");
+  if (T < 0 || E <= 0 || H <= 0 || H > ((int64_t)1 << 24) || T > ((int64_t)1 << 21))
+    return set_error(ctx, HAR_CUDA_ERR_GEOMETRY,
+                     "router_logits: need E > 0, 0 < H <= 2^24 and 0 <= T <= 2^21");
+  if (T == 0) return HAR_CUDA_OK;
+  HAR_TRY(use_device(ctx));
+  return launch_router_logits(ctx, gate_inp_dev, E, (int)H, x_dev, T, logits_dev);
+}
+
+int32_t har_cuda_route(har_cuda_ctx *ctx, const float *gate_inp_dev, int32_t E, int64_t H,
+                       const float *x_dev, int64_t T, int32_t k, int32_t *ids_dev,
+                       float *weights_dev) {
+  if (!ctx) return HAR_CUDA_ERR_ARG;
+  if (!gate_inp_dev || !x_dev || !ids_dev || !weights_dev)
+    return set_error(ctx, HAR_CUDA_ERR_ARG, "route: null pointer");
+  if (T < 0 || E <= 0 || k <= 0 || k > E || k > 32 || E > 8192 || H <= 0 ||
+      H > ((int64_t)1 << 24) || T > ((int64_t)1 << 21))
+    return set_error(ctx, HAR_CUDA_ERR_GEOMETRY,
+                     "route: need 0 < k <= min(E, 32), E <= 8192, 0 < H <= 2^24, T <= 2^21");
+  if (T == 0) return HAR_CUDA_OK;
+  HAR_TRY(use_device(ctx));
+  // logits live in the scratch arena only until route_topk has read them
+  HAR_TRY(ensure_scratch(ctx, sizeof(float) * (size_t)T * (size_t)E));
+  float *logits = static_cast<float *>(ctx->scratch);
+  HAR_TRY(launch_router_logits(ctx, gate_inp_dev, E, (int)H, x_dev, T, logits));
+  return launch_route_topk(ctx, logits, T, E, k, ids_dev, weights_dev);
+}
+
 int32_t har_cuda_group_by_expert(har_cuda_ctx *ctx, const int32_t *ids_dev, int64_t T,
                                  int32_t k, int32_t E, int32_t *counts_dev,
                                  int32_t *offsets_dev, int32_t *order_dev) {
@@ -513,6 +545,20 @@ int32_t har_cuda_moe_ffn(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer,
   if (!x_dev || !ids_dev || !weights_dev || !y_dev)
     return set_error(ctx, HAR_CUDA_ERR_ARG, "moe_ffn: null pointer");
   HAR_TRY(use_device(ctx));
+  return run_moe_ffn(ctx, layer, x_dev, T, k, ids_dev, weights_dev, y_dev, flags);
+}
+
+int32_t har_cuda_routed_moe(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer,
+                            const float *gate_inp_dev, const float *x_dev, int64_t T, int32_t k,
+                            int32_t *ids_dev, float *weights_dev, float *y_dev, uint32_t flags) {
+  HAR_TRY(check_moe_args(ctx, layer, T, k, flags));
+  if (flags & HAR_CUDA_MOE_EMPTY_SLOTS)
+    return set_error(ctx, HAR_CUDA_ERR_ARG, "routed_moe: EMPTY_SLOTS is for the EP exchange only");
+  if (T == 0) return HAR_CUDA_OK;
+  if (!gate_inp_dev || !x_dev || !ids_dev || !weights_dev || !y_dev)
+    return set_error(ctx, HAR_CUDA_ERR_ARG, "routed_moe: null pointer");
+  HAR_TRY(har_cuda_route(ctx, gate_inp_dev, (int32_t)layer->E, layer->H, x_dev, T, k, ids_dev,
+                         weights_dev));
   return run_moe_ffn(ctx, layer, x_dev, T, k, ids_dev, weights_dev, y_dev, flags);
 }
 

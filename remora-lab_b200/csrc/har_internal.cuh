@@ -192,6 +192,8 @@ int32_t launch_route_topk(har_cuda_ctx *ctx, const float *logits, int64_t T, int
                           int32_t *ids, float *weights);
 int32_t launch_group(har_cuda_ctx *ctx, const int32_t *ids, int64_t T, int k, int E,
                      int32_t *counts, int32_t *offsets, int32_t *order, int32_t *inv);
+int32_t launch_router_logits(har_cuda_ctx *ctx, const float *W, int E, int H, const float *x,
+                             int64_t T, float *logits);
 int32_t run_moe_ffn(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const float *x,
                     int64_t T, int k, const int32_t *ids, const float *weights, float *y,
                     uint32_t flags);

@@ -313,4 +313,66 @@ int32_t launch_group(har_cuda_ctx *ctx, const int32_t *ids, int64_t T, int k, in
                            1, nullptr, nullptr, 0, 0);
 }
 
+// ---------------------------------------------------------------------------
+// router_logits_kernel: logits[t][e] = sum_h W[e][h] * x[t][h] for an f32
+// router matrix W [E][H] (ffn_gate_inp).  Restates routed_moe's
+// self.matvec(ffn_gate_inp) (har-native-qwen35moe.rs:1168-1172), whose F32
+// arm is dot_f32_row (:154-163): one f32 accumulator per (token, expert),
+// h ascending, each product rounded before it is added (Rust never fuses).
+// So every (t, e) is one sequential chain of __fmul_rn/__fadd_rn — bit-exact
+// with the reference, which the top-k selection needs.
+//
+// A CTA covers 32 experts (one per lane) x 32 tokens (4 per thread, 8
+// warps), staging 64-wide slices of W (transposed, padded: lane-consecutive
+// reads) and of x (warp-broadcast reads) in shared memory; the four tokens'
+// chains give each thread four independent adds per W value.
+// ---------------------------------------------------------------------------
+constexpr int RL_E = 32, RL_WARPS = 8, RL_TPT = 4, RL_TT = RL_WARPS * RL_TPT, RL_KC = 64;
+
+__global__ void __launch_bounds__(RL_WARPS * 32) router_logits_kernel(
+    const float *__restrict__ W, const float *__restrict__ x, int64_t T, int E, int H,
+    float *__restrict__ logits) {
+  __shared__ float ws[RL_KC][RL_E + 1];
+  __shared__ __align__(16) float xs[RL_TT][RL_KC];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int e0 = blockIdx.x * RL_E;
+  const int64_t t0 = (int64_t)blockIdx.y * RL_TT;
+  float s[RL_TPT];
+#pragma unroll
+  for (int j = 0; j < RL_TPT; ++j) s[j] = 0.0f;
+  for (int h0 = 0; h0 < H; h0 += RL_KC) {
+    const int kc = min(RL_KC, H - h0);
+    __syncthreads();  // the previous slice is consumed
+    for (int i = threadIdx.x; i < RL_E * RL_KC; i += RL_WARPS * 32) {
+      const int r = i / RL_KC, c = i % RL_KC;
+      ws[c][r] = (e0 + r < E && c < kc) ? W[(int64_t)(e0 + r) * H + h0 + c] : 0.0f;
+      const int64_t t = t0 + r;
+      xs[r][c] = (t < T && c < kc) ? x[t * H + h0 + c] : 0.0f;
+    }
+    __syncthreads();
+    const float *xr = xs[warp * RL_TPT];
+    for (int c = 0; c < kc; ++c) {
+      const float w = ws[c][lane];
+#pragma unroll
+      for (int j = 0; j < RL_TPT; ++j) s[j] = __fadd_rn(s[j], __fmul_rn(w, xr[j * RL_KC + c]));
+    }
+  }
+  const int e = e0 + lane;
+  if (e < E) {
+#pragma unroll
+    for (int j = 0; j < RL_TPT; ++j) {
+      const int64_t t = t0 + warp * RL_TPT + j;
+      if (t < T) logits[t * E + e] = s[j];
+    }
+  }
+}
+
+int32_t launch_router_logits(har_cuda_ctx *ctx, const float *W, int E, int H, const float *x,
+                             int64_t T, float *logits) {
+  const dim3 grid((unsigned)((E + RL_E - 1) / RL_E), (unsigned)((T + RL_TT - 1) / RL_TT));
+  prof_begin(ctx);
+  router_logits_kernel<<<grid, RL_WARPS * 32, 0, ctx->stream>>>(W, x, T, E, H, logits);
+  return check_launch(ctx, "router_logits_kernel");
+}
+
 }  // namespace har

@@ -44,6 +44,7 @@ MOE_FORCE_TC = 0x8
 
 # Every symbol include/har_cuda.h declares (tests check the library exports them).
 EXPORTS = [
+    "har_cuda_router_logits", "har_cuda_route", "har_cuda_routed_moe",
     "har_cuda_abi_version", "har_cuda_ctx_create", "har_cuda_ctx_destroy", "har_cuda_last_error",
     "har_cuda_ctx_set_stream", "har_cuda_synchronize", "har_cuda_launch_count",
     "har_cuda_weights_upload_q4k", "har_cuda_weights_wrap_q4k", "har_cuda_weights_free",
@@ -97,6 +98,9 @@ def load_library() -> C.CDLL:
         "har_cuda_q8k_quantize": (i32, [vp, vp, i64, i64, vp]),
         "har_cuda_q4k_gemv": (i32, [vp, vp, i64, vp, i32, i64, vp]),
         "har_cuda_route_topk": (i32, [vp, vp, i64, i32, i32, vp, vp]),
+        "har_cuda_router_logits": (i32, [vp, vp, i32, i64, vp, i64, vp]),
+        "har_cuda_route": (i32, [vp, vp, i32, i64, vp, i64, i32, vp, vp]),
+        "har_cuda_routed_moe": (i32, [vp, vp, vp, vp, i64, i32, vp, vp, vp, u32]),
         "har_cuda_group_by_expert": (i32, [vp, vp, i64, i32, i32, vp, vp, vp]),
         "har_cuda_moe_layer_create": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, pp]),
         "har_cuda_moe_layer_free": (i32, [vp]),
@@ -224,6 +228,42 @@ class Context:
         self.check(self.lib.har_cuda_route_topk(self.handle, _dptr(logits), T, E, k, _dptr(ids),
                                                 _dptr(weights)))
         return ids, weights
+
+    def router_logits(self, gate_inp, x, logits):
+        """routed_moe's router GEMV, self.matvec(ffn_gate_inp)
+        (har-native-qwen35moe.rs:1168-1172): gate_inp f32 [E][H], x f32
+        [T][H] -> logits f32 [T][E], bit-exact with the reference."""
+        E, H = gate_inp.shape
+        T = x.shape[0]
+        if x.shape[1] != H or tuple(logits.shape) != (T, E):
+            raise HarCudaError(ERR_GEOMETRY, "router_logits: x [T][H], logits [T][E]")
+        self.check(self.lib.har_cuda_router_logits(self.handle, _dptr(gate_inp), E, H, _dptr(x),
+                                                   T, _dptr(logits)))
+        return logits
+
+    def route(self, gate_inp, x, k: int, ids, weights):
+        """routed_moe's selection (har-native-qwen35moe.rs:1167-1204) from the
+        token rows: router GEMV, softmax over all E, top-k, renormalise."""
+        E, H = gate_inp.shape
+        T = x.shape[0]
+        if x.shape[1] != H or tuple(ids.shape) != (T, k) or tuple(weights.shape) != (T, k):
+            raise HarCudaError(ERR_GEOMETRY, "route: x [T][H], ids/weights [T][k]")
+        self.check(self.lib.har_cuda_route(self.handle, _dptr(gate_inp), E, H, _dptr(x), T, k,
+                                           _dptr(ids), _dptr(weights)))
+        return ids, weights
+
+    def routed_moe(self, layer: "MoeLayer", gate_inp, x, k: int, ids, weights, y,
+                   flags: int = 0):
+        """routed_moe (har-native-qwen35moe.rs:1167-1215): route x with the
+        f32 router gate_inp [E][H], write the route record to ids/weights
+        [T][k] and the layer's output to y [T][H]."""
+        T = x.shape[0]
+        if tuple(ids.shape) != (T, k) or tuple(weights.shape) != (T, k):
+            raise HarCudaError(ERR_GEOMETRY, "routed_moe: ids/weights [T][k]")
+        self.check(self.lib.har_cuda_routed_moe(self.handle, layer.handle, _dptr(gate_inp),
+                                                _dptr(x), T, k, _dptr(ids), _dptr(weights),
+                                                _dptr(y), flags))
+        return y
 
     def group_by_expert(self, ids, E: int, counts, offsets, order):
         T, k = ids.shape
