@@ -96,6 +96,19 @@ int32_t har_cuda_weights_upload_q4k(har_cuda_ctx *ctx, const void *host_bytes, i
 /* Borrow an existing 16-byte-aligned device buffer (not freed by the library). */
 int32_t har_cuda_weights_wrap_q4k(har_cuda_ctx *ctx, const void *dev_bytes, int64_t E,
                                   int64_t N, int64_t K, har_cuda_weights **out);
+/* Any supported GGML block type: the type ids HAR's GGUF reader matches
+ * (har/crates/har-demo/src/bin/har-native-qwen35moe.rs:37-41), rows of
+ * K/256 super-blocks (Q4_K 144 B, Q6_K 210 B; row_bytes_for_type, :176-199),
+ * laid out [E][N][K/256] like the GGUF expert tensors.  Each entry point
+ * accepts only the type it computes on (HAR_CUDA_ERR_UNSUPPORTED otherwise):
+ * Q4_K for the Q4_K GEMV and the MoE layers, Q6_K for har_cuda_q6k_gemv. */
+#define HAR_CUDA_GGML_F32 0
+#define HAR_CUDA_GGML_Q4_K 12
+#define HAR_CUDA_GGML_Q6_K 14
+int32_t har_cuda_weights_upload(har_cuda_ctx *ctx, int32_t ggml_type, const void *host_bytes,
+                                int64_t E, int64_t N, int64_t K, har_cuda_weights **out);
+int32_t har_cuda_weights_wrap(har_cuda_ctx *ctx, int32_t ggml_type, const void *dev_bytes,
+                              int64_t E, int64_t N, int64_t K, har_cuda_weights **out);
 int32_t har_cuda_weights_free(har_cuda_weights *w);
 const void *har_cuda_weights_device_ptr(const har_cuda_weights *w);
 
@@ -115,6 +128,16 @@ int32_t har_cuda_q8k_quantize(har_cuda_ctx *ctx, const float *x_dev, int64_t M, 
  * act_kind HAR_CUDA_ACT_F32: x_dev is f32 [M][K]; HAR_CUDA_ACT_Q8K: Q8_K rows. */
 int32_t har_cuda_q4k_gemv(har_cuda_ctx *ctx, const har_cuda_weights *w, int64_t expert,
                           const void *x_dev, int32_t act_kind, int64_t M, float *y_dev);
+
+/* ---- Q6_K GEMV --------------------------------------------------------------
+ * y[m][n] = sum_k W_e[n][k] * x[m][k] for Q6_K weights (ql[128], qh[64], int8
+ * scales[16], f16 d per 210-byte super-block) and f32 activations x_dev
+ * [M][K] (16-byte aligned); y_dev f32 [M][N].  Replaces the Q6_K arm of
+ * dot_quant_row / q6k_dot (har/crates/har-demo/src/bin/har-native-qwen3.rs:174-232)
+ * as NativeQwen35Moe::matvec reaches it for Q6_K tensors
+ * (har/crates/har-demo/src/bin/har-native-qwen35moe.rs:551-556,583-624). */
+int32_t har_cuda_q6k_gemv(har_cuda_ctx *ctx, const har_cuda_weights *w, int64_t expert,
+                          const float *x_dev, int64_t M, float *y_dev);
 
 /* ---- router top-k ---------------------------------------------------------
  * Per token: softmax over all E logits with max subtraction, experts ordered

@@ -220,6 +220,54 @@ float haro_dot_quant_row(const uint8_t *row, const float *input, int64_t k) {
     return sum;
 }
 
+/* har/crates/har-demo/src/bin/har-native-qwen3.rs:174-205: one Q6_K block
+ * (ql[128] @0, qh[64] @128, int8 scales[16] @192, f16 d @208) against 256
+ * inputs, with q6k_dot's operation order: per (half, lane) the four terms
+ * s*q*x summed left to right, times d, added to one f32 sum. */
+float haro_q6k_dot(const uint8_t *block, const float *input) {
+    const uint8_t *ql = block, *qh = block + 128, *scales = block + 192;
+    const float d = haro_half_to_f32((uint16_t)(block[208] | (block[209] << 8)));
+    float sum = 0.0f;
+    for (int half = 0; half < 2; ++half) {
+        const int ql_base = half * 64, qh_base = half * 32, scale_base = half * 8;
+        const int input_base = half * 128;
+        for (int lane = 0; lane < 32; ++lane) {
+            const uint8_t high = qh[qh_base + lane];
+            const uint8_t low_0 = ql[ql_base + lane];
+            const uint8_t low_1 = ql[ql_base + 32 + lane];
+            const int16_t q1 = (int16_t)((low_0 & 0x0f) | ((high & 0x03) << 4)) - 32;
+            const int16_t q2 = (int16_t)((low_1 & 0x0f) | (((high >> 2) & 0x03) << 4)) - 32;
+            const int16_t q3 = (int16_t)((low_0 >> 4) | (((high >> 4) & 0x03) << 4)) - 32;
+            const int16_t q4 = (int16_t)((low_1 >> 4) | (((high >> 6) & 0x03) << 4)) - 32;
+            const float s1 = (float)(int8_t)scales[scale_base + lane / 16];
+            const float s2 = (float)(int8_t)scales[scale_base + lane / 16 + 2];
+            const float s3 = (float)(int8_t)scales[scale_base + lane / 16 + 4];
+            const float s4 = (float)(int8_t)scales[scale_base + lane / 16 + 6];
+            sum += d * (s1 * (float)q1 * input[input_base + lane] +
+                        s2 * (float)q2 * input[input_base + 32 + lane] +
+                        s3 * (float)q3 * input[input_base + 64 + lane] +
+                        s4 * (float)q4 * input[input_base + 96 + lane]);
+        }
+    }
+    return sum;
+}
+
+/* har/crates/har-demo/src/bin/har-native-qwen3.rs:207-232 (Q6_K arm): the
+ * row sum adds the per-block sums in block order. */
+float haro_dot_quant_row_q6k(const uint8_t *row, const float *input, int64_t k) {
+    float sum = 0.0f;
+    for (int64_t b = 0; b < k / HARO_QK_K; ++b)
+        sum += haro_q6k_dot(row + b * HARO_Q6K_BLOCK_BYTES, input + b * HARO_QK_K);
+    return sum;
+}
+
+/* matvec over a Q6_K tensor's rows (har-native-qwen35moe.rs:561-624 with
+ * dot_row's Q6_K arm, :551-556): out[r] = dot_quant_row(row r, x). */
+void haro_q6k_matvec(const uint8_t *w, int64_t rows, int64_t k, const float *x, float *out) {
+    const int64_t rb = k / HARO_QK_K * HARO_Q6K_BLOCK_BYTES;
+    for (int64_t r = 0; r < rows; ++r) out[r] = haro_dot_quant_row_q6k(w + r * rb, x, k);
+}
+
 /* har/crates/har-demo/src/bin/har-native-qwen35moe.rs:154-163 */
 float haro_dot_f32_row(const float *row, const float *input, int64_t k) {
     float sum = 0.0f;

@@ -33,6 +33,7 @@ extern "C" {
 #define HARO_QK_K 256
 #define HARO_Q4K_BLOCK_BYTES 144
 #define HARO_Q8K_BLOCK_BYTES 292
+#define HARO_Q6K_BLOCK_BYTES 210
 #define HARO_ROUTER_EPS 1.0e-9f
 
 /* ---- a1: binary16 -> f32 ------------------------------------------------ */
@@ -67,6 +68,13 @@ void haro_q4k_matvec(const uint8_t *w, int64_t rows, int64_t dim,
 float haro_q4k_dot(const uint8_t *block, const float *x);
 /* har/crates/har-demo/src/bin/har-native-qwen3.rs:207-232 (Q4_K arm) */
 float haro_dot_quant_row(const uint8_t *row, const float *x, int64_t k);
+/* ---- Q6_K ------------------------------------------------------------------ */
+/* har/crates/har-demo/src/bin/har-native-qwen3.rs:174-205 */
+float haro_q6k_dot(const uint8_t *block, const float *x);
+/* har/crates/har-demo/src/bin/har-native-qwen3.rs:207-232 (Q6_K arm) */
+float haro_dot_quant_row_q6k(const uint8_t *row, const float *x, int64_t k);
+/* rows x k Q6_K tensor times x (the per-row dot above for every row) */
+void haro_q6k_matvec(const uint8_t *w, int64_t rows, int64_t k, const float *x, float *out);
 /* har/crates/har-demo/src/bin/har-native-qwen35moe.rs:154-163 */
 float haro_dot_f32_row(const float *row, const float *x, int64_t k);
 

@@ -58,6 +58,8 @@ def lib():
         "haro_sigmoid": (C.c_float, [C.c_float]),
         "haro_route_topk": (None, [_f32p, C.c_int, C.c_int, _i32p, _f32p]),
         "haro_router_logits": (None, [_f32p, _i64, _i64, _f32p, _f32p]),
+        "haro_q6k_dot": (C.c_float, [_u8p, _f32p]),
+        "haro_q6k_matvec": (None, [_u8p, _i64, _i64, _f32p, _f32p]),
         "haro_group_by_expert": (None, [_i64, C.c_int, C.c_int, _i32p, _i32p, _i32p, _i32p]),
         "haro_q8k_quantize": (None, [_f32p, _i64, _u8p]),
         "haro_q8k_dot_row": (C.c_float, [_u8p, _u8p, _i64]),
@@ -167,6 +169,40 @@ def route_topk(logits: np.ndarray, k: int, exp_mode: int = 0):
         w[t] = w_row
     lib().haro_set_exp_mode(0)
     return ids, w
+
+
+Q6K_BLOCK_BYTES = 210
+
+
+def q6k_dot(block: np.ndarray, x: np.ndarray) -> float:
+    """har/crates/har-demo/src/bin/har-native-qwen3.rs:174-205"""
+    return lib().haro_q6k_dot(np.ascontiguousarray(block, np.uint8),
+                              np.ascontiguousarray(x, np.float32))
+
+
+def q6k_matvec(w: np.ndarray, rows: int, K: int, x: np.ndarray) -> np.ndarray:
+    """Q6_K rows [rows][K/256*210] times x: dot_quant_row's Q6_K arm per row
+    (har-native-qwen3.rs:207-232), for every row of x [M][K] -> [M][rows]."""
+    w = np.ascontiguousarray(w, np.uint8).reshape(-1)
+    x = np.ascontiguousarray(x, np.float32).reshape(-1, K)
+    out = np.empty((x.shape[0], rows), np.float32)
+    for m in range(x.shape[0]):
+        row = np.empty(rows, np.float32)
+        lib().haro_q6k_matvec(w, rows, K, np.ascontiguousarray(x[m]), row)
+        out[m] = row
+    return out
+
+
+def random_q6k(seed: int, rows: int, K: int, d_lo: float = 1e-3, d_hi: float = 4e-3) -> np.ndarray:
+    """Seeded Q6_K test tensor [rows][K/256*210]: uniform random codes and
+    int8 scales, d a random finite f16 in [d_lo, d_hi).  Any bytes are a
+    valid Q6_K block apart from d, so no quantiser is involved."""
+    rng = np.random.default_rng(seed)
+    nb = rows * (K // QK_K)
+    b = rng.integers(0, 256, size=(nb, Q6K_BLOCK_BYTES), dtype=np.uint8)
+    d = rng.uniform(d_lo, d_hi, size=nb).astype(np.float16).view(np.uint8).reshape(nb, 2)
+    b[:, 208:210] = d
+    return b.reshape(rows, (K // QK_K) * Q6K_BLOCK_BYTES)
 
 
 def router_logits(gate_inp: np.ndarray, x: np.ndarray) -> np.ndarray:

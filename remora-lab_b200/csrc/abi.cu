@@ -119,11 +119,16 @@ static int32_t use_device(har_cuda_ctx *ctx) {
   return HAR_CUDA_OK;
 }
 
-static int32_t check_weights(har_cuda_ctx *ctx, const har_cuda_weights *w, const char *name) {
+static int32_t check_weights(har_cuda_ctx *ctx, const har_cuda_weights *w, const char *name,
+                             int32_t type = GGML_Q4_K) {
   if (!w) return set_error(ctx, HAR_CUDA_ERR_ARG, std::string(name) + " is null");
   if (!w->dev) return set_error(ctx, HAR_CUDA_ERR_NOT_INIT, std::string(name) + " has no data");
   if (w->device != ctx->device)
     return set_error(ctx, HAR_CUDA_ERR_ARG, std::string(name) + " lives on another device");
+  if (w->type != type)
+    return set_error(ctx, HAR_CUDA_ERR_UNSUPPORTED,
+                     std::string(name) + " has GGML type " + std::to_string(w->type) +
+                         ", this call needs type " + std::to_string(type));
   return HAR_CUDA_OK;
 }
 
@@ -285,10 +290,13 @@ int32_t har_cuda_synchronize(har_cuda_ctx *ctx, int64_t timeout_ms) {
   return HAR_CUDA_OK;
 }
 
-static int32_t make_weights(har_cuda_ctx *ctx, int64_t E, int64_t N, int64_t K,
+static int32_t make_weights(har_cuda_ctx *ctx, int32_t type, int64_t E, int64_t N, int64_t K,
                             har_cuda_weights **out) {
   if (!ctx || !out) return HAR_CUDA_ERR_ARG;
   *out = nullptr;
+  if (type != GGML_Q4_K && type != GGML_Q6_K)
+    return set_error(ctx, HAR_CUDA_ERR_UNSUPPORTED,
+                     "weights: GGML type " + std::to_string(type) + " (supported: 12 Q4_K, 14 Q6_K)");
   if (E <= 0 || N <= 0 || K <= 0)
     return set_error(ctx, HAR_CUDA_ERR_GEOMETRY, "weights: E, N and K must be positive");
   if (K % QK != 0)
@@ -298,7 +306,8 @@ static int32_t make_weights(har_cuda_ctx *ctx, int64_t E, int64_t N, int64_t K,
   w->E = E;
   w->N = N;
   w->K = K;
-  w->row_bytes = K / QK * Q4K_BYTES;
+  w->type = type;
+  w->row_bytes = K / QK * (type == GGML_Q6_K ? Q6K_BYTES : Q4K_BYTES);
   w->expert_bytes = w->row_bytes * N;
   w->device = ctx->device;
   *out = w;
@@ -307,7 +316,17 @@ static int32_t make_weights(har_cuda_ctx *ctx, int64_t E, int64_t N, int64_t K,
 
 int32_t har_cuda_weights_upload_q4k(har_cuda_ctx *ctx, const void *host_bytes, int64_t E,
                                     int64_t N, int64_t K, har_cuda_weights **out) {
-  HAR_TRY(make_weights(ctx, E, N, K, out));
+  return har_cuda_weights_upload(ctx, GGML_Q4_K, host_bytes, E, N, K, out);
+}
+
+int32_t har_cuda_weights_wrap_q4k(har_cuda_ctx *ctx, const void *dev_bytes, int64_t E,
+                                  int64_t N, int64_t K, har_cuda_weights **out) {
+  return har_cuda_weights_wrap(ctx, GGML_Q4_K, dev_bytes, E, N, K, out);
+}
+
+int32_t har_cuda_weights_upload(har_cuda_ctx *ctx, int32_t ggml_type, const void *host_bytes,
+                                int64_t E, int64_t N, int64_t K, har_cuda_weights **out) {
+  HAR_TRY(make_weights(ctx, ggml_type, E, N, K, out));
   har_cuda_weights *w = *out;
   if (!host_bytes) {
     delete w;
@@ -336,9 +355,9 @@ int32_t har_cuda_weights_upload_q4k(har_cuda_ctx *ctx, const void *host_bytes, i
   return HAR_CUDA_OK;
 }
 
-int32_t har_cuda_weights_wrap_q4k(har_cuda_ctx *ctx, const void *dev_bytes, int64_t E,
-                                  int64_t N, int64_t K, har_cuda_weights **out) {
-  HAR_TRY(make_weights(ctx, E, N, K, out));
+int32_t har_cuda_weights_wrap(har_cuda_ctx *ctx, int32_t ggml_type, const void *dev_bytes,
+                              int64_t E, int64_t N, int64_t K, har_cuda_weights **out) {
+  HAR_TRY(make_weights(ctx, ggml_type, E, N, K, out));
   if (!dev_bytes || ((uintptr_t)dev_bytes & 15u)) {
     delete *out;
     *out = nullptr;
@@ -386,6 +405,23 @@ int32_t har_cuda_q4k_gemv(har_cuda_ctx *ctx, const har_cuda_weights *w, int64_t 
   if (M == 0) return HAR_CUDA_OK;
   HAR_TRY(use_device(ctx));
   return launch_gemv(ctx, w, expert, x_dev, act_kind, M, y_dev);
+}
+
+int32_t har_cuda_q6k_gemv(har_cuda_ctx *ctx, const har_cuda_weights *w, int64_t expert,
+                          const float *x_dev, int64_t M, float *y_dev) {
+  if (!ctx) return HAR_CUDA_ERR_ARG;
+  HAR_TRY(check_weights(ctx, w, "q6k_gemv: weights", GGML_Q6_K));
+  if (!x_dev || !y_dev) return set_error(ctx, HAR_CUDA_ERR_ARG, "q6k_gemv: null pointer");
+  if (expert < 0 || expert >= w->E)
+    return set_error(ctx, HAR_CUDA_ERR_ARG, "q6k_gemv: expert " + std::to_string(expert) +
+                                                " out of range [0, " + std::to_string(w->E) + ")");
+  if (M < 0 || M > ((int64_t)1 << 19))
+    return set_error(ctx, HAR_CUDA_ERR_GEOMETRY, "q6k_gemv: need 0 <= M <= 2^19");
+  if (((uintptr_t)x_dev & 15u) || ((uintptr_t)y_dev & 3u))
+    return set_error(ctx, HAR_CUDA_ERR_ARG, "q6k_gemv: x must be 16-byte aligned, y 4-byte");
+  if (M == 0) return HAR_CUDA_OK;
+  HAR_TRY(use_device(ctx));
+  return launch_q6k_gemv(ctx, w, expert, x_dev, M, y_dev);
 }
 
 int32_t har_cuda_route_topk(har_cuda_ctx *ctx, const float *logits_dev, int64_t T, int32_t E,

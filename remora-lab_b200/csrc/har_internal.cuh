@@ -17,6 +17,10 @@ namespace har {
 
 constexpr int QK = 256;           // values per super-block
 constexpr int Q4K_BYTES = 144;    // bytes per Q4_K super-block
+constexpr int Q6K_BYTES = 210;    // bytes per Q6_K super-block
+// GGML tensor type ids (the ids HAR's GGUF reader matches,
+// har/crates/har-demo/src/bin/har-native-qwen35moe.rs:37-41)
+constexpr int GGML_F32 = 0, GGML_Q4_K = 12, GGML_Q6_K = 14;
 constexpr int Q8K_BYTES = 292;    // bytes per Q8_K block
 constexpr float ROUTER_EPS = 1.0e-9f;
 
@@ -153,7 +157,8 @@ struct har_cuda_weights {
   const uint8_t *dev = nullptr;
   bool owned = false;
   int64_t E = 0, N = 0, K = 0;
-  int64_t row_bytes = 0;  // K/256*144
+  int32_t type = har::GGML_Q4_K;  // har::GGML_Q4_K or har::GGML_Q6_K
+  int64_t row_bytes = 0;  // K/256 * (144 or 210)
   int64_t expert_bytes = 0;
   int device = 0;
 };
@@ -188,6 +193,8 @@ int32_t launch_q8k_quantize(har_cuda_ctx *ctx, const float *x, int64_t M, int64_
                             uint8_t *out);
 int32_t launch_gemv(har_cuda_ctx *ctx, const har_cuda_weights *w, int64_t expert,
                     const void *x, int act_kind, int64_t M, float *y);
+int32_t launch_q6k_gemv(har_cuda_ctx *ctx, const har_cuda_weights *w, int64_t expert,
+                        const float *x, int64_t M, float *y);
 int32_t launch_route_topk(har_cuda_ctx *ctx, const float *logits, int64_t T, int E, int k,
                           int32_t *ids, float *weights);
 int32_t launch_group(har_cuda_ctx *ctx, const int32_t *ids, int64_t T, int k, int E,

@@ -28,6 +28,10 @@ LIB_PATH = os.path.join(HERE, "libhar_cuda.so")
 QK_K = 256
 Q4K_BLOCK_BYTES = 144
 Q8K_BLOCK_BYTES = 292
+Q6K_BLOCK_BYTES = 210
+# GGML tensor type ids (har/crates/har-demo/src/bin/har-native-qwen35moe.rs:37-41)
+GGML_F32, GGML_Q4_K, GGML_Q6_K = 0, 12, 14
+BLOCK_BYTES = {GGML_Q4_K: Q4K_BLOCK_BYTES, GGML_Q6_K: Q6K_BLOCK_BYTES}
 
 OK = 0
 ERR_ARG, ERR_GEOMETRY, ERR_CUDA, ERR_NCCL, ERR_TIMEOUT = -1, -2, -3, -4, -5
@@ -44,6 +48,7 @@ MOE_FORCE_TC = 0x8
 
 # Every symbol include/har_cuda.h declares (tests check the library exports them).
 EXPORTS = [
+    "har_cuda_weights_upload", "har_cuda_weights_wrap", "har_cuda_q6k_gemv",
     "har_cuda_router_logits", "har_cuda_route", "har_cuda_routed_moe",
     "har_cuda_abi_version", "har_cuda_ctx_create", "har_cuda_ctx_destroy", "har_cuda_last_error",
     "har_cuda_ctx_set_stream", "har_cuda_synchronize", "har_cuda_launch_count",
@@ -94,6 +99,9 @@ def load_library() -> C.CDLL:
         "har_cuda_weights_upload_q4k": (i32, [vp, vp, i64, i64, i64, pp]),
         "har_cuda_weights_wrap_q4k": (i32, [vp, vp, i64, i64, i64, pp]),
         "har_cuda_weights_free": (i32, [vp]),
+        "har_cuda_weights_upload": (i32, [vp, i32, vp, i64, i64, i64, pp]),
+        "har_cuda_weights_wrap": (i32, [vp, i32, vp, i64, i64, i64, pp]),
+        "har_cuda_q6k_gemv": (i32, [vp, vp, i64, vp, i64, vp]),
         "har_cuda_weights_device_ptr": (vp, [vp]),
         "har_cuda_q8k_quantize": (i32, [vp, vp, i64, i64, vp]),
         "har_cuda_q4k_gemv": (i32, [vp, vp, i64, vp, i32, i64, vp]),
@@ -199,6 +207,27 @@ class Context:
                                                         C.byref(h)))
         return Q4KWeights(self, h, E, N, K)
 
+    def upload(self, ggml_type: int, host_bytes: np.ndarray, E: int, N: int,
+               K: int) -> "Q4KWeights":
+        """Upload a GGUF block tensor [E][N][K/256] of a supported type."""
+        host_bytes = np.ascontiguousarray(host_bytes, np.uint8)
+        if ggml_type not in BLOCK_BYTES:
+            raise HarCudaError(ERR_UNSUPPORTED, f"GGML type {ggml_type}")
+        if host_bytes.size != E * N * (K // QK_K) * BLOCK_BYTES[ggml_type]:
+            raise HarCudaError(ERR_GEOMETRY, "byte count does not match E*N*K/256*block_bytes")
+        h = C.c_void_p()
+        self.check(self.lib.har_cuda_weights_upload(self.handle, ggml_type, _hptr(host_bytes), E,
+                                                    N, K, C.byref(h)))
+        return Q4KWeights(self, h, E, N, K, ggml_type)
+
+    def wrap(self, ggml_type: int, dev_tensor, E: int, N: int, K: int) -> "Q4KWeights":
+        h = C.c_void_p()
+        self.check(self.lib.har_cuda_weights_wrap(self.handle, ggml_type, _dptr(dev_tensor), E, N,
+                                                  K, C.byref(h)))
+        w = Q4KWeights(self, h, E, N, K, ggml_type)
+        w.keepalive = dev_tensor
+        return w
+
     def wrap_q4k(self, dev_tensor, E: int, N: int, K: int) -> "Q4KWeights":
         h = C.c_void_p()
         self.check(self.lib.har_cuda_weights_wrap_q4k(self.handle, _dptr(dev_tensor), E, N, K,
@@ -220,6 +249,12 @@ class Context:
 
     def q4k_gemv(self, w: "Q4KWeights", expert: int, x, act_kind: int, M: int, y):
         self.check(self.lib.har_cuda_q4k_gemv(self.handle, w.handle, expert, _dptr(x), act_kind, M,
+                                              _dptr(y)))
+        return y
+
+    def q6k_gemv(self, w: "Q4KWeights", expert: int, x, M: int, y):
+        """y [M][N] = W_e x for Q6_K weights and f32 activations x [M][K]."""
+        self.check(self.lib.har_cuda_q6k_gemv(self.handle, w.handle, expert, _dptr(x), M,
                                               _dptr(y)))
         return y
 
@@ -399,11 +434,13 @@ class EpComm:
 
 
 class Q4KWeights:
-    """A device-resident Q4_K tensor [E][N][K/256] (GGUF `*_exps` layout)."""
+    """A device-resident block tensor [E][N][K/256] (GGUF `*_exps` layout),
+    Q4_K unless ggml_type says otherwise."""
 
-    def __init__(self, ctx: Context, handle, E, N, K):
+    def __init__(self, ctx: Context, handle, E, N, K, ggml_type: int = GGML_Q4_K):
         self.ctx, self.handle, self.E, self.N, self.K = ctx, handle, E, N, K
-        self.row_bytes = K // QK_K * Q4K_BLOCK_BYTES
+        self.ggml_type = ggml_type
+        self.row_bytes = K // QK_K * BLOCK_BYTES[ggml_type]
         self.keepalive = None
 
     @property
