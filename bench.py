@@ -642,6 +642,41 @@ def run_gemv_roofline(args, torch):
         gbs = nb / (ms * 1e-3) / 1e9
         res[act] = {"ms_per_gemv": round(ms, 5), "weight_gbs": round(gbs, 1), "frac": round(gbs / hbm, 4),
                     "clocks": clk}
+    # Q6_K (the GGUF type of LM heads and of some expert tensors): two 65536 x
+    # 4096 Q6_K matrices (220 MB each) of random codes and scales, f32
+    # activations, alternating as above.
+    n6 = GEMV_N_SMALL
+    q6bytes = n6 * (K // 256) * 210
+    q6 = []
+    for i in range(2):
+        t = torch.randint(0, 256, (q6bytes,), dtype=torch.uint8, device=dev,
+                          generator=torch.Generator(dev).manual_seed(9300 + i))
+        t.view(-1, 210)[:, 208:210] = torch.tensor([0x00, 0x1C], dtype=torch.uint8, device=dev)
+        keep.append(t)
+        q6.append(ctx.wrap(har_cuda.GGML_Q6_K, t, 1, n6, K))
+    y6 = torch.empty((1, n6), dtype=torch.float32, device=dev)
+    with torch.cuda.stream(stream):
+        for j in range(per):
+            ctx.q6k_gemv(q6[j % 2], 0, x, 1, y6)
+    torch.cuda.synchronize()
+    g6 = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g6, stream=stream):
+        for j in range(per):
+            ctx.q6k_gemv(q6[j % 2], 0, x, 1, y6)
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, args.warmup)):
+            g6.replay()
+    torch.cuda.synchronize()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        ev0.record(stream)
+        for _ in range(args.steps):
+            g6.replay()
+        ev1.record(stream)
+    torch.cuda.synchronize()
+    ms6 = ev0.elapsed_time(ev1) / (args.steps * per)
+    gbs6 = q6bytes / (ms6 * 1e-3) / 1e9
     q = res["q8k"]
     return {
         "metric": "Q4_K decode GEMV weight GB/s (batch 1)", "value": q["weight_gbs"], "unit": "GB/s",
@@ -660,6 +695,9 @@ def run_gemv_roofline(args, torch):
                             "ms_per_gemv": res["f32"]["ms_per_gemv"]},
         "rows_65536": {"weight_gbs": res["q8k_small"]["weight_gbs"], "frac": res["q8k_small"]["frac"],
                        "ms_per_gemv": res["q8k_small"]["ms_per_gemv"]},
+        "q6k_f32_65536": {"kernel": "q6k_gemv_kernel", "weight_gbs": round(gbs6, 1),
+                          "frac": round(gbs6 / hbm, 4), "ms_per_gemv": round(ms6, 5),
+                          "rows": n6, "K": K},
         "clocks": q["clocks"],
     }
 

@@ -65,6 +65,7 @@ typedef struct har_cuda_ctx har_cuda_ctx;
 typedef struct har_cuda_weights har_cuda_weights;
 typedef struct har_cuda_moe_layer har_cuda_moe_layer;
 typedef struct har_cuda_ep har_cuda_ep;
+typedef struct har_cuda_gguf har_cuda_gguf;
 
 /* ---- context ------------------------------------------------------------
  * Replaces the device/queue pair HAR opens per model
@@ -197,7 +198,8 @@ int32_t har_cuda_moe_ffn(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer,
                          const float *weights_dev, float *y_dev, uint32_t flags);
 /* routed_moe (har/crates/har-demo/src/bin/har-native-qwen35moe.rs:1167-1215)
  * on the device: har_cuda_route with the layer's E and H (gate_inp_dev f32
- * [E][H], the layer's ffn_gate_inp), writing the route record to ids_dev
+ * [E][H], the layer's ffn_gate_inp; NULL = the router a layer loaded from
+ * GGUF carries), writing the route record to ids_dev
  * [T][k] / weights_dev [T][k], then har_cuda_moe_ffn on that routing. */
 int32_t har_cuda_routed_moe(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer,
                             const float *gate_inp_dev, const float *x_dev, int64_t T, int32_t k,
@@ -241,6 +243,53 @@ int32_t har_cuda_moe_stack_host(har_cuda_ctx *ctx, const har_cuda_moe_layer *con
                                 int32_t L, const float *x_host, int64_t T, int32_t k,
                                 const int32_t *ids_host, const float *weights_host,
                                 float *y_host, uint32_t flags);
+
+/* ---- GGUF expert loader ------------------------------------------------------
+ * Opens a GGUF file (versions 1-3) and reads its directory the way
+ * GgufReader::inspect does (har/crates/har-model/src/lib.rs:126-399):
+ * metadata (general.alignment, default 32), tensor infos, the aligned data
+ * offset and each tensor's payload size from the GGML type tables
+ * (:605-640).  Host-only: no GPU is needed to open or query a file.  On
+ * failure the message goes to err (may be NULL).  The handle keeps the file
+ * open and, once a tensor has been loaded, two 64 MiB pinned staging buffers;
+ * it is not thread-safe. */
+int32_t har_cuda_gguf_open(const char *path, char *err, size_t err_len, har_cuda_gguf **out);
+int32_t har_cuda_gguf_close(har_cuda_gguf *g);
+int32_t har_cuda_gguf_last_error(const har_cuda_gguf *g, char *buf, size_t len);
+int32_t har_cuda_gguf_header(const har_cuda_gguf *g, uint32_t *version, uint64_t *tensor_count,
+                             uint64_t *metadata_count, uint64_t *alignment,
+                             uint64_t *data_offset);
+/* Tensor `index` (file order): name, GGML type, rank, dims (up to 16, GGML
+ * order: dims[0] is the row length), absolute file offset, payload bytes. */
+int32_t har_cuda_gguf_tensor_info(const har_cuda_gguf *g, int64_t index, char *name,
+                                  size_t name_len, uint32_t *ggml_type, uint32_t *rank,
+                                  uint64_t *dims, uint64_t *file_offset, uint64_t *payload_bytes);
+/* Index of the tensor called `name`, or -1. */
+int64_t har_cuda_gguf_find(const har_cuda_gguf *g, const char *name);
+/* A metadata value as a number, as metadata_number reads it
+ * (har/crates/har-model/src/lib.rs:541-543), or a string value. */
+int32_t har_cuda_gguf_meta_u64(const har_cuda_gguf *g, const char *key, uint64_t *value);
+int32_t har_cuda_gguf_meta_string(const har_cuda_gguf *g, const char *key, char *buf,
+                                  size_t len);
+/* Upload a Q4_K or Q6_K tensor straight into the device layout: GGML dims
+ * [K, N, E] (an `*_exps` tensor, expert e at e*N*row_bytes as expert_matvec
+ * reads it, har/crates/har-demo/src/bin/har-native-qwen35moe.rs:626-689, and
+ * as ExpertIndex slices it, har/crates/har-storage/src/gguf.rs:300-403) or
+ * [K, N] (E = 1), byte for byte.  The weights own their device memory. */
+int32_t har_cuda_weights_from_gguf(har_cuda_ctx *ctx, har_cuda_gguf *g, const char *name,
+                                   har_cuda_weights **out);
+/* Copy an F32 tensor of exactly `count` elements to dst_dev. */
+int32_t har_cuda_gguf_read_f32(har_cuda_ctx *ctx, har_cuda_gguf *g, const char *name,
+                               float *dst_dev, int64_t count);
+/* One MoE layer from blk.<layer>.ffn_{gate,up,down}_exps.weight, the shared
+ * expert ffn_{gate,up,down}_shexp.weight and its gate row
+ * ffn_gate_inp_shexp.weight when present, and the f32 router
+ * ffn_gate_inp.weight when present — the tensors routed_moe and
+ * compose_moe_route read (har-native-qwen35moe.rs:979-1048,1167-1215).  The
+ * layer owns all of them (har_cuda_moe_layer_free releases them);
+ * har_cuda_routed_moe with gate_inp_dev = NULL uses the layer's router. */
+int32_t har_cuda_moe_layer_from_gguf(har_cuda_ctx *ctx, har_cuda_gguf *g, int32_t layer,
+                                     har_cuda_moe_layer **out);
 
 /* ---- expert parallelism over the GPUs of one box (NCCL over NVLink) ----------------------
  * No counterpart in the reference, which runs every expert on one CPU

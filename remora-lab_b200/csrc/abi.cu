@@ -548,6 +548,12 @@ int32_t har_cuda_moe_layer_create(har_cuda_ctx *ctx, const har_cuda_weights *gat
 
 int32_t har_cuda_moe_layer_free(har_cuda_moe_layer *layer) {
   if (!layer) return HAR_CUDA_ERR_ARG;
+  for (har_cuda_weights *w : layer->owned)
+    if (w) har_cuda_weights_free(w);
+  if (layer->owned_dev) {
+    cudaSetDevice(layer->gate->device);
+    cudaFree(layer->owned_dev);
+  }
   delete layer;
   return HAR_CUDA_OK;
 }
@@ -591,7 +597,10 @@ int32_t har_cuda_routed_moe(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer,
   if (flags & HAR_CUDA_MOE_EMPTY_SLOTS)
     return set_error(ctx, HAR_CUDA_ERR_ARG, "routed_moe: EMPTY_SLOTS is for the EP exchange only");
   if (T == 0) return HAR_CUDA_OK;
-  if (!gate_inp_dev || !x_dev || !ids_dev || !weights_dev || !y_dev)
+  if (!gate_inp_dev) gate_inp_dev = layer->router;  // the layer's own (GGUF) router
+  if (!gate_inp_dev)
+    return set_error(ctx, HAR_CUDA_ERR_ARG, "routed_moe: no router (argument null, layer has none)");
+  if (!x_dev || !ids_dev || !weights_dev || !y_dev)
     return set_error(ctx, HAR_CUDA_ERR_ARG, "routed_moe: null pointer");
   HAR_TRY(har_cuda_route(ctx, gate_inp_dev, (int32_t)layer->E, layer->H, x_dev, T, k, ids_dev,
                          weights_dev));

@@ -177,6 +177,11 @@ struct har_cuda_moe_layer {
   // bytes, box of 128 rows x one 144-byte super-block (tc_maps: encoded).
   bool tc_maps = false;
   TmaDesc map_gate, map_up, map_down, map_sh_gate, map_sh_up, map_sh_down;
+  // A layer loaded from a GGUF file owns its tensors: the weights, and one
+  // device buffer holding the f32 router [E][H] and shared-expert gate row.
+  std::vector<har_cuda_weights *> owned;
+  void *owned_dev = nullptr;
+  const float *router = nullptr;  // ffn_gate_inp [E][H], or null
 };
 
 namespace har {

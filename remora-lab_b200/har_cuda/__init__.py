@@ -48,6 +48,10 @@ MOE_FORCE_TC = 0x8
 
 # Every symbol include/har_cuda.h declares (tests check the library exports them).
 EXPORTS = [
+    "har_cuda_gguf_open", "har_cuda_gguf_close", "har_cuda_gguf_last_error",
+    "har_cuda_gguf_header", "har_cuda_gguf_tensor_info", "har_cuda_gguf_find",
+    "har_cuda_gguf_meta_u64", "har_cuda_gguf_meta_string", "har_cuda_weights_from_gguf",
+    "har_cuda_gguf_read_f32", "har_cuda_moe_layer_from_gguf",
     "har_cuda_weights_upload", "har_cuda_weights_wrap", "har_cuda_q6k_gemv",
     "har_cuda_router_logits", "har_cuda_route", "har_cuda_routed_moe",
     "har_cuda_abi_version", "har_cuda_ctx_create", "har_cuda_ctx_destroy", "har_cuda_last_error",
@@ -79,6 +83,14 @@ def load_library() -> C.CDLL:
         return _lib
     if not os.path.exists(LIB_PATH):
         raise ImportError(f"libhar_cuda.so not built at {LIB_PATH}; run remora-lab_b200/build.py")
+    # The library links libnccl.so.2.  Loaded first, it would pull in the
+    # system NCCL, which lacks symbols torch's own (newer) NCCL provides and
+    # makes a later `import torch` fail; with torch loaded first both share
+    # torch's NCCL.
+    try:
+        import torch  # noqa: F401
+    except ImportError:
+        pass
     L = C.CDLL(LIB_PATH)
     vp, i32, i64, u32, u64 = C.c_void_p, C.c_int32, C.c_int64, C.c_uint32, C.c_uint64
     pp = C.POINTER(C.c_void_p)
@@ -102,6 +114,20 @@ def load_library() -> C.CDLL:
         "har_cuda_weights_upload": (i32, [vp, i32, vp, i64, i64, i64, pp]),
         "har_cuda_weights_wrap": (i32, [vp, i32, vp, i64, i64, i64, pp]),
         "har_cuda_q6k_gemv": (i32, [vp, vp, i64, vp, i64, vp]),
+        "har_cuda_gguf_open": (i32, [C.c_char_p, C.c_char_p, C.c_size_t, pp]),
+        "har_cuda_gguf_close": (i32, [vp]),
+        "har_cuda_gguf_last_error": (i32, [vp, C.c_char_p, C.c_size_t]),
+        "har_cuda_gguf_header": (i32, [vp, C.POINTER(C.c_uint32), C.POINTER(u64),
+                                       C.POINTER(u64), C.POINTER(u64), C.POINTER(u64)]),
+        "har_cuda_gguf_tensor_info": (i32, [vp, i64, C.c_char_p, C.c_size_t,
+                                            C.POINTER(C.c_uint32), C.POINTER(C.c_uint32),
+                                            C.POINTER(u64), C.POINTER(u64), C.POINTER(u64)]),
+        "har_cuda_gguf_find": (i64, [vp, C.c_char_p]),
+        "har_cuda_gguf_meta_u64": (i32, [vp, C.c_char_p, C.POINTER(u64)]),
+        "har_cuda_gguf_meta_string": (i32, [vp, C.c_char_p, C.c_char_p, C.c_size_t]),
+        "har_cuda_weights_from_gguf": (i32, [vp, vp, C.c_char_p, pp]),
+        "har_cuda_gguf_read_f32": (i32, [vp, vp, C.c_char_p, vp, i64]),
+        "har_cuda_moe_layer_from_gguf": (i32, [vp, vp, i32, pp]),
         "har_cuda_weights_device_ptr": (vp, [vp]),
         "har_cuda_q8k_quantize": (i32, [vp, vp, i64, i64, vp]),
         "har_cuda_q4k_gemv": (i32, [vp, vp, i64, vp, i32, i64, vp]),
@@ -251,6 +277,29 @@ class Context:
         self.check(self.lib.har_cuda_q4k_gemv(self.handle, w.handle, expert, _dptr(x), act_kind, M,
                                               _dptr(y)))
         return y
+
+    # ---- GGUF ---------------------------------------------------------------
+    def weights_from_gguf(self, g: "Gguf", name: str) -> "Q4KWeights":
+        """Upload a Q4_K/Q6_K tensor of a GGUF file into the device layout."""
+        h = C.c_void_p()
+        self.check(self.lib.har_cuda_weights_from_gguf(self.handle, g.handle, name.encode(),
+                                                       C.byref(h)))
+        info = g.tensor(name)
+        d = info["dims"]
+        E = d[2] if len(d) == 3 else 1
+        return Q4KWeights(self, h, E, d[1], d[0], info["type"])
+
+    def gguf_read_f32(self, g: "Gguf", name: str, dst):
+        self.check(self.lib.har_cuda_gguf_read_f32(self.handle, g.handle, name.encode(), _dptr(dst),
+                                                   dst.numel()))
+        return dst
+
+    def moe_layer_from_gguf(self, g: "Gguf", layer: int) -> "MoeLayer":
+        """blk.<layer>'s expert, shared-expert and router tensors as one layer
+        that owns them (har-native-qwen35moe.rs:979-1048,1167-1215)."""
+        h = C.c_void_p()
+        self.check(self.lib.har_cuda_moe_layer_from_gguf(self.handle, g.handle, layer, C.byref(h)))
+        return MoeLayer(self, h, None)
 
     def q6k_gemv(self, w: "Q4KWeights", expert: int, x, M: int, y):
         """y [M][N] = W_e x for Q6_K weights and f32 activations x [M][K]."""
@@ -459,6 +508,75 @@ class Q4KWeights:
             pass
 
 
+class Gguf:
+    """A GGUF file's directory (GgufReader::inspect, har/crates/har-model/src/lib.rs:126-399).
+    Host-only: opening and querying need no GPU."""
+
+    def __init__(self, path: str):
+        self.lib = load_library()
+        h = C.c_void_p()
+        err = C.create_string_buffer(512)
+        st = self.lib.har_cuda_gguf_open(os.fsencode(path), err, 512, C.byref(h))
+        if st != OK:
+            raise HarCudaError(st, err.value.decode(errors="replace"))
+        self.handle = h
+        v, tc, mc, al, do = (C.c_uint32(), C.c_uint64(), C.c_uint64(), C.c_uint64(), C.c_uint64())
+        self.lib.har_cuda_gguf_header(h, C.byref(v), C.byref(tc), C.byref(mc), C.byref(al),
+                                      C.byref(do))
+        self.version, self.tensor_count, self.metadata_count = v.value, tc.value, mc.value
+        self.alignment, self.data_offset = al.value, do.value
+
+    def _err(self) -> str:
+        buf = C.create_string_buffer(512)
+        self.lib.har_cuda_gguf_last_error(self.handle, buf, 512)
+        return buf.value.decode(errors="replace")
+
+    def tensor_info(self, index: int) -> dict:
+        name = C.create_string_buffer(4096)
+        t, r = C.c_uint32(), C.c_uint32()
+        dims = (C.c_uint64 * 16)()
+        off, pay = C.c_uint64(), C.c_uint64()
+        st = self.lib.har_cuda_gguf_tensor_info(self.handle, index, name, 4096, C.byref(t),
+                                                C.byref(r), dims, C.byref(off), C.byref(pay))
+        if st != OK:
+            raise HarCudaError(st, self._err())
+        return {"name": name.value.decode(), "type": t.value, "dims": list(dims[:r.value]),
+                "file_offset": off.value, "payload_bytes": pay.value}
+
+    def tensors(self):
+        return [self.tensor_info(i) for i in range(self.tensor_count)]
+
+    def find(self, name: str) -> int:
+        return int(self.lib.har_cuda_gguf_find(self.handle, name.encode()))
+
+    def tensor(self, name: str) -> dict:
+        i = self.find(name)
+        if i < 0:
+            raise HarCudaError(ERR_ARG, f"no tensor {name}")
+        return self.tensor_info(i)
+
+    def meta_u64(self, key: str):
+        v = C.c_uint64()
+        st = self.lib.har_cuda_gguf_meta_u64(self.handle, key.encode(), C.byref(v))
+        return v.value if st == OK else None
+
+    def meta_string(self, key: str):
+        buf = C.create_string_buffer(4096)
+        st = self.lib.har_cuda_gguf_meta_string(self.handle, key.encode(), buf, 4096)
+        return buf.value.decode(errors="replace") if st == OK else None
+
+    def close(self):
+        if getattr(self, "handle", None):
+            self.lib.har_cuda_gguf_close(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 class MoeLayer:
     def __init__(self, ctx: Context, handle, refs):
         self.ctx, self.handle, self.refs = ctx, handle, refs
@@ -558,12 +676,45 @@ class CudaMoeModel:
                                   np.asarray(weights, np.float32).reshape(1, -1), self.flags)
         return y[0]
 
-    def routed_moe(self, layer: int, x: np.ndarray, router_logits: np.ndarray):
-        """Router top-k on the GPU, then compose_moe_route; returns (out, ids, weights)."""
+    def routed_moe(self, layer: int, x: np.ndarray, router_logits: np.ndarray = None):
+        """routed_moe (har-native-qwen35moe.rs:1167-1215); returns (out, ids,
+        weights).  Without router_logits the layer's own f32 router (a layer
+        loaded from GGUF) computes them on the device; with them, only the
+        softmax + top-k runs on the device before compose_moe_route."""
         torch = self._torch
+        if router_logits is None:
+            xd = self._dev(np.asarray(x, np.float32).reshape(1, -1), torch.float32)
+            ids = torch.empty((1, self.k), dtype=torch.int32, device=xd.device)
+            w = torch.empty((1, self.k), dtype=torch.float32, device=xd.device)
+            y = torch.empty_like(xd)
+            self.ctx.check(self.ctx.lib.har_cuda_routed_moe(
+                self.ctx.handle, self.layers[layer].handle, None, _dptr(xd), 1, self.k,
+                _dptr(ids), _dptr(w), _dptr(y), self.flags))
+            return y.cpu().numpy()[0], ids.cpu().numpy()[0], w.cpu().numpy()[0]
         lg = self._dev(np.asarray(router_logits, np.float32).reshape(1, -1), torch.float32)
         ids = torch.empty((1, self.k), dtype=torch.int32, device=lg.device)
         w = torch.empty((1, self.k), dtype=torch.float32, device=lg.device)
         self.ctx.route_topk(lg, self.k, ids, w)
         ids_h, w_h = ids.cpu().numpy(), w.cpu().numpy()
         return self.compose_moe_route(layer, x, ids_h[0], w_h[0]), ids_h[0], w_h[0]
+
+    @classmethod
+    def from_gguf(cls, ctx: Context, path: str, k: int = None, flags: int = 0):
+        """Every block's MoE layer of a GGUF file on the device; k defaults to
+        the file's {arch}.expert_used_count."""
+        g = Gguf(path)
+        arch = g.meta_string("general.architecture") or ""
+        blocks = g.meta_u64(f"{arch}.block_count") or 0
+        layers = [ctx.moe_layer_from_gguf(g, b) for b in range(blocks)
+                  if g.find(f"blk.{b}.ffn_gate_exps.weight") >= 0]
+        if not layers:
+            raise HarCudaError(ERR_ARG, f"{path}: no MoE layers")
+        info = g.tensor("blk.0.ffn_gate_exps.weight") if g.find("blk.0.ffn_gate_exps.weight") >= 0 \
+            else g.tensor_info(g.find(next(t["name"] for t in g.tensors()
+                                           if t["name"].endswith("ffn_gate_exps.weight"))))
+        H, I, E = info["dims"]
+        if k is None:
+            k = g.meta_u64(f"{arch}.expert_used_count") or 8
+        m = cls(ctx, layers, E, H, I, k, flags)
+        m.gguf = g
+        return m
