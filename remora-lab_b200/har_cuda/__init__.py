@@ -299,7 +299,10 @@ class Context:
         that owns them (har-native-qwen35moe.rs:979-1048,1167-1215)."""
         h = C.c_void_p()
         self.check(self.lib.har_cuda_moe_layer_from_gguf(self.handle, g.handle, layer, C.byref(h)))
-        return MoeLayer(self, h, None)
+        H, I, E = g.tensor(f"blk.{layer}.ffn_gate_exps.weight")["dims"]
+        ml = MoeLayer(self, h, None, E, H, I)
+        ml.shared = g.find(f"blk.{layer}.ffn_gate_shexp.weight") >= 0
+        return ml
 
     def q6k_gemv(self, w: "Q4KWeights", expert: int, x, M: int, y):
         """y [M][N] = W_e x for Q6_K weights and f32 activations x [M][K]."""
@@ -361,7 +364,7 @@ class Context:
             self.handle, gate.handle, up.handle, down.handle,
             sg.handle if sg else None, su.handle if su else None, sd.handle if sd else None,
             _dptr(sh_gate_inp), C.byref(h)))
-        return MoeLayer(self, h, (gate, up, down, sg, su, sd, sh_gate_inp))
+        return MoeLayer(self, h, (gate, up, down, sg, su, sd, sh_gate_inp), gate.E, gate.K, gate.N)
 
     def moe_ffn(self, layer: "MoeLayer", x, ids, weights, y, flags: int = 0):
         T, k = ids.shape
@@ -578,8 +581,14 @@ class Gguf:
 
 
 class MoeLayer:
-    def __init__(self, ctx: Context, handle, refs):
+    def __init__(self, ctx: Context, handle, refs, E: int = 0, H: int = 0, I: int = 0):
         self.ctx, self.handle, self.refs = ctx, handle, refs
+        self.E, self.H, self.I = E, H, I
+        self.shared = refs is None or refs[3] is not None
+
+    def expert_bytes(self) -> int:
+        """Q4_K bytes of one expert's gate, up and down."""
+        return 3 * self.I * (self.H // QK_K) * Q4K_BLOCK_BYTES
 
     def free(self):
         if self.handle:
@@ -718,3 +727,120 @@ class CudaMoeModel:
         m = cls(ctx, layers, E, H, I, k, flags)
         m.gguf = g
         return m
+
+
+class StepOutcome:
+    """One sequence's result of a step (har/crates/har-serve/src/adapter.rs:74-113);
+    plain decode steps only: no drafts, consumed_state == next."""
+
+    __slots__ = ("next", "logits", "drafts", "draft_states", "consumed_state")
+
+    def __init__(self, next_state: np.ndarray, logits: np.ndarray):
+        self.next = next_state
+        self.logits = logits
+        self.drafts = []
+        self.draft_states = []
+        self.consumed_state = next_state
+
+
+class CudaMoeServingModel:
+    """A BatchStepModel (har/crates/har-serve/src/adapter.rs:28-72) over
+    har-cuda: the serving seam's contract with the Q4_K MoE stack on the GPU,
+    in the role MoEModel plays for the CPU (har/crates/har-serve/src/moe.rs:182-282).
+
+    One step for a batch of (hidden, token): x = hidden + embed[token]; each
+    MoE layer routes x with its f32 router on the device and adds its output
+    to x (routed_moe + residual, har-native-qwen35moe.rs:1152-1215); logits =
+    out · x with the LM head (Q4_K or Q6_K) GEMV.  Every sequence of the batch
+    shares each weight read: one routed_moe per layer and one GEMV per step
+    for the whole batch.  `next` is the hidden state after the layers (the
+    reference's toy MoEModel returns its input state instead; a real model's
+    next state is its last layer's output).  A GPU error raises HarCudaError
+    (the fail-closed rule of vulkan.rs:18-19); nothing falls back to the CPU.
+    """
+
+    def __init__(self, ctx: Context, layers, embed: np.ndarray, out: Q4KWeights, k: int,
+                 eos: int, routers=None, flags: int = 0):
+        import torch
+        self.ctx, self.layers, self.k, self._eos, self.flags = ctx, list(layers), k, eos, flags
+        self.out = out
+        self.H = out.K
+        self.vocab = out.N
+        dev = torch.device("cuda", ctx.device)
+        self.embed = torch.from_numpy(np.ascontiguousarray(embed, np.float32).reshape(-1, self.H)).to(dev)
+        if self.embed.shape[0] != self.vocab:
+            raise HarCudaError(ERR_GEOMETRY, "embed must be [vocab][H] with the LM head's vocab")
+        self.routers = list(routers) if routers is not None else [None] * len(self.layers)
+        if len(self.routers) != len(self.layers):
+            raise HarCudaError(ERR_GEOMETRY, "one router (or None: the layer's own) per layer")
+        self._torch = torch
+        self._dev = dev
+        self.last_routes = None  # [(ids [B][k], weights [B][k]) per layer] of the last step
+        self.telemetry = {"positions": 0, "expert_reads": 0, "shared_reads": 0}
+
+    def _step_device(self, x):
+        torch = self._torch
+        B = x.shape[0]
+        routes = []
+        for layer, router in zip(self.layers, self.routers):
+            ids = torch.empty((B, self.k), dtype=torch.int32, device=self._dev)
+            w = torch.empty((B, self.k), dtype=torch.float32, device=self._dev)
+            y = torch.empty_like(x)
+            self.ctx.routed_moe(layer, router, x, self.k, ids, w, y, self.flags | MOE_ADD_RESIDUAL)
+            routes.append((ids, w))
+            x = y
+        logits = torch.empty((B, self.vocab), dtype=torch.float32, device=self._dev)
+        if self.out.ggml_type == GGML_Q6_K:
+            self.ctx.q6k_gemv(self.out, 0, x, B, logits)
+        else:
+            self.ctx.q4k_gemv(self.out, 0, x, ACT_F32, B, logits)
+        return x, logits, routes
+
+    def batch_step(self, inputs):
+        """BatchStepModel::batch_step: inputs [(hidden [H], token)] ->
+        [StepOutcome], one per input, in order."""
+        torch = self._torch
+        if not inputs:
+            return []
+        h = np.stack([np.asarray(hv, np.float32).reshape(self.H) for hv, _ in inputs])
+        tok = np.asarray([t for _, t in inputs], np.int64)
+        if tok.min() < 0 or tok.max() >= self.vocab:
+            raise HarCudaError(ERR_ARG, "token id outside the vocabulary")
+        x = torch.from_numpy(h).to(self._dev) + self.embed[torch.from_numpy(tok).to(self._dev)]
+        x, logits, routes = self._step_device(x.contiguous())
+        nxt, lg = x.cpu().numpy(), logits.cpu().numpy()
+        self.ctx.synchronize()
+        self.last_routes = [(i.cpu().numpy(), w.cpu().numpy()) for i, w in routes]
+        self.telemetry["positions"] += len(inputs)
+        self.telemetry["expert_reads"] += sum(len(np.unique(i)) for i, _ in self.last_routes)
+        self.telemetry["shared_reads"] += len(self.layers)
+        return [StepOutcome(nxt[i], lg[i]) for i in range(len(inputs))]
+
+    def prefill_batch(self, inputs):
+        """The trait's default prefill (adapter.rs:42-61): batch_step folded
+        one token at a time per sequence."""
+        out = []
+        for h, tokens in inputs:
+            hidden = np.asarray(h, np.float32)
+            states, logits = [], []
+            for t in tokens:
+                o = self.batch_step([(hidden, t)])[0]
+                states.append(o.next)
+                logits.append(o.logits)
+                hidden = o.next
+            out.append((states, logits))
+        return out
+
+    def initial_hidden(self) -> np.ndarray:
+        return np.zeros(self.H, np.float32)
+
+    def eos(self) -> int:
+        return self._eos
+
+    def weight_bytes_per_row(self) -> int:
+        """Per-token worst case, as MoEModel counts it (moe.rs:274-281): the
+        shared expert plus top_k routed experts per layer, plus the LM head."""
+        total = self.out.nbytes
+        for layer in self.layers:
+            total += (self.k + (1 if layer.shared else 0)) * layer.expert_bytes()
+        return total
