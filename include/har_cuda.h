@@ -75,7 +75,9 @@ int32_t har_cuda_ctx_create(int32_t device, har_cuda_ctx **out);
 int32_t har_cuda_ctx_destroy(har_cuda_ctx *ctx);
 /* Copies the last error message (NUL-terminated, truncated to len). */
 int32_t har_cuda_last_error(const har_cuda_ctx *ctx, char *buf, size_t len);
-/* Launch on a caller-owned cudaStream_t (NULL restores the context's own). */
+/* Launch on a caller-owned cudaStream_t (NULL restores the context's own,
+ * a non-blocking stream; pass cudaStreamLegacy, 0x1, to run on the legacy
+ * default stream and order with other default-stream work). */
 int32_t har_cuda_ctx_set_stream(har_cuda_ctx *ctx, void *cuda_stream);
 /* Experts with at least `min_tokens` tokens in a moe_ffn call run on the
  * tensor-core (tcgen05) kernels, the rest on the CUDA-core GEMV kernels;
@@ -238,7 +240,8 @@ int32_t har_cuda_moe_stack(har_cuda_ctx *ctx, const har_cuda_moe_layer *const *l
 /* The stack with host buffers (x [T][H], ids/weights [L][T][k], y [T][H]):
  * copies in, runs, copies out and waits (bounded).  A call repeated with the
  * same layers, shapes, flags and stream replays a CUDA graph of its device work
- * (captured on the second such call); the inputs are read afresh every call. */
+ * (captured on the second such call; not on the legacy or per-thread default
+ * stream, where capture is not allowed); the inputs are read afresh every call. */
 int32_t har_cuda_moe_stack_host(har_cuda_ctx *ctx, const har_cuda_moe_layer *const *layers,
                                 int32_t L, const float *x_host, int64_t T, int32_t k,
                                 const int32_t *ids_host, const float *weights_host,

@@ -716,7 +716,10 @@ int32_t har_cuda_moe_stack_host(har_cuda_ctx *ctx, const har_cuda_moe_layer *con
     g.stream = ctx->stream;
   }
   g.epoch = ctx->epoch;
-  if (!g.exec && g.seen >= 1 && !ctx->prof_on) {
+  // stream capture is not allowed on the legacy or per-thread default stream
+  // (handles 0, 0x1, 0x2): there every call runs eagerly
+  const bool capturable = (uintptr_t)ctx->stream > (uintptr_t)0x2;
+  if (!g.exec && g.seen >= 1 && !ctx->prof_on && capturable) {
     cudaGraph_t graph = nullptr;
     bool ok = cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal) == cudaSuccess;
     const int32_t st = ok ? enqueue() : HAR_CUDA_OK;

@@ -34,6 +34,7 @@ GGML_F32, GGML_Q4_K, GGML_Q6_K = 0, 12, 14
 BLOCK_BYTES = {GGML_Q4_K: Q4K_BLOCK_BYTES, GGML_Q6_K: Q6K_BLOCK_BYTES}
 
 OK = 0
+CUDA_STREAM_LEGACY = 0x1  # cudaStreamLegacy: the legacy default stream's handle value
 ERR_ARG, ERR_GEOMETRY, ERR_CUDA, ERR_NCCL, ERR_TIMEOUT = -1, -2, -3, -4, -5
 ERR_NOT_INIT, ERR_OOM, ERR_UNSUPPORTED, ERR_DEVICE = -6, -7, -8, -9
 STATUS_NAMES = {0: "OK", -1: "ARG", -2: "GEOMETRY", -3: "CUDA", -4: "NCCL", -5: "TIMEOUT",
@@ -188,9 +189,14 @@ class Context:
             self.bind_torch_stream()
 
     def bind_torch_stream(self):
+        """Launch on torch's current stream of the device.  torch's default
+        stream is the legacy default stream, whose handle is 0; the ABI reads
+        NULL as "the context's own stream", so it is passed as
+        cudaStreamLegacy (0x1), which orders with torch's default-stream work."""
         import torch
         s = torch.cuda.current_stream(self.device)
-        self.check(self.lib.har_cuda_ctx_set_stream(self.handle, C.c_void_p(s.cuda_stream)))
+        self.check(self.lib.har_cuda_ctx_set_stream(self.handle,
+                                                    C.c_void_p(s.cuda_stream or CUDA_STREAM_LEGACY)))
 
     def set_tc_min_tokens(self, n: int):
         """Experts with >= n tokens take the tensor-core kernels (0 = default)."""
@@ -675,6 +681,7 @@ class CudaMoeModel:
         xd = self._dev(x.reshape(1, -1), torch.float32)
         y = torch.empty((1, w.N), dtype=torch.float32, device=xd.device)
         self.ctx.q4k_gemv(w, expert, xd, ACT_F32, 1, y)
+        self.ctx.synchronize()
         return y.cpu().numpy()[0]
 
     def compose_moe_route(self, layer: int, x: np.ndarray, experts, weights) -> np.ndarray:
@@ -699,6 +706,7 @@ class CudaMoeModel:
             self.ctx.check(self.ctx.lib.har_cuda_routed_moe(
                 self.ctx.handle, self.layers[layer].handle, None, _dptr(xd), 1, self.k,
                 _dptr(ids), _dptr(w), _dptr(y), self.flags))
+            self.ctx.synchronize()
             return y.cpu().numpy()[0], ids.cpu().numpy()[0], w.cpu().numpy()[0]
         lg = self._dev(np.asarray(router_logits, np.float32).reshape(1, -1), torch.float32)
         ids = torch.empty((1, self.k), dtype=torch.int32, device=lg.device)
@@ -808,8 +816,8 @@ class CudaMoeServingModel:
             raise HarCudaError(ERR_ARG, "token id outside the vocabulary")
         x = torch.from_numpy(h).to(self._dev) + self.embed[torch.from_numpy(tok).to(self._dev)]
         x, logits, routes = self._step_device(x.contiguous())
-        nxt, lg = x.cpu().numpy(), logits.cpu().numpy()
         self.ctx.synchronize()
+        nxt, lg = x.cpu().numpy(), logits.cpu().numpy()
         self.last_routes = [(i.cpu().numpy(), w.cpu().numpy()) for i, w in routes]
         self.telemetry["positions"] += len(inputs)
         self.telemetry["expert_reads"] += sum(len(np.unique(i)) for i, _ in self.last_routes)

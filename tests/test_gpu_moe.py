@@ -193,14 +193,22 @@ def test_stack_host_repeated_calls(ctx, alice):
         return y.cpu().numpy()
 
     f = har_cuda.MOE_ADD_RESIDUAL
-    for call in range(4):
-        x = haro.normal_f32(60 + call, 0, 8 * H).reshape(8, H)
-        rw = [haro.zipf_routing(70 + 2 * call + l, 8, 64, K) for l in range(2)]
-        ids = np.stack([a for a, _ in rw])
-        w = np.stack([b for _, b in rw])
-        flags = f if call < 3 else f | har_cuda.MOE_FORCE_GEMV
-        yh = ctx.moe_stack_host(layers, x, ids, w, flags)
-        assert np.array_equal(yh, device_stack(x, ids, w, flags)), call
+    # graph capture needs a real stream (not the legacy default one)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        ctx.bind_torch_stream()
+        try:
+            for call in range(4):
+                x = haro.normal_f32(60 + call, 0, 8 * H).reshape(8, H)
+                rw = [haro.zipf_routing(70 + 2 * call + l, 8, 64, K) for l in range(2)]
+                ids = np.stack([a for a, _ in rw])
+                w = np.stack([b for _, b in rw])
+                flags = f if call < 3 else f | har_cuda.MOE_FORCE_GEMV
+                yh = ctx.moe_stack_host(layers, x, ids, w, flags)
+                assert np.array_equal(yh, device_stack(x, ids, w, flags)), call
+        finally:
+            torch.cuda.synchronize()
+    ctx.bind_torch_stream()
 
 
 def test_moe_argument_errors(ctx, alice):
