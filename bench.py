@@ -695,7 +695,7 @@ def run_gemv_roofline(args, torch):
                             "ms_per_gemv": res["f32"]["ms_per_gemv"]},
         "rows_65536": {"weight_gbs": res["q8k_small"]["weight_gbs"], "frac": res["q8k_small"]["frac"],
                        "ms_per_gemv": res["q8k_small"]["ms_per_gemv"]},
-        "q6k_f32_65536": {"kernel": "q6k_gemv_kernel", "weight_gbs": round(gbs6, 1),
+        "q6k_f32_65536": {"kernel": "q6k_gemv_stream_kernel", "weight_gbs": round(gbs6, 1),
                           "frac": round(gbs6 / hbm, 4), "ms_per_gemv": round(ms6, 5),
                           "rows": n6, "K": K},
         "clocks": q["clocks"],

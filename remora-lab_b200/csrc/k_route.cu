@@ -17,6 +17,7 @@
 // counts per expert with __match_any_sync, a scan turns counts into offsets,
 // and a second pass writes positions.
 #include "har_internal.cuh"
+#include "tc_ptx.cuh"
 
 namespace har {
 
@@ -367,9 +368,89 @@ __global__ void __launch_bounds__(RL_WARPS * 32) router_logits_kernel(
   }
 }
 
+// router_logits_pipe_kernel: the same chains (bit-identical results) for H a
+// multiple of 4, with the slices of W and x brought into shared memory by
+// cp.async through an RL_S-deep ring, so the L2 latency of slice i+RL_S-1
+// overlaps the arithmetic on slice i and the chain runs at its own latency.
+// Slices are stored untransposed, [row][h] with a row stride of RL_LD floats:
+// lane e reads a float4 of its row (rows 68 floats apart put the eight lanes
+// of a quarter-warp on distinct banks), a warp's token rows are broadcast.
+constexpr int RL_S = 4, RL_LD = RL_KC + 4;
+constexpr int RL_STAGE = 2 * RL_E * RL_LD;  // floats per stage: W rows, then x rows
+static_assert(RL_TT == RL_E, "the loader fills W and x slices with one index space");
+
+__global__ void __launch_bounds__(RL_WARPS * 32) router_logits_pipe_kernel(
+    const float *__restrict__ W, const float *__restrict__ x, int64_t T, int E, int H,
+    float *__restrict__ logits) {
+  extern __shared__ __align__(16) float rls[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int e0 = blockIdx.x * RL_E;
+  const int64_t t0 = (int64_t)blockIdx.y * RL_TT;
+  const int nchunk = (H + RL_KC - 1) / RL_KC;
+  // issue slice `ch` into ring slot ch % RL_S (16-byte copies; rows past E or
+  // T and columns past H are zero-filled and never read by the arithmetic)
+  auto load = [&](int ch) {
+    float *ws = rls + (ch % RL_S) * RL_STAGE, *xs = ws + RL_E * RL_LD;
+    const int h0 = ch * RL_KC;
+    for (int i = threadIdx.x; i < 2 * RL_E * (RL_KC / 4); i += RL_WARPS * 32) {
+      const bool isx = i >= RL_E * (RL_KC / 4);
+      const int j = isx ? i - RL_E * (RL_KC / 4) : i;
+      const int r = j / (RL_KC / 4), c = (j % (RL_KC / 4)) * 4;
+      const bool ok = (isx ? t0 + r < T : e0 + r < E) && h0 + c < H;
+      const float *src = !ok ? W : isx ? x + (t0 + r) * H + h0 + c : W + (int64_t)(e0 + r) * H + h0 + c;
+      tc::cp_async16((isx ? xs : ws) + r * RL_LD + c, src, ok ? 16u : 0u);
+    }
+  };
+#pragma unroll
+  for (int ch = 0; ch < RL_S - 1; ++ch) {
+    if (ch < nchunk) load(ch);
+    tc::cp_async_commit();
+  }
+  float s[RL_TPT];
+#pragma unroll
+  for (int j = 0; j < RL_TPT; ++j) s[j] = 0.0f;
+  for (int ch = 0; ch < nchunk; ++ch) {
+    tc::cp_async_wait<RL_S - 2>();  // slice ch has landed (this thread's copies)
+    __syncthreads();                // ... everyone's, and slice ch-1 is consumed
+    if (ch + RL_S - 1 < nchunk) load(ch + RL_S - 1);
+    tc::cp_async_commit();          // (an empty group keeps the count uniform)
+    const float *ws = rls + (ch % RL_S) * RL_STAGE, *xs = ws + RL_E * RL_LD;
+    const float *wr = ws + lane * RL_LD, *xr = xs + warp * RL_TPT * RL_LD;
+    const int kc = min(RL_KC, H - ch * RL_KC);
+    for (int c = 0; c < kc; c += 4) {
+      const float4 w = *reinterpret_cast<const float4 *>(wr + c);
+#pragma unroll
+      for (int j = 0; j < RL_TPT; ++j) {
+        const float4 v = *reinterpret_cast<const float4 *>(xr + j * RL_LD + c);
+        s[j] = __fadd_rn(s[j], __fmul_rn(w.x, v.x));
+        s[j] = __fadd_rn(s[j], __fmul_rn(w.y, v.y));
+        s[j] = __fadd_rn(s[j], __fmul_rn(w.z, v.z));
+        s[j] = __fadd_rn(s[j], __fmul_rn(w.w, v.w));
+      }
+    }
+  }
+  tc::cp_async_wait_all();
+  const int e = e0 + lane;
+  if (e < E) {
+#pragma unroll
+    for (int j = 0; j < RL_TPT; ++j) {
+      const int64_t t = t0 + warp * RL_TPT + j;
+      if (t < T) logits[t * E + e] = s[j];
+    }
+  }
+}
+
 int32_t launch_router_logits(har_cuda_ctx *ctx, const float *W, int E, int H, const float *x,
                              int64_t T, float *logits) {
   const dim3 grid((unsigned)((E + RL_E - 1) / RL_E), (unsigned)((T + RL_TT - 1) / RL_TT));
+  if (H % 4 == 0 && ((uintptr_t)W & 15u) == 0 && ((uintptr_t)x & 15u) == 0) {
+    const size_t smem = (size_t)RL_S * RL_STAGE * sizeof(float);
+    cudaFuncSetAttribute(router_logits_pipe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)smem);
+    prof_begin(ctx);
+    router_logits_pipe_kernel<<<grid, RL_WARPS * 32, smem, ctx->stream>>>(W, x, T, E, H, logits);
+    return check_launch(ctx, "router_logits_pipe_kernel");
+  }
   prof_begin(ctx);
   router_logits_kernel<<<grid, RL_WARPS * 32, 0, ctx->stream>>>(W, x, T, E, H, logits);
   return check_launch(ctx, "router_logits_kernel");

@@ -125,6 +125,9 @@ __device__ __forceinline__ void cp_async16(void *dst, const void *src, uint32_t 
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+// waits until at most N of this thread's committed groups are still in flight
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 // Generic-proxy shared-memory writes become visible to the tensor core (async proxy).
 __device__ __forceinline__ void fence_proxy_async_smem() {

@@ -72,7 +72,10 @@ def test_q6k_zero_block_dot_is_zero():
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("N,K,M", [(1, 256, 1), (7, 512, 2), (333, 768, 3), (4096, 4096, 1),
-                                   (2048, 2048, 5), (64, 5120, 9), (300, 2048, 16)])
+                                   (2048, 2048, 5), (64, 5120, 9), (300, 2048, 16),
+                                   # batch-1 rows streamed through shared memory (K % 2048 == 0):
+                                   # a ragged last stage, a two-stage ring, fewer rows than SMs
+                                   (5000, 2048, 1), (150, 6144, 1), (7, 2048, 1)])
 def test_q6k_gemv_matches_restatement(N, K, M):
     import torch
     import har_cuda
