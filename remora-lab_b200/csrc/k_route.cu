@@ -376,6 +376,24 @@ __global__ void __launch_bounds__(RL_WARPS * 32) router_logits_kernel(
 // lane e reads a float4 of its row (rows 68 floats apart put the eight lanes
 // of a quarter-warp on distinct banks), a warp's token rows are broadcast.
 constexpr int RL_S = 4, RL_LD = RL_KC + 4;
+
+// NT of a warp's token chains over one staged slice (kc values, a multiple of 4)
+template <int NT>
+__device__ __forceinline__ void rl_slice(const float *wr, const float *xr, int kc,
+                                         float (&s)[RL_TPT]) {
+#pragma unroll 4
+  for (int c = 0; c < kc; c += 4) {
+    const float4 w = *reinterpret_cast<const float4 *>(wr + c);
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      const float4 v = *reinterpret_cast<const float4 *>(xr + j * RL_LD + c);
+      s[j] = __fadd_rn(s[j], __fmul_rn(w.x, v.x));
+      s[j] = __fadd_rn(s[j], __fmul_rn(w.y, v.y));
+      s[j] = __fadd_rn(s[j], __fmul_rn(w.z, v.z));
+      s[j] = __fadd_rn(s[j], __fmul_rn(w.w, v.w));
+    }
+  }
+}
 constexpr int RL_STAGE = 2 * RL_E * RL_LD;  // floats per stage: W rows, then x rows
 static_assert(RL_TT == RL_E, "the loader fills W and x slices with one index space");
 
@@ -409,6 +427,8 @@ __global__ void __launch_bounds__(RL_WARPS * 32) router_logits_pipe_kernel(
   float s[RL_TPT];
 #pragma unroll
   for (int j = 0; j < RL_TPT; ++j) s[j] = 0.0f;
+  const int64_t left = T - (t0 + warp * RL_TPT);
+  const int nt = left <= 0 ? 0 : (left < RL_TPT ? (int)left : RL_TPT);
   for (int ch = 0; ch < nchunk; ++ch) {
     tc::cp_async_wait<RL_S - 2>();  // slice ch has landed (this thread's copies)
     __syncthreads();                // ... everyone's, and slice ch-1 is consumed
@@ -417,16 +437,13 @@ __global__ void __launch_bounds__(RL_WARPS * 32) router_logits_pipe_kernel(
     const float *ws = rls + (ch % RL_S) * RL_STAGE, *xs = ws + RL_E * RL_LD;
     const float *wr = ws + lane * RL_LD, *xr = xs + warp * RL_TPT * RL_LD;
     const int kc = min(RL_KC, H - ch * RL_KC);
-    for (int c = 0; c < kc; c += 4) {
-      const float4 w = *reinterpret_cast<const float4 *>(wr + c);
-#pragma unroll
-      for (int j = 0; j < RL_TPT; ++j) {
-        const float4 v = *reinterpret_cast<const float4 *>(xr + j * RL_LD + c);
-        s[j] = __fadd_rn(s[j], __fmul_rn(w.x, v.x));
-        s[j] = __fadd_rn(s[j], __fmul_rn(w.y, v.y));
-        s[j] = __fadd_rn(s[j], __fmul_rn(w.z, v.z));
-        s[j] = __fadd_rn(s[j], __fmul_rn(w.w, v.w));
-      }
+    // only the chains of tokens below T: a warp past T only helps load
+    switch (nt) {
+      case 4: rl_slice<4>(wr, xr, kc, s); break;
+      case 3: rl_slice<3>(wr, xr, kc, s); break;
+      case 2: rl_slice<2>(wr, xr, kc, s); break;
+      case 1: rl_slice<1>(wr, xr, kc, s); break;
+      default: break;
     }
   }
   tc::cp_async_wait_all();
