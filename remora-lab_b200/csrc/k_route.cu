@@ -38,44 +38,55 @@ __global__ void __launch_bounds__(128) route_topk_kernel(const float *__restrict
   for (int i = lane; i < E; i += 32) mx = fmaxf(mx, l[i]);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+#pragma unroll 4
   for (int i = lane; i < E; i += 32) p[i] = (float)exp((double)__fsub_rn(l[i], mx));
   __syncwarp();
   float den = 0.0f;
-  if (lane == 0) {
-    for (int i = 0; i < E; ++i) den = __fadd_rn(den, p[i]);  // exps.iter().sum()
+  if (lane == 0) {  // exps.iter().sum(): one chain in index order
+    int i = 0;
+    if (E % 4 == 0) {  // the warp's row is then 16-byte aligned: four values per load
+      const float4 *p4 = reinterpret_cast<const float4 *>(p);
+#pragma unroll 8
+      for (; i < E; i += 4) {
+        const float4 v = p4[i >> 2];
+        den = __fadd_rn(den, v.x);
+        den = __fadd_rn(den, v.y);
+        den = __fadd_rn(den, v.z);
+        den = __fadd_rn(den, v.w);
+      }
+    }
+    for (; i < E; ++i) den = __fadd_rn(den, p[i]);
     den = fmaxf(den, ROUTER_EPS);
   }
   den = __shfl_sync(0xffffffffu, den, 0);
+#pragma unroll 4
   for (int i = lane; i < E; i += 32) p[i] = __fdiv_rn(p[i], den);
   __syncwarp();
-  // k rounds of warp arg-max over (p desc, index asc); selected entries are
-  // marked by setting their sign bit (all p >= +0, so -p never wins).
+  // k rounds of warp arg-max over (p desc, index asc).  Every p is >= +0, so
+  // its bits order like its value (and a positive NaN above +inf, as
+  // total_cmp orders it); selected entries are marked by their sign bit.
+  // Each lane's best (scanned in index order, strict >: the lowest index of
+  // a tie) goes into one warp max of the bits and one warp min of the index
+  // among the lanes holding that max.
   int sel_id = 0;
   float sel_p = 0.0f;
   for (int s = 0; s < k; ++s) {
-    float bp = -1.0f;
+    uint32_t bb = 0;
     int bi = 0x7fffffff;
     for (int i = lane; i < E; i += 32) {
-      const float v = p[i];
-      if (!(__float_as_uint(v) >> 31) && (v > bp || (v == bp && i < bi))) {
-        bp = v;
+      const uint32_t v = __float_as_uint(p[i]);
+      if (v < 0x80000000u && (v > bb || bi == 0x7fffffff)) {
+        bb = v;
         bi = i;
       }
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float op = __shfl_xor_sync(0xffffffffu, bp, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (op > bp || (op == bp && oi < bi)) {
-        bp = op;
-        bi = oi;
-      }
-    }
+    const uint32_t mb = __reduce_max_sync(0xffffffffu, bb);
+    const int wi = (int)__reduce_min_sync(0xffffffffu, bb == mb ? (uint32_t)bi : 0x7fffffffu);
     if (lane == s) {
-      sel_id = bi;
-      sel_p = bp;
+      sel_id = wi;
+      sel_p = __uint_as_float(mb);
     }
-    if (lane == 0) p[bi] = __uint_as_float(__float_as_uint(bp) | 0x80000000u);
+    if (lane == 0) p[wi] = __uint_as_float(mb | 0x80000000u);
     __syncwarp();
   }
   float tot = 0.0f;
@@ -457,10 +468,86 @@ __global__ void __launch_bounds__(RL_WARPS * 32) router_logits_pipe_kernel(
   }
 }
 
+// router_logits_small_kernel: decode-sized batches (T <= RS_T).  The same
+// chains again, spread thin: one warp per CTA owns 8 experts x 4 tokens, lane
+// (expert e0 + lane/4, token lane%4), so E/8 CTAs share the router's reads.
+// A lone warp per SM has nothing to hide its latencies behind, so the kernel
+// keeps the instructions around each chain's dependent adds few: 128-wide
+// slices through a 6-deep cp.async ring, each lane copying one fixed 16-byte
+// column of all 12 staged rows (8 router rows, 4 token rows) from row pointers
+// computed once, and a fully unrolled pass over a full slice.
+constexpr int RS_E = 8, RS_T = 4, RS_ROWS = RS_E + RS_T, RS_KC = 128, RS_LD = RS_KC + 4, RS_S = 6;
+
+__global__ void __launch_bounds__(32) router_logits_small_kernel(
+    const float *__restrict__ W, const float *__restrict__ x, int64_t T, int E, int H,
+    float *__restrict__ logits) {
+  __shared__ __align__(16) float rss[RS_S][RS_ROWS * RS_LD];
+  const int lane = threadIdx.x, el = lane >> 2, tl = lane & 3;
+  const int e0 = blockIdx.x * RS_E;
+  const int nchunk = (H + RS_KC - 1) / RS_KC;
+  // this lane's column of every staged row, and which rows exist
+  const float *src[RS_ROWS];
+  uint32_t rows_ok = 0;
+#pragma unroll
+  for (int r = 0; r < RS_ROWS; ++r) {
+    const bool ok = r < RS_E ? e0 + r < E : (int64_t)(r - RS_E) < T;
+    src[r] = (r < RS_E ? W + (int64_t)(ok ? e0 + r : 0) * H
+                       : x + (int64_t)(ok ? r - RS_E : 0) * H) + 4 * lane;
+    rows_ok |= (ok ? 1u : 0u) << r;
+  }
+  auto load = [&](int ch) {
+    float *st = rss[ch % RS_S] + 4 * lane;
+    const int h = ch * RS_KC + 4 * lane;
+    const uint32_t ok = h < H ? rows_ok : 0u;
+#pragma unroll
+    for (int r = 0; r < RS_ROWS; ++r)
+      tc::cp_async16(st + r * RS_LD, (ok >> r) & 1u ? src[r] + ch * RS_KC : W,
+                     (ok >> r) & 1u ? 16u : 0u);
+  };
+#pragma unroll
+  for (int ch = 0; ch < RS_S - 1; ++ch) {
+    if (ch < nchunk) load(ch);
+    tc::cp_async_commit();
+  }
+  float s = 0.0f;
+  for (int ch = 0; ch < nchunk; ++ch) {
+    tc::cp_async_wait<RS_S - 2>();
+    __syncwarp();
+    if (ch + RS_S - 1 < nchunk) load(ch + RS_S - 1);
+    tc::cp_async_commit();
+    const float *wr = rss[ch % RS_S] + el * RS_LD, *xr = rss[ch % RS_S] + (RS_E + tl) * RS_LD;
+    const int kc = min(RS_KC, H - ch * RS_KC);
+    auto step = [&](int c) {
+      const float4 w = *reinterpret_cast<const float4 *>(wr + c);
+      const float4 v = *reinterpret_cast<const float4 *>(xr + c);
+      s = __fadd_rn(s, __fmul_rn(w.x, v.x));
+      s = __fadd_rn(s, __fmul_rn(w.y, v.y));
+      s = __fadd_rn(s, __fmul_rn(w.z, v.z));
+      s = __fadd_rn(s, __fmul_rn(w.w, v.w));
+    };
+    if (kc == RS_KC) {
+#pragma unroll
+      for (int c = 0; c < RS_KC; c += 4) step(c);
+    } else {
+      for (int c = 0; c < kc; c += 4) step(c);
+    }
+    __syncwarp();  // the slot is refilled at the next iteration
+  }
+  tc::cp_async_wait_all();
+  if (e0 + el < E && tl < T) logits[(int64_t)tl * E + e0 + el] = s;
+}
+
 int32_t launch_router_logits(har_cuda_ctx *ctx, const float *W, int E, int H, const float *x,
                              int64_t T, float *logits) {
   const dim3 grid((unsigned)((E + RL_E - 1) / RL_E), (unsigned)((T + RL_TT - 1) / RL_TT));
-  if (H % 4 == 0 && ((uintptr_t)W & 15u) == 0 && ((uintptr_t)x & 15u) == 0) {
+  const bool vec = H % 4 == 0 && ((uintptr_t)W & 15u) == 0 && ((uintptr_t)x & 15u) == 0;
+  if (vec && T <= RS_T) {
+    prof_begin(ctx);
+    router_logits_small_kernel<<<(unsigned)((E + RS_E - 1) / RS_E), 32, 0, ctx->stream>>>(
+        W, x, T, E, H, logits);
+    return check_launch(ctx, "router_logits_small_kernel");
+  }
+  if (vec) {
     const size_t smem = (size_t)RL_S * RL_STAGE * sizeof(float);
     cudaFuncSetAttribute(router_logits_pipe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)smem);
