@@ -216,3 +216,35 @@ def test_weights_from_gguf_q4k_q6k_and_f32(tmp_path):
     w6.free()
     g.close()
     ctx.close()
+
+
+class _DeviceBytes:
+    """A read-only view of n device bytes at ptr, for torch.as_tensor."""
+
+    def __init__(self, ptr, n):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "|u1", "data": (ptr, True),
+                                         "version": 3}
+
+
+@pytest.mark.gpu
+def test_large_tensor_streams_through_both_stages_byte_exact(tmp_path):
+    """A tensor larger than one 64 MiB staging buffer arrives in pieces that
+    alternate between the two pinned buffers (an Alice `*_exps` tensor is
+    302 MB); the device copy equals the file's bytes exactly."""
+    import torch
+
+    ctx = har_cuda.Context(0)
+    E, N, K = 160, 512, 2048                      # 160 x 589,824 B = 94.4 MB: two pieces
+    nbytes = E * N * (K // 256) * 144
+    payload = np.random.default_rng(5).integers(0, 256, nbytes, dtype=np.uint8)
+    p = tmp_path / "big.gguf"
+    write_gguf(p, [], [("blk.0.ffn_up_exps.weight", [K, N, E], GT_Q4K, payload)])
+    g = har_cuda.Gguf(str(p))
+    w = ctx.weights_from_gguf(g, "blk.0.ffn_up_exps.weight")
+    torch.cuda.synchronize()
+    ptr = ctx.lib.har_cuda_weights_device_ptr(w.handle)
+    got = torch.as_tensor(_DeviceBytes(ptr, nbytes), device="cuda").cpu().numpy()
+    assert np.array_equal(got, payload)
+    w.free()
+    g.close()
+    ctx.close()
