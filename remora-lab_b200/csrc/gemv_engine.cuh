@@ -177,10 +177,13 @@ __device__ __forceinline__ float chunk_dot(const WChunk &w, int chunk, const Lan
   float slo = 0.0f, shi = 0.0f;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
+    // the word's four low (high) nibbles, one per byte; each becomes an exact
+    // f32 by a byte permute into the mantissa of 2^23 and one subtraction
+    const uint32_t lo = q[i] & 0x0F0F0F0Fu, hi = (q[i] >> 4) & 0x0F0F0F0Fu;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      slo = fmaf(u4_to_f32((q[i] >> (8 * j)) & 15u), a.lo[4 * i + j], slo);
-      shi = fmaf(u4_to_f32((q[i] >> (8 * j + 4)) & 15u), a.hi[4 * i + j], shi);
+      slo = fmaf(u8_to_f32(lo, j), a.lo[4 * i + j], slo);
+      shi = fmaf(u8_to_f32(hi, j), a.hi[4 * i + j], shi);
     }
   }
   const ChunkScales s = chunk_scales(w.hdr, chunk & 3);

@@ -79,6 +79,10 @@ __device__ __forceinline__ ChunkScales chunk_scales(uint4 hdr, int c) {
 __device__ __forceinline__ float u4_to_f32(uint32_t v) {
   return __int_as_float(0x4B000000 | v) - 8388608.0f;
 }
+// byte j (0..3) of v as an exact f32 (the same value as u4_to_f32 of that byte)
+__device__ __forceinline__ float u8_to_f32(uint32_t v, int j) {
+  return __uint_as_float(__byte_perm(v, 0x4B000000u, 0x7440u | (uint32_t)j)) - 8388608.0f;
+}
 
 __device__ __forceinline__ uint4 ldg_nc_v4(const void *p) {
   uint4 r;

@@ -219,10 +219,10 @@ def test_weights_from_gguf_q4k_q6k_and_f32(tmp_path):
 
 
 class _DeviceBytes:
-    """A read-only view of n device bytes at ptr, for torch.as_tensor."""
+    """A view of n device bytes at ptr, for torch.as_tensor (only read here)."""
 
     def __init__(self, ptr, n):
-        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "|u1", "data": (ptr, True),
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "|u1", "data": (ptr, False),
                                          "version": 3}
 
 
