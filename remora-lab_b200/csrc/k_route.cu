@@ -389,9 +389,9 @@ __global__ void __launch_bounds__(RL_WARPS * 32) router_logits_kernel(
 constexpr int RL_S = 4, RL_LD = RL_KC + 4;
 
 // NT of a warp's token chains over one staged slice (kc values, a multiple of 4)
-template <int NT>
+template <int NT, int TPT>
 __device__ __forceinline__ void rl_slice(const float *wr, const float *xr, int kc,
-                                         float (&s)[RL_TPT]) {
+                                         float (&s)[TPT]) {
 #pragma unroll 4
   for (int c = 0; c < kc; c += 4) {
     const float4 w = *reinterpret_cast<const float4 *>(wr + c);
@@ -405,29 +405,35 @@ __device__ __forceinline__ void rl_slice(const float *wr, const float *xr, int k
     }
   }
 }
-constexpr int RL_STAGE = 2 * RL_E * RL_LD;  // floats per stage: W rows, then x rows
-static_assert(RL_TT == RL_E, "the loader fills W and x slices with one index space");
+// floats per stage: 32 router rows, then the CTA's 8 * TPT token rows
+template <int TPT>
+__host__ __device__ constexpr int rl_stage() { return (RL_E + RL_WARPS * TPT) * RL_LD; }
 
+// TPT tokens per thread: 4 for large T (fewer router reads per term), 2 up to
+// T = 512 (twice the CTAs, so the SMs hold more warps to hide latency with).
+template <int TPT>
 __global__ void __launch_bounds__(RL_WARPS * 32) router_logits_pipe_kernel(
     const float *__restrict__ W, const float *__restrict__ x, int64_t T, int E, int H,
     float *__restrict__ logits) {
+  constexpr int TT = RL_WARPS * TPT, STAGE = rl_stage<TPT>();
   extern __shared__ __align__(16) float rls[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int e0 = blockIdx.x * RL_E;
-  const int64_t t0 = (int64_t)blockIdx.y * RL_TT;
+  const int64_t t0 = (int64_t)blockIdx.y * TT;
   const int nchunk = (H + RL_KC - 1) / RL_KC;
   // issue slice `ch` into ring slot ch % RL_S (16-byte copies; rows past E or
   // T and columns past H are zero-filled and never read by the arithmetic)
   auto load = [&](int ch) {
-    float *ws = rls + (ch % RL_S) * RL_STAGE, *xs = ws + RL_E * RL_LD;
+    float *st = rls + (ch % RL_S) * STAGE;
     const int h0 = ch * RL_KC;
-    for (int i = threadIdx.x; i < 2 * RL_E * (RL_KC / 4); i += RL_WARPS * 32) {
-      const bool isx = i >= RL_E * (RL_KC / 4);
-      const int j = isx ? i - RL_E * (RL_KC / 4) : i;
-      const int r = j / (RL_KC / 4), c = (j % (RL_KC / 4)) * 4;
-      const bool ok = (isx ? t0 + r < T : e0 + r < E) && h0 + c < H;
-      const float *src = !ok ? W : isx ? x + (t0 + r) * H + h0 + c : W + (int64_t)(e0 + r) * H + h0 + c;
-      tc::cp_async16((isx ? xs : ws) + r * RL_LD + c, src, ok ? 16u : 0u);
+    for (int i = threadIdx.x; i < (RL_E + TT) * (RL_KC / 4); i += RL_WARPS * 32) {
+      const int r = i / (RL_KC / 4), c = (i % (RL_KC / 4)) * 4;  // staged row r
+      const bool isx = r >= RL_E;
+      const bool ok = (isx ? t0 + (r - RL_E) < T : e0 + r < E) && h0 + c < H;
+      const float *src = !ok ? W
+                         : isx ? x + (t0 + (r - RL_E)) * H + h0 + c
+                               : W + (int64_t)(e0 + r) * H + h0 + c;
+      tc::cp_async16(st + r * RL_LD + c, src, ok ? 16u : 0u);
     }
   };
 #pragma unroll
@@ -435,34 +441,39 @@ __global__ void __launch_bounds__(RL_WARPS * 32) router_logits_pipe_kernel(
     if (ch < nchunk) load(ch);
     tc::cp_async_commit();
   }
-  float s[RL_TPT];
+  float s[TPT];
 #pragma unroll
-  for (int j = 0; j < RL_TPT; ++j) s[j] = 0.0f;
-  const int64_t left = T - (t0 + warp * RL_TPT);
-  const int nt = left <= 0 ? 0 : (left < RL_TPT ? (int)left : RL_TPT);
+  for (int j = 0; j < TPT; ++j) s[j] = 0.0f;
+  const int64_t left = T - (t0 + warp * TPT);
+  const int nt = left <= 0 ? 0 : (left < TPT ? (int)left : TPT);
   for (int ch = 0; ch < nchunk; ++ch) {
     tc::cp_async_wait<RL_S - 2>();  // slice ch has landed (this thread's copies)
     __syncthreads();                // ... everyone's, and slice ch-1 is consumed
     if (ch + RL_S - 1 < nchunk) load(ch + RL_S - 1);
     tc::cp_async_commit();          // (an empty group keeps the count uniform)
-    const float *ws = rls + (ch % RL_S) * RL_STAGE, *xs = ws + RL_E * RL_LD;
-    const float *wr = ws + lane * RL_LD, *xr = xs + warp * RL_TPT * RL_LD;
+    const float *st = rls + (ch % RL_S) * STAGE;
+    const float *wr = st + lane * RL_LD, *xr = st + (RL_E + warp * TPT) * RL_LD;
     const int kc = min(RL_KC, H - ch * RL_KC);
     // only the chains of tokens below T: a warp past T only helps load
-    switch (nt) {
-      case 4: rl_slice<4>(wr, xr, kc, s); break;
-      case 3: rl_slice<3>(wr, xr, kc, s); break;
-      case 2: rl_slice<2>(wr, xr, kc, s); break;
-      case 1: rl_slice<1>(wr, xr, kc, s); break;
-      default: break;
+    if (nt == TPT) {
+      rl_slice<TPT>(wr, xr, kc, s);
+    } else if (TPT == 4) {
+      switch (nt) {
+        case 3: rl_slice<3>(wr, xr, kc, s); break;
+        case 2: rl_slice<2>(wr, xr, kc, s); break;
+        case 1: rl_slice<1>(wr, xr, kc, s); break;
+        default: break;
+      }
+    } else if (nt == 1) {
+      rl_slice<1>(wr, xr, kc, s);
     }
   }
   tc::cp_async_wait_all();
   const int e = e0 + lane;
   if (e < E) {
 #pragma unroll
-    for (int j = 0; j < RL_TPT; ++j) {
-      const int64_t t = t0 + warp * RL_TPT + j;
+    for (int j = 0; j < TPT; ++j) {
+      const int64_t t = t0 + warp * TPT + j;
       if (t < T) logits[t * E + e] = s[j];
     }
   }
@@ -548,12 +559,16 @@ int32_t launch_router_logits(har_cuda_ctx *ctx, const float *W, int E, int H, co
     return check_launch(ctx, "router_logits_small_kernel");
   }
   if (vec) {
-    const size_t smem = (size_t)RL_S * RL_STAGE * sizeof(float);
-    cudaFuncSetAttribute(router_logits_pipe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)smem);
-    prof_begin(ctx);
-    router_logits_pipe_kernel<<<grid, RL_WARPS * 32, smem, ctx->stream>>>(W, x, T, E, H, logits);
-    return check_launch(ctx, "router_logits_pipe_kernel");
+    auto run = [&](auto kern, size_t stage, int tt) {
+      const size_t smem = (size_t)RL_S * stage * sizeof(float);
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      const dim3 g((unsigned)((E + RL_E - 1) / RL_E), (unsigned)((T + tt - 1) / tt));
+      prof_begin(ctx);
+      kern<<<g, RL_WARPS * 32, smem, ctx->stream>>>(W, x, T, E, H, logits);
+      return check_launch(ctx, "router_logits_pipe_kernel");
+    };
+    if (T <= 512) return run(router_logits_pipe_kernel<2>, rl_stage<2>(), RL_WARPS * 2);
+    return run(router_logits_pipe_kernel<4>, rl_stage<4>(), RL_WARPS * 4);
   }
   prof_begin(ctx);
   router_logits_kernel<<<grid, RL_WARPS * 32, 0, ctx->stream>>>(W, x, T, E, H, logits);

@@ -43,7 +43,9 @@ def _router(E, H, seed, dup=None):
 @pytest.mark.parametrize("T,E,H", [(1, 512, 2048), (37, 100, 333), (256, 512, 2048),
                                    (70, 33, 64), (5, 8, 1),
                                    # decode-sized batches (T <= 4), E not a multiple of 8
-                                   (2, 512, 2048), (4, 100, 512), (3, 7, 64)])
+                                   (2, 512, 2048), (4, 100, 512), (3, 7, 64),
+                                   # T > 512: four tokens per thread, a ragged last tile
+                                   (600, 64, 256)])
 def test_router_logits_bit_exact(T, E, H):
     import torch
     from gpu_util import to_dev
