@@ -548,10 +548,11 @@ int32_t har_cuda_moe_layer_create(har_cuda_ctx *ctx, const har_cuda_weights *gat
 
 int32_t har_cuda_moe_layer_free(har_cuda_moe_layer *layer) {
   if (!layer) return HAR_CUDA_ERR_ARG;
+  const int device = layer->gate ? layer->gate->device : 0;  // before the weights go
   for (har_cuda_weights *w : layer->owned)
     if (w) har_cuda_weights_free(w);
   if (layer->owned_dev) {
-    cudaSetDevice(layer->gate->device);
+    cudaSetDevice(device);
     cudaFree(layer->owned_dev);
   }
   delete layer;

@@ -252,13 +252,13 @@ struct har_cuda_gguf {
   };
   std::vector<Tensor> tensors;
   std::unordered_map<std::string, size_t> by_name;
-  std::string last_error;
+  mutable std::string last_error;  // set by const queries too
   void *stage[2] = {nullptr, nullptr};  // pinned, portable (any device)
 };
 
 namespace {
 
-int32_t gerr(har_cuda_gguf *g, int32_t code, const std::string &m) {
+int32_t gerr(const har_cuda_gguf *g, int32_t code, const std::string &m) {
   g->last_error = m;
   return code;
 }
@@ -489,7 +489,9 @@ int32_t har_cuda_gguf_open(const char *path, char *err, size_t err_len, har_cuda
   for (size_t i = 0; i < g->tensors.size(); ++i) {
     auto &t = g->tensors[i];
     uint64_t el = 1;
-    for (uint64_t d : t.dims) el *= d;
+    for (uint64_t d : t.dims)
+      if (__builtin_mul_overflow(el, d, &el) || el > (1ull << 62))
+        return fail(HAR_CUDA_ERR_GEOMETRY, "tensor " + t.name + " has more than 2^62 elements");
     const uint64_t known = payload_for(t.type, el);
     t.payload = known ? known : span[i];
     g->by_name.emplace(t.name, i);
@@ -531,7 +533,7 @@ int32_t har_cuda_gguf_tensor_info(const har_cuda_gguf *g, int64_t index, char *n
                                   uint64_t *dims, uint64_t *file_offset, uint64_t *payload_bytes) {
   if (!g) return HAR_CUDA_ERR_ARG;
   if (index < 0 || (uint64_t)index >= g->tensors.size())
-    return gerr(const_cast<har_cuda_gguf *>(g), HAR_CUDA_ERR_ARG,
+    return gerr(g, HAR_CUDA_ERR_ARG,
                 "tensor index " + std::to_string(index) + " out of range");
   const auto &t = g->tensors[(size_t)index];
   copy_msg(t.name, name, name_len);
@@ -554,9 +556,9 @@ int32_t har_cuda_gguf_meta_u64(const har_cuda_gguf *g, const char *key, uint64_t
   if (!g || !key || !value) return HAR_CUDA_ERR_ARG;
   auto it = g->meta.find(key);
   if (it == g->meta.end())
-    return gerr(const_cast<har_cuda_gguf *>(g), HAR_CUDA_ERR_ARG, std::string("no metadata key ") + key);
+    return gerr(g, HAR_CUDA_ERR_ARG, std::string("no metadata key ") + key);
   if (meta_number(it->second, value)) return HAR_CUDA_OK;
-  return gerr(const_cast<har_cuda_gguf *>(g), HAR_CUDA_ERR_ARG,
+  return gerr(g, HAR_CUDA_ERR_ARG,
               std::string("metadata ") + key + " is not a non-negative integer");
 }
 
@@ -565,7 +567,7 @@ int32_t har_cuda_gguf_meta_string(const har_cuda_gguf *g, const char *key, char 
   if (!g || !key || !buf || !len) return HAR_CUDA_ERR_ARG;
   auto it = g->meta.find(key);
   if (it == g->meta.end() || it->second.kind != Meta::STRING)
-    return gerr(const_cast<har_cuda_gguf *>(g), HAR_CUDA_ERR_ARG,
+    return gerr(g, HAR_CUDA_ERR_ARG,
                 std::string("no string metadata key ") + key);
   copy_msg(it->second.s, buf, len);
   return HAR_CUDA_OK;

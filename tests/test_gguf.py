@@ -102,6 +102,8 @@ def _header(version=3, tensors=0, kv=0):
      har_cuda.ERR_GEOMETRY),                                           # rank 17
     (_header(kv=1) + struct.pack("<Q", 1) + b"k" + struct.pack("<I", 8) + struct.pack("<Q", 50),
      har_cuda.ERR_GEOMETRY),                                           # string past the end
+    (_header(tensors=1) + struct.pack("<Q", 1) + b"t" + struct.pack("<IQQIQ", 2, 2**40, 2**40, 0, 0),
+     har_cuda.ERR_GEOMETRY),                                           # element count overflows
 ])
 def test_malformed_files_fail_closed(tmp_path, blob, code):
     p = tmp_path / "bad.gguf"
