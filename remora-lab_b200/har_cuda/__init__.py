@@ -726,10 +726,7 @@ class CudaMoeModel:
                   if g.find(f"blk.{b}.ffn_gate_exps.weight") >= 0]
         if not layers:
             raise HarCudaError(ERR_ARG, f"{path}: no MoE layers")
-        info = g.tensor("blk.0.ffn_gate_exps.weight") if g.find("blk.0.ffn_gate_exps.weight") >= 0 \
-            else g.tensor_info(g.find(next(t["name"] for t in g.tensors()
-                                           if t["name"].endswith("ffn_gate_exps.weight"))))
-        H, I, E = info["dims"]
+        E, H, I = layers[0].E, layers[0].H, layers[0].I
         if k is None:
             k = g.meta_u64(f"{arch}.expert_used_count") or 8
         m = cls(ctx, layers, E, H, I, k, flags)
