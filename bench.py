@@ -677,6 +677,38 @@ def run_gemv_roofline(args, torch):
     torch.cuda.synchronize()
     ms6 = ev0.elapsed_time(ev1) / (args.steps * per)
     gbs6 = q6bytes / (ms6 * 1e-3) / 1e9
+    # The router on the device (har_cuda_router_logits / har_cuda_route) at the
+    # Alice shape, E = 512, H = 2048, k = 10: per call, CUDA-graph replays of
+    # 20 calls, at the decode and batch sizes it serves.
+    router = {}
+    E_r, H_r, k_r = 512, 2048, 10
+    gr = torch.Generator(dev).manual_seed(9400)
+    w_r = torch.randn(E_r, H_r, device=dev, generator=gr) * 0.02
+    for T_r in (1, 64, 256, 4096):
+        x_r = torch.randn(T_r, H_r, device=dev, generator=gr)
+        lg = torch.empty(T_r, E_r, device=dev)
+        ids_r = torch.empty(T_r, k_r, dtype=torch.int32, device=dev)
+        wt_r = torch.empty(T_r, k_r, device=dev)
+        for name, fn in (("logits", lambda: ctx.router_logits(w_r, x_r, lg)),
+                         ("route", lambda: ctx.route(w_r, x_r, k_r, ids_r, wt_r))):
+            with torch.cuda.stream(stream):
+                for _ in range(3):
+                    fn()
+            torch.cuda.synchronize()
+            gg = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gg, stream=stream):
+                for _ in range(20):
+                    fn()
+            with torch.cuda.stream(stream):
+                gg.replay()
+                ev0.record(stream)
+                for _ in range(10):
+                    gg.replay()
+                ev1.record(stream)
+            torch.cuda.synchronize()
+            router[f"{name}_T{T_r}_us"] = round(ev0.elapsed_time(ev1) / 200 * 1000, 2)
+            del gg
+    ctx.synchronize()
     q = res["q8k"]
     return {
         "metric": "Q4_K decode GEMV weight GB/s (batch 1)", "value": q["weight_gbs"], "unit": "GB/s",
@@ -695,6 +727,7 @@ def run_gemv_roofline(args, torch):
                             "ms_per_gemv": res["f32"]["ms_per_gemv"]},
         "rows_65536": {"weight_gbs": res["q8k_small"]["weight_gbs"], "frac": res["q8k_small"]["frac"],
                        "ms_per_gemv": res["q8k_small"]["ms_per_gemv"]},
+        "router": dict(router, E=E_r, H=H_r, k=k_r),
         "q6k_f32_65536": {"kernel": "q6k_gemv_stream_kernel", "weight_gbs": round(gbs6, 1),
                           "frac": round(gbs6 / hbm, 4), "ms_per_gemv": round(ms6, 5),
                           "rows": n6, "K": K},
