@@ -206,6 +206,18 @@ int32_t har_cuda_moe_ffn(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer,
 int32_t har_cuda_routed_moe(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer,
                             const float *gate_inp_dev, const float *x_dev, int64_t T, int32_t k,
                             int32_t *ids_dev, float *weights_dev, float *y_dev, uint32_t flags);
+/* A stack of L routed layers in one call: for each layer, routed_moe's
+ * selection on the device from that layer's input (gate_inp_devs[l], or the
+ * layer's own GGUF router when gate_inp_devs or its entry is NULL), then the
+ * layer, y_l = moe_l(y_{l-1}) [+ residual with HAR_CUDA_MOE_ADD_RESIDUAL] —
+ * the FFN half of NativeQwen35Moe::forward's layer loop
+ * (har/crates/har-demo/src/bin/har-native-qwen35moe.rs:1152-1215), attention
+ * and norms omitted.  Route records go to ids_dev / weights_dev [L][T][k];
+ * x_dev and y_dev may alias.  All work is enqueued on the context's stream. */
+int32_t har_cuda_routed_moe_stack(har_cuda_ctx *ctx, const har_cuda_moe_layer *const *layers,
+                                  int32_t L, const float *const *gate_inp_devs,
+                                  const float *x_dev, int64_t T, int32_t k, int32_t *ids_dev,
+                                  float *weights_dev, float *y_dev, uint32_t flags);
 /* The same with host buffers: copies x/ids/weights in and y out on the
  * context's stream and waits (bounded) — the call a BatchStepModel makes. */
 int32_t har_cuda_moe_ffn_host(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer,

@@ -608,6 +608,38 @@ int32_t har_cuda_routed_moe(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer,
   return run_moe_ffn(ctx, layer, x_dev, T, k, ids_dev, weights_dev, y_dev, flags);
 }
 
+int32_t har_cuda_routed_moe_stack(har_cuda_ctx *ctx, const har_cuda_moe_layer *const *layers,
+                                  int32_t L, const float *const *gate_inp_devs,
+                                  const float *x_dev, int64_t T, int32_t k, int32_t *ids_dev,
+                                  float *weights_dev, float *y_dev, uint32_t flags) {
+  if (!ctx) return HAR_CUDA_ERR_ARG;
+  if (!layers || L <= 0) return set_error(ctx, HAR_CUDA_ERR_ARG, "routed_moe_stack: no layers");
+  for (int l = 0; l < L; ++l) {
+    HAR_TRY(check_moe_args(ctx, layers[l], T, k, flags));
+    if (layers[l]->H != layers[0]->H)
+      return set_error(ctx, HAR_CUDA_ERR_GEOMETRY, "routed_moe_stack: layers of different H");
+    if (!(gate_inp_devs && gate_inp_devs[l]) && !layers[l]->router)
+      return set_error(ctx, HAR_CUDA_ERR_ARG,
+                       "routed_moe_stack: layer " + std::to_string(l) + " has no router");
+  }
+  if (flags & HAR_CUDA_MOE_EMPTY_SLOTS)
+    return set_error(ctx, HAR_CUDA_ERR_ARG, "routed_moe_stack: EMPTY_SLOTS is for the EP exchange only");
+  if (T == 0) return HAR_CUDA_OK;
+  if (!x_dev || !ids_dev || !weights_dev || !y_dev)
+    return set_error(ctx, HAR_CUDA_ERR_ARG, "routed_moe_stack: null pointer");
+  HAR_TRY(use_device(ctx));
+  const float *in = x_dev;
+  for (int l = 0; l < L; ++l) {
+    const float *gi = gate_inp_devs && gate_inp_devs[l] ? gate_inp_devs[l] : layers[l]->router;
+    int32_t *ids = ids_dev + (size_t)l * T * k;
+    float *w = weights_dev + (size_t)l * T * k;
+    HAR_TRY(har_cuda_route(ctx, gi, (int32_t)layers[l]->E, layers[l]->H, in, T, k, ids, w));
+    HAR_TRY(run_moe_ffn(ctx, layers[l], in, T, k, ids, w, y_dev, flags));
+    in = y_dev;  // in-place chaining: the router and the layer read y before it is rewritten
+  }
+  return HAR_CUDA_OK;
+}
+
 int32_t har_cuda_moe_ffn_host(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer,
                               const float *x_host, int64_t T, int32_t k,
                               const int32_t *ids_host, const float *weights_host,

@@ -49,6 +49,7 @@ MOE_FORCE_TC = 0x8
 
 # Every symbol include/har_cuda.h declares (tests check the library exports them).
 EXPORTS = [
+    "har_cuda_routed_moe_stack",
     "har_cuda_gguf_open", "har_cuda_gguf_close", "har_cuda_gguf_last_error",
     "har_cuda_gguf_header", "har_cuda_gguf_tensor_info", "har_cuda_gguf_find",
     "har_cuda_gguf_meta_u64", "har_cuda_gguf_meta_string", "har_cuda_weights_from_gguf",
@@ -136,6 +137,7 @@ def load_library() -> C.CDLL:
         "har_cuda_router_logits": (i32, [vp, vp, i32, i64, vp, i64, vp]),
         "har_cuda_route": (i32, [vp, vp, i32, i64, vp, i64, i32, vp, vp]),
         "har_cuda_routed_moe": (i32, [vp, vp, vp, vp, i64, i32, vp, vp, vp, u32]),
+        "har_cuda_routed_moe_stack": (i32, [vp, vp, i32, vp, vp, i64, i32, vp, vp, vp, u32]),
         "har_cuda_group_by_expert": (i32, [vp, vp, i64, i32, i32, vp, vp, vp]),
         "har_cuda_moe_layer_create": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, pp]),
         "har_cuda_moe_layer_free": (i32, [vp]),
@@ -356,6 +358,25 @@ class Context:
         self.check(self.lib.har_cuda_routed_moe(self.handle, layer.handle, _dptr(gate_inp),
                                                 _dptr(x), T, k, _dptr(ids), _dptr(weights),
                                                 _dptr(y), flags))
+        return y
+
+    def routed_moe_stack(self, layers, routers, x, k: int, ids, weights, y, flags: int = 0):
+        """L routed layers in one call (har_cuda_routed_moe_stack): routers is a
+        list of f32 [E][H] device tensors or None entries (the layer's own
+        router), or None for all; ids/weights [L][T][k] receive the route
+        records."""
+        L = len(layers)
+        T = x.shape[0]
+        if tuple(ids.shape) != (L, T, k) or tuple(weights.shape) != (L, T, k):
+            raise HarCudaError(ERR_GEOMETRY, "routed_moe_stack: ids/weights [L][T][k]")
+        arr = (C.c_void_p * L)(*[l.handle for l in layers])
+        rt = None
+        if routers is not None:
+            if len(routers) != L:
+                raise HarCudaError(ERR_GEOMETRY, "routed_moe_stack: one router entry per layer")
+            rt = (C.c_void_p * L)(*[_dptr(r) for r in routers])
+        self.check(self.lib.har_cuda_routed_moe_stack(self.handle, arr, L, rt, _dptr(x), T, k,
+                                                      _dptr(ids), _dptr(weights), _dptr(y), flags))
         return y
 
     def group_by_expert(self, ids, E: int, counts, offsets, order):
@@ -785,15 +806,15 @@ class CudaMoeServingModel:
 
     def _step_device(self, x):
         torch = self._torch
-        B = x.shape[0]
-        routes = []
-        for layer, router in zip(self.layers, self.routers):
-            ids = torch.empty((B, self.k), dtype=torch.int32, device=self._dev)
-            w = torch.empty((B, self.k), dtype=torch.float32, device=self._dev)
-            y = torch.empty_like(x)
-            self.ctx.routed_moe(layer, router, x, self.k, ids, w, y, self.flags | MOE_ADD_RESIDUAL)
-            routes.append((ids, w))
-            x = y
+        B, L = x.shape[0], len(self.layers)
+        # every layer routed and applied in one library call
+        ids = torch.empty((L, B, self.k), dtype=torch.int32, device=self._dev)
+        w = torch.empty((L, B, self.k), dtype=torch.float32, device=self._dev)
+        y = torch.empty_like(x)
+        self.ctx.routed_moe_stack(self.layers, self.routers, x, self.k, ids, w, y,
+                                  self.flags | MOE_ADD_RESIDUAL)
+        routes = [(ids[l], w[l]) for l in range(L)]
+        x = y
         logits = torch.empty((B, self.vocab), dtype=torch.float32, device=self._dev)
         if self.out.ggml_type == GGML_Q6_K:
             self.ctx.q6k_gemv(self.out, 0, x, B, logits)

@@ -100,3 +100,34 @@ def test_batched_equals_isolated_and_prefill(served):
     assert np.array_equal(logits[1], b.logits)
     with pytest.raises(har_cuda.HarCudaError):
         model.batch_step([(hs[0], V)])                     # token outside the vocabulary
+
+
+@pytest.mark.parametrize("flags", [0, har_cuda.MOE_FORCE_GEMV])
+def test_routed_stack_equals_per_layer_calls(served, flags):
+    """har_cuda_routed_moe_stack (every layer routed on the device in one call)
+    equals routed_moe called layer by layer, bit for bit, route records
+    included; input and output may alias."""
+    import torch
+
+    ctx, moe, head, host, embed, out = served
+    T, k = 5, K_USED
+    x = torch.from_numpy(haro.normal_f32(1600, 0, T * H, 0.0, 0.5).reshape(T, H)).cuda()
+    f = flags | har_cuda.MOE_ADD_RESIDUAL
+    ids = torch.empty((2, T, k), dtype=torch.int32, device="cuda")
+    w = torch.empty((2, T, k), dtype=torch.float32, device="cuda")
+    y = torch.empty_like(x)
+    ctx.routed_moe_stack(moe.layers, None, x, k, ids, w, y, f)
+    cur = x.clone()
+    for l in range(2):
+        i1 = torch.empty((T, k), dtype=torch.int32, device="cuda")
+        w1 = torch.empty((T, k), dtype=torch.float32, device="cuda")
+        nxt = torch.empty_like(cur)
+        ctx.routed_moe(moe.layers[l], None, cur, k, i1, w1, nxt, f)
+        assert torch.equal(i1, ids[l]) and torch.equal(w1, w[l])
+        cur = nxt
+    ctx.synchronize()
+    assert torch.equal(cur, y)
+    xa = x.clone()                                   # aliased input and output
+    ctx.routed_moe_stack(moe.layers, [None, None], xa, k, ids, w, xa, f)
+    ctx.synchronize()
+    assert torch.equal(xa, y)
