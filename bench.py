@@ -65,6 +65,10 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-only", action="store_true",
                     help="run warm-up + a few steps only (for ncu launch lists)")
+    ap.add_argument("--routed-decode", action="store_true",
+                    help="one JSON line for serving-style decode: the 48-layer stack with every "
+                         "layer routed on the device (har_cuda_routed_moe_stack) at T = 1, 8, 64; "
+                         "not the driver's bench line")
     ap.add_argument("--layers", type=int, default=None,
                     help="override the layer count (small ncu captures only; the bench "
                          "line always uses the config's 48)")
@@ -735,6 +739,71 @@ def run_gemv_roofline(args, torch):
     }
 
 
+def run_routed_decode(args, torch):
+    """Serving-style decode over config 5's 48-layer stack: each step routes
+    every layer on the device from that layer's input (f32 routers
+    N(0, 0.02) [E][H], the reference's routed_moe order) and applies it with the
+    residual, all in one har_cuda_routed_moe_stack call captured in a CUDA
+    graph; T tokens per step.  Weight GB/s counts each distinct routed expert
+    of every layer once (read from the step's route records) plus the shared
+    expert."""
+    import har_cuda
+
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    ctx = har_cuda.Context(local, use_torch_stream=False)
+    stream = torch.cuda.Stream(dev)
+    ctx.lib.har_cuda_ctx_set_stream(ctx.handle, __import__("ctypes").c_void_p(stream.cuda_stream))
+    layers, keep, _, _, _, _ = build_stack(ctx, torch, 5, 0)
+    L = len(layers)
+    g = torch.Generator(dev).manual_seed(9500)
+    routers = [torch.randn(E, H, device=dev, generator=g) * 0.02 for _ in range(L)]
+    peaks = load_peaks()
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    out = {}
+    for T in (1, 8, 64):
+        x = torch.randn(T, H, device=dev, generator=g)
+        y = torch.empty_like(x)
+        ids = torch.empty((L, T, TOPK), dtype=torch.int32, device=dev)
+        w = torch.empty((L, T, TOPK), dtype=torch.float32, device=dev)
+        step = lambda: ctx.routed_moe_stack(layers, routers, x, TOPK, ids, w, y,  # noqa: E731
+                                            har_cuda.MOE_ADD_RESIDUAL)
+        with torch.cuda.stream(stream):
+            for _ in range(max(3, args.warmup)):
+                step()
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=stream):
+            step()
+        ev0 = torch.cuda.Event(enable_timing=True)
+        ev1 = torch.cuda.Event(enable_timing=True)
+        n = max(3, min(args.steps, 50))
+        with torch.cuda.stream(stream):
+            gr.replay()
+            ev0.record(stream)
+            for _ in range(n):
+                gr.replay()
+            ev1.record(stream)
+        torch.cuda.synchronize()
+        ctx.synchronize()
+        ms = ev0.elapsed_time(ev1) / n
+        d = ids.cpu().numpy()
+        wbytes = sum((len(np.unique(d[l])) + 1) * EXPERT_BYTES for l in range(L))
+        out[f"T{T}"] = {"ms_per_step": round(ms, 4), "tokens_per_s": round(T / (ms * 1e-3), 1),
+                        "weight_gbs": round(wbytes / (ms * 1e-3) / 1e9, 1),
+                        "hbm_frac": round(wbytes / (ms * 1e-3) / 1e9 / hbm, 4)}
+        del gr
+    t1 = out["T1"]
+    return {"metric": "routed decode step, 48 Alice-shaped layers, device routing",
+            "value": t1["tokens_per_s"], "unit": "tokens/s (T=1)", "n_gpus": 1,
+            "ms_per_step": t1["ms_per_step"], "higher_is_better": True, "dtype": "f32 x, Q4_K W",
+            "data": "synthetic: N(0,0.02) Q4_K weights and f32 routers, N(0,1) tokens",
+            "config": {"workload": "config 5 stack, har_cuda_routed_moe_stack in one CUDA graph",
+                       "layers": L, "experts": E, "k": TOPK, "hidden": H, "inter": I},
+            "by_batch": out, "peak_hbm_gbs": hbm}
+
+
 def load_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -766,6 +835,9 @@ def main():
     try:
         if args.impl == "reference":
             out = run_reference(args)
+        elif args.routed_decode:
+            import torch
+            out = run_routed_decode(args, torch)
         elif args.config == 1:
             import torch
             out = run_gemv_roofline(args, torch)

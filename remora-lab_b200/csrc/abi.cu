@@ -465,6 +465,10 @@ int32_t har_cuda_route(har_cuda_ctx *ctx, const float *gate_inp_dev, int32_t E, 
   // logits live in the scratch arena only until route_topk has read them
   HAR_TRY(ensure_scratch(ctx, sizeof(float) * (size_t)T * (size_t)E));
   float *logits = static_cast<float *>(ctx->scratch);
+  bool fused = false;  // decode batches: logits and top-k in one launch
+  HAR_TRY(launch_route_fused(ctx, gate_inp_dev, E, (int)H, x_dev, T, k, logits, ids_dev,
+                             weights_dev, &fused));
+  if (fused) return HAR_CUDA_OK;
   HAR_TRY(launch_router_logits(ctx, gate_inp_dev, E, (int)H, x_dev, T, logits));
   return launch_route_topk(ctx, logits, T, E, k, ids_dev, weights_dev);
 }

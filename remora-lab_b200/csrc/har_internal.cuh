@@ -124,7 +124,8 @@ struct har_cuda_ctx {
   cudaStream_t own_stream = nullptr;  // the context's own stream
   int num_sms = 148;
   std::string last_error;
-  int *d_status = nullptr;            // device error word (bit flags)
+  int *d_status = nullptr;            // [0]: device error word (bit flags); [1]: the fused
+                                      // router's completion counter (zero between calls)
   void *scratch = nullptr;            // grow-only scratch arena
   size_t scratch_bytes = 0;
   void *host_pinned = nullptr;        // pinned staging for *_host entry points
@@ -210,6 +211,9 @@ int32_t launch_group(har_cuda_ctx *ctx, const int32_t *ids, int64_t T, int k, in
                      int32_t *counts, int32_t *offsets, int32_t *order, int32_t *inv);
 int32_t launch_router_logits(har_cuda_ctx *ctx, const float *W, int E, int H, const float *x,
                              int64_t T, float *logits);
+int32_t launch_route_fused(har_cuda_ctx *ctx, const float *W, int E, int H, const float *x,
+                           int64_t T, int k, float *logits, int32_t *ids, float *weights,
+                           bool *done);
 int32_t run_moe_ffn(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const float *x,
                     int64_t T, int k, const int32_t *ids, const float *weights, float *y,
                     uint32_t flags);

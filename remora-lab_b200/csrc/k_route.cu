@@ -24,22 +24,18 @@ namespace har {
 // ---------------------------------------------------------------------------
 // route_topk: one warp per token; the warp's exps live in shared memory.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(128) route_topk_kernel(const float *__restrict__ logits,
-                                                         int64_t T, int E, int k,
-                                                         int32_t *__restrict__ ids,
-                                                         float *__restrict__ weights) {
-  extern __shared__ float rsm[];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t t = (int64_t)blockIdx.x * 4 + warp;
-  if (t >= T) return;
-  float *p = rsm + (size_t)warp * E;
-  const float *l = logits + t * E;
+// One token's selection by one warp: l its E logits (read through L2, so a
+// warp may read logits other CTAs of the same kernel wrote), p E floats of
+// shared memory (16-byte aligned when E % 4 == 0), results to ids[0..k) and
+// weights[0..k).
+__device__ __forceinline__ void topk_warp(const float *l, int E, int k, float *p, int lane,
+                                          int32_t *ids, float *weights) {
   float mx = -INFINITY;
-  for (int i = lane; i < E; i += 32) mx = fmaxf(mx, l[i]);
+  for (int i = lane; i < E; i += 32) mx = fmaxf(mx, __ldcg(l + i));
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
 #pragma unroll 4
-  for (int i = lane; i < E; i += 32) p[i] = (float)exp((double)__fsub_rn(l[i], mx));
+  for (int i = lane; i < E; i += 32) p[i] = (float)exp((double)__fsub_rn(__ldcg(l + i), mx));
   __syncwarp();
   float den = 0.0f;
   if (lane == 0) {  // exps.iter().sum(): one chain in index order
@@ -93,9 +89,20 @@ __global__ void __launch_bounds__(128) route_topk_kernel(const float *__restrict
   for (int s = 0; s < k; ++s) tot = __fadd_rn(tot, __shfl_sync(0xffffffffu, sel_p, s));
   tot = fmaxf(tot, ROUTER_EPS);
   if (lane < k) {
-    ids[t * k + lane] = sel_id;
-    weights[t * k + lane] = __fdiv_rn(sel_p, tot);
+    ids[lane] = sel_id;
+    weights[lane] = __fdiv_rn(sel_p, tot);
   }
+}
+
+__global__ void __launch_bounds__(128) route_topk_kernel(const float *__restrict__ logits,
+                                                         int64_t T, int E, int k,
+                                                         int32_t *__restrict__ ids,
+                                                         float *__restrict__ weights) {
+  extern __shared__ float rsm[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t t = (int64_t)blockIdx.x * 4 + warp;
+  if (t >= T) return;
+  topk_warp(logits + t * E, E, k, rsm + (size_t)warp * E, lane, ids + t * k, weights + t * k);
 }
 
 int32_t launch_route_topk(har_cuda_ctx *ctx, const float *logits, int64_t T, int E, int k,
@@ -491,7 +498,8 @@ constexpr int RS_E = 8, RS_T = 4, RS_ROWS = RS_E + RS_T, RS_KC = 128, RS_LD = RS
 
 __global__ void __launch_bounds__(32) router_logits_small_kernel(
     const float *__restrict__ W, const float *__restrict__ x, int64_t T, int E, int H,
-    float *__restrict__ logits) {
+    float *__restrict__ logits, int k, int32_t *__restrict__ ids, float *__restrict__ weights,
+    int *counter) {
   __shared__ __align__(16) float rss[RS_S][RS_ROWS * RS_LD];
   const int lane = threadIdx.x, el = lane >> 2, tl = lane & 3;
   const int e0 = blockIdx.x * RS_E;
@@ -546,6 +554,38 @@ __global__ void __launch_bounds__(32) router_logits_small_kernel(
   }
   tc::cp_async_wait_all();
   if (e0 + el < E && tl < T) logits[(int64_t)tl * E + e0 + el] = s;
+  if (counter) {
+    // routed_moe's selection fused in: the CTA that finishes last (all logits
+    // written and fenced) runs the top-k of every token, then re-arms the counter
+    __threadfence();
+    __syncwarp();
+    int last = 0;
+    if (lane == 0) last = atomicAdd(counter, 1) == (int)gridDim.x - 1;
+    if (__shfl_sync(0xffffffffu, last, 0)) {
+      __threadfence();
+      float *p = &rss[0][0];  // the ring is idle: every copy has landed and been read
+      for (int t = 0; t < (int)T; ++t)
+        topk_warp(logits + (int64_t)t * E, E, k, p, lane, ids + (int64_t)t * k,
+                  weights + (int64_t)t * k);
+      if (lane == 0) *counter = 0;
+    }
+  }
+}
+
+// Router logits and top-k in one launch for decode batches; *done = false
+// (nothing launched) when the shape is not one the fused kernel takes.
+int32_t launch_route_fused(har_cuda_ctx *ctx, const float *W, int E, int H, const float *x,
+                           int64_t T, int k, float *logits, int32_t *ids, float *weights,
+                           bool *done) {
+  *done = false;
+  const bool vec = H % 4 == 0 && ((uintptr_t)W & 15u) == 0 && ((uintptr_t)x & 15u) == 0;
+  if (!vec || T > RS_T || T < 1 || (size_t)E > sizeof(float) * RS_S * RS_ROWS * RS_LD / 4)
+    return HAR_CUDA_OK;
+  prof_begin(ctx);
+  router_logits_small_kernel<<<(unsigned)((E + RS_E - 1) / RS_E), 32, 0, ctx->stream>>>(
+      W, x, T, E, H, logits, k, ids, weights, ctx->d_status + 1);
+  *done = true;
+  return check_launch(ctx, "router_logits_small_kernel");
 }
 
 int32_t launch_router_logits(har_cuda_ctx *ctx, const float *W, int E, int H, const float *x,
@@ -555,7 +595,7 @@ int32_t launch_router_logits(har_cuda_ctx *ctx, const float *W, int E, int H, co
   if (vec && T <= RS_T) {
     prof_begin(ctx);
     router_logits_small_kernel<<<(unsigned)((E + RS_E - 1) / RS_E), 32, 0, ctx->stream>>>(
-        W, x, T, E, H, logits);
+        W, x, T, E, H, logits, 0, nullptr, nullptr, nullptr);
     return check_launch(ctx, "router_logits_small_kernel");
   }
   if (vec) {
