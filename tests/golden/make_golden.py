@@ -7,6 +7,8 @@
 2. oracle_vectors.npz — small seeded inputs and the C oracle's outputs (HAR's
    CPU arithmetic restated, oracle/har_oracle.c).  These pin the oracle
    against regressions and give the GPU tests fixed expected outputs.
+3. oracle_vectors_router_q6k.npz — the same for the router GEMV
+   (routed_moe's matvec(ffn_gate_inp)) and the Q6_K dot / matvec.
 
 Run from the repository root:  python tests/golden/make_golden.py
 """
@@ -66,6 +68,10 @@ KATS = {
         "source": "har/crates/har-serve/src/bin/har-serve-vulkan-batched-smoke.rs:63-76",
         "max_abs_logit_error": 1e-4,
     },
+    "q6k_geometry": {
+        "source": "har/crates/har-demo/src/bin/har-native-qwen3.rs:37; har/crates/har-model/src/lib.rs:609,626",
+        "ggml_type": 14, "block_values": 256, "block_bytes": 210,
+    },
     "router_constants": {
         "source": "har/crates/har-demo/src/bin/har-native-qwen35moe.rs:45-46",
         "TOP_K": 8, "ROUTER_EPS": 1e-9,
@@ -110,6 +116,17 @@ def main():
                         moe_wg=wg, moe_wu=wu, moe_wd=wd, moe_sg=sg, moe_su=su, moe_sd=sd,
                         moe_gi=gi, moe_x=xm, moe_ids=mids, moe_w=mw, moe_y=ym,
                         moe_dims=np.array([E, H, I, T, k], np.int64))
+    # router GEMV: 5 tokens, 48 experts, H = 320 (not a multiple of 64); Q6_K:
+    # 12 rows x 768 values, 2 tokens
+    rw = haro.normal_f32(rng_seed + 12, 0, 48 * 320, 0.0, 0.02).reshape(48, 320)
+    rx = haro.normal_f32(rng_seed + 13, 0, 5 * 320).reshape(5, 320)
+    rl = haro.router_logits(rw, rx)
+    q6 = haro.random_q6k(rng_seed + 14, 12, 768)
+    q6x = haro.normal_f32(rng_seed + 15, 0, 2 * 768).reshape(2, 768)
+    q6y = haro.q6k_matvec(q6, 12, 768, q6x)
+    np.savez_compressed(os.path.join(HERE, "oracle_vectors_router_q6k.npz"),
+                        router_w=rw, router_x=rx, router_logits=rl,
+                        q6k_w=q6, q6k_x=q6x, q6k_y=q6y)
     print("wrote", HERE)
 
 

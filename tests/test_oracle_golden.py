@@ -95,3 +95,27 @@ def test_correctly_rounded_exp_mode_keeps_ids():
     i1, w1 = haro.route_topk(lg, 10, exp_mode=1)
     assert np.array_equal(i0, i1)
     assert rel_max(w1, w0) < 1e-6
+
+
+def test_router_and_q6k_golden():
+    """The router GEMV and Q6_K restatements against their frozen outputs
+    (tests/golden/oracle_vectors_router_q6k.npz, written by make_golden.py)."""
+    import os
+    from _common import GOLDEN
+    R = np.load(os.path.join(GOLDEN, "oracle_vectors_router_q6k.npz"))
+    got = haro.router_logits(R["router_w"], R["router_x"])
+    assert np.array_equal(got.view(np.uint32), R["router_logits"].view(np.uint32))
+    y = haro.q6k_matvec(R["q6k_w"], 12, 768, R["q6k_x"])
+    assert np.array_equal(y.view(np.uint32), R["q6k_y"].view(np.uint32))
+
+
+def test_q6k_geometry_known_answer():
+    """har-native-qwen3.rs:37 and har-model/src/lib.rs:609,626: Q6_K is GGML
+    type 14, 210 bytes per 256 values — the oracle, the host layer and the
+    GGUF type table agree."""
+    import har_cuda
+    from _common import kats
+    k = kats()["q6k_geometry"]
+    assert haro.Q6K_BLOCK_BYTES == k["block_bytes"] == har_cuda.Q6K_BLOCK_BYTES
+    assert har_cuda.GGML_Q6_K == k["ggml_type"]
+    assert har_cuda.BLOCK_BYTES[k["ggml_type"]] == k["block_bytes"]
