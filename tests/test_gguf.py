@@ -250,3 +250,23 @@ def test_large_tensor_streams_through_both_stages_byte_exact(tmp_path):
     w.free()
     g.close()
     ctx.close()
+
+
+def test_version_1_and_string_alignment(tmp_path):
+    """read_directory accepts versions 1..3 (har-model/src/lib.rs:325-331), and
+    metadata_number parses a value's text (:541-543), so an alignment stored as
+    the string "64" counts; a negative one falls back to 32."""
+    payload = np.zeros(144, np.uint8)
+    p = tmp_path / "v1.gguf"
+    where = write_gguf(p, [("general.alignment", STRING, "64")],
+                       [("t.weight", [256, 1], GT_Q4K, payload)], alignment=64, version=1)
+    g = har_cuda.Gguf(str(p))
+    assert g.version == 1 and g.alignment == 64 and g.data_offset % 64 == 0
+    assert g.tensor_info(0)["file_offset"] == where["t.weight"]
+    g.close()
+    from gguf_writer import I32
+    q = tmp_path / "neg.gguf"
+    write_gguf(q, [("general.alignment", I32, -8)], [("t.weight", [256, 1], GT_Q4K, payload)])
+    g = har_cuda.Gguf(str(q))
+    assert g.alignment == 32
+    g.close()
