@@ -232,8 +232,9 @@ int32_t har_cuda_moe_ffn_host(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer
  * that loads the library until exit; calls needing more return
  * HAR_CUDA_ERR_GEOMETRY (T <= 148 tokens at E = 512, H = 2048, I = 512, k = 10
  * with f32 activations, 276 with HAR_CUDA_MOE_ACT_Q8K).
- * The first call on a device looks up the array's address (make it before any
- * stream capture).  All calls on a device share the array: calls that overlap
+ * The first call in each CUDA context looks up the array's address in that
+ * context (make it before any stream capture); the address is cached per
+ * context, so a device reset or a non-primary context gets its own lookup.  All calls on a device share the array: calls that overlap
  * on the GPU race and must be serialised by the caller.  Arguments, results
  * and error behaviour are those of har_cuda_moe_ffn. */
 #define HAR_CUDA_NOALLOC_SCRATCH_BYTES (32u << 20)
@@ -253,7 +254,9 @@ int32_t har_cuda_moe_stack(har_cuda_ctx *ctx, const har_cuda_moe_layer *const *l
  * copies in, runs, copies out and waits (bounded).  A call repeated with the
  * same layers, shapes, flags and stream replays a CUDA graph of its device work
  * (captured on the second such call; not on the legacy or per-thread default
- * stream, where capture is not allowed); the inputs are read afresh every call. */
+ * stream, where capture is not allowed); the inputs are read afresh every call.
+ * Layers are identified by an id assigned at creation, never by address, so a
+ * layer freed and recreated at the same address is a new key. */
 int32_t har_cuda_moe_stack_host(har_cuda_ctx *ctx, const har_cuda_moe_layer *const *layers,
                                 int32_t L, const float *x_host, int64_t T, int32_t k,
                                 const int32_t *ids_host, const float *weights_host,
@@ -318,6 +321,26 @@ int32_t har_cuda_moe_layer_from_gguf(har_cuda_ctx *ctx, har_cuda_gguf *g, int32_
  * shared expert and partial sums.  Results equal har_cuda_moe_ffn on the
  * unsharded layer up to f32 summation order.  All ranks call collectively with
  * the same T, k and flags (ADD_RESIDUAL, ACT_Q8K, FORCE_*). */
+/* The two device steps of the exchange on their own, without a communicator:
+ * for callers that move the rows with their own transport, and for checking
+ * the plan and the combine on one GPU.
+ * har_cuda_ep_plan writes, for every destination d < world and token t < T,
+ * row d*T + t: sids [world*T][k] = the d-local expert id of each slot (-1 where
+ * the expert lives on another rank; rank d holds experts [d*E/world,
+ * (d+1)*E/world)), sw [world*T][k] = the slot's weight (0 where -1), and
+ * sx [world*T][H] = x[t] when at least one slot lives on d (the row is left
+ * unwritten otherwise).  Out-of-range ids set the device error word
+ * (HAR_CUDA_ERR_DEVICE at the next har_cuda_synchronize).
+ * har_cuda_ep_combine writes y[t] = (x[t] with HAR_CUDA_MOE_ADD_RESIDUAL) +
+ * shared[t] + back[0][t] + ... + back[world-1][t], each addition rounded to
+ * f32 in that order; shared_dev may be null (no shared expert) and x_dev may
+ * alias y_dev. */
+int32_t har_cuda_ep_plan(har_cuda_ctx *ctx, const float *x_dev, int64_t H, int64_t T, int32_t k,
+                         const int32_t *ids_dev, const float *weights_dev, int32_t E, int32_t world,
+                         float *sx_dev, int32_t *sids_dev, float *sw_dev);
+int32_t har_cuda_ep_combine(har_cuda_ctx *ctx, const float *x_dev, int64_t H, int64_t T,
+                            int32_t world, const float *shared_dev, const float *back_dev,
+                            uint32_t flags, float *y_dev);
 /* An NCCL unique id (rank 0 creates it; the caller broadcasts the bytes). */
 int32_t har_cuda_ep_unique_id(uint8_t *out, size_t len);
 /* Collective: every rank of `world` joins the communicator on ctx's device. */

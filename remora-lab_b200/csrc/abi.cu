@@ -6,6 +6,7 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <atomic>
 #include <chrono>
 #include <thread>
 
@@ -517,7 +518,9 @@ int32_t har_cuda_moe_layer_create(har_cuda_ctx *ctx, const har_cuda_weights *gat
   }
   if (I % QK != 0 || H % QK != 0)
     return set_error(ctx, HAR_CUDA_ERR_GEOMETRY, "moe_layer: H and I must be multiples of 256");
+  static std::atomic<uint64_t> next_gen{1};
   har_cuda_moe_layer *l = new har_cuda_moe_layer();
+  l->gen = next_gen.fetch_add(1);
   l->gate = gate;
   l->up = up;
   l->down = down;
@@ -739,7 +742,8 @@ int32_t har_cuda_moe_stack_host(har_cuda_ctx *ctx, const har_cuda_moe_layer *con
   // stream, and no reallocation since) replays a CUDA graph of its device work:
   // the second such call captures it (by then every buffer has its size).
   auto &g = ctx->host_graph;
-  const std::vector<const void *> key(layers, layers + L);
+  std::vector<uint64_t> key((size_t)L);
+  for (int l = 0; l < L; ++l) key[l] = layers[l]->gen;
   const bool same = g.layers == key && g.T == T && g.k == k && g.flags == flags &&
                     g.tc_min == ctx->tc_min_tokens && g.epoch == ctx->epoch && g.stream == ctx->stream;
   if (!same) {

@@ -112,6 +112,37 @@ __device__ __forceinline__ float group_sum(float v) {
   return v;
 }
 
+// sigmoid(gi . x) of one token row, computed by one warp: lane l accumulates
+// the 4-value chunks l, l + 32, ... with fmaf (x, y, z, w in order), then the
+// lanes are summed by a shuffle tree.  Every kernel that needs the shared
+// expert's gate calls this, so a token's gate never depends on which kernel
+// computed it or on the other tokens of the call.  x is 16-byte aligned, H a
+// multiple of 4 (both checked by the callers).
+__device__ __forceinline__ float shared_gate_warp(const float *gi, const float *x, int H, int lane) {
+  float s = 0.0f;
+  const float4 *x4 = reinterpret_cast<const float4 *>(x);
+  if (((uintptr_t)gi & 15u) == 0) {
+    const float4 *g4 = reinterpret_cast<const float4 *>(gi);
+#pragma unroll 4
+    for (int i = lane; i < H / 4; i += 32) {
+      const float4 a = __ldg(g4 + i), b = x4[i];
+      s = fmaf(a.x, b.x, s);
+      s = fmaf(a.y, b.y, s);
+      s = fmaf(a.z, b.z, s);
+      s = fmaf(a.w, b.w, s);
+    }
+  } else {
+    for (int i = lane; i < H / 4; i += 32) {
+      const float4 b = x4[i];
+      s = fmaf(__ldg(gi + 4 * i), b.x, s);
+      s = fmaf(__ldg(gi + 4 * i + 1), b.y, s);
+      s = fmaf(__ldg(gi + 4 * i + 2), b.z, s);
+      s = fmaf(__ldg(gi + 4 * i + 3), b.w, s);
+    }
+  }
+  return sigmoid_f(warp_sum(s));
+}
+
 }  // namespace har
 
 // ---------------------------------------------------------------------------
@@ -138,7 +169,7 @@ struct har_cuda_ctx {
   // CUDA graph of the last repeated har_cuda_moe_stack_host call (copies in,
   // the stack, copy out), replayed while the call's key is unchanged
   struct HostGraph {
-    std::vector<const void *> layers;
+    std::vector<uint64_t> layers;  // the layers' generation ids (never their addresses)
     int64_t T = 0;
     int32_t k = 0;
     uint32_t flags = 0;
@@ -187,6 +218,10 @@ struct har_cuda_moe_layer {
   std::vector<har_cuda_weights *> owned;
   void *owned_dev = nullptr;
   const float *router = nullptr;  // ffn_gate_inp [E][H], or null
+  // Process-unique id assigned at creation.  Caches key on it rather than on
+  // the layer's address: a layer freed and another created at the same heap
+  // address (with other weights) must not hit an entry of the first.
+  uint64_t gen = 0;
 };
 
 namespace har {

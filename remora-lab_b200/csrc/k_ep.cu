@@ -26,6 +26,8 @@
 // terms are summed per rank, then across ranks).
 #include <nccl.h>
 
+#include <algorithm>
+#include <climits>
 #include <cstring>
 #include <string>
 
@@ -81,29 +83,22 @@ __global__ void __launch_bounds__(128) ep_plan_kernel(const float *__restrict__ 
 }
 
 // g[t] = sigmoid(gate_inp . x[t]) (1 without a gate row) and ids0[t] = 0: the
-// shared expert as the only slot of a one-expert layer.  Same dot order as the
-// single-GPU combine kernel.
-__global__ void __launch_bounds__(256) ep_gate_kernel(const float *__restrict__ x, int H,
+// shared expert as the only slot of a one-expert layer.  One warp per token,
+// the same dot as the single-GPU layer's gate (shared_gate_warp).
+__global__ void __launch_bounds__(256) ep_gate_kernel(const float *__restrict__ x, int H, int T,
                                                       const float *__restrict__ gi,
                                                       float *__restrict__ g,
                                                       int32_t *__restrict__ ids0) {
-  const int t = blockIdx.x;
-  __shared__ float red[8];
-  float s = 0.0f;
-  if (gi)
-    for (int h = threadIdx.x; h < H; h += blockDim.x) s = fmaf(gi[h], x[(int64_t)t * H + h], s);
-  s = warp_sum(s);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    float v = 0.0f;
-    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) v += red[i];
-    g[t] = gi ? sigmoid_f(v) : 1.0f;
+  const int t = blockIdx.x * 8 + (int)(threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (t >= T) return;
+  const float v = gi ? shared_gate_warp(gi, x + (int64_t)t * H, H, lane) : 1.0f;
+  if (lane == 0) {
+    g[t] = v;
     ids0[t] = 0;
   }
 }
 
-// y[t] = (x[t] with the residual flag) + shared[t] + sum_d back[d][t].
+// y[t] = (x[t] with the residual flag) + shared[t] (when given) + sum_d back[d][t].
 __global__ void __launch_bounds__(256) ep_combine_kernel(const float *x, int H, int T, int G,
                                                          const float *__restrict__ ysh,
                                                          const float *__restrict__ back,
@@ -112,7 +107,7 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(const float *x, int H, 
   for (int h = threadIdx.x; h < H; h += blockDim.x) {
     const int64_t i = (int64_t)t * H + h;
     float acc = residual ? x[i] : 0.0f;
-    acc = __fadd_rn(acc, ysh[i]);
+    if (ysh) acc = __fadd_rn(acc, ysh[i]);
     for (int d = 0; d < G; ++d) acc = __fadd_rn(acc, back[((int64_t)d * T + t) * H + h]);
     y[i] = acc;
   }
@@ -187,6 +182,16 @@ int32_t ep_layer(har_cuda_ctx *ctx, har_cuda_ep *ep, const har_cuda_moe_layer *l
   const EpLayout L = ep_layout(G, T, k, H);
   int32_t st = ep_reserve(ctx, ep, L.total);
   if (st) return st;
+  const uint32_t mode0 =
+      flags & (HAR_CUDA_MOE_ACT_Q8K | HAR_CUDA_MOE_FORCE_GEMV | HAR_CUDA_MOE_FORCE_TC);
+  // Both expert calls of the layer share the context's scratch arena: size it
+  // for the larger one before the first launch, so the arena never grows (a
+  // synchronising reallocation) between the two calls.
+  {
+    size_t need = moe_scratch_bytes(ctx, local, (int64_t)G * T, k, mode0 | HAR_CUDA_MOE_EMPTY_SLOTS);
+    if (shared) need = std::max(need, moe_scratch_bytes(ctx, shared, T, 1, mode0));
+    if ((st = ensure_scratch(ctx, need))) return st;
+  }
   uint8_t *B = (uint8_t *)ep->buf;
   float *sx = (float *)(B + L.sx), *sw = (float *)(B + L.sw), *rx = (float *)(B + L.rx);
   float *rw = (float *)(B + L.rw), *part = (float *)(B + L.part), *back = (float *)(B + L.back);
@@ -222,7 +227,8 @@ int32_t ep_layer(har_cuda_ctx *ctx, har_cuda_ep *ep, const har_cuda_moe_layer *l
   // 3. the shared expert on the rank's tokens, meanwhile
   if (shared) {
     prof_begin(ctx);
-    ep_gate_kernel<<<(unsigned)T, 256, 0, ctx->stream>>>(x, (int)H, gate_inp, g, ids0);
+    ep_gate_kernel<<<(unsigned)((T + 7) / 8), 256, 0, ctx->stream>>>(x, (int)H, (int)T, gate_inp, g,
+                                                                     ids0);
     if ((st = check_launch(ctx, "ep_gate_kernel"))) return st;
     if ((st = run_moe_ffn(ctx, shared, x, T, 1, ids0, g, ysh, mode))) return st;
   } else if (cudaMemsetAsync(ysh, 0, 4 * (size_t)T * H, ctx->stream) != cudaSuccess) {
@@ -338,6 +344,48 @@ int32_t har_cuda_ep_free(har_cuda_ep *ep) {
   }
   delete ep;
   return HAR_CUDA_OK;
+}
+
+int32_t har_cuda_ep_plan(har_cuda_ctx *ctx, const float *x_dev, int64_t H, int64_t T, int32_t k,
+                         const int32_t *ids_dev, const float *weights_dev, int32_t E, int32_t world,
+                         float *sx_dev, int32_t *sids_dev, float *sw_dev) {
+  if (!ctx) return HAR_CUDA_ERR_ARG;
+  if (!x_dev || !ids_dev || !weights_dev || !sx_dev || !sids_dev || !sw_dev)
+    return set_error(ctx, HAR_CUDA_ERR_ARG, "ep_plan: null pointer");
+  if (world < 1 || E < world || E % world || k <= 0 || k > E || T < 0 || H <= 0 || H % 4 ||
+      (int64_t)world * T > INT32_MAX || (int64_t)world * T * k > ((int64_t)1 << 24))
+    return set_error(ctx, HAR_CUDA_ERR_GEOMETRY,
+                     "ep_plan: need world | E, 0 < k <= E, H a multiple of 4, world*T*k <= 2^24");
+  if (((uintptr_t)x_dev & 15u) || ((uintptr_t)sx_dev & 15u))
+    return set_error(ctx, HAR_CUDA_ERR_ARG, "ep_plan: x and sx must be 16-byte aligned");
+  if (cudaSetDevice(ctx->device) != cudaSuccess)
+    return set_error(ctx, HAR_CUDA_ERR_CUDA, "ep_plan: cudaSetDevice failed");
+  if (T == 0) return HAR_CUDA_OK;
+  prof_begin(ctx);
+  ep_plan_kernel<<<(unsigned)(world * T), 128, 0, ctx->stream>>>(x_dev, (int)H, ids_dev, weights_dev,
+                                                                (int)T, k, E, E / world, sx_dev,
+                                                                sids_dev, sw_dev, ctx->d_status);
+  return check_launch(ctx, "ep_plan_kernel");
+}
+
+int32_t har_cuda_ep_combine(har_cuda_ctx *ctx, const float *x_dev, int64_t H, int64_t T,
+                            int32_t world, const float *shared_dev, const float *back_dev,
+                            uint32_t flags, float *y_dev) {
+  if (!ctx) return HAR_CUDA_ERR_ARG;
+  if (!x_dev || !back_dev || !y_dev) return set_error(ctx, HAR_CUDA_ERR_ARG, "ep_combine: null pointer");
+  if (world < 1 || T < 0 || T > INT32_MAX || H <= 0 || H > INT32_MAX)
+    return set_error(ctx, HAR_CUDA_ERR_GEOMETRY, "ep_combine: need world >= 1, T >= 0, H > 0");
+  if (flags & ~HAR_CUDA_MOE_ADD_RESIDUAL)
+    return set_error(ctx, HAR_CUDA_ERR_ARG, "ep_combine: only HAR_CUDA_MOE_ADD_RESIDUAL applies");
+  if (cudaSetDevice(ctx->device) != cudaSuccess)
+    return set_error(ctx, HAR_CUDA_ERR_CUDA, "ep_combine: cudaSetDevice failed");
+  if (T == 0) return HAR_CUDA_OK;
+  prof_begin(ctx);
+  ep_combine_kernel<<<(unsigned)T, 256, 0, ctx->stream>>>(x_dev, (int)H, (int)T, world, shared_dev,
+                                                         back_dev,
+                                                         (flags & HAR_CUDA_MOE_ADD_RESIDUAL) ? 1 : 0,
+                                                         y_dev);
+  return check_launch(ctx, "ep_combine_kernel");
 }
 
 int32_t har_cuda_ep_moe_ffn(har_cuda_ctx *ctx, har_cuda_ep *ep, const har_cuda_moe_layer *local,

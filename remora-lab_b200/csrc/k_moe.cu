@@ -48,7 +48,19 @@ struct MoeDev {
   float *a;             // [n + T][I] f32
   const uint8_t *aact;  // a rows (f32, = a) or their Q8_K image
   float *ybuf;          // [n + T][H] f32
+  const float *gsh;     // [T] sigmoid(gate_inp . x[t]) of the shared expert, or null (gate 1)
 };
+
+// gsh[t] = sigmoid(gi . x[t]), one warp per token: the shared expert's gate,
+// computed before any kernel of the layer writes y (which may alias x).
+__global__ void __launch_bounds__(256) shared_gate_kernel(const float *__restrict__ gi,
+                                                          const float *__restrict__ x, int H, int T,
+                                                          float *__restrict__ gsh) {
+  const int t = blockIdx.x * 8 + (int)(threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (t >= T) return;
+  const float g = shared_gate_warp(gi, x + (int64_t)t * H, H, lane);
+  if (lane == 0) gsh[t] = g;
+}
 
 __device__ __forceinline__ float silu_f(float v) { return v / (1.0f + expf(-v)); }
 
@@ -230,47 +242,23 @@ __global__ void __launch_bounds__(256) moe_down_kernel(MoeDev p, int rows_per_ti
 // to eight slots before it adds them -- in slot order, as the reference does.
 constexpr int COMB_T = 128;
 
-__global__ void __launch_bounds__(COMB_T) moe_combine_kernel(MoeDev p, const float *__restrict__ x,
+__global__ void __launch_bounds__(COMB_T) moe_combine_kernel(MoeDev p, const float *x,
                                                              const float *__restrict__ weights,
-                                                             const float *__restrict__ sh_gate_inp,
                                                              float *y, int add_residual) {
+  // x may alias y (in-place layer stacks): each thread reads x[t] only at the
+  // four columns it writes, and the shared expert's gate was computed from x
+  // by an earlier kernel (p.gsh), so no block reads what a sibling wrote.
   constexpr int SLOTS = 32;  // slots of the token cached in shared memory
-  __shared__ float red[COMB_T / 32];
   __shared__ int spos[SLOTS];
   __shared__ float sw[SLOTS];
   const int64_t t = blockIdx.x;
   const float *xt = x + t * p.H;
-  float g = 1.0f;
-  if (p.has_shared && sh_gate_inp) {
-    float s = 0.0f;
-    if (((uintptr_t)sh_gate_inp & 15u) == 0) {
-      // float4 loads, several in flight per thread (a decode-sized call is
-      // latency-bound here: one dependent load pair per step cost ~10 us)
-      const float4 *g4 = reinterpret_cast<const float4 *>(sh_gate_inp);
-      const float4 *x4 = reinterpret_cast<const float4 *>(xt);
-#pragma unroll 4
-      for (int i = threadIdx.x; i < p.H / 4; i += blockDim.x) {
-        const float4 a = __ldg(g4 + i), b = x4[i];
-        s = fmaf(a.x, b.x, s);
-        s = fmaf(a.y, b.y, s);
-        s = fmaf(a.z, b.z, s);
-        s = fmaf(a.w, b.w, s);
-      }
-    } else {
-      for (int h = threadIdx.x; h < p.H; h += blockDim.x) s = fmaf(sh_gate_inp[h], xt[h], s);
-    }
-    s = warp_sum(s);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
-    __syncthreads();
-    s = 0.0f;
-    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) s += red[w];
-    g = sigmoid_f(s);
-  }
+  const float g = p.gsh ? p.gsh[t] : 1.0f;
   for (int s = threadIdx.x; s < p.k && s < SLOTS; s += blockDim.x) {
     spos[s] = p.inv[t * p.k + s];
     sw[s] = weights[t * p.k + s];
   }
-  __syncthreads();  // every read of x[t] by the gate dot precedes the writes below
+  __syncthreads();
   // four consecutive h per thread (float4); per element the same operation
   // order as the reference: slots in order, then the shared expert, then x
   const int H4 = p.H / 4;
@@ -386,7 +374,7 @@ static size_t al256(size_t v) { return (v + 255) & ~(size_t)255; }
 // Scratch layout of one moe_ffn call (offsets in bytes, 256-byte aligned).
 struct MoeScratch {
   size_t o_counts, o_offsets, o_order, o_inv, o_ne, o_nne, o_xq, o_a, o_aq, o_y;
-  size_t o_ttinfo, o_ntt, o_x16, o_a16, total;
+  size_t o_ttinfo, o_ntt, o_x16, o_a16, o_gsh, total;
 };
 
 // Experts with at least this many tokens take the tensor-core path
@@ -450,6 +438,7 @@ static MoeScratch moe_layout(const har_cuda_moe_layer *layer, int64_t T, int k, 
   s.o_ntt = take(4);
   s.o_x16 = tc ? take(4 * (size_t)(slots * H)) : 0;  // token rows in slot order (f16 hi/lo)
   s.o_a16 = tc ? take(4 * (size_t)(slots * I)) : 0;
+  s.o_gsh = take(4 * (size_t)T);
   s.total = off;
   return s;
 }
@@ -519,6 +508,10 @@ int32_t run_moe_ffn_in(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const
   p.n_ne = (const int32_t *)(S + o_nne);
   p.a = (float *)(S + o_a);
   p.ybuf = (float *)(S + o_y);
+  // the shared expert's gate: by the gather kernel when it visits the shared
+  // slots (tensor-core shared expert), else by its own kernel, before y is written
+  const bool gate_row = has_sh && layer->sh_gate_inp;
+  p.gsh = gate_row ? (const float *)(S + L.o_gsh) : nullptr;
   if (q8) {
     p.xact = S + o_xq;
     p.xrow = xq_row;
@@ -574,8 +567,15 @@ int32_t run_moe_ffn_in(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const
         return st;
     }
     if ((st = launch_gather_f16(ctx, x, H, p.order, ids, p.counts, p.offsets + E, thr, (int)n, k,
-                                (int)T, tp.shared_tc, (__half *)(S + L.o_x16))))
+                                (int)T, tp.shared_tc, (__half *)(S + L.o_x16),
+                                tp.shared_tc ? layer->sh_gate_inp : nullptr, (float *)(S + L.o_gsh))))
       return st;
+  }
+  if (gate_row && !(tc && shared_tc)) {
+    prof_begin(ctx);
+    shared_gate_kernel<<<(unsigned)((T + 7) / 8), 256, 0, ctx->stream>>>(layer->sh_gate_inp, x, H, (int)T,
+                                                                        (float *)(S + L.o_gsh));
+    if ((st = check_launch(ctx, "shared_gate_kernel"))) return st;
   }
   // upper bound of tensor-core token tiles: each big expert has >= thr tokens
   const int64_t max_tc_tt =
@@ -617,7 +617,7 @@ int32_t run_moe_ffn_in(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const
   }
   prof_begin(ctx);
   moe_combine_kernel<<<dim3((unsigned)T, (unsigned)((H / 4 + COMB_T - 1) / COMB_T)), COMB_T, 0, ctx->stream>>>(
-      p, x, weights, layer->sh_gate_inp, y, (flags & HAR_CUDA_MOE_ADD_RESIDUAL) ? 1 : 0);
+      p, x, weights, y, (flags & HAR_CUDA_MOE_ADD_RESIDUAL) ? 1 : 0);
   return check_launch(ctx, "moe_combine_kernel");
 }
 

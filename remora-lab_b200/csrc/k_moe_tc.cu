@@ -530,16 +530,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
 // K order (0, 2, 1, 3) inside each group of four (the weight operand's order),
 // for every slot whose expert runs on the tensor-core path: routed slot s holds entry order[s] (token order[s] / k,
 // expert ids[order[s]]); slot n + t is the shared expert's row of token t.
-// One CTA per slot; slots of CUDA-core experts are skipped.
-// One warp per slot, GATHER_WARPS slots per block: the slot's index chain
-// (order -> ids -> counts) of several slots is in flight at once.
+// Slots of CUDA-core experts are skipped.  One warp per slot, GATHER_WARPS
+// slots per block: the slot's index chain (order -> ids -> counts) of several
+// slots is in flight at once.  The warp of shared slot n + t also writes the
+// shared expert's gate gsh[t] = sigmoid(gi . x[t]) when gi is given.
 constexpr int GATHER_WARPS = 8;
 
 __global__ void __launch_bounds__(GATHER_WARPS * 32) gather_f16_kernel(
     const float *__restrict__ x, int H, const int32_t *__restrict__ order,
     const int32_t *__restrict__ ids, const int32_t *__restrict__ counts,
     const int32_t *__restrict__ n_valid, int thr, int n, int k, int T, int shared_tc,
-    __half *__restrict__ xg) {
+    __half *__restrict__ xg, const float *__restrict__ gi, float *__restrict__ gsh) {
   const int slot = blockIdx.x * GATHER_WARPS + (int)(threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (slot >= n + T) return;
   int tok;
@@ -566,15 +567,20 @@ __global__ void __launch_bounds__(GATHER_WARPS * 32) gather_f16_kernel(
     dhi[i] = make_uint2(*reinterpret_cast<const uint32_t *>(&a), *reinterpret_cast<const uint32_t *>(&b));
     dlo[i] = make_uint2(*reinterpret_cast<const uint32_t *>(&la), *reinterpret_cast<const uint32_t *>(&lb));
   }
+  if (slot >= n && gi) {
+    const float g = shared_gate_warp(gi, x + (int64_t)tok * H, H, lane);
+    if (lane == 0) gsh[tok] = g;
+  }
 }
 
 int32_t launch_gather_f16(har_cuda_ctx *ctx, const float *x, int H, const int32_t *order,
                           const int32_t *ids, const int32_t *counts, const int32_t *n_valid,
-                          int thr, int n, int k, int T, int shared_tc, __half *xg) {
+                          int thr, int n, int k, int T, int shared_tc, __half *xg,
+                          const float *gi, float *gsh) {
   prof_begin(ctx);
   const unsigned grid = (unsigned)((n + T + GATHER_WARPS - 1) / GATHER_WARPS);
   gather_f16_kernel<<<grid, GATHER_WARPS * 32, 0, ctx->stream>>>(x, H, order, ids, counts, n_valid, thr,
-                                                                n, k, T, shared_tc, xg);
+                                                                n, k, T, shared_tc, xg, gi, gsh);
   return check_launch(ctx, "gather_f16_kernel");
 }
 

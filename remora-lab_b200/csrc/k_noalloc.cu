@@ -13,15 +13,18 @@
 // The scratch is a file-scope __device__ array of HAR_CUDA_NOALLOC_SCRATCH_BYTES
 // (32 MiB).  Every GPU that loads this library's device code holds it until
 // the process exits.  Host code cannot use the array's name as a device
-// address (on the host it names a stand-in object), so the first call on
-// each device looks up the real address with cudaGetSymbolAddress while that
-// device is current, and caches it per device; that first call should be
-// made before any stream capture.  All calls on a device share the array and
+// address (on the host it names a stand-in object), so the first call in
+// each CUDA context looks up the real address with cudaGetSymbolAddress while
+// that context is current, and caches it per context; that first call should
+// be made before any stream capture.  All calls on a device share the array and
 // it keeps the last call's contents: the kernels write every scratch word
 // before reading it, so nothing needs clearing between calls, but calls that
 // overlap on the GPU (two streams or two contexts on one device) race on it
 // and must be serialised by the caller.
+#include <cuda.h>
+
 #include <mutex>
+#include <vector>
 
 #include "har_internal.cuh"
 
@@ -29,27 +32,59 @@ namespace har {
 
 static __device__ __align__(256) uint8_t noalloc_scratch[HAR_CUDA_NOALLOC_SCRATCH_BYTES];
 
-constexpr int kMaxDevices = 64;
-static void *noalloc_ptr[kMaxDevices] = {};
+// Cached device addresses of noalloc_scratch, one per CUDA context.  The key
+// is the current driver context, not the device index: after a
+// cudaDeviceReset (or under a context other than the device's primary one)
+// the array lives at a new address, which a per-device cache would miss.
+struct NoallocEntry {
+  CUcontext cu;
+  void *ptr;
+};
+static std::vector<NoallocEntry> noalloc_cache;
 static std::mutex noalloc_mu;
 
-// Device address of noalloc_scratch on ctx->device (looked up once per device).
-static int32_t noalloc_scratch_ptr(har_cuda_ctx *ctx, uint8_t **out) {
-  if (ctx->device < 0 || ctx->device >= kMaxDevices)
-    return set_error(ctx, HAR_CUDA_ERR_UNSUPPORTED, "moe_ffn_noalloc: device index above 63");
-  std::lock_guard<std::mutex> lock(noalloc_mu);
-  if (!noalloc_ptr[ctx->device]) {
+using CtxGetCurrentFn = CUresult (*)(CUcontext *);
+
+static CtxGetCurrentFn ctx_get_current_fn() {
+  static CtxGetCurrentFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
     void *p = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&p, noalloc_scratch);
-    if (e != cudaSuccess || !p) {
-      cudaGetLastError();
-      return set_error(ctx, HAR_CUDA_ERR_CUDA,
-                       std::string("moe_ffn_noalloc: cudaGetSymbolAddress failed: ") +
-                           cudaGetErrorString(e));
-    }
-    noalloc_ptr[ctx->device] = p;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (CtxGetCurrentFn)p;
+    cudaGetLastError();
+  });
+  return fn;
+}
+
+// Device address of noalloc_scratch in the current context (ctx->device is
+// current; looked up once per context).
+static int32_t noalloc_scratch_ptr(har_cuda_ctx *ctx, uint8_t **out) {
+  CtxGetCurrentFn get = ctx_get_current_fn();
+  CUcontext cu = nullptr;
+  // cudaFree(0) makes the runtime bind the device's context to this thread
+  if (!get || cudaFree(0) != cudaSuccess || get(&cu) != CUDA_SUCCESS || !cu) {
+    cudaGetLastError();
+    return set_error(ctx, HAR_CUDA_ERR_CUDA, "moe_ffn_noalloc: no current CUDA context");
   }
-  *out = (uint8_t *)noalloc_ptr[ctx->device];
+  std::lock_guard<std::mutex> lock(noalloc_mu);
+  for (const NoallocEntry &e : noalloc_cache)
+    if (e.cu == cu) {
+      *out = (uint8_t *)e.ptr;
+      return HAR_CUDA_OK;
+    }
+  void *p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, noalloc_scratch);
+  if (e != cudaSuccess || !p) {
+    cudaGetLastError();
+    return set_error(ctx, HAR_CUDA_ERR_CUDA,
+                     std::string("moe_ffn_noalloc: cudaGetSymbolAddress failed: ") +
+                         cudaGetErrorString(e));
+  }
+  noalloc_cache.push_back({cu, p});
+  *out = (uint8_t *)p;
   return HAR_CUDA_OK;
 }
 

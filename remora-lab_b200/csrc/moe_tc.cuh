@@ -56,6 +56,7 @@ int32_t launch_moe_tc(har_cuda_ctx *ctx, const TcMaps &maps, const TcParams &p, 
 // n_valid = the number of grouped entries (offsets[E]); later routed slots are empty.
 int32_t launch_gather_f16(har_cuda_ctx *ctx, const float *x, int H, const int32_t *order,
                           const int32_t *ids, const int32_t *counts, const int32_t *n_valid,
-                          int thr, int n, int k, int T, int shared_tc, __half *xg);
+                          int thr, int n, int k, int T, int shared_tc, __half *xg,
+                          const float *gi, float *gsh);
 
 }  // namespace har

@@ -65,7 +65,7 @@ EXPORTS = [
     "har_cuda_gen_q4k", "har_cuda_moe_stack_host", "har_cuda_profile_begin",
     "har_cuda_profile_end", "har_cuda_moe_ffn_noalloc", "har_cuda_ctx_set_tc_min_tokens",
     "har_cuda_ep_unique_id", "har_cuda_ep_create", "har_cuda_ep_free", "har_cuda_ep_moe_ffn",
-    "har_cuda_ep_moe_stack",
+    "har_cuda_ep_moe_stack", "har_cuda_ep_plan", "har_cuda_ep_combine",
 ]
 
 
@@ -108,6 +108,8 @@ def load_library() -> C.CDLL:
         "har_cuda_ep_free": (i32, [vp]),
         "har_cuda_ep_moe_ffn": (i32, [vp, vp, vp, vp, vp, vp, i64, i32, vp, vp, vp, u32]),
         "har_cuda_ep_moe_stack": (i32, [vp, vp, vp, vp, vp, i32, vp, i64, i32, vp, vp, vp, u32]),
+        "har_cuda_ep_plan": (i32, [vp, vp, i64, i64, i32, vp, vp, i32, i32, vp, vp, vp]),
+        "har_cuda_ep_combine": (i32, [vp, vp, i64, i64, i32, vp, vp, u32, vp]),
         "har_cuda_synchronize": (i32, [vp, i64]),
         "har_cuda_launch_count": (i64, [vp]),
         "har_cuda_weights_upload_q4k": (i32, [vp, vp, i64, i64, i64, pp]),
@@ -479,6 +481,20 @@ class Context:
             self.handle, ep.handle, la, sa, ga, L, _dptr(x), T, k, _dptr(ids), _dptr(weights),
             _dptr(y), flags))
         return y
+
+    def ep_plan(self, x, ids, weights, E: int, world: int, sx, sids, sw):
+        """ep_plan_kernel alone: the dispatch rows [world*T] for every destination."""
+        T, k = ids.shape
+        self.check(self.lib.har_cuda_ep_plan(self.handle, _dptr(x), x.shape[1], T, k, _dptr(ids),
+                                             _dptr(weights), E, world, _dptr(sx), _dptr(sids),
+                                             _dptr(sw)))
+
+    def ep_combine(self, x, world: int, shared, back, y, flags: int = 0):
+        """ep_combine_kernel alone: y = residual + shared + back[0] + ... + back[world-1]."""
+        T, H = x.shape
+        self.check(self.lib.har_cuda_ep_combine(self.handle, _dptr(x), H, T, world,
+                                                _dptr(shared) if shared is not None else None,
+                                                _dptr(back), flags, _dptr(y)))
 
 
 def ep_unique_id() -> bytes:

@@ -1,0 +1,226 @@
+"""GPU parity at the exact shapes of the benchmark configurations, and the
+in-place and caching hazards of the layer entry points.
+
+- Config 4: one Alice-shaped layer at prefill, 4096
+  tokens, uniform top-10 over 512 experts (~80 tokens per expert, every expert
+  touched) plus the shared expert.  The whole layer runs on the GPU; a seeded
+  sample of 256 tokens is checked against the oracle's compose_moe_route
+  (har-native-qwen35moe.rs:979-1048).
+- Config 5 (what bench.py times): the 48-layer stack that
+  bench.py builds (same seeds), 256 tokens, Zipf(1.1) top-10 per layer.  Every
+  layer runs on the GPU; a token subset is checked layer by layer against the
+  oracle, each layer fed the GPU's output of the layer before, and the stack
+  entry point must equal the chain of per-layer calls bit for bit.
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+import haro  # noqa: E402
+import har_cuda  # noqa: E402
+from _common import TC_NRMS, assert_close, verdict, rel_max  # noqa: E402
+from gpu_util import Layer, to_dev  # noqa: E402
+
+E, H, I, K = 512, 2048, 512, 10
+RES = har_cuda.MOE_ADD_RESIDUAL
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    c = har_cuda.Context(0)
+    yield c
+    torch.cuda.synchronize()
+    c.close()
+
+
+def uniform_routing(T, seed):
+    """Top-10 distinct experts per token from seeded N(0,1) router logits, softmax weights."""
+    return haro.route_topk(haro.normal_f32(seed, 0, T * E).reshape(T, E), K)
+
+
+def test_config4_prefill_layer(ctx):
+    lay = Layer(ctx, E, H, I, seed=4000)
+    T = 4096
+    x = haro.normal_f32(4001, 0, T * H).reshape(T, H)
+    ids, w = uniform_routing(T, 4002)
+    counts = np.bincount(ids.ravel(), minlength=E)
+    assert counts.min() > 0 and 60 <= counts.mean() <= 100  # every expert, ~80 tokens each
+    y = lay.run(ctx, x, ids, w)
+    assert np.isfinite(y).all()
+    sample = np.sort(np.random.default_rng(4003).choice(T, 256, replace=False))
+    ref = lay.oracle(x[sample], ids[sample], w[sample])
+    assert_close(y[sample], ref, nrms=TC_NRMS, what="config4 default path")
+    n, m = verdict(y[sample], ref)
+    print(f"config4: nrms {n:.3e} max|d| {m:.3e} max|d|/max|ref| {rel_max(y[sample], ref):.3e}")
+    # the tensor-core and CUDA-core paths agree on the same tokens
+    y_gemv = lay.run(ctx, x[sample], ids[sample], w[sample], har_cuda.MOE_FORCE_GEMV)
+    assert_close(y_gemv, ref, what="config4 tokens on the CUDA-core path")
+
+
+def _expert_rows(buf, e_list, rows, K_):
+    """Host copy of the Q4_K rows of experts e_list from a device [E*rows][K/256*144] tensor."""
+    rb = K_ // 256 * 144
+    t = buf.view(-1, rows * rb)[torch.as_tensor(e_list, device=buf.device)]
+    return t.cpu().numpy().reshape(len(e_list) * rows, rb)
+
+
+def test_config5_full_stack_layer_by_layer(ctx):
+    import bench
+    layers, keep, x, ids, w, _ = bench.build_stack(ctx, torch, 5, 0)
+    L, T = len(layers), x.shape[0]
+    assert (L, T) == (48, 256)
+    sub = np.array([0, 37, 101, 180, 255])
+    xd = to_dev(x)
+    idd, wd = to_dev(ids), to_dev(w)
+    # every layer on the GPU, one call per layer
+    outs = []
+    cur = xd
+    for l in range(L):
+        y = torch.empty_like(xd)
+        ctx.moe_ffn(layers[l], cur, idd[l], wd[l], y, RES)
+        outs.append(y[torch.as_tensor(sub, device=y.device)].cpu())
+        cur = y
+    torch.cuda.synchronize()
+    ctx.synchronize()
+    # the stack entry point (in place) equals the chain bit for bit
+    ys = xd.clone()
+    ctx.moe_stack(layers, ys, idd, wd, ys, RES)
+    torch.cuda.synchronize()
+    assert torch.equal(ys.cpu(), cur.cpu())
+    # each layer against the oracle on the token subset, fed the GPU's previous output
+    worst = 0.0
+    prev = x[sub]
+    for l in range(L):
+        t, gi = keep[l]
+        lid = ids[l][sub]
+        used = np.unique(lid)
+        remap = {int(e): j for j, e in enumerate(used)}
+        cid = np.vectorize(remap.get)(lid).astype(np.int32)
+        hg = _expert_rows(t["gate"], used, I, H)
+        hu = _expert_rows(t["up"], used, I, H)
+        hd = _expert_rows(t["down"], used, H, I)
+        sh = (t["sg"].cpu().numpy().reshape(I, -1), t["su"].cpu().numpy().reshape(I, -1),
+              t["sd"].cpu().numpy().reshape(H, -1))
+        ref = haro.moe_ffn(hg, hu, hd, sh, gi.cpu().numpy(), len(used), H, I, prev, cid,
+                           w[l][sub], add_residual=True)
+        got = outs[l].numpy()
+        # the residual dominates y = x + moe(x): check the layer's own output
+        assert_close(got - prev, ref - prev, nrms=TC_NRMS, what=f"config5 layer {l}")
+        worst = max(worst, verdict(got - prev, ref - prev)[0])
+        prev = got
+    print(f"config5: worst per-layer nrms {worst:.3e}")
+
+
+def test_in_place_layer_with_shared_gate_large_T(ctx):
+    # y aliasing x at prefill sizes: the shared expert's gate is computed from x
+    # before any block writes y, so in place equals out of place bit for bit
+    lay = Layer(ctx, 64, H, I, seed=4100)
+    T = 2048
+    x = haro.normal_f32(4101, 0, T * H).reshape(T, H)
+    ids, w = haro.zipf_routing(4102, T, 64, K)
+    for flags in (RES, RES | har_cuda.MOE_FORCE_GEMV):
+        xd, idd, wd = to_dev(x), to_dev(ids), to_dev(w)
+        out = torch.empty_like(xd)
+        ctx.moe_ffn(lay.layer, xd, idd, wd, out, flags)
+        ctx.moe_ffn(lay.layer, xd, idd, wd, xd, flags)  # in place
+        torch.cuda.synchronize()
+        assert torch.equal(out, xd), flags
+        # and as a two-layer stack
+        ids2 = np.stack([ids, ids[::-1].copy()])
+        w2 = np.stack([w, w[::-1].copy()])
+        xa = to_dev(x)
+        xb = to_dev(x)
+        yb = torch.empty_like(xb)
+        ctx.moe_stack([lay.layer, lay.layer], xa, to_dev(ids2), to_dev(w2), xa, flags)
+        ctx.moe_stack([lay.layer, lay.layer], xb, to_dev(ids2), to_dev(w2), yb, flags)
+        torch.cuda.synchronize()
+        assert torch.equal(xa, yb), flags
+
+
+def test_stack_host_graph_not_reused_for_recreated_layer(ctx):
+    # har_cuda_moe_stack_host caches a CUDA graph keyed on its layers.  A layer
+    # freed and another created (often at the same address) with other weights
+    # must not replay the first layer's graph: the old weights stay alive here,
+    # so a stale replay would show as a wrong answer, never as a fault.
+    a = Layer(ctx, 16, H, I, seed=4200)
+    b = Layer(ctx, 16, H, I, seed=4300)
+    x = haro.normal_f32(4201, 0, 8 * H).reshape(8, H)
+    ids, w = haro.zipf_routing(4202, 8, 16, 4)
+    ids, w = ids[None], w[None]
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        ctx.bind_torch_stream()
+        try:
+            lay_a = ctx.moe_layer(*a.weights[:3], a.weights[3], a.gi_dev)
+            ya = [ctx.moe_stack_host([lay_a], x, ids, w, RES) for _ in range(3)]  # 2nd captures, 3rd replays
+            lay_a.free()
+            lay_b = ctx.moe_layer(*b.weights[:3], b.weights[3], b.gi_dev)
+            yb = ctx.moe_stack_host([lay_b], x, ids, w, RES)
+            yd = torch.empty((8, H), dtype=torch.float32, device="cuda")
+            ctx.moe_stack([lay_b], to_dev(x), to_dev(ids), to_dev(w), yd, RES)
+            torch.cuda.synchronize()
+            assert np.array_equal(ya[0], ya[2])
+            assert np.array_equal(yb, yd.cpu().numpy())
+            assert not np.array_equal(yb, ya[0])
+            lay_b.free()
+        finally:
+            torch.cuda.synchronize()
+    ctx.bind_torch_stream()
+
+
+def test_ep_plan_and_combine_kernels(ctx):
+    # the expert-parallel exchange's two device steps on one GPU against numpy:
+    # plan rows for world 2/4/8, then the combine of synthetic partial sums
+    T, k = 37, K
+    x = haro.normal_f32(4401, 0, T * H).reshape(T, H)
+    ids, w = uniform_routing(T, 4402)
+    for world in (2, 4, 8):
+        El = E // world
+        sx = torch.zeros((world * T, H), dtype=torch.float32, device="cuda")
+        sids = torch.zeros((world * T, k), dtype=torch.int32, device="cuda")
+        sw = torch.zeros((world * T, k), dtype=torch.float32, device="cuda")
+        ctx.ep_plan(to_dev(x), to_dev(ids), to_dev(w), E, world, sx, sids, sw)
+        torch.cuda.synchronize()
+        owner = ids // El
+        lids = np.where(owner[None] == np.arange(world)[:, None, None],
+                        ids[None] - np.arange(world)[:, None, None] * El, -1).reshape(world * T, k)
+        lw = np.where(lids >= 0, np.broadcast_to(w, (world, T, k)).reshape(world * T, k), 0)
+        assert np.array_equal(sids.cpu().numpy(), lids), world
+        assert np.array_equal(sw.cpu().numpy(), lw.astype(np.float32)), world
+        got_x = sx.cpu().numpy().reshape(world, T, H)
+        for d in range(world):
+            for t in range(T):
+                if (owner[t] == d).any():
+                    assert np.array_equal(got_x[d, t], x[t]), (world, d, t)
+                else:
+                    assert not got_x[d, t].any(), (world, d, t)  # left unwritten
+        # combine: residual + shared + partials in rank order, f32 adds in sequence
+        sh = haro.normal_f32(4403 + world, 0, T * H).reshape(T, H)
+        back = haro.normal_f32(4413 + world, 0, world * T * H).reshape(world, T, H)
+        y = torch.empty((T, H), dtype=torch.float32, device="cuda")
+        ctx.ep_combine(to_dev(x), world, to_dev(sh), to_dev(back), y, RES)
+        torch.cuda.synchronize()
+        ref = (x + sh).astype(np.float32)
+        for d in range(world):
+            ref = (ref + back[d]).astype(np.float32)
+        assert np.array_equal(y.cpu().numpy(), ref), world
+        y0 = torch.empty((T, H), dtype=torch.float32, device="cuda")
+        ctx.ep_combine(to_dev(x), world, None, to_dev(back), y0, 0)
+        torch.cuda.synchronize()
+        ref0 = back[0].copy()
+        for d in range(1, world):
+            ref0 = (ref0 + back[d]).astype(np.float32)
+        assert np.array_equal(y0.cpu().numpy(), (np.float32(0) + ref0).astype(np.float32)), world
+    # an out-of-range expert id sets the device error word
+    bad = ids.copy()
+    bad[3, 2] = E + 7
+    sx = torch.zeros((2 * T, H), dtype=torch.float32, device="cuda")
+    si = torch.zeros((2 * T, k), dtype=torch.int32, device="cuda")
+    sw = torch.zeros((2 * T, k), dtype=torch.float32, device="cuda")
+    ctx.ep_plan(to_dev(x), to_dev(bad), to_dev(w), E, 2, sx, si, sw)
+    with pytest.raises(har_cuda.HarCudaError):
+        ctx.synchronize()
+    ctx.synchronize()
