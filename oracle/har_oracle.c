@@ -416,8 +416,74 @@ void haro_moe_ffn(const uint8_t *w_gate, const uint8_t *w_up, const uint8_t *w_d
  * which is correctly rounded; the GPU router computes the same. */
 static int haro_exp_mode = 0;
 void haro_set_exp_mode(int mode) { haro_exp_mode = mode; }
+
+/* glibc's expf restated (the function Rust's f32::exp calls): Szabolcs
+ * Nagy's table-driven method, published in ARM's optimized-routines and used
+ * by glibc since 2.28.  In double precision: k = round(x * 32/ln2) through
+ * the 1.5 * 2^52 shift, r = x * 32/ln2 - k, exp(x) = 2^(k/32) * P(r) with
+ * 2^(i/32) from a table (rounded to nearest double) and P a cubic with the
+ * method's published coefficients; one rounding to float at the end.  On
+ * x86-64 with FMA glibc runs the variant whose reduction and polynomial use
+ * fused multiply-adds, which fma() restates here.  The device router
+ * (expf_ref in the library) computes the same steps; haro_expf_mismatches
+ * checks this function against the host's expf. */
+static const uint64_t haro_exp2_i32[32] = {
+    0x3ff0000000000000ull, 0x3ff059b0d3158574ull, 0x3ff0b5586cf9890full, 0x3ff11301d0125b51ull,
+    0x3ff172b83c7d517bull, 0x3ff1d4873168b9aaull, 0x3ff2387a6e756238ull, 0x3ff29e9df51fdee1ull,
+    0x3ff306fe0a31b715ull, 0x3ff371a7373aa9cbull, 0x3ff3dea64c123422ull, 0x3ff44e086061892dull,
+    0x3ff4bfdad5362a27ull, 0x3ff5342b569d4f82ull, 0x3ff5ab07dd485429ull, 0x3ff6247eb03a5585ull,
+    0x3ff6a09e667f3bcdull, 0x3ff71f75e8ec5f74ull, 0x3ff7a11473eb0187ull, 0x3ff82589994cce13ull,
+    0x3ff8ace5422aa0dbull, 0x3ff93737b0cdc5e5ull, 0x3ff9c49182a3f090ull, 0x3ffa5503b23e255dull,
+    0x3ffae89f995ad3adull, 0x3ffb7f76f2fb5e47ull, 0x3ffc199bdd85529cull, 0x3ffcb720dcef9069ull,
+    0x3ffd5818dcfba487ull, 0x3ffdfc97337b9b5full, 0x3ffea4afa2a490daull, 0x3fff50765b6e4540ull};
+
+void haro_exp2_table(uint64_t *out) { memcpy(out, haro_exp2_i32, sizeof(haro_exp2_i32)); }
+
+float haro_expf_restated(float x) {
+    if (x < -0x1.9fe368p6f) return 0.0f;      /* below log(2^-150) */
+    if (x > 0x1.62e42ep6f) return INFINITY;    /* above log(2^128) */
+    const double inv = 0x1.71547652b82fep+0 * 32.0, shift = 0x1.8p+52;
+    const double c0 = 0x1.c6af84b912394p-5 / 32768.0, c1 = 0x1.ebfce50fac4f3p-3 / 1024.0,
+                 c2 = 0x1.62e42ff0c52d6p-1 / 32.0;
+    const double xd = (double)x;
+    double kd = fma(inv, xd, shift);
+    uint64_t ki;
+    memcpy(&ki, &kd, 8);
+    kd -= shift;
+    const double r = fma(inv, xd, -kd);
+    const uint32_t i = (uint32_t)(ki & 31u);
+    const uint64_t sb = haro_exp2_i32[i] + ((ki - i) << 47);
+    double sd;
+    memcpy(&sd, &sb, 8);
+    const double q = fma(c0, r, c1);
+    const double r2 = r * r;
+    double y = fma(c2, r, 1.0);
+    y = fma(q, r2, y);
+    return (float)(y * sd);
+}
+
+/* Floats with bit patterns lo..hi (inclusive, walked upward) where the
+ * restatement and the host's expf differ; *first gets the first such pattern. */
+uint64_t haro_expf_mismatches(uint32_t lo, uint32_t hi, uint32_t *first) {
+    uint64_t bad = 0;
+    for (uint32_t u = lo;; ++u) {
+        float x, a, b;
+        memcpy(&x, &u, 4);
+        a = expf(x);
+        b = haro_expf_restated(x);
+        if (memcmp(&a, &b, 4) != 0) {
+            if (!bad && first) *first = u;
+            ++bad;
+        }
+        if (u == hi) break;
+    }
+    return bad;
+}
+
 static float haro_router_exp(float v) {
-    return haro_exp_mode ? (float)exp((double)v) : expf(v);
+    if (haro_exp_mode == 1) return (float)exp((double)v);
+    if (haro_exp_mode == 2) return haro_expf_restated(v);
+    return expf(v);
 }
 
 /* f32::total_cmp(b, a) ordering then lower index (descending by p). Returns

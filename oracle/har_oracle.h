@@ -116,6 +116,12 @@ void haro_compose_moe_route(const uint8_t *w_gate, const uint8_t *w_up,
 void haro_route_topk(const float *logits, int E, int k, int32_t *ids, float *weights);
 /* 0: exp = glibc expf (the reference's f32::exp); 1: correctly rounded exp. */
 void haro_set_exp_mode(int mode);
+/* glibc's expf restated (Nagy's table-driven method, fused multiply-adds as on
+ * x86-64 with FMA), its 2^(i/32) table, and a counter of the floats in a bit
+ * pattern range where it differs from the host's expf. */
+float haro_expf_restated(float x);
+void haro_exp2_table(uint64_t *out);
+uint64_t haro_expf_mismatches(uint32_t lo, uint32_t hi, uint32_t *first);
 
 /* ---- a9: expert-major grouping ------------------------------------------- */
 /* har/crates/har-serve/src/moe.rs:195-202: groups[e] = positions routed to e

@@ -71,6 +71,9 @@ def lib():
         "haro_zipf_routing": (None, [C.c_uint64, _i64, C.c_int, C.c_int, C.c_double, _i32p, _f32p]),
         "haro_online_cpus": (C.c_int, []),
         "haro_set_exp_mode": (None, [C.c_int]),
+        "haro_expf_restated": (C.c_float, [C.c_float]),
+        "haro_exp2_table": (None, [C.POINTER(C.c_uint64)]),
+        "haro_expf_mismatches": (C.c_uint64, [C.c_uint32, C.c_uint32, C.POINTER(C.c_uint32)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -154,8 +157,10 @@ def sigmoid(v: float) -> float:
 def route_topk(logits: np.ndarray, k: int, exp_mode: int = 0):
     """har/crates/har-demo/src/bin/har-native-qwen35moe.rs:1167-1204, per row.
 
-    exp_mode 0 uses glibc's expf (the reference's f32::exp); 1 a correctly
-    rounded exp (what the GPU router computes)."""
+    exp_mode 0 uses glibc's expf (the reference's f32::exp); 2 its
+    restatement (haro_expf_restated, the steps the GPU router computes; equal
+    to mode 0 bit for bit); 1 the correctly rounded exp (differs from glibc's
+    on ~1 in 11,500 inputs)."""
     lib().haro_set_exp_mode(exp_mode)
     logits = np.ascontiguousarray(logits, np.float32)
     T, E = logits.shape
@@ -317,3 +322,24 @@ def moe_ffn(w_gate, w_up, w_down, shared, sh_gate_inp, E, H, I, x, ids, weights,
 
 def online_cpus() -> int:
     return lib().haro_online_cpus()
+
+
+def expf_restated(x: float) -> float:
+    """glibc's expf restated (Nagy's table-driven method), as the GPU router computes it."""
+    return lib().haro_expf_restated(x)
+
+
+def exp2_table():
+    """The restatement's 32-entry table of 2^(i/32) as IEEE double bit patterns."""
+    out = (C.c_uint64 * 32)()
+    lib().haro_exp2_table(out)
+    return list(out)
+
+
+def expf_mismatches(lo_bits: int, hi_bits: int):
+    """(count, first bit pattern) of floats in [lo_bits, hi_bits] where the
+    restatement differs from the host's expf (ctypes releases the GIL: callers
+    may run ranges on several threads)."""
+    first = C.c_uint32(0)
+    n = lib().haro_expf_mismatches(lo_bits, hi_bits, C.byref(first))
+    return int(n), int(first.value)

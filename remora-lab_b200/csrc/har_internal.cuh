@@ -92,11 +92,52 @@ __device__ __forceinline__ uint4 ldg_nc_v4(const void *p) {
   return r;
 }
 
-// sigmoid of har-native-qwen35moe.rs:207-214
+// expf as the reference computes it.  Rust's f32::exp is glibc's expf, which
+// since glibc 2.28 is Szabolcs Nagy's table-driven method (published in ARM's
+// optimized-routines): in double precision, k = round(x * 32/ln2) and
+// r = x * 32/ln2 - k, exp(x) = 2^(k/32) * P(r) with 2^(i/32) from a 32-entry
+// table and P a cubic; the double result is rounded once to float.  On x86-64
+// hosts with FMA (the ifunc variant glibc selects there) the reduction and
+// the polynomial use fused multiply-adds, restated here with fma().  Checked
+// against the host's expf on every float in [-104, 0] (the router's domain:
+// logit - max), bit for bit.  The table holds 2^(i/32) rounded to nearest
+// double; the three coefficients are the method's published values.
+__device__ const uint64_t EXP2_I32[32] = {
+    0x3ff0000000000000ull, 0x3ff059b0d3158574ull, 0x3ff0b5586cf9890full, 0x3ff11301d0125b51ull,
+    0x3ff172b83c7d517bull, 0x3ff1d4873168b9aaull, 0x3ff2387a6e756238ull, 0x3ff29e9df51fdee1ull,
+    0x3ff306fe0a31b715ull, 0x3ff371a7373aa9cbull, 0x3ff3dea64c123422ull, 0x3ff44e086061892dull,
+    0x3ff4bfdad5362a27ull, 0x3ff5342b569d4f82ull, 0x3ff5ab07dd485429ull, 0x3ff6247eb03a5585ull,
+    0x3ff6a09e667f3bcdull, 0x3ff71f75e8ec5f74ull, 0x3ff7a11473eb0187ull, 0x3ff82589994cce13ull,
+    0x3ff8ace5422aa0dbull, 0x3ff93737b0cdc5e5ull, 0x3ff9c49182a3f090ull, 0x3ffa5503b23e255dull,
+    0x3ffae89f995ad3adull, 0x3ffb7f76f2fb5e47ull, 0x3ffc199bdd85529cull, 0x3ffcb720dcef9069ull,
+    0x3ffd5818dcfba487ull, 0x3ffdfc97337b9b5full, 0x3ffea4afa2a490daull, 0x3fff50765b6e4540ull};
+
+__device__ __forceinline__ float expf_ref(float x) {
+  if (x < -0x1.9fe368p6f) return 0.0f;             // below log(2^-150): rounds to zero
+  if (x > 0x1.62e42ep6f) return __int_as_float(0x7f800000);  // above log(2^128): overflow
+  const double inv = 0x1.71547652b82fep+0 * 32.0, shift = 0x1.8p+52;
+  const double c0 = 0x1.c6af84b912394p-5 / 32768.0, c1 = 0x1.ebfce50fac4f3p-3 / 1024.0,
+               c2 = 0x1.62e42ff0c52d6p-1 / 32.0;
+  const double xd = (double)x;
+  double kd = __fma_rn(inv, xd, shift);             // round(x * 32/ln2) in the low bits
+  const uint64_t ki = (uint64_t)__double_as_longlong(kd);
+  kd -= shift;
+  const double r = __fma_rn(inv, xd, -kd);          // |r| <= 1/2
+  const uint32_t i = (uint32_t)(ki & 31u);
+  // 2^(k/32) = 2^(i/32) * 2^((k - i)/32): add (k - i)/32 to the table entry's exponent
+  const double s = __longlong_as_double((long long)(__ldg(&EXP2_I32[i]) + ((ki - i) << 47)));
+  const double q = __fma_rn(c0, r, c1);
+  const double r2 = __dmul_rn(r, r);
+  double y = __fma_rn(c2, r, 1.0);
+  y = __fma_rn(q, r2, y);
+  return __double2float_rn(__dmul_rn(y, s));
+}
+
+// sigmoid of har-native-qwen35moe.rs:207-214, with the reference's exp
 __device__ __forceinline__ float sigmoid_f(float v) {
-  if (v >= 0.0f) return 1.0f / (1.0f + expf(-v));
-  const float e = expf(v);
-  return e / (1.0f + e);
+  if (v >= 0.0f) return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf_ref(-v)));
+  const float e = expf_ref(v);
+  return __fdiv_rn(e, __fadd_rn(1.0f, e));
 }
 
 __device__ __forceinline__ float warp_sum(float v) {

@@ -5,10 +5,8 @@
 // reference's f32 operation order: max fold, exp(l - max), sequential sum in
 // index order clamped to >= 1e-9, p = e / sum, order by p descending then
 // lower index, take k, renormalise by the sequential sum of the selected p
-// (clamped to >= 1e-9).  exp is the correctly rounded value (f32 result of
-// exp evaluated in double); the reference's f32::exp (glibc expf) differs
-// from it on about 1 in 11,500 inputs, which can move a weight by an ulp but
-// not the selected ids.
+// (clamped to >= 1e-9).  exp is expf_ref, the reference's f32::exp (glibc's
+// expf) restated, so ids and weights are bit-exact.
 //
 // group_kernel restates MoEModel::forward_batch's grouping
 // (har/crates/har-serve/src/moe.rs:195-202): groups[e] holds the entries
@@ -35,7 +33,7 @@ __device__ __forceinline__ void topk_warp(const float *l, int E, int k, float *p
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
 #pragma unroll 4
-  for (int i = lane; i < E; i += 32) p[i] = (float)exp((double)__fsub_rn(__ldcg(l + i), mx));
+  for (int i = lane; i < E; i += 32) p[i] = expf_ref(__fsub_rn(__ldcg(l + i), mx));
   __syncwarp();
   float den = 0.0f;
   if (lane == 0) {  // exps.iter().sum(): one chain in index order

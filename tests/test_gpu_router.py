@@ -81,13 +81,10 @@ def test_route_from_tokens_bit_exact(T, E, H, k):
     torch.cuda.synchronize()
     ctx.synchronize()
     logits = haro.router_logits(w, x)
-    ref_ids, ref_w = haro.route_topk(logits, k, exp_mode=1)   # the GPU's exp
     har_ids, har_w = haro.route_topk(logits, k, exp_mode=0)   # glibc expf, as Rust
     gi, gw = ids.cpu().numpy(), wts.cpu().numpy()
-    assert np.array_equal(gi, ref_ids)
     assert np.array_equal(gi, har_ids)
-    assert np.array_equal(gw.view(np.uint32), ref_w.view(np.uint32))
-    assert np.max(np.abs(gw - har_w) / np.maximum(np.abs(har_w), 1e-30)) <= 1e-6
+    assert np.array_equal(gw.view(np.uint32), har_w.view(np.uint32))
     ctx.close()
 
 
@@ -112,7 +109,7 @@ def test_routed_moe_matches_oracle(T, flags):
     ctx.routed_moe(L.layer, to_dev(w), xd, k, ids, wts, y, flags)
     torch.cuda.synchronize()
     ctx.synchronize()
-    ref_ids, ref_w = haro.route_topk(haro.router_logits(w, x), k, exp_mode=1)
+    ref_ids, ref_w = haro.route_topk(haro.router_logits(w, x), k, exp_mode=0)
     assert np.array_equal(ids.cpu().numpy(), ref_ids)
     assert np.array_equal(wts.cpu().numpy().view(np.uint32), ref_w.view(np.uint32))
     ref = L.oracle(x, ref_ids, ref_w)

@@ -52,7 +52,7 @@ def _oracle_step(host, embed, out, h, t):
     routes = []
     for b in range(2):
         hg, hu, hd, sh, gi, rt = host[b]
-        ids, w = haro.route_topk(haro.router_logits(rt, x), K_USED, exp_mode=1)
+        ids, w = haro.route_topk(haro.router_logits(rt, x), K_USED, exp_mode=0)
         routes.append(ids[0])
         x = haro.moe_ffn(hg, hu, hd, sh, gi, E, H, I, x, ids, w, add_residual=True)
     return x[0], haro.q6k_matvec(out, V, H, x)[0], routes
