@@ -9,8 +9,9 @@ in-place and caching hazards of the layer entry points.
 - Config 5 (what bench.py times): the 48-layer stack that
   bench.py builds (same seeds), 256 tokens, Zipf(1.1) top-10 per layer.  Every
   layer runs on the GPU; a token subset is checked layer by layer against the
-  oracle, each layer fed the GPU's output of the layer before, and the stack
-  entry point must equal the chain of per-layer calls bit for bit.
+  oracle, each layer fed the GPU's (RMS-normalised) output of the layer
+  before, and the stack entry point must equal the chain of per-layer calls
+  bit for bit.
 """
 import numpy as np
 import pytest
@@ -68,31 +69,44 @@ def _expert_rows(buf, e_list, rows, K_):
 
 
 def test_config5_full_stack_layer_by_layer(ctx):
+    # The stack without the attention blocks and norms between its layers
+    # (BASELINE's "attention omitted") is y = x + moe(x) 48 times; SwiGLU makes
+    # moe(x) grow like |x|^2, so from N(0,1) inputs the residual stream
+    # overflows after a dozen layers -- in the reference's f32 as here.  The
+    # per-layer parity chain therefore RMS-normalises each layer's input (the
+    # test's own step, not the library's); the stack entry point is checked
+    # against the plain chain of per-layer calls bit for bit, overflow included.
     import bench
     layers, keep, x, ids, w, _ = bench.build_stack(ctx, torch, 5, 0)
     L, T = len(layers), x.shape[0]
     assert (L, T) == (48, 256)
     sub = np.array([0, 37, 101, 180, 255])
+    subd = torch.as_tensor(sub, device="cuda")
     xd = to_dev(x)
     idd, wd = to_dev(ids), to_dev(w)
-    # every layer on the GPU, one call per layer
-    outs = []
+    # 1. the stack entry point (in place) equals the chain of per-layer calls
     cur = xd
     for l in range(L):
         y = torch.empty_like(xd)
         ctx.moe_ffn(layers[l], cur, idd[l], wd[l], y, RES)
-        outs.append(y[torch.as_tensor(sub, device=y.device)].cpu())
         cur = y
-    torch.cuda.synchronize()
-    ctx.synchronize()
-    # the stack entry point (in place) equals the chain bit for bit
     ys = xd.clone()
     ctx.moe_stack(layers, ys, idd, wd, ys, RES)
     torch.cuda.synchronize()
-    assert torch.equal(ys.cpu(), cur.cpu())
-    # each layer against the oracle on the token subset, fed the GPU's previous output
+    ctx.synchronize()
+    assert torch.equal(ys.view(torch.int32), cur.view(torch.int32))
+    # 2. every layer against the oracle on a token subset, inputs RMS-normalised
+    ins, outs = [], []
+    cur = xd
+    for l in range(L):
+        inp = (cur / cur.pow(2).mean(dim=1, keepdim=True).sqrt()).contiguous()
+        y = torch.empty_like(xd)
+        ctx.moe_ffn(layers[l], inp, idd[l], wd[l], y, RES)
+        ins.append(inp[subd].cpu().numpy())
+        outs.append(y[subd].cpu().numpy())
+        cur = y
+    torch.cuda.synchronize()
     worst = 0.0
-    prev = x[sub]
     for l in range(L):
         t, gi = keep[l]
         lid = ids[l][sub]
@@ -104,13 +118,14 @@ def test_config5_full_stack_layer_by_layer(ctx):
         hd = _expert_rows(t["down"], used, H, I)
         sh = (t["sg"].cpu().numpy().reshape(I, -1), t["su"].cpu().numpy().reshape(I, -1),
               t["sd"].cpu().numpy().reshape(H, -1))
+        prev = ins[l]
         ref = haro.moe_ffn(hg, hu, hd, sh, gi.cpu().numpy(), len(used), H, I, prev, cid,
                            w[l][sub], add_residual=True)
-        got = outs[l].numpy()
+        got = outs[l]
+        assert np.isfinite(got).all(), l
         # the residual dominates y = x + moe(x): check the layer's own output
         assert_close(got - prev, ref - prev, nrms=TC_NRMS, what=f"config5 layer {l}")
         worst = max(worst, verdict(got - prev, ref - prev)[0])
-        prev = got
     print(f"config5: worst per-layer nrms {worst:.3e}")
 
 
