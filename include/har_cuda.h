@@ -60,6 +60,9 @@ extern "C" {
 #define HAR_CUDA_MOE_FORCE_TC 0x8u     /* every expert on the tcgen05 tensor-core path */
 #define HAR_CUDA_MOE_EMPTY_SLOTS 0x10u /* expert id -1 marks an empty slot (no contribution);
                                           used by the expert-parallel exchange */
+#define HAR_CUDA_MOE_TC_F16W 0x20u     /* tensor-core experts round each dequantised weight
+                                          to f16 (faster; max relative error ~4e-4, not
+                                          HAR's 5e-5 RMS verdict, which the default meets) */
 
 typedef struct har_cuda_ctx har_cuda_ctx;
 typedef struct har_cuda_weights har_cuda_weights;

@@ -285,8 +285,12 @@ int32_t har_cuda_synchronize(har_cuda_ctx *ctx, int64_t timeout_ms) {
   if (word != 0) {
     cudaMemsetAsync(ctx->d_status, 0, sizeof(int), ctx->stream);
     cudaStreamSynchronize(ctx->stream);
-    return set_error(ctx, word & DEV_ERR_TIMEOUT ? HAR_CUDA_ERR_TIMEOUT : HAR_CUDA_ERR_DEVICE,
-                     "a kernel reported device error word " + std::to_string(word));
+    std::string why = "a kernel reported device error word " + std::to_string(word);
+    if (word & DEV_ERR_TIMEOUT) why += " (a bounded wait ran out)";
+    if (word & DEV_ERR_BOUNDS) why += " (an expert id out of range)";
+    if (word & DEV_ERR_RANGE)
+      why += " (a Q4_K block outside the tensor-core path's range: run it with HAR_CUDA_MOE_FORCE_GEMV)";
+    return set_error(ctx, word & DEV_ERR_TIMEOUT ? HAR_CUDA_ERR_TIMEOUT : HAR_CUDA_ERR_DEVICE, why);
   }
   return HAR_CUDA_OK;
 }
@@ -581,7 +585,7 @@ int32_t har::check_moe_args(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, 
   if ((flags & HAR_CUDA_MOE_ACT_Q8K) && (flags & HAR_CUDA_MOE_FORCE_TC))
     return set_error(ctx, HAR_CUDA_ERR_UNSUPPORTED,
                      "moe_ffn: the tensor-core path has no Q8_K activation mode");
-  if (flags & ~0x1Fu) return set_error(ctx, HAR_CUDA_ERR_ARG, "moe_ffn: unknown flag bits");
+  if (flags & ~0x3Fu) return set_error(ctx, HAR_CUDA_ERR_ARG, "moe_ffn: unknown flag bits");
   return HAR_CUDA_OK;
 }
 

@@ -27,6 +27,9 @@ constexpr float ROUTER_EPS = 1.0e-9f;
 // Device error words (bit flags) written by kernels; read by har_cuda_synchronize.
 constexpr int DEV_ERR_TIMEOUT = 1;
 constexpr int DEV_ERR_BOUNDS = 2;
+// a Q4_K block the tensor-core path cannot represent exactly (min offset above
+// 2^29 times its scale step); the call's results are not valid
+constexpr int DEV_ERR_RANGE = 4;
 
 // ---------------------------------------------------------------------------
 // Q4_K super-block header: 16 bytes = {d|dmin<<16, sc/m bytes 0-3, 4-7, 8-11}

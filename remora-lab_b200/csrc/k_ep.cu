@@ -182,8 +182,8 @@ int32_t ep_layer(har_cuda_ctx *ctx, har_cuda_ep *ep, const har_cuda_moe_layer *l
   const EpLayout L = ep_layout(G, T, k, H);
   int32_t st = ep_reserve(ctx, ep, L.total);
   if (st) return st;
-  const uint32_t mode0 =
-      flags & (HAR_CUDA_MOE_ACT_Q8K | HAR_CUDA_MOE_FORCE_GEMV | HAR_CUDA_MOE_FORCE_TC);
+  const uint32_t mode0 = flags & (HAR_CUDA_MOE_ACT_Q8K | HAR_CUDA_MOE_FORCE_GEMV |
+                                  HAR_CUDA_MOE_FORCE_TC | HAR_CUDA_MOE_TC_F16W);
   // Both expert calls of the layer share the context's scratch arena: size it
   // for the larger one before the first launch, so the arena never grows (a
   // synchronising reallocation) between the two calls.
@@ -198,8 +198,7 @@ int32_t ep_layer(har_cuda_ctx *ctx, har_cuda_ep *ep, const har_cuda_moe_layer *l
   float *ysh = (float *)(B + L.ysh), *g = (float *)(B + L.g);
   int32_t *sids = (int32_t *)(B + L.sids), *rids = (int32_t *)(B + L.rids);
   int32_t *ids0 = (int32_t *)(B + L.ids0);
-  const uint32_t mode =
-      flags & (HAR_CUDA_MOE_ACT_Q8K | HAR_CUDA_MOE_FORCE_GEMV | HAR_CUDA_MOE_FORCE_TC);
+  const uint32_t mode = mode0;
   // Compute runs on ctx->stream, the exchanges on ep->cs; events order them:
   // plan -> dispatch -> local experts -> return -> combine, with the shared
   // expert (it needs only this rank's x) computing while the dispatch moves
@@ -280,7 +279,7 @@ int32_t ep_check(har_cuda_ctx *ctx, har_cuda_ep *ep, const har_cuda_moe_layer *l
     return set_error(ctx, HAR_CUDA_ERR_UNSUPPORTED,
                      "ep: the tensor-core path has no Q8_K activation mode");
   if (flags & ~(HAR_CUDA_MOE_ADD_RESIDUAL | HAR_CUDA_MOE_ACT_Q8K | HAR_CUDA_MOE_FORCE_GEMV |
-                HAR_CUDA_MOE_FORCE_TC))
+                HAR_CUDA_MOE_FORCE_TC | HAR_CUDA_MOE_TC_F16W))
     return set_error(ctx, HAR_CUDA_ERR_ARG, "ep: unknown flag bits");
   return HAR_CUDA_OK;
 }

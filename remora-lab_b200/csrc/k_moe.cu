@@ -374,7 +374,7 @@ static size_t al256(size_t v) { return (v + 255) & ~(size_t)255; }
 // Scratch layout of one moe_ffn call (offsets in bytes, 256-byte aligned).
 struct MoeScratch {
   size_t o_counts, o_offsets, o_order, o_inv, o_ne, o_nne, o_xq, o_a, o_aq, o_y;
-  size_t o_ttinfo, o_ntt, o_x16, o_a16, o_gsh, total;
+  size_t o_ttinfo, o_ntt, o_x16, o_a16, o_xs16, o_as16, o_gsh, total;
 };
 
 // Experts with at least this many tokens take the tensor-core path
@@ -438,6 +438,9 @@ static MoeScratch moe_layout(const har_cuda_moe_layer *layer, int64_t T, int k, 
   s.o_ntt = take(4);
   s.o_x16 = tc ? take(4 * (size_t)(slots * H)) : 0;  // token rows in slot order (f16 hi/lo)
   s.o_a16 = tc ? take(4 * (size_t)(slots * I)) : 0;
+  // min-term operands of the B rows: [2 * slots][K/16] f16
+  s.o_xs16 = tc ? take(2 * (size_t)(2 * slots * (H / 16))) : 0;
+  s.o_as16 = tc ? take(2 * (size_t)(2 * slots * (I / 16))) : 0;
   s.o_gsh = take(4 * (size_t)T);
   s.total = off;
   return s;
@@ -471,6 +474,7 @@ int32_t run_moe_ffn_in(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const
   const int has_sh = layer->sh_gate ? 1 : 0;
   const int64_t xq_row = (int64_t)(H / QK) * Q8K_BYTES, aq_row = (int64_t)(I / QK) * Q8K_BYTES;
   const bool tc = tc_possible(ctx, layer, T, k, flags);
+  const bool f16w = (flags & HAR_CUDA_MOE_TC_F16W) != 0;  // the f16-weight tensor-core variant
   const int thr = tc ? tc_threshold(ctx, flags) : INT_MAX;
   const bool shared_tc = has_sh && tc && T >= thr;
   if (tc && ((H % TC_M) || (I % TC_M) || (H % TC_KS) || (I % TC_KS)))
@@ -556,8 +560,17 @@ int32_t run_moe_ffn_in(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const
       dmaps.sh1 = layer->map_sh_down;
     }
     // token rows in slot order (f16 hi/lo row pairs): the B operands, one box
-    // of 32/64 rows x 64 values per K-step
+    // of 32/64 rows x 64 values per K-step; and their min-term operands, two
+    // boxes of 32/64 rows x 8 values per super-block
     const uint64_t rows2 = 2 * (uint64_t)(n + T);
+    for (int bx = 0; bx < TC_NBOX; ++bx) {
+      if ((st = encode_tmap_2d(ctx, &gmaps.s16[bx], S + L.o_xs16, 2, rows2, (uint64_t)(H / 16),
+                               (uint64_t)(H / 16) * 2, 32u << bx, 8, false)))
+        return st;
+      if ((st = encode_tmap_2d(ctx, &dmaps.s16[bx], S + L.o_as16, 2, rows2, (uint64_t)(I / 16),
+                               (uint64_t)(I / 16) * 2, 32u << bx, 8, false)))
+        return st;
+    }
     for (int bx = 0; bx < TC_NBOX; ++bx) {
       if ((st = encode_tmap_2d(ctx, &gmaps.b[bx], S + L.o_x16, 2, rows2, (uint64_t)H,
                                (uint64_t)H * 2, 32u << bx, 64, true)))
@@ -567,7 +580,7 @@ int32_t run_moe_ffn_in(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const
         return st;
     }
     if ((st = launch_gather_f16(ctx, x, H, p.order, ids, p.counts, p.offsets + E, thr, (int)n, k,
-                                (int)T, tp.shared_tc, (__half *)(S + L.o_x16),
+                                (int)T, tp.shared_tc, (__half *)(S + L.o_x16), (__half *)(S + L.o_xs16),
                                 tp.shared_tc ? layer->sh_gate_inp : nullptr, (float *)(S + L.o_gsh))))
       return st;
   }
@@ -597,8 +610,15 @@ int32_t run_moe_ffn_in(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const
     g.rows = I;
     g.K = H;
     g.out_ld = I;
-    if ((st = launch_moe_tc(ctx, gmaps, g, 2, (int)std::min<int64_t>(INT_MAX, max_tc_tt * (I / TC_M)))))
-      return st;
+    g.w0 = p.gate;
+    g.w1 = p.up;
+    g.sw0 = p.sh_gate;
+    g.sw1 = p.sh_up;
+    g.row_bytes = p.rb_h;
+    g.s16_out = (__half *)(S + L.o_as16);
+    st = f16w ? launch_moe_tc_f16w(ctx, gmaps, g, 2, (int)std::min<int64_t>(INT_MAX, max_tc_tt * (I / TC_M)))
+              : launch_moe_tc(ctx, gmaps, g, 2, (int)std::min<int64_t>(INT_MAX, max_tc_tt * (I / TC_M)));
+    if (st) return st;
   }
   if (q8 && (st = launch_q8k_quantize(ctx, p.a, n + (has_sh ? T : 0), I, S + o_aq))) return st;
   if (gemv_work) {
@@ -612,8 +632,13 @@ int32_t run_moe_ffn_in(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const
     d.rows = H;
     d.K = I;
     d.out_ld = H;
-    if ((st = launch_moe_tc(ctx, dmaps, d, 1, (int)std::min<int64_t>(INT_MAX, max_tc_tt * (H / TC_M)))))
-      return st;
+    d.w0 = d.w1 = p.down;
+    d.sw0 = d.sw1 = p.sh_down;
+    d.row_bytes = p.rb_i;
+    d.s16_out = nullptr;
+    st = f16w ? launch_moe_tc_f16w(ctx, dmaps, d, 1, (int)std::min<int64_t>(INT_MAX, max_tc_tt * (H / TC_M)))
+              : launch_moe_tc(ctx, dmaps, d, 1, (int)std::min<int64_t>(INT_MAX, max_tc_tt * (H / TC_M)));
+    if (st) return st;
   }
   prof_begin(ctx);
   moe_combine_kernel<<<dim3((unsigned)T, (unsigned)((H / 4 + COMB_T - 1) / COMB_T)), COMB_T, 0, ctx->stream>>>(

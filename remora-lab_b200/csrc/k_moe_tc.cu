@@ -8,19 +8,30 @@
 // rows x up to 32 tokens, so a tile of W is dequantised once for up to 32
 // tokens.  Each token is two B rows, the f16 value and the f16 remainder
 // (hi = f16(x), lo = f16(x - hi)), so activations reach the tensor cores with
-// ~22 significant bits and only the weights are rounded to f16; the epilogue
-// adds the two accumulator columns.  D = W_tile * X^T accumulates in TMEM (f32).
-//   gate/up: two accumulators (gate rows and up rows of the same 128
-//            intermediate indices); epilogue a = silu(g) * u -> a16 (hi/lo f16
-//            rows of the slot, the down GEMM's B operand).
-//   down:    one accumulator; epilogue ybuf[slot][h] (f32), then the common
-//            combine kernel applies the routing weights in slot order.
+// ~22 significant bits; the epilogue adds the two accumulator columns.
 //
-// With few tokens per expert the MMAs are narrow (N = 32..64) and issue
-// rate matters: one SM's share of HBM bandwidth is ~40 Q4_K weights per cycle,
-// and a K-step (NA x 4 MMAs of 128 x 16 weights) must issue in ~400 cycles.
-// The issuing warp stays warp-uniform, elects its lane once and issues a
-// K-step's MMAs from one asm block (~40 cycles per MMA, measured).
+// Numerics (f32-grade: HAR's differential verdict, normalised RMS <= 5e-5,
+// holds with a wide margin).  A Q4_K weight of sub-block j of super-block b is
+// w = d_b*sc_j*q - dmin_b*m_j (q4k.rs:77-89).  Split the row's dot product by
+// super-block:
+//   sum_k w_k x_k = sum_b s_b * [ sum_{k in b} (sc_j q_k 2^-e_b) x_k
+//                                 + sum_j c_bj S_bj(x) ],
+//   s_b = d_b 2^e_b,  c_bj = -m_j dmin_b / s_b,
+// S_bj(x) = the sum of x over sub-block j of super-block b.  sc*q*2^-e is a
+// small integer times a power of two, exact in f16, so the tensor cores see
+// exact weights; the min term is one more K=16 MMA per super-block whose A
+// operand is c_bj split into f16 hi + lo (8 x 2 values per row, from shared
+// memory) and whose B operand is S_bj split the same way (precomputed per
+// token row).  Each super-block accumulates into its own TMEM unit, which the
+// epilogue scales by s_b in f32.  e_b >= 0 is the smallest shift that keeps
+// |c_bj| < 2^15 (e_b = 0 unless dmin > 512 d); d = 0 drops the sc*q term.
+// Nothing is rounded to f16 but the hi/lo splits (~22 bits each).
+//   gate/up: two accumulators per unit (gate rows and up rows of the same 128
+//            intermediate indices); after the last unit a = silu(g) * u ->
+//            a16 (hi/lo f16 rows of the slot, the down GEMM's B operand) and
+//            a's sub-block sums (the down GEMM's min-term operand).
+//   down:    ybuf[slot][h] (f32); the common combine kernel then applies the
+//            routing weights in slot order.
 //
 // One persistent CTA per SM, warp-specialised, every handoff an mbarrier:
 //   TMA threads:  one loads raw Q4_K boxes (128 rows x one 144-byte
@@ -28,34 +39,31 @@
 //                 another loads 128-byte-swizzled f16 token tiles (64 values x
 //                 32/64 rows: the smallest box covering the tile's hi/lo rows,
 //                 which sit in slot order) into a B ring whose 16 KB slots
-//                 hold 128/box-rows K-steps each.
+//                 hold 128/box-rows K-steps each, and per super-block the same
+//                 rows' min-term operand (16 values each) into an S ring.
 //   dequant warps: four teams of four, team t taking the K-steps ks = t
-//                 (mod 4), turn the raw blocks into f16 weights with packed-f16
-//                 arithmetic and store them straight into the team's
-//                 tensor-memory stage with tcgen05.st (warp w owns TMEM lanes
-//                 32*(w%4).. = those rows).  Keeping the weight operand out of
-//                 shared memory keeps its write and its tensor-core read off
-//                 the shared-memory bandwidth.  The dequantisation is most of
-//                 the kernel's instruction stream, hence the 16 warps.
-//   MMA warp:     4 x tcgen05.mma (K=16, A from TMEM, B from shared memory)
-//                 per matrix per K-step; tcgen05.commit frees the weight stage
-//                 and the B slot, and signals the epilogue at the end of a tile.
-//   epilogue warps: tcgen05.ld the accumulator (hi and lo columns of each
-//                 token), add, apply the epilogue, store, then free the
-//                 accumulator columns.
+//                 (mod 4), turn the raw blocks into the f16 values sc*q*2^-e
+//                 and store them straight into the team's tensor-memory stage
+//                 with tcgen05.st (warp w owns TMEM lanes 32*(w%4).. = those
+//                 rows); each team also writes c_bj hi/lo of its two
+//                 sub-blocks of those rows into a shared-memory A' ring.
+//   MMA warp:     per super-block unit, 4 K-steps of 4 x tcgen05.mma (K=16, A
+//                 from TMEM, B from shared memory) per matrix into a fresh
+//                 accumulator, then the min-term MMA (A' and S from shared
+//                 memory); tcgen05.commit frees the stages and slots, and
+//                 hands the unit to the epilogue.
+//   epilogue warps: eight, two per TMEM lane group (tokens 0..15 and 16..31
+//                 of a tile): per unit tcgen05.ld the hi and lo columns and
+//                 accumulate s_b * (hi + lo) in registers, then free the unit;
+//                 after the tile's last unit, the output.
 // No multicast: every TMA load reads this GPU's memory into this CTA only.
-// Operands are f16 (same tensor rate as bf16, 3 more mantissa bits): each
-// weight is rounded once to f16 from d*sc*(q - 8) (exact) plus a centred
-// per-sub-block offset rounded to f16; activations are hi/lo f16 pairs;
-// accumulation is f32.
 // K order: inside every group of four K values both operands hold positions
 // (0, 2, 1, 3) -- the order in which nibble pairs come out of a 32-bit word
 // with one mask each -- which leaves every dot product unchanged.
 #include <algorithm>
 
 #include "gemv_engine.cuh"
-#include "moe_tc.cuh"
-#include "tc_ptx.cuh"
+#include "tc_pipeline.cuh"
 
 namespace har {
 
@@ -65,186 +73,123 @@ namespace har {
 template <int NA>
 struct TcSmem {
   static constexpr int RAW_SLOTS = NA == 2 ? 4 : 6;
-  static constexpr int B_SLOTS = 4;
+  static constexpr int B_SLOTS = 3;
+  static constexpr int S_SLOTS = 4;               // min-term B operands in flight (one per unit)
+  static constexpr int AP_SLOTS = 2;              // min-term A operands in flight
   static constexpr int BSL = 128 * 128;           // 16 KB: 128 rows of 64 f16
   static constexpr int RAWSL = NA * TC_M * Q4K_BYTES;
-  static constexpr int OFF_B = 0;                 // 1024-aligned swizzled buffers first
-  static constexpr int OFF_RAW = OFF_B + B_SLOTS * BSL;
+  static constexpr int SSL = 64 * 16 * 2;         // up to 64 B rows x 16 f16 (two 8-value boxes)
+  static constexpr int APM = TC_M * 16 * 2;       // one matrix's A': 128 rows x 16 f16
+  static constexpr int APSL = NA * APM;
+  // The 1024-aligned swizzled B ring first; the small no-swizzle rings next
+  // (their descriptors' strides stay well inside the buffer); the raw ring last.
+  static constexpr int OFF_B = 0;
+  static constexpr int OFF_S = OFF_B + B_SLOTS * BSL;
+  static constexpr int OFF_AP = OFF_S + S_SLOTS * SSL;
+  static constexpr int OFF_RAW = OFF_AP + AP_SLOTS * APSL;
   static constexpr int BYTES = OFF_RAW + RAW_SLOTS * RAWSL;
+  static_assert(OFF_RAW % 1024 == 0, "raw slots start on 1024-byte boundaries");
 };
 
-// Tensor-memory plan (512 columns x 128 lanes): accumulators in 64-column
-// quarters at [0, A_COL0), then one f16 weight stage per dequant team of
-// SW = NA x 32 columns (one 64-value K-step of each matrix: row = lane, two
-// f16 per column).  A tile whose token box has bw B rows (2 per token) takes
-// ceil(NA * bw / 64) quarters: matrix m's accumulator sits at column m * bw
-// of the tile's first quarter.
-template <int NA>
-struct TcTmem {
-  static constexpr int A_STAGES = TC_DQ_TEAMS;
-  static constexpr int SW = NA * 32;
-  static constexpr int A_COL0 = TC_TMEM_COLS - A_STAGES * SW;
-  static constexpr int NQ = A_COL0 / 64;
-  static __device__ __forceinline__ int quarters(int bw) {
-    return (NA * bw + 63) / 64;
+// A super-block's unit scale s = d * 2^e and the factor 2^-e its sc values
+// take (0 when d = 0: the sc*q term vanishes and the unit carries only the
+// min term, with s = dmin / 512).  e = 0 unless dmin >= 512 |d|; then e is
+// taken from the exponent fields so that |dmin / s| < 512 and every
+// c_j = -m_j * dmin / s (m_j <= 63) stays below 2^15 in f16.  ok = false when
+// that needs e > 20, beyond which sc * 2^-e / 16 is no longer exact in f16 (a
+// block whose min offset exceeds 2^29 times its scale step; quantisers do not
+// produce one).  The dequant warps and the epilogue both call this on the
+// same header word, so they agree bit for bit.
+struct TcUnitScale {
+  float s, a_mul, dmin;
+  bool ok;
+};
+__device__ __forceinline__ TcUnitScale tc_unit_scale(uint32_t dm) {
+  TcUnitScale u;
+  const float d = f16_bits_to_f32(dm), dmin = f16_bits_to_f32(dm >> 16);
+  u.dmin = dmin;
+  u.ok = true;
+  if (d != 0.0f) {
+    // with |dmin| < 2^(ed+1) and |d| >= 2^er: |dmin / d| < 2^(ed - er + 1) = 2^(e + 9)
+    int e = 0;
+    if (fabsf(dmin) >= 512.0f * fabsf(d)) {
+      const int ed = (int)((__float_as_uint(dmin) >> 23) & 255u), er = (int)((__float_as_uint(d) >> 23) & 255u);
+      e = ed - er - 8;
+    }
+    if (e > 20) {
+      u.ok = false;
+      e = 20;
+    }
+    u.s = __fmul_rn(d, __uint_as_float((uint32_t)(127 + e) << 23));
+    u.a_mul = __uint_as_float((uint32_t)(127 - e) << 23);
+  } else {
+    u.s = dmin != 0.0f ? __fmul_rn(dmin, 1.0f / 512.0f) : 1.0f;
+    u.a_mul = 0.0f;
   }
-};
-
-// Smallest token-tile box covering n tokens: 0 = 32 B rows (16 tokens), 1 = 64.
-__device__ __forceinline__ int tc_box(int n) { return n <= 16 ? 0 : 1; }
-
-// Accumulator quarters of the next tile: `qc` is the ring cursor (the MMA
-// warps and the epilogue walk the same tiles, so they agree); a tile that does
-// not fit before the end wraps to quarter 0.  Returns the first quarter.
-template <typename TM>
-__device__ __forceinline__ int tc_take_quarters(int &qc, int nq) {
-  if (qc + nq > TM::NQ) qc = 0;
-  const int q0 = qc;
-  qc += nq;
-  if (qc == TM::NQ) qc = 0;
-  return q0;
+  return u;
 }
 
 // Dequantise one 64-value K-step (chunk c of 4) of a raw Q4_K block in
 // shared memory (`blk` = the 144-byte block of this lane's row) into 32 f16x2
-// words: o[0..16) the low-nibble sub-block 2c, o[16..32) the high-nibble
-// sub-block 2c+1, each word-pair holding values (4i, 4i+2), (4i+1, 4i+3).
-//
-// Each weight is computed centred, w = d*sc*(q - 8) + (8*d*sc - dmin*m):
-// the offset c = 8*d*sc - dmin*m sits near the middle of the sub-block's
-// range, so rounding it to f16 costs little.  (Rounding the raw offset
-// -dmin*m instead, as large as the weights, puts one shared error on all 32
-// weights of a sub-block and about doubles the error of a dot product.)
-// Packed f16 arithmetic, two values per instruction:
-//   a mask and a shift put two nibbles in mantissa bits 4..7 under the
-//   exponent of 64: (v & 0x00F000F0) | 0x54005400 = (64 + q0, 64 + q2);
-//   hfma2(64 + q, sc, -72 sc) = sc*(q - 8) exactly (|.| <= 504, and 72*sc has
-//   at most 10 significant bits);
-//   hfma2(sc*(q - 8), d, c) = the weight rounded once to f16 (d is the block's
-//   f16 scale, exact; c is rounded to f16 from f32).
-__device__ __forceinline__ void tc_dequant_step(const uint8_t *blk, int c, uint32_t (&o)[32]) {
+// words of sc*q*2^-e: o[0..16) the low-nibble sub-block 2c, o[16..32) the
+// high-nibble sub-block 2c+1, each word-pair holding values (4i, 4i+2),
+// (4i+1, 4i+3); and the min-term A operand of those two sub-blocks,
+// c_j = -m_j * dmin / s for j = 2c, 2c+1 as f16 (hi, lo) pairs, into ap
+// (this row's 32 bytes of the unit's A': K = 2j, 2j + 1 in the K-major
+// no-swizzle layout, 8 values per 16-byte core-matrix row).
+// Packed f16 arithmetic for the weights, two values per instruction, exact:
+//   one mask-and-or puts a nibble pair under the exponent of 1024 (ulp 1):
+//   (v & 0x000F000F) | 0x64006400 = (1024 + q0, 1024 + q2) for the low
+//   nibbles of bytes 0 and 2, and (v & 0x00F000F0) | 0x64006400 =
+//   (1024 + 16 q0', ...) for their high nibbles; bytes 1 and 3 take the same
+//   masks on v >> 8;
+//   hfma2(1024 + q, f, -1024 f) = f*q and hfma2(1024 + 16 q, f/16, -64 f) = f*q
+//   with f = sc * 2^-e: f, f/16, 1024 f and 64 f are exact in f16 (sc <= 63,
+//   e <= 20) and so is the result, so the fma's one rounding changes nothing.
+// c_j is rounded in f32 (dmin / s through a fast reciprocal, a few ulp) and
+// split into f16 hi + lo: ~22 bits, like the activations.
+__device__ __forceinline__ void tc_dequant_step(const uint8_t *blk, int c, uint32_t (&o)[32],
+                                                uint8_t *ap, bool &range_ok) {
   const uint4 hdr = *reinterpret_cast<const uint4 *>(blk);
   const uint4 qa = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * c);
   const uint4 qb = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * c);
+  const TcUnitScale us = tc_unit_scale(hdr.x);
+  range_ok &= us.ok;
   int sc0, m0, sc1, m1;
   q4k_scale_min(hdr.y, hdr.z, hdr.w, 2 * c, sc0, m0);
   q4k_scale_min(hdr.y, hdr.z, hdr.w, 2 * c + 1, sc1, m1);
-  const __half2 d2 = __half2half2(__ushort_as_half((unsigned short)(hdr.x & 0xffffu)));
-  const float d = f16_bits_to_f32(hdr.x & 0xffffu), dmin = f16_bits_to_f32(hdr.x >> 16);
-  const __half2 s_lo = __half2half2(__int2half_rn(sc0));
-  const __half2 n_lo = __half2half2(__int2half_rn(-72 * sc0));
-  const __half2 c_lo = __half2half2(__float2half_rn(8.0f * d * (float)sc0 - dmin * (float)m0));
-  const __half2 s_hi = __half2half2(__int2half_rn(sc1));
-  const __half2 n_hi = __half2half2(__int2half_rn(-72 * sc1));
-  const __half2 c_hi = __half2half2(__float2half_rn(8.0f * d * (float)sc1 - dmin * (float)m1));
+  // the min-term operand of sub-blocks 2c, 2c + 1 (packed conversions: two values each)
+  const float qm = __fdividef(us.dmin, us.s);
+  const float c0 = -__fmul_rn((float)m0, qm), c1 = -__fmul_rn((float)m1, qm);
+  const __half2 hh = __floats2half2_rn(c0, c1);
+  const float2 hf = __half22float2(hh);
+  const __half2 ll = __floats2half2_rn(__fsub_rn(c0, hf.x), __fsub_rn(c1, hf.y));
+  const uint32_t hw = *reinterpret_cast<const uint32_t *>(&hh), lw = *reinterpret_cast<const uint32_t *>(&ll);
+  *reinterpret_cast<uint2 *>(ap + (c >> 1) * 128 + (c & 1) * 8) =
+      make_uint2(__byte_perm(hw, lw, 0x5410), __byte_perm(hw, lw, 0x7632));  // (hi0, lo0), (hi1, lo1)
+  // the weights
+  const float f0 = __fmul_rn((float)sc0, us.a_mul), f1 = __fmul_rn((float)sc1, us.a_mul);
+  const __half2 s_lo = __float2half2_rn(f0);
+  const __half2 n_lo = __float2half2_rn(-1024.0f * f0);
+  const __half2 s_hi = __float2half2_rn(0.0625f * f1);
+  const __half2 n_hi = __float2half2_rn(-64.0f * f1);
   const uint32_t q[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
 #pragma unroll
   for (int i = 0; i < 8; ++i) {  // word i: bytes 4i .. 4i+3 of the chunk
-    const uint32_t w = q[i];
-    const uint32_t pa = ((w << 4) & 0x00F000F0u) | 0x54005400u;  // low nibbles of bytes 0, 2
-    const uint32_t pb = ((w >> 4) & 0x00F000F0u) | 0x54005400u;  // low nibbles of bytes 1, 3
-    const uint32_t pc = (w & 0x00F000F0u) | 0x54005400u;         // high nibbles of bytes 0, 2
-    const uint32_t pd = ((w >> 8) & 0x00F000F0u) | 0x54005400u;  // high nibbles of bytes 1, 3
-    const __half2 a = __hfma2(__hfma2(*reinterpret_cast<const __half2 *>(&pa), s_lo, n_lo), d2, c_lo);
-    const __half2 b = __hfma2(__hfma2(*reinterpret_cast<const __half2 *>(&pb), s_lo, n_lo), d2, c_lo);
-    const __half2 e = __hfma2(__hfma2(*reinterpret_cast<const __half2 *>(&pc), s_hi, n_hi), d2, c_hi);
-    const __half2 f = __hfma2(__hfma2(*reinterpret_cast<const __half2 *>(&pd), s_hi, n_hi), d2, c_hi);
+    const uint32_t w = q[i], t = w >> 8;
+    const uint32_t pa = (w & 0x000F000Fu) | 0x64006400u;  // low nibbles of bytes 0, 2
+    const uint32_t pb = (t & 0x000F000Fu) | 0x64006400u;  // low nibbles of bytes 1, 3
+    const uint32_t pc = (w & 0x00F000F0u) | 0x64006400u;  // high nibbles of bytes 0, 2
+    const uint32_t pd = (t & 0x00F000F0u) | 0x64006400u;  // high nibbles of bytes 1, 3
+    const __half2 a = __hfma2(*reinterpret_cast<const __half2 *>(&pa), s_lo, n_lo);
+    const __half2 b = __hfma2(*reinterpret_cast<const __half2 *>(&pb), s_lo, n_lo);
+    const __half2 e = __hfma2(*reinterpret_cast<const __half2 *>(&pc), s_hi, n_hi);
+    const __half2 f = __hfma2(*reinterpret_cast<const __half2 *>(&pd), s_hi, n_hi);
     o[2 * i] = *reinterpret_cast<const uint32_t *>(&a);
     o[2 * i + 1] = *reinterpret_cast<const uint32_t *>(&b);
     o[16 + 2 * i] = *reinterpret_cast<const uint32_t *>(&e);
     o[16 + 2 * i + 1] = *reinterpret_cast<const uint32_t *>(&f);
   }
-}
-
-// Position of K index k in the (0, 2, 1, 3)-per-group order of the operands.
-__host__ __device__ __forceinline__ int tc_kperm(int k) {
-  return (k & ~3) | ((k & 1) << 1) | ((k >> 1) & 1);
-}
-
-__device__ __forceinline__ float tc_silu(float v) { return v / (1.0f + expf(-v)); }
-
-// Bounded wait shared by the roles: false (and the CTA-wide abort flag set)
-// when the barrier phase did not complete within TC_WAIT_LIMIT polls.
-// Waiters with sleep_ns > 0 sleep between polls (up to sleep_ns): the
-// producers and the epilogue, off the critical path; the MMA issuer and the
-// dequantisers spin.
-__device__ __forceinline__ bool tc_wait(uint64_t *bar, uint32_t parity, volatile int *abort_s,
-                                        uint32_t sleep_ns = 0) {
-  if (*abort_s) return false;
-  if (sleep_ns ? tc::mbar_wait_lazy(bar, parity, TC_WAIT_LIMIT, sleep_ns)
-               : tc::mbar_wait(bar, parity, TC_WAIT_LIMIT))
-    return true;
-  *abort_s = 1;
-  return false;
-}
-// The same for a whole warp, which leaves converged (the warp-wide tcgen05
-// forms need it so): one warp-wide test first, then lane 0 polls and the
-// outcome is broadcast.
-__device__ __forceinline__ bool tc_wait_warp(uint64_t *bar, uint32_t parity, volatile int *abort_s,
-                                             int lane, uint32_t sleep_ns = 0) {
-  if (__all_sync(0xffffffffu, tc::mbar_try_wait(bar, parity))) return true;
-  bool ok = true;
-  if (lane == 0) ok = tc_wait(bar, parity, abort_s, sleep_ns);
-  return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-}
-
-// MMA issuer state carried across tiles.
-struct TcIssuer {
-  uint32_t lead, b_base, a_base, af, ae;  // af / ae: shared addresses of a_full[0] / a_empty[0]
-  uint64_t *a_full, *b_full, *b_empty;
-  uint32_t ph;     // phase of the current group of four stages
-  uint32_t b_it;   // B slot uses so far
-  uint32_t a_rdy;  // non-blocking test of the next K-step's stage
-  uint32_t b_rdy;  // ... and of the next B slot
-};
-
-// K-step J (0..3) of a group: weight stage J; B slots hold KPB = 128 / BW
-// K-steps and a new slot opens when J % KPB == 0.  False when a bounded wait
-// gave up.
-template <int NA, int BW, typename L, int J>
-__device__ __forceinline__ bool tc_issue_kstep(TcIssuer &is, uint32_t dcol, uint32_t idesc, bool first,
-                                               uint64_t &bslot, int &bs, volatile int *abort_s, int lane) {
-  constexpr int KPB = 128 / BW, BS = L::B_SLOTS;
-  constexpr uint32_t SUB = BW * 128 / 16;  // one K-step of B, descriptor units
-  constexpr int SW = TcTmem<NA>::SW;
-  if (J % KPB == 0) {
-    bs = (int)(is.b_it % BS);
-    if (!__all_sync(0xffffffffu, is.b_rdy != 0) &&
-        !tc_wait_warp(is.b_full + bs, (is.b_it / BS) & 1u, abort_s, lane))
-      return false;
-    bslot = tc::desc_sw128(is.b_base + (uint32_t)(bs * L::BSL));
-    is.b_rdy = tc::mbar_test_wait(is.b_full + (is.b_it + 1u) % BS, ((is.b_it + 1u) / BS) & 1u);
-  }
-  if (!__all_sync(0xffffffffu, is.a_rdy != 0) && !tc_wait_warp(is.a_full + J, is.ph, abort_s, lane))
-    return false;
-  tc::tc_fence_after();
-  is.a_rdy = tc::mbar_test_wait_at<((J + 1) & 3) * 8>(is.af, J == 3 ? is.ph ^ 1u : is.ph);
-  tc::mma_kstep_ts_imm<NA, BW>(is.lead, dcol, is.a_base + (uint32_t)(J * SW),
-                               bslot + (uint64_t)((J % KPB) * SUB), idesc, first ? 0u : 1u);
-  tc::mma_commit_at<J * 8>(is.lead, is.ae);
-  if (J % KPB == KPB - 1) {
-    tc::mma_commit_w(is.lead, is.b_empty + bs);
-    ++is.b_it;
-  }
-  return true;
-}
-
-// The MMAs of one tile: its K-steps in groups of four, one per weight stage.
-// False when a bounded wait gave up.
-template <int NA, int BW, typename L>
-__device__ __forceinline__ bool tc_issue_tile(TcIssuer &is, uint32_t dcol, uint32_t idesc, int ksteps,
-                                              volatile int *abort_s, int lane) {
-  uint64_t bslot = 0;
-  int bs = 0;
-  for (int g = 0; g < ksteps; g += 4) {
-    if (!tc_issue_kstep<NA, BW, L, 0>(is, dcol, idesc, g == 0, bslot, bs, abort_s, lane) ||
-        !tc_issue_kstep<NA, BW, L, 1>(is, dcol, idesc, false, bslot, bs, abort_s, lane) ||
-        !tc_issue_kstep<NA, BW, L, 2>(is, dcol, idesc, false, bslot, bs, abort_s, lane) ||
-        !tc_issue_kstep<NA, BW, L, 3>(is, dcol, idesc, false, bslot, bs, abort_s, lane))
-      return false;
-    is.ph ^= 1u;
-  }
-  return true;
 }
 
 // NA = number of A matrices (2: gate and up with SwiGLU epilogue; 1: one
@@ -259,11 +204,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
   using TM = TcTmem<NA>;
   static_assert(!PAIR || NA == 2, "row-block pairs run on the two-matrix path");
   extern __shared__ uint8_t tc_raw[];
-  constexpr int RS = L::RAW_SLOTS, BS = L::B_SLOTS, AS = TM::A_STAGES, NQ = TM::NQ;
-  __shared__ uint64_t bars[2 * RS + 2 * BS + 2 * AS + 2 * NQ];
+  constexpr int RS = L::RAW_SLOTS, BS = L::B_SLOTS, SS = L::S_SLOTS, PS = L::AP_SLOTS;
+  constexpr int AS = TM::A_STAGES, NQ = TM::NQ;
+  __shared__ uint64_t bars[2 * RS + 2 * BS + 2 * AS + 2 * NQ + 2 * SS + 2 * PS];
   uint64_t *raw_full = bars, *raw_empty = bars + RS, *b_full = bars + 2 * RS, *b_empty = bars + 2 * RS + BS;
   uint64_t *a_full = bars + 2 * RS + 2 * BS, *a_empty = a_full + AS;
   uint64_t *acc_full = a_empty + AS, *acc_empty = acc_full + NQ;
+  uint64_t *s_full = acc_empty + NQ, *s_empty = s_full + SS;
+  uint64_t *ap_full = s_empty + SS, *ap_empty = ap_full + PS;
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
   volatile int *abort_s = &abort_flag;
@@ -285,11 +233,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
     }
     for (int q = 0; q < NQ; ++q) {
       tc::mbar_init(acc_full + q, 1);
-      tc::mbar_init(acc_empty + q, 4);
+      tc::mbar_init(acc_empty + q, TC_EPI_WARPS);
     }
     for (int s = 0; s < BS; ++s) {
       tc::mbar_init(b_full + s, 1);
       tc::mbar_init(b_empty + s, 1);
+    }
+    for (int s = 0; s < SS; ++s) {
+      tc::mbar_init(s_full + s, 1);
+      tc::mbar_init(s_empty + s, 1);
+    }
+    for (int s = 0; s < PS; ++s) {
+      tc::mbar_init(ap_full + s, TC_DQ_WARPS);  // every team writes its sub-blocks of A'
+      tc::mbar_init(ap_empty + s, 1);
     }
     tc::fence_mbar_init();
     abort_flag = 0;
@@ -297,6 +253,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
   if (tid == 0) {
     tc::tma_prefetch_desc(&maps.a0);
     tc::tma_prefetch_desc(&maps.b[0]);
+    tc::tma_prefetch_desc(&maps.s16[0]);
   }
   tc::tc_fence_before();
   __syncthreads();
@@ -338,9 +295,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
       }
     }
   } else if (warp == TC_WARP_BTMA) {
-    // ---------------- producer: token tiles (box sized to the tile) ----------------
+    // ---- producer: token tiles (box sized to the tile) and their min-term operands ----
     if (lane == 0) {
-      uint32_t b_it = 0;
+      uint32_t b_it = 0, s_it = 0;
       bool ok = true;
       int2 nxt = p.tt_info[min((int)blockIdx.x, max(total - 1, 0)) / RT];
       for (int tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
@@ -349,9 +306,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
         const int ntok = cur.x >> 16, slot0 = cur.y;
         const int bx = tc_box(ntok);
         const void *bm = &maps.b[bx];
+        const void *sm16 = &maps.s16[bx];
         const int bw = 32 << bx, kpb = 128 / bw;  // B rows of the tile; K-steps per B slot
         const uint32_t sub_bytes = (uint32_t)bw * 128u;
         for (int s0 = 0; ok && s0 < KSTEPS; s0 += kpb) {
+          if ((s0 & 3) == 0) {  // a super-block starts: its min-term operand, two 8-value boxes
+            const int ss = s_it % SS;
+            if (!(ok = tc_wait(s_empty + ss, ((s_it / SS) & 1u) ^ 1u, abort_s, 256))) break;
+            tc::mbar_expect_tx(s_full + ss, (uint32_t)(2 * bw * 16));
+            uint8_t *sdst = sm + L::OFF_S + ss * L::SSL;
+            tc::tma_load_2d(sdst, sm16, 4 * s0, 2 * slot0, s_full + ss);
+            tc::tma_load_2d(sdst + bw * 16, sm16, 4 * s0 + 8, 2 * slot0, s_full + ss);
+            ++s_it;
+          }
           const int bs = b_it % BS, nsub = min(kpb, KSTEPS - s0);
           if (!(ok = tc_wait(b_empty + bs, ((b_it / BS) & 1u) ^ 1u, abort_s, 256))) break;
           tc::mbar_expect_tx(b_full + bs, sub_bytes * (uint32_t)nsub);
@@ -365,17 +332,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
   } else if (warp == TC_WARP_MMA) {
     // ---------------- MMA issuer (whole warp, one elected lane issues) ----------------
     // Global K-step gs (over this CTA's tiles) sits in weight stage gs % 4
-    // (every tile has a multiple of 4 K-steps); its fill completes phase
-    // gs / 4 of a_full[gs % 4], and B slot use b_it completes phase b_it / BS
-    // of b_full[b_it % BS].  The issuer is the critical path: a single warp
+    // (every unit is 4 K-steps); its fill completes phase gs / 4 of
+    // a_full[gs % 4], and B slot use b_it completes phase b_it / BS of
+    // b_full[b_it % BS].  The issuer is the critical path: a single warp
     // whose every instruction between two K-steps' MMAs leaves the tensor
-    // pipe idle.  So the K-steps of a tile run as groups of four unrolled
-    // over the stages (stage, barrier and column offsets are immediates), and
-    // the barrier of the next K-step (and of the next B slot) is tested
-    // without blocking before the current MMAs are issued; the blocking wait
-    // runs only when that test failed.  A stage (slot) cannot complete its
-    // next phase before this warp commits the current one, so an early
-    // positive test stays valid.
+    // pipe idle.  So a unit's K-steps run unrolled over the stages (stage,
+    // barrier and column offsets are immediates), and the barrier of the next
+    // K-step (and of the next B slot) is tested without blocking before the
+    // current MMAs are issued; the blocking wait runs only when that test
+    // failed.  A stage (slot) cannot complete its next phase before this warp
+    // commits the current one, so an early positive test stays valid.
     const uint32_t lead = tc::elect_one();
     TcIssuer is;
     is.lead = lead;
@@ -391,6 +357,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
     is.a_rdy = tc::mbar_test_wait(a_full, 0);
     is.b_rdy = tc::mbar_test_wait(b_full, 0);
     uint32_t par = 0;  // par bit q: parity of quarter q's uses
+    uint32_t un = 0;   // units issued so far (A' slot un % PS, S slot un % SS)
+    const uint32_t ap_base = tc::smem_u32(sm + L::OFF_AP), s_base = tc::smem_u32(sm + L::OFF_S);
     int qc = 0;
     bool ok = true;
     int2 nxt = p.tt_info[min((int)blockIdx.x, max(total - 1, 0)) / RT];
@@ -399,22 +367,42 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
       nxt = p.tt_info[min(tile + (int)gridDim.x, total - 1) / RT];
       const int ntok = cur.x >> 16;
       const int bw = 32 << tc_box(ntok), nq = TM::quarters(bw);
-      const int q0 = tc_take_quarters<TM>(qc, nq);
-      for (int u = 0; ok && u < nq; ++u)
-        ok = tc_wait_warp(acc_empty + q0 + u, ((par >> (q0 + u)) & 1u) ^ 1u, abort_s, lane);
-      if (!ok) break;
-      tc::tc_fence_after();
       const uint32_t idesc = tc::idesc_f16(TC_M, (2 * ntok + 15) & ~15);
-      const uint32_t dcol = tmem + (uint32_t)(q0 * 64);
-      ok = bw == 32 ? tc_issue_tile<NA, 32, L>(is, dcol, idesc, KSTEPS, abort_s, lane)
-                    : tc_issue_tile<NA, 64, L>(is, dcol, idesc, KSTEPS, abort_s, lane);
-      if (!ok) break;
-      for (int u = 0; u < nq; ++u) tc::mma_commit_w(lead, acc_full + q0 + u);
-      par ^= ((1u << nq) - 1u) << q0;
+      for (int b = 0; ok && b < KSB; ++b, ++un) {  // one accumulator unit per super-block
+        const int q0 = tc_take_quarters<TM>(qc, nq);
+        for (int u = 0; ok && u < nq; ++u)
+          ok = tc_wait_warp(acc_empty + q0 + u, ((par >> (q0 + u)) & 1u) ^ 1u, abort_s, lane);
+        if (!ok) break;
+        tc::tc_fence_after();
+        const uint32_t dcol = tmem + (uint32_t)(q0 * 64);
+        ok = bw == 32 ? tc_issue_tile<NA, 32, L>(is, dcol, idesc, 4, abort_s, lane)
+                      : tc_issue_tile<NA, 64, L>(is, dcol, idesc, 4, abort_s, lane);
+        if (!ok) break;
+        // the min term: A' (the rows' c hi/lo) x S (the tokens' sub-block sums hi/lo), K = 16
+        const int ps = (int)(un % PS), ss = (int)(un % SS);
+        if (!(ok = tc_wait_warp(ap_full + ps, (un / PS) & 1u, abort_s, lane))) break;
+        if (!(ok = tc_wait_warp(s_full + ss, (un / SS) & 1u, abort_s, lane))) break;
+        tc::tc_fence_after();
+        const uint64_t bdesc = tc::desc_noswz(s_base + (uint32_t)(ss * L::SSL), (uint32_t)bw * 16u, 128u);
+#pragma unroll
+        for (int m = 0; m < NA; ++m)
+          tc::mma_f16_ss_w(lead, dcol + (uint32_t)(m * bw),
+                           tc::desc_noswz(ap_base + (uint32_t)(ps * L::APSL + m * L::APM), 128u, 256u),
+                           bdesc, idesc);
+        tc::mma_commit_w(lead, ap_empty + ps);
+        tc::mma_commit_w(lead, s_empty + ss);
+        for (int u = 0; u < nq; ++u) tc::mma_commit_w(lead, acc_full + q0 + u);
+        par ^= ((1u << nq) - 1u) << q0;
+      }
     }
   } else if (warp < TC_WARP_DQ0) {
-    // ---------------- epilogue: TMEM -> global ----------------
-    const int g = warp & 3;  // TMEM lane group this warp may access
+    // ---------------- epilogue: TMEM -> registers -> global ----------------
+    // Warp (g, h): TMEM lanes 32g.. (rows 32g + lane of each matrix), tokens
+    // 16h .. 16h + 15 of each tile.  Per unit (super-block b) and matrix m:
+    //   acc[m][t] += s_b * (hi + lo)
+    // with s_b from the block header's d and dmin (read from the weights one
+    // unit ahead: an L2 hit, the raw-weight TMA has just brought the block in).
+    const int g = warp & 3, h = (warp - TC_WARP_EPI0) >> 2;
     const uint32_t lane_addr = (uint32_t)(32 * g) << 16;
     uint32_t par = 0;
     int qc = 0;
@@ -423,95 +411,130 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
     for (int tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
       const int2 cur = nxt;  // the next tile's entry is loaded one tile ahead
       nxt = p.tt_info[min(tile + (int)gridDim.x, total - 1) / RT];
-      const int ntok = cur.x >> 16, slot0 = cur.y;
+      const int ntok = cur.x >> 16, slot0 = cur.y, e = cur.x & 0xffff;
       const int bw = 32 << tc_box(ntok), nq = TM::quarters(bw);
-      const int q0 = tc_take_quarters<TM>(qc, nq);
-      for (int u = 0; ok && u < nq; ++u)
-        ok = tc_wait_warp(acc_full + q0 + u, (par >> (q0 + u)) & 1u, abort_s, lane, 256);
+      const int nmine = min(max(ntok - 16 * h, 0), 16);  // this warp's tokens (warp-uniform)
+      const int r0 = (tile % RT) * (PAIR ? 2 * TC_M : TC_M);
+      const int row = r0 + 32 * g + lane;
+      const bool sh = e == p.E;
+      const int64_t grow = sh ? row : (int64_t)e * p.rows + row;
+      const uint8_t *hp0 = (sh ? p.sw0 : p.w0) + grow * p.row_bytes;
+      const uint8_t *hp1 = PAIR ? hp0 + (int64_t)TC_M * p.row_bytes : (sh ? p.sw1 : p.w1) + grow * p.row_bytes;
+      float acc[NA][16];
+#pragma unroll
+      for (int m = 0; m < NA; ++m)
+#pragma unroll
+        for (int t = 0; t < 16; ++t) acc[m][t] = 0.0f;
+      uint32_t dm0 = __ldg(reinterpret_cast<const uint32_t *>(hp0));
+      uint32_t dm1 = NA == 2 ? __ldg(reinterpret_cast<const uint32_t *>(hp1)) : 0u;
+      for (int b = 0; ok && b < KSB; ++b) {
+        const int q0 = tc_take_quarters<TM>(qc, nq);
+        const uint32_t cd0 = dm0, cd1 = dm1;
+        if (b + 1 < KSB) {  // the next unit's header words, in flight during this unit
+          dm0 = __ldg(reinterpret_cast<const uint32_t *>(hp0 + (int64_t)(b + 1) * Q4K_BYTES));
+          if (NA == 2) dm1 = __ldg(reinterpret_cast<const uint32_t *>(hp1 + (int64_t)(b + 1) * Q4K_BYTES));
+        }
+        for (int u = 0; ok && u < nq; ++u)
+          ok = tc_wait_warp(acc_full + q0 + u, (par >> (q0 + u)) & 1u, abort_s, lane, 128);
+        if (!ok) break;
+        tc::tc_fence_after();
+        const uint32_t dcol = tmem + lane_addr + (uint32_t)(q0 * 64) + (uint32_t)(32 * h);
+#pragma unroll
+        for (int m = 0; m < NA; ++m) {
+          const float sb = tc_unit_scale(m == 0 ? cd0 : cd1).s;
+#pragma unroll
+          for (int c4 = 0; c4 < 4; ++c4) {
+            if (4 * c4 >= nmine) break;  // warp-uniform
+            uint32_t v[8];
+            tc::tmem_ld8(dcol + (uint32_t)(m * bw + 8 * c4), v);  // tokens 4c4 .. 4c4+3: hi, lo
+            tc::tmem_wait_ld();
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+              acc[m][4 * c4 + c] =
+                  fmaf(sb, __uint_as_float(v[2 * c]) + __uint_as_float(v[2 * c + 1]), acc[m][4 * c4 + c]);
+          }
+        }
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0)
+          for (int u = 0; u < nq; ++u) tc::mbar_arrive(acc_empty + q0 + u);
+        par ^= ((1u << nq) - 1u) << q0;
+      }
       if (!ok) break;
-      tc::tc_fence_after();
-      const int row = (tile % RT) * (PAIR ? 2 * TC_M : TC_M) + 32 * g + lane;
-      const uint32_t dcol = tmem + lane_addr + (uint32_t)(q0 * 64);
-      const int prow = tc_kperm(row);  // a16 feeds the down GEMM's K axis
-      // column 2t holds token t's hi part, 2t+1 its lo part; 16 columns = 8 tokens
-      for (int col = 0; col < 2 * ntok; col += 16) {
-        const int t0 = col >> 1;
-        uint32_t v[16];
-        tc::tmem_ld16(dcol + (uint32_t)col, v);                          // matrix 0
-        tc::tmem_wait_ld();
-        float gv[8];
+      // the tile's outputs: tokens 16h + t < ntok of this warp
 #pragma unroll
-        for (int c = 0; c < 8; ++c) gv[c] = __uint_as_float(v[2 * c]) + __uint_as_float(v[2 * c + 1]);
+      for (int t = 0; t < 16; ++t) {
+        if (t >= nmine) break;  // warp-uniform
+        const int64_t slot = (int64_t)slot0 + 16 * h + t;
         if (PAIR) {
-          tc::tmem_ld16(dcol + (uint32_t)(bw + col), v);                 // rows + 128
-          tc::tmem_wait_ld();
-#pragma unroll
-          for (int c = 0; c < 8; ++c)
-            if (t0 + c < ntok) {
-              float *dst = p.ybuf + ((int64_t)slot0 + t0 + c) * p.out_ld + row;
-              dst[0] = gv[c];
-              dst[TC_M] = __uint_as_float(v[2 * c]) + __uint_as_float(v[2 * c + 1]);
-            }
+          float *dst = p.ybuf + slot * p.out_ld + row;
+          dst[0] = acc[0][t];
+          dst[TC_M] = acc[NA - 1][t];
         } else if (NA == 2) {
-          tc::tmem_ld16(dcol + (uint32_t)(bw + col), v);                 // matrix 1
-          tc::tmem_wait_ld();
-#pragma unroll
-          for (int c = 0; c < 8; ++c)
-            if (t0 + c < ntok) {
-              const float uv = __uint_as_float(v[2 * c]) + __uint_as_float(v[2 * c + 1]);
-              const float av = __fmul_rn(tc_silu(gv[c]), uv);
-              const __half hi = __float2half_rn(av);
-              const __half lo = __float2half_rn(av - __half2float(hi));
-              __half *dst = p.a16 + 2 * ((int64_t)slot0 + t0 + c) * p.out_ld + prow;
-              dst[0] = hi;
-              dst[p.out_ld] = lo;
-            }
+          const float av = __fmul_rn(tc_silu(acc[0][t]), acc[NA - 1][t]);
+          const __half hi = __float2half_rn(av);
+          const __half lo = __float2half_rn(av - __half2float(hi));
+          __half *dst = p.a16 + 2 * slot * p.out_ld + tc_kperm(row);  // a16 feeds the down GEMM's K axis
+          dst[0] = hi;
+          dst[p.out_ld] = lo;
+          // the down GEMM's min-term operand: the sum of a over these 32 rows
+          // (one sub-block), hi and lo, each twice
+          const float sa = warp_sum(av);
+          if (lane == 0) {
+            const __half shi = __float2half_rn(sa);
+            const __half slo = __float2half_rn(__fsub_rn(sa, __half2float(shi)));
+            const int ld16 = p.out_ld / 16, sbk = (r0 + 32 * g) / 32;
+            *reinterpret_cast<uint32_t *>(p.s16_out + 2 * slot * ld16 + 2 * sbk) =
+                (uint32_t)__half_as_ushort(shi) * 0x10001u;
+            *reinterpret_cast<uint32_t *>(p.s16_out + (2 * slot + 1) * ld16 + 2 * sbk) =
+                (uint32_t)__half_as_ushort(slo) * 0x10001u;
+          }
         } else {
-#pragma unroll
-          for (int c = 0; c < 8; ++c)
-            if (t0 + c < ntok) p.ybuf[((int64_t)slot0 + t0 + c) * p.out_ld + row] = gv[c];
+          p.ybuf[slot * p.out_ld + row] = acc[0][t];
         }
       }
-      tc::tc_fence_before();
-      __syncwarp();
-      if (lane == 0)
-        for (int u = 0; u < nq; ++u) tc::mbar_arrive(acc_empty + q0 + u);
-      par ^= ((1u << nq) - 1u) << q0;
     }
   } else {
     // ---------------- dequantisers: raw Q4_K -> f16 weight stages in TMEM ----------------
-    // Team t (four warps) takes the K-steps ks = t (mod 4) -- one of the four
-    // K-steps of every raw slot -- and fills weight stage t with them.  Warp
-    // w may store only TMEM lanes 32*(w%4)..: it owns weight rows
-    // 32*(w%4)+lane of every matrix.
+    // Team t (four warps) takes the K-steps ks = t (mod 4) -- chunk t of every
+    // super-block, so one K-step per unit -- and fills weight stage t with it,
+    // and the unit's min-term operand A' for sub-blocks 2t, 2t + 1.  Warp w
+    // may store only TMEM lanes 32*(w%4)..: it owns weight rows 32*(w%4)+lane
+    // of every matrix.
     const int g = warp & 3, team = (warp - TC_WARP_DQ0) >> 2;
     const int r = 32 * g + lane;
     const uint32_t lane_addr = (uint32_t)(32 * g) << 16;
     const uint32_t acol = tmem + lane_addr + (uint32_t)(TM::A_COL0 + team * TM::SW);
-    uint32_t u = 0;  // this team's K-steps so far (and raw slots: one K-step each)
-    bool ok = true;
+    uint8_t *ap_row = sm + L::OFF_AP + (r >> 3) * 256 + (r & 7) * 16;
+    uint32_t u = 0;  // this team's K-steps so far = units so far (and raw slots: one each)
+    bool ok = true, range_ok = true;
     for (int tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
       for (int ks = team; ks < KSTEPS; ks += TC_DQ_TEAMS, ++u) {
-        const int rs = (int)(u % RS);
+        const int rs = (int)(u % RS), ps = (int)(u % PS);
         if (!(ok = tc_wait_warp(raw_full + rs, (u / RS) & 1u, abort_s, lane))) break;
+        if (!(ok = tc_wait_warp(ap_empty + ps, ((u / PS) & 1u) ^ 1u, abort_s, lane))) break;
         if (!(ok = tc_wait_warp(a_empty + team, (u & 1u) ^ 1u, abort_s, lane))) break;
         tc::tc_fence_after();
         const uint8_t *raw = sm + L::OFF_RAW + rs * L::RAWSL;
 #pragma unroll
         for (int m = 0; m < NA; ++m) {  // team t holds chunk t of the super-block
           uint32_t o[32];
-          tc_dequant_step(raw + (m * TC_M + r) * Q4K_BYTES, team, o);
+          tc_dequant_step(raw + (m * TC_M + r) * Q4K_BYTES, team, o, ap_row + ps * L::APSL + m * L::APM,
+                          range_ok);
           tc::tmem_st32(acol + (uint32_t)(m * 32), o);
         }
         tc::tmem_wait_st();
+        tc::fence_proxy_async_smem();  // the A' stores (generic proxy), seen by the tensor core
         tc::tc_fence_before();
         __syncwarp();
         if (lane == 0) {
           tc::mbar_arrive(a_full + team);
+          tc::mbar_arrive(ap_full + ps);
           tc::mbar_arrive(raw_empty + rs);
         }
       }
     }
+    if (!__all_sync(0xffffffffu, range_ok) && lane == 0) atomicOr(p.status, DEV_ERR_RANGE);
   }
 
   // ---------------- teardown ----------------
@@ -530,6 +553,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
 // K order (0, 2, 1, 3) inside each group of four (the weight operand's order),
 // for every slot whose expert runs on the tensor-core path: routed slot s holds entry order[s] (token order[s] / k,
 // expert ids[order[s]]); slot n + t is the shared expert's row of token t.
+// Rows 2 slot and 2 slot + 1 of xs16 [2 slots][H/16] get the f16 hi and lo of
+// the slot's 32-value sub-block sums, each twice: the min-term operand.
 // Slots of CUDA-core experts are skipped.  One warp per slot, GATHER_WARPS
 // slots per block: the slot's index chain (order -> ids -> counts) of several
 // slots is in flight at once.  The warp of shared slot n + t also writes the
@@ -540,7 +565,8 @@ __global__ void __launch_bounds__(GATHER_WARPS * 32) gather_f16_kernel(
     const float *__restrict__ x, int H, const int32_t *__restrict__ order,
     const int32_t *__restrict__ ids, const int32_t *__restrict__ counts,
     const int32_t *__restrict__ n_valid, int thr, int n, int k, int T, int shared_tc,
-    __half *__restrict__ xg, const float *__restrict__ gi, float *__restrict__ gsh) {
+    __half *__restrict__ xg, __half *__restrict__ xs16, const float *__restrict__ gi,
+    float *__restrict__ gsh) {
   const int slot = blockIdx.x * GATHER_WARPS + (int)(threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (slot >= n + T) return;
   int tok;
@@ -558,6 +584,9 @@ __global__ void __launch_bounds__(GATHER_WARPS * 32) gather_f16_kernel(
   const float4 *src = reinterpret_cast<const float4 *>(x + (int64_t)tok * H);
   uint2 *dhi = reinterpret_cast<uint2 *>(xg + 2 * (int64_t)slot * H);
   uint2 *dlo = dhi + H / 4;
+  const int ld16 = H / 16;
+  uint32_t *shi = reinterpret_cast<uint32_t *>(xs16 + 2 * (int64_t)slot * ld16);
+  uint32_t *slo = reinterpret_cast<uint32_t *>(xs16 + (2 * (int64_t)slot + 1) * ld16);
 #pragma unroll 4
   for (int i = lane; i < H / 4; i += 32) {
     const float4 v = src[i];  // K order (0, 2, 1, 3) inside each group of four
@@ -566,6 +595,17 @@ __global__ void __launch_bounds__(GATHER_WARPS * 32) gather_f16_kernel(
     const __half2 la = __floats2half2_rn(v.x - fa.x, v.z - fa.y), lb = __floats2half2_rn(v.y - fb.x, v.w - fb.y);
     dhi[i] = make_uint2(*reinterpret_cast<const uint32_t *>(&a), *reinterpret_cast<const uint32_t *>(&b));
     dlo[i] = make_uint2(*reinterpret_cast<const uint32_t *>(&la), *reinterpret_cast<const uint32_t *>(&lb));
+    // sub-block sums: lanes 8j .. 8j+7 hold the 32 values of sub-block i / 8
+    float sum = (v.x + v.y) + (v.z + v.w);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+    if ((lane & 7) == 0) {
+      const __half hh = __float2half_rn(sum);
+      const __half ll = __float2half_rn(__fsub_rn(sum, __half2float(hh)));
+      shi[i >> 3] = (uint32_t)__half_as_ushort(hh) * 0x10001u;
+      slo[i >> 3] = (uint32_t)__half_as_ushort(ll) * 0x10001u;
+    }
   }
   if (slot >= n && gi) {
     const float g = shared_gate_warp(gi, x + (int64_t)tok * H, H, lane);
@@ -575,12 +615,12 @@ __global__ void __launch_bounds__(GATHER_WARPS * 32) gather_f16_kernel(
 
 int32_t launch_gather_f16(har_cuda_ctx *ctx, const float *x, int H, const int32_t *order,
                           const int32_t *ids, const int32_t *counts, const int32_t *n_valid,
-                          int thr, int n, int k, int T, int shared_tc, __half *xg,
+                          int thr, int n, int k, int T, int shared_tc, __half *xg, __half *xs16,
                           const float *gi, float *gsh) {
   prof_begin(ctx);
   const unsigned grid = (unsigned)((n + T + GATHER_WARPS - 1) / GATHER_WARPS);
   gather_f16_kernel<<<grid, GATHER_WARPS * 32, 0, ctx->stream>>>(x, H, order, ids, counts, n_valid, thr,
-                                                                n, k, T, shared_tc, xg, gi, gsh);
+                                                                n, k, T, shared_tc, xg, xs16, gi, gsh);
   return check_launch(ctx, "gather_f16_kernel");
 }
 

@@ -171,6 +171,19 @@ __device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr) {
   return d;
 }
 
+// Shared-memory matrix descriptor: K-major, no swizzle.  Core matrices are
+// 8 rows x 16 bytes (rows 16 B apart); lbo = byte distance between core
+// matrices adjacent in K, sbo = between core matrices adjacent in M/N
+// (layout type 0, SWIZZLE_NONE).
+__device__ __forceinline__ uint64_t desc_noswz(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1u << 46;
+  return d;
+}
+
 // Instruction descriptor of kind::f16: A and B f16, D f32, both K-major,
 // N >> 3 at bit 17, M >> 4 at bit 24.
 __host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
@@ -266,6 +279,19 @@ __device__ __forceinline__ void mma_f16_ts_w(uint32_t lead, uint32_t d_tmem, uin
       "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(lead)
       : "memory");
 }
+// Warp-wide form of one MMA with both operands in shared memory,
+// D[tmem] += A[desc] * B[desc]^T, issued by the elected lane.
+__device__ __forceinline__ void mma_f16_ss_w(uint32_t lead, uint32_t d_tmem, uint64_t adesc,
+                                             uint64_t bdesc, uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred e, p;\n\t"
+      "setp.ne.b32 e, %4, 0;\n\t"
+      "setp.eq.b32 p, %4, %4;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(lead)
+      : "memory");
+}
+
 // The MMAs of one 64-value K-step (4 x K=16) for NA = 1 or 2 matrices, from
 // one asm block: matrix m accumulates at column d + m*bw and reads its weights
 // from TMEM columns a + m*32 + kk*8; B advances 32 bytes (2 descriptor units)
@@ -404,6 +430,14 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
         "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
         "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+// Warp-collective: this thread's TMEM lane, 8 consecutive 32-bit columns.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7])
       : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_wait_ld() {

@@ -46,6 +46,8 @@ MOE_ADD_RESIDUAL = 0x1
 MOE_ACT_Q8K = 0x2
 MOE_FORCE_GEMV = 0x4
 MOE_FORCE_TC = 0x8
+MOE_EMPTY_SLOTS = 0x10
+MOE_TC_F16W = 0x20
 
 # Every symbol include/har_cuda.h declares (tests check the library exports them).
 EXPORTS = [

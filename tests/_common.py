@@ -14,13 +14,17 @@ import numpy as np
 
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 REL_MAX_TOL = 1e-3
-# HAR's differential verdict (har-execution/src/lib.rs:185-195): the f32
-# CUDA-core GEMV path meets it.
+# HAR's differential verdict (har-execution/src/lib.rs:185-195): every path
+# meets it.
 VERDICT_NRMS = 5e-5
-# RMS bound of the tensor-core path, where each dequantised weight is rounded
-# once to f16 (activations go in as hi/lo f16 pairs): about 4e-4 measured on
-# the Alice layer; the max-relative bound REL_MAX_TOL is the north star's.
-TC_NRMS = 6e-4
+# The tensor-core path computes sc*q exactly in f16 and the min term on the
+# tensor cores from f16 hi/lo splits, scaling each super-block in f32, with
+# activations as hi/lo f16 pairs (~22 bits): it meets the same verdict.
+TC_NRMS = VERDICT_NRMS
+# The opt-in HAR_CUDA_MOE_TC_F16W variant rounds each dequantised weight once
+# to f16: about 4e-4 normalised RMS on the Alice layer (max relative error
+# within the north star's 1e-3), not HAR's verdict.
+F16W_NRMS = 6e-4
 
 
 def kats():
