@@ -349,11 +349,28 @@ def run_ours(args, torch):
         else:
             ctx.moe_stack(layers, xin, idin, win, yout, flags)
 
+    # The norm-free stack (BASELINE's "attention omitted": y = x + moe(x) per
+    # layer) grows like |x|^2 per layer, so from N(0,1) inputs its activations
+    # leave f16 range after about a dozen layers (and f32 range soon after, in
+    # the reference's arithmetic as here).  The tensor-core path reports that
+    # through the device error word; the work per step does not depend on the
+    # values, so the run records the report and goes on.  Per-layer parity at
+    # this shape is tested on RMS-normalised inputs (tests/test_gpu_configs.py).
+    range_flagged = [False]
+
+    def sync_range():
+        try:
+            ctx.synchronize()
+        except har_cuda.HarCudaError as e:
+            if e.status != har_cuda.ERR_DEVICE or "f16 range" not in str(e):
+                raise
+            range_flagged[0] = True
+
     # eager warm-up (allocates the scratch arena), then capture one step in a graph
     with torch.cuda.stream(stream):
         for _ in range(2):
             step(xd, idd, wd, yd)
-    ctx.synchronize()
+    sync_range()
     torch.cuda.synchronize()
     n0 = ctx.launch_count
     g = torch.cuda.CUDAGraph()
@@ -414,7 +431,12 @@ def run_ours(args, torch):
     e2e_steps = max(3, min(args.steps, 20))
     if ep is None:
         def e2e_step():
-            ctx.moe_stack_host(layers, x, ids, w, flags)
+            try:
+                ctx.moe_stack_host(layers, x, ids, w, flags)
+            except har_cuda.HarCudaError as e:  # the call completed; only the range report
+                if e.status != har_cuda.ERR_DEVICE or "f16 range" not in str(e):
+                    raise
+                range_flagged[0] = True
     else:
         xh = torch.from_numpy(x).pin_memory()
         ih = torch.from_numpy(ids).pin_memory()
@@ -429,7 +451,7 @@ def run_ours(args, torch):
                 step(xd, idd, wd, yd)
                 yh.copy_(yd, non_blocking=True)
             stream.synchronize()
-            ctx.synchronize()
+            sync_range()
     for _ in range(2):
         e2e_step()
     if dist:
@@ -567,6 +589,12 @@ def run_ours(args, torch):
                     "h2d_bytes_per_step": int(x.nbytes + ids.nbytes + w.nbytes),
                     "d2h_bytes_per_step": int(x.nbytes)},
             "clocks": clk,
+            "numerics": {"range_flagged": range_flagged[0],
+                         "note": "the norm-free stack's activations leave f16 range after about a "
+                                 "dozen layers from N(0,1) inputs (the reference's f32 overflows "
+                                 "later); the tensor-core path reports it and the timed work is "
+                                 "value-independent; per-layer parity at this shape is tested on "
+                                 "RMS-normalised inputs"},
             "variant_tc_f16w": None if var is None else {
                 "flag": "HAR_CUDA_MOE_TC_F16W",
                 "numerics": "weights rounded to f16: max|d|/max|ref| ~4e-4, nrms ~4e-4 (north "
@@ -868,7 +896,11 @@ def run_routed_decode(args, torch):
                 gr.replay()
             ev1.record(stream)
         torch.cuda.synchronize()
-        ctx.synchronize()
+        try:  # the norm-free stack leaves f16 range from N(0,1) inputs (see run_ours)
+            ctx.synchronize()
+        except har_cuda.HarCudaError as e:
+            if e.status != har_cuda.ERR_DEVICE or "f16 range" not in str(e):
+                raise
         ms = ev0.elapsed_time(ev1) / n
         d = ids.cpu().numpy()
         wbytes = sum((len(np.unique(d[l])) + 1) * EXPERT_BYTES for l in range(L))

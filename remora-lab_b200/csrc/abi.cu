@@ -289,7 +289,8 @@ int32_t har_cuda_synchronize(har_cuda_ctx *ctx, int64_t timeout_ms) {
     if (word & DEV_ERR_TIMEOUT) why += " (a bounded wait ran out)";
     if (word & DEV_ERR_BOUNDS) why += " (an expert id out of range)";
     if (word & DEV_ERR_RANGE)
-      why += " (a Q4_K block outside the tensor-core path's range: run it with HAR_CUDA_MOE_FORCE_GEMV)";
+      why += " (a value beyond the tensor-core path's f16 range -- |x|, a sub-block sum or a SwiGLU "
+             "output >= 65520 -- or an unrepresentable Q4_K block: run it with HAR_CUDA_MOE_FORCE_GEMV)";
     return set_error(ctx, word & DEV_ERR_TIMEOUT ? HAR_CUDA_ERR_TIMEOUT : HAR_CUDA_ERR_DEVICE, why);
   }
   return HAR_CUDA_OK;
@@ -784,9 +785,11 @@ int32_t har_cuda_moe_stack_host(har_cuda_ctx *ctx, const har_cuda_moe_layer *con
   } else {
     HAR_TRY(enqueue());
   }
-  HAR_TRY(har_cuda_synchronize(ctx, 600000));
-  memcpy(y_host, hp + in_b, xb);
-  return HAR_CUDA_OK;
+  // a device error word (HAR_CUDA_ERR_DEVICE) comes from a finished stream:
+  // the results are copied out as computed and the status marks them invalid
+  const int32_t st = har_cuda_synchronize(ctx, 600000);
+  if (st == HAR_CUDA_OK || st == HAR_CUDA_ERR_DEVICE) memcpy(y_host, hp + in_b, xb);
+  return st;
 }
 
 int32_t har_cuda_gen_q4k(har_cuda_ctx *ctx, void *dev_bytes, int64_t rows, int64_t K,

@@ -27,8 +27,11 @@ constexpr float ROUTER_EPS = 1.0e-9f;
 // Device error words (bit flags) written by kernels; read by har_cuda_synchronize.
 constexpr int DEV_ERR_TIMEOUT = 1;
 constexpr int DEV_ERR_BOUNDS = 2;
-// a Q4_K block the tensor-core path cannot represent exactly (min offset above
-// 2^29 times its scale step); the call's results are not valid
+// a value outside the tensor-core path's range: an activation, a sub-block sum
+// of activations or a SwiGLU output of magnitude >= 65520 (f16 overflows), or
+// a Q4_K block whose min offset exceeds 2^29 times its scale step; the call's
+// results are not valid (the CUDA-core path, HAR_CUDA_MOE_FORCE_GEMV, has no
+// such limit)
 constexpr int DEV_ERR_RANGE = 4;
 
 // ---------------------------------------------------------------------------

@@ -472,6 +472,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
           dst[TC_M] = acc[NA - 1][t];
         } else if (NA == 2) {
           const float av = __fmul_rn(tc_silu(acc[0][t]), acc[NA - 1][t]);
+          if (!(fabsf(av) < 65520.0f)) atomicOr(p.status, DEV_ERR_RANGE);  // beyond f16 (or NaN)
           const __half hi = __float2half_rn(av);
           const __half lo = __float2half_rn(av - __half2float(hi));
           __half *dst = p.a16 + 2 * slot * p.out_ld + tc_kperm(row);  // a16 feeds the down GEMM's K axis
@@ -481,6 +482,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
           // (one sub-block), hi and lo, each twice
           const float sa = warp_sum(av);
           if (lane == 0) {
+            if (!(fabsf(sa) < 65520.0f)) atomicOr(p.status, DEV_ERR_RANGE);
             const __half shi = __float2half_rn(sa);
             const __half slo = __float2half_rn(__fsub_rn(sa, __half2float(shi)));
             const int ld16 = p.out_ld / 16, sbk = (r0 + 32 * g) / 32;
@@ -566,7 +568,7 @@ __global__ void __launch_bounds__(GATHER_WARPS * 32) gather_f16_kernel(
     const int32_t *__restrict__ ids, const int32_t *__restrict__ counts,
     const int32_t *__restrict__ n_valid, int thr, int n, int k, int T, int shared_tc,
     __half *__restrict__ xg, __half *__restrict__ xs16, const float *__restrict__ gi,
-    float *__restrict__ gsh) {
+    float *__restrict__ gsh, int *status) {
   const int slot = blockIdx.x * GATHER_WARPS + (int)(threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (slot >= n + T) return;
   int tok;
@@ -587,6 +589,7 @@ __global__ void __launch_bounds__(GATHER_WARPS * 32) gather_f16_kernel(
   const int ld16 = H / 16;
   uint32_t *shi = reinterpret_cast<uint32_t *>(xs16 + 2 * (int64_t)slot * ld16);
   uint32_t *slo = reinterpret_cast<uint32_t *>(xs16 + (2 * (int64_t)slot + 1) * ld16);
+  float vmax = 0.0f;  // the largest magnitude converted to f16 (overflow check)
 #pragma unroll 4
   for (int i = lane; i < H / 4; i += 32) {
     const float4 v = src[i];  // K order (0, 2, 1, 3) inside each group of four
@@ -600,6 +603,7 @@ __global__ void __launch_bounds__(GATHER_WARPS * 32) gather_f16_kernel(
     sum += __shfl_xor_sync(0xffffffffu, sum, 1);
     sum += __shfl_xor_sync(0xffffffffu, sum, 2);
     sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+    vmax = fmaxf(vmax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fmaxf(fabsf(v.z), fabsf(v.w)), fabsf(sum))));
     if ((lane & 7) == 0) {
       const __half hh = __float2half_rn(sum);
       const __half ll = __float2half_rn(__fsub_rn(sum, __half2float(hh)));
@@ -607,6 +611,7 @@ __global__ void __launch_bounds__(GATHER_WARPS * 32) gather_f16_kernel(
       slo[i >> 3] = (uint32_t)__half_as_ushort(ll) * 0x10001u;
     }
   }
+  if (__any_sync(0xffffffffu, !(vmax < 65520.0f)) && lane == 0) atomicOr(status, DEV_ERR_RANGE);
   if (slot >= n && gi) {
     const float g = shared_gate_warp(gi, x + (int64_t)tok * H, H, lane);
     if (lane == 0) gsh[tok] = g;
@@ -617,10 +622,11 @@ int32_t launch_gather_f16(har_cuda_ctx *ctx, const float *x, int H, const int32_
                           const int32_t *ids, const int32_t *counts, const int32_t *n_valid,
                           int thr, int n, int k, int T, int shared_tc, __half *xg, __half *xs16,
                           const float *gi, float *gsh) {
+  int *status = ctx->d_status;
   prof_begin(ctx);
   const unsigned grid = (unsigned)((n + T + GATHER_WARPS - 1) / GATHER_WARPS);
   gather_f16_kernel<<<grid, GATHER_WARPS * 32, 0, ctx->stream>>>(x, H, order, ids, counts, n_valid, thr,
-                                                                n, k, T, shared_tc, xg, xs16, gi, gsh);
+                                                                n, k, T, shared_tc, xg, xs16, gi, gsh, status);
   return check_launch(ctx, "gather_f16_kernel");
 }
 

@@ -303,6 +303,7 @@ __global__ void __launch_bounds__(F16W_THREADS, 1) moe_tc_f16w_kernel(const __gr
             if (t0 + c < ntok) {
               const float uv = __uint_as_float(v[2 * c]) + __uint_as_float(v[2 * c + 1]);
               const float av = __fmul_rn(tc_silu(gv[c]), uv);
+              if (!(fabsf(av) < 65520.0f)) atomicOr(p.status, DEV_ERR_RANGE);  // beyond f16 (or NaN)
               const __half hi = __float2half_rn(av);
               const __half lo = __float2half_rn(av - __half2float(hi));
               __half *dst = p.a16 + 2 * ((int64_t)slot0 + t0 + c) * p.out_ld + prow;

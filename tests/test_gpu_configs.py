@@ -90,11 +90,26 @@ def test_config5_full_stack_layer_by_layer(ctx):
         y = torch.empty_like(xd)
         ctx.moe_ffn(layers[l], cur, idd[l], wd[l], y, RES)
         cur = y
+    torch.cuda.synchronize()
+    try:  # the chain overflows too (reported below for the stack call)
+        ctx.synchronize()
+    except har_cuda.HarCudaError:
+        pass
     ys = xd.clone()
     ctx.moe_stack(layers, ys, idd, wd, ys, RES)
     torch.cuda.synchronize()
+    # the norm-free activations leave f16 range: the tensor-core path reports it
+    with pytest.raises(har_cuda.HarCudaError) as e:
+        ctx.synchronize()
+    assert e.value.status == har_cuda.ERR_DEVICE and "f16 range" in str(e.value)
     ctx.synchronize()
     assert torch.equal(ys.view(torch.int32), cur.view(torch.int32))
+    # the first layers stay in range: no report
+    y3 = xd.clone()
+    ctx.moe_stack(layers[:3], y3, idd[:3].contiguous(), wd[:3].contiguous(), y3, RES)
+    torch.cuda.synchronize()
+    ctx.synchronize()
+    assert torch.isfinite(y3).all()
     # 2. every layer against the oracle on a token subset, inputs RMS-normalised
     ins, outs = [], []
     cur = xd
@@ -106,6 +121,7 @@ def test_config5_full_stack_layer_by_layer(ctx):
         outs.append(y[subd].cpu().numpy())
         cur = y
     torch.cuda.synchronize()
+    ctx.synchronize()  # normalised inputs: every layer in range
     worst = 0.0
     for l in range(L):
         t, gi = keep[l]

@@ -116,19 +116,34 @@ def test_tc_f16w_variant(ctx, small):
 
 
 def test_tc_zero_and_offset_blocks(ctx):
-    # super-blocks with d = 0 (only the min term) and with dmin >= 512 d (the
-    # unit scale's shift e > 0), written by hand into a layer's weights
+    # super-blocks with d = 0 (only the min term) and with d shrunk 1024-fold
+    # under an unchanged dmin (dmin >= 512 d: the unit scale's shift e > 0),
+    # written by hand into a layer's weights; values stay in f16 range
     lay = Layer(ctx, 4, 1024, 256, seed=77, shared=False)
     for dev_t, host in ((lay.dg, lay.hg), (lay.du, lay.hu), (lay.dd, lay.hd)):
         hb = host.reshape(-1, 144)
         hb[0::3, 0:2] = 0                          # d = 0 in every third block
         d16 = np.frombuffer(hb[1::3, 0:2].tobytes(), np.float16).astype(np.float32)
-        dm = (np.abs(d16) * 2000.0).astype(np.float16)  # dmin ~ 2000 d: e = 2..3
-        hb[1::3, 2:4] = dm.view(np.uint8).reshape(-1, 2)
+        hb[1::3, 0:2] = (d16 / 1024.0).astype(np.float16).view(np.uint8).reshape(-1, 2)
         dev_t.copy_(torch.from_numpy(host.reshape(-1)).to(dev_t.device))
     torch.cuda.synchronize()
     x = haro.normal_f32(45, 0, 24 * 1024).reshape(24, 1024)
     ids, w = haro.zipf_routing(46, 24, 4, 2)
     ref = lay.oracle(x, ids, w)
-    assert_close(lay.run(ctx, x, ids, w, FORCE_TC), ref, nrms=TC_NRMS, what="tc d=0 / large dmin")
-    assert_close(lay.run(ctx, x, ids, w, har_cuda.MOE_FORCE_GEMV), ref, what="gemv d=0 / large dmin")
+    assert_close(lay.run(ctx, x, ids, w, FORCE_TC), ref, nrms=TC_NRMS, what="tc d=0 / small d")
+    assert_close(lay.run(ctx, x, ids, w, har_cuda.MOE_FORCE_GEMV), ref, what="gemv d=0 / small d")
+
+
+def test_tc_reports_values_beyond_f16(ctx, small):
+    # activations travel as f16 hi/lo pairs on the tensor-core path: a token
+    # with |x| >= 65520 sets the device error word instead of returning
+    # silent infinities; the CUDA-core path takes it
+    x = haro.normal_f32(47, 0, 3 * 2048).reshape(3, 2048)
+    x[1, 5] = 1.0e5
+    ids, w = haro.route_topk(haro.normal_f32(48, 0, 3 * 64).reshape(3, 64), 10)
+    with pytest.raises(har_cuda.HarCudaError) as e:
+        small.run(ctx, x, ids, w, FORCE_TC)
+    assert e.value.status == har_cuda.ERR_DEVICE
+    ctx.synchronize()
+    y = small.run(ctx, x, ids, w, har_cuda.MOE_FORCE_GEMV)
+    assert np.isfinite(y).all()
