@@ -63,6 +63,9 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="target CPU time of the cpu_baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tc-f16w", action="store_true",
+                    help="run the opt-in f16-weight tensor-core variant (HAR_CUDA_MOE_TC_F16W) "
+                         "as the timed path")
     ap.add_argument("--profile-only", action="store_true",
                     help="run warm-up + a few steps only (for ncu launch lists)")
     ap.add_argument("--routed-decode", action="store_true",
@@ -334,7 +337,8 @@ def run_ours(args, torch):
         local_distinct = distinct
         L = len(layers)
     T = cfg["T"]
-    flags = har_cuda.MOE_ADD_RESIDUAL | (har_cuda.MOE_ACT_Q8K if args.act == "q8k" else 0)
+    flags = har_cuda.MOE_ADD_RESIDUAL | (har_cuda.MOE_ACT_Q8K if args.act == "q8k" else 0) | \
+        (har_cuda.MOE_TC_F16W if args.tc_f16w else 0)
     dev = torch.device("cuda", local)
     xd = torch.from_numpy(x).to(dev)
     idd = torch.from_numpy(ids).to(dev)
@@ -469,7 +473,7 @@ def run_ours(args, torch):
     # dequantised weight rounded to f16, max relative error ~4e-4, not HAR's
     # 5e-5 RMS verdict), timed the same way for comparison
     var = None
-    if args.act == "f32":
+    if args.act == "f32" and not args.tc_f16w:
         vflags = flags | har_cuda.MOE_TC_F16W
         with torch.cuda.stream(stream):
             step_v = (lambda: ctx.ep_moe_stack(ep, locals_, shareds, gates, xd, idd, wd, yd, vflags)) \
@@ -518,11 +522,12 @@ def run_ours(args, torch):
     peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
     # the dominant kernel: the tensor-core gate/up GEMM (every expert takes the
     # tensor-core path at the default threshold); the GEMV kernel otherwise
-    rk = "moe_tc_gate_up_kernel" if "moe_tc_gate_up_kernel" in kern else "moe_gate_up_kernel"
+    rk = next((n for n in ("moe_tc_gate_up_kernel", "moe_tc_f16w_gate_up_kernel") if n in kern),
+              "moe_gate_up_kernel")
     gu = kern.get(rk, [1, 1.0])
     # all launches of the kernel in one step: bytes they move / time they take
     achieved = sum(gu_bytes) / (gu[1] * 1e-3) / 1e9
-    traffic = load_traffic(rk)
+    traffic = load_traffic(rk + ("@config4" if args.config == 4 else ""))
     # config 4 (prefill, ~80 tokens per expert) is bound by the tensor pipe:
     # its roofline is the gate/up kernel's algorithmic FLOPs (2 per multiply-add
     # of the routed and shared experts' gate and up GEMMs) per launch over the
@@ -560,6 +565,8 @@ def run_ours(args, torch):
             "dtype": ("f16 x f16 -> f32 (tcgen05: exact sc*q weights and hi/lo f16 activations, "
                       "super-block scales and mins applied in f32)"
                       if "moe_tc_gate_up_kernel" in kern else
+                      "f16 x f16 -> f32 (tcgen05; Q4_K weights rounded to f16 on chip: "
+                      "HAR_CUDA_MOE_TC_F16W)" if "moe_tc_f16w_gate_up_kernel" in kern else
                       "int8 x q4 (dp4a) -> i32, f32 combine" if args.act == "q8k" else "f32"),
             "data": "synthetic: N(0,0.02) weights quantised to Q4_K on device; N(0,1) f32 "
                     "activations; " + ("uniform top-10 routing (softmax weights of N(0,1) "
@@ -928,7 +935,8 @@ def load_peaks():
 
 
 def load_traffic(kernel: str):
-    """DRAM bytes per launch of `kernel` from the committed ncu summary, if any."""
+    """DRAM bytes per launch of `kernel` (key "name" or "name@configN") from the
+    committed ncu summaries, if any."""
     p = os.path.join(ROOT, "profiles", "traffic.json")
     try:
         with open(p) as f:
