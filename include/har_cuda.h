@@ -346,9 +346,24 @@ int32_t har_cuda_ep_combine(har_cuda_ctx *ctx, const float *x_dev, int64_t H, in
                             uint32_t flags, float *y_dev);
 /* An NCCL unique id (rank 0 creates it; the caller broadcasts the bytes). */
 int32_t har_cuda_ep_unique_id(uint8_t *out, size_t len);
-/* Collective: every rank of `world` joins the communicator on ctx's device. */
+/* Collective: every rank of `world` joins the communicator on ctx's device.
+ * The communicator is non-blocking and every wait on it is bounded (this call
+ * waits up to 300 s for all ranks to join; each exchange's enqueue up to the
+ * same bound): on expiry the communicator is aborted and the call returns
+ * HAR_CUDA_ERR_TIMEOUT, replacing the unbounded device-fence waits of the
+ * reference's device layer (har-vulkan/src/lib.rs:2174) with the fail-closed
+ * rule of its serving seam (har-serve/src/vulkan.rs:18-19). */
 int32_t har_cuda_ep_create(har_cuda_ctx *ctx, const uint8_t *unique_id, size_t len, int32_t world,
                            int32_t rank, har_cuda_ep **out);
+/* The same with the bound given: timeout_ms for joining and for each exchange. */
+int32_t har_cuda_ep_create_timeout(har_cuda_ctx *ctx, const uint8_t *unique_id, size_t len,
+                                   int32_t world, int32_t rank, int64_t timeout_ms,
+                                   har_cuda_ep **out);
+/* Abort the communicator: its NCCL work in flight ends with an error instead of
+ * waiting for peers (call it when har_cuda_synchronize timed out on an exchange
+ * whose peer is gone); later EP calls on it return HAR_CUDA_ERR_NOT_INIT.  The
+ * handle still needs har_cuda_ep_free. */
+int32_t har_cuda_ep_abort(har_cuda_ep *ep);
 int32_t har_cuda_ep_free(har_cuda_ep *ep);
 /* One layer; ids are global expert ids [T][k] of this rank's T tokens. */
 int32_t har_cuda_ep_moe_ffn(har_cuda_ctx *ctx, har_cuda_ep *ep, const har_cuda_moe_layer *local,

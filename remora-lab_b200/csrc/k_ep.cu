@@ -27,6 +27,8 @@
 #include <nccl.h>
 
 #include <algorithm>
+#include <chrono>
+#include <thread>
 #include <climits>
 #include <cstring>
 #include <string>
@@ -35,7 +37,8 @@
 
 struct har_cuda_ep {
   int world = 1, rank = 0, device = 0;
-  ncclComm_t comm = nullptr;
+  ncclComm_t comm = nullptr;  // non-blocking: every NCCL call is polled against a deadline
+  int64_t op_timeout_ms = 60000;  // bound on an exchange's host-side enqueue
   void *buf = nullptr;  // exchange buffers, grown on demand
   size_t bytes = 0;
   // the exchanges run on their own stream, joined to the caller's by events,
@@ -48,6 +51,35 @@ namespace har {
 
 static int32_t nccl_error(har_cuda_ctx *ctx, const char *what, ncclResult_t r) {
   return set_error(ctx, HAR_CUDA_ERR_NCCL, std::string(what) + ": " + ncclGetErrorString(r));
+}
+
+// The communicator is non-blocking (ncclConfig_t::blocking = 0): an NCCL call
+// may return ncclInProgress and finish in the background.  Poll its state
+// until it settles or `timeout_ms` passes; on expiry abort the communicator
+// (every rank's later calls then fail instead of waiting for a peer that will
+// never come) and report HAR_CUDA_ERR_TIMEOUT.  The same bound covers a
+// communicator's creation, which waits for every rank to join.
+static int32_t nccl_settle(har_cuda_ctx *ctx, ncclComm_t *comm, ncclResult_t r, const char *what,
+                           int64_t timeout_ms) {
+  if (r != ncclSuccess && r != ncclInProgress) return nccl_error(ctx, what, r);
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    ncclResult_t state = ncclSuccess;
+    const ncclResult_t q = ncclCommGetAsyncError(*comm, &state);
+    if (q != ncclSuccess) return nccl_error(ctx, "ncclCommGetAsyncError", q);
+    if (state == ncclSuccess) return HAR_CUDA_OK;
+    if (state != ncclInProgress) return nccl_error(ctx, what, state);
+    const int64_t ms = std::chrono::duration_cast<std::chrono::milliseconds>(
+                           std::chrono::steady_clock::now() - t0).count();
+    if (ms > timeout_ms) {
+      ncclCommAbort(*comm);
+      *comm = nullptr;
+      return set_error(ctx, HAR_CUDA_ERR_TIMEOUT,
+                       std::string(what) + " did not complete within " + std::to_string(timeout_ms) +
+                           " ms (a rank missing or gone); the communicator was aborted");
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(100));
+  }
 }
 
 // Row (d, t) of the dispatch: d-local ids and weights of token t's slots, and
@@ -166,9 +198,9 @@ int32_t ep_all_to_all(har_cuda_ctx *ctx, har_cuda_ep *ep, const void *send, void
   for (int d = 0; d < ep->world; ++d) {
     ncclResult_t r = ncclSend((const uint8_t *)send + (size_t)d * n * esize, n, type, d, ep->comm,
                               ep->cs);
-    if (r != ncclSuccess) return nccl_error(ctx, "ncclSend", r);
+    if (r != ncclSuccess && r != ncclInProgress) return nccl_error(ctx, "ncclSend", r);
     r = ncclRecv((uint8_t *)recv + (size_t)d * n * esize, n, type, d, ep->comm, ep->cs);
-    if (r != ncclSuccess) return nccl_error(ctx, "ncclRecv", r);
+    if (r != ncclSuccess && r != ncclInProgress) return nccl_error(ctx, "ncclRecv", r);
   }
   return HAR_CUDA_OK;
 }
@@ -222,7 +254,7 @@ int32_t ep_layer(har_cuda_ctx *ctx, har_cuda_ep *ep, const har_cuda_moe_layer *l
   if (!st) st = ep_all_to_all(ctx, ep, sw, rw, (size_t)T * k, ncclFloat32, 4);
   r = ncclGroupEnd();
   if (st) return st;
-  if (r != ncclSuccess) return nccl_error(ctx, "ncclGroupEnd", r);
+  if ((st = nccl_settle(ctx, &ep->comm, r, "ep dispatch", ep->op_timeout_ms))) return st;
   // 3. the shared expert on the rank's tokens, meanwhile
   if (shared) {
     prof_begin(ctx);
@@ -245,7 +277,7 @@ int32_t ep_layer(har_cuda_ctx *ctx, har_cuda_ep *ep, const har_cuda_moe_layer *l
   st = ep_all_to_all(ctx, ep, part, back, (size_t)T * H, ncclFloat32, 4);
   r = ncclGroupEnd();
   if (st) return st;
-  if (r != ncclSuccess) return nccl_error(ctx, "ncclGroupEnd", r);
+  if ((st = nccl_settle(ctx, &ep->comm, r, "ep return", ep->op_timeout_ms))) return st;
   if ((st = join(ep->cs, ctx->stream, ep->ev[3]))) return st;
   // 6. residual + shared + partials in rank order
   prof_begin(ctx);
@@ -257,7 +289,8 @@ int32_t ep_layer(har_cuda_ctx *ctx, har_cuda_ep *ep, const har_cuda_moe_layer *l
 int32_t ep_check(har_cuda_ctx *ctx, har_cuda_ep *ep, const har_cuda_moe_layer *local,
                  const har_cuda_moe_layer *shared, int64_t T, int k, uint32_t flags) {
   if (!ctx) return HAR_CUDA_ERR_ARG;
-  if (!ep || !ep->comm) return set_error(ctx, HAR_CUDA_ERR_NOT_INIT, "ep: no communicator");
+  if (!ep || !ep->comm)
+    return set_error(ctx, HAR_CUDA_ERR_NOT_INIT, "ep: no communicator (never created, or aborted)");
   if (ep->device != ctx->device)
     return set_error(ctx, HAR_CUDA_ERR_ARG, "ep: communicator belongs to another device");
   if (!local) return set_error(ctx, HAR_CUDA_ERR_ARG, "ep: local layer is null");
@@ -296,12 +329,14 @@ int32_t har_cuda_ep_unique_id(uint8_t *out, size_t len) {
   return HAR_CUDA_OK;
 }
 
-int32_t har_cuda_ep_create(har_cuda_ctx *ctx, const uint8_t *unique_id, size_t len, int32_t world,
-                           int32_t rank, har_cuda_ep **out) {
+int32_t har_cuda_ep_create_timeout(har_cuda_ctx *ctx, const uint8_t *unique_id, size_t len,
+                                   int32_t world, int32_t rank, int64_t timeout_ms,
+                                   har_cuda_ep **out) {
   if (!ctx || !unique_id || !out || len < sizeof(ncclUniqueId)) return HAR_CUDA_ERR_ARG;
   *out = nullptr;
   if (world < 1 || rank < 0 || rank >= world)
     return set_error(ctx, HAR_CUDA_ERR_ARG, "ep_create: need 0 <= rank < world");
+  if (timeout_ms <= 0) return set_error(ctx, HAR_CUDA_ERR_ARG, "ep_create: timeout_ms must be positive");
   if (cudaSetDevice(ctx->device) != cudaSuccess)
     return set_error(ctx, HAR_CUDA_ERR_CUDA, "ep_create: cudaSetDevice failed");
   ncclUniqueId id;
@@ -310,6 +345,7 @@ int32_t har_cuda_ep_create(har_cuda_ctx *ctx, const uint8_t *unique_id, size_t l
   ep->world = world;
   ep->rank = rank;
   ep->device = ctx->device;
+  ep->op_timeout_ms = timeout_ms;
   bool ok = cudaStreamCreateWithFlags(&ep->cs, cudaStreamNonBlocking) == cudaSuccess;
   for (int i = 0; i < 4 && ok; ++i)
     ok = cudaEventCreateWithFlags(&ep->ev[i], cudaEventDisableTiming) == cudaSuccess;
@@ -317,13 +353,31 @@ int32_t har_cuda_ep_create(har_cuda_ctx *ctx, const uint8_t *unique_id, size_t l
     har_cuda_ep_free(ep);
     return set_error(ctx, HAR_CUDA_ERR_CUDA, "ep_create: stream or event creation failed");
   }
-  ncclResult_t r = ncclCommInitRank(&ep->comm, world, id, rank);
-  if (r != ncclSuccess) {
-    ep->comm = nullptr;
-    har_cuda_ep_free(ep);
-    return nccl_error(ctx, "ncclCommInitRank", r);
+  ncclConfig_t config = NCCL_CONFIG_INITIALIZER;
+  config.blocking = 0;  // init and group calls return at once; nccl_settle bounds them
+  ncclResult_t r = ncclCommInitRankConfig(&ep->comm, world, id, rank, &config);
+  const int32_t st = ep->comm ? nccl_settle(ctx, &ep->comm, r, "ep_create: joining the communicator",
+                                            timeout_ms)
+                              : nccl_error(ctx, "ncclCommInitRankConfig", r);
+  if (st) {
+    har_cuda_ep_free(ep);  // an aborted communicator is already gone
+    return st;
   }
   *out = ep;
+  return HAR_CUDA_OK;
+}
+
+int32_t har_cuda_ep_create(har_cuda_ctx *ctx, const uint8_t *unique_id, size_t len, int32_t world,
+                           int32_t rank, har_cuda_ep **out) {
+  return har_cuda_ep_create_timeout(ctx, unique_id, len, world, rank, 300000, out);
+}
+
+int32_t har_cuda_ep_abort(har_cuda_ep *ep) {
+  if (!ep) return HAR_CUDA_ERR_ARG;
+  if (ep->comm) {
+    ncclCommAbort(ep->comm);
+    ep->comm = nullptr;
+  }
   return HAR_CUDA_OK;
 }
 
@@ -334,7 +388,22 @@ int32_t har_cuda_ep_free(har_cuda_ep *ep) {
     cudaDeviceSynchronize();
     cudaFree(ep->buf);
   }
-  if (ep->comm) ncclCommDestroy(ep->comm);
+  if (ep->comm) {
+    // finalize (non-blocking: poll, bounded), then destroy; a communicator
+    // whose finalize does not settle is aborted instead
+    ncclResult_t r = ncclCommFinalize(ep->comm);
+    const auto t0 = std::chrono::steady_clock::now();
+    ncclResult_t state = r;
+    while (r == ncclSuccess || r == ncclInProgress) {
+      if (ncclCommGetAsyncError(ep->comm, &state) != ncclSuccess || state != ncclInProgress) break;
+      if (std::chrono::steady_clock::now() - t0 > std::chrono::milliseconds(ep->op_timeout_ms)) break;
+      std::this_thread::sleep_for(std::chrono::microseconds(100));
+    }
+    if ((r == ncclSuccess || r == ncclInProgress) && state == ncclSuccess)
+      ncclCommDestroy(ep->comm);
+    else
+      ncclCommAbort(ep->comm);
+  }
   for (int i = 0; i < 4; ++i)
     if (ep->ev[i]) cudaEventDestroy(ep->ev[i]);
   if (ep->cs) {

@@ -68,6 +68,7 @@ EXPORTS = [
     "har_cuda_profile_end", "har_cuda_moe_ffn_noalloc", "har_cuda_ctx_set_tc_min_tokens",
     "har_cuda_ep_unique_id", "har_cuda_ep_create", "har_cuda_ep_free", "har_cuda_ep_moe_ffn",
     "har_cuda_ep_moe_stack", "har_cuda_ep_plan", "har_cuda_ep_combine",
+    "har_cuda_ep_create_timeout", "har_cuda_ep_abort",
 ]
 
 
@@ -108,6 +109,8 @@ def load_library() -> C.CDLL:
         "har_cuda_ep_unique_id": (i32, [vp, C.c_size_t]),
         "har_cuda_ep_create": (i32, [vp, vp, C.c_size_t, i32, i32, pp]),
         "har_cuda_ep_free": (i32, [vp]),
+        "har_cuda_ep_create_timeout": (i32, [vp, vp, C.c_size_t, i32, i32, i64, pp]),
+        "har_cuda_ep_abort": (i32, [vp]),
         "har_cuda_ep_moe_ffn": (i32, [vp, vp, vp, vp, vp, vp, i64, i32, vp, vp, vp, u32]),
         "har_cuda_ep_moe_stack": (i32, [vp, vp, vp, vp, vp, i32, vp, i64, i32, vp, vp, vp, u32]),
         "har_cuda_ep_plan": (i32, [vp, vp, i64, i64, i32, vp, vp, i32, i32, vp, vp, vp]),
@@ -456,12 +459,15 @@ class Context:
         return y
 
     # ---- expert parallelism -------------------------------------------------
-    def ep_create(self, unique_id: bytes, world: int, rank: int) -> "EpComm":
-        """Collective over `world` ranks: join the NCCL communicator on this device."""
+    def ep_create(self, unique_id: bytes, world: int, rank: int,
+                  timeout_ms: int = 300000) -> "EpComm":
+        """Collective over `world` ranks: join the NCCL communicator on this
+        device; raises HarCudaError (ERR_TIMEOUT) when not every rank joins
+        within timeout_ms (the same bound then holds for each exchange)."""
         buf = (C.c_uint8 * len(unique_id)).from_buffer_copy(unique_id)
         h = C.c_void_p()
-        self.check(self.lib.har_cuda_ep_create(self.handle, buf, len(unique_id), world, rank,
-                                               C.byref(h)))
+        self.check(self.lib.har_cuda_ep_create_timeout(self.handle, buf, len(unique_id), world,
+                                                       rank, timeout_ms, C.byref(h)))
         return EpComm(self, h, world, rank)
 
     def ep_moe_ffn(self, ep: "EpComm", local: "MoeLayer", shared, gate_inp, x, ids, weights, y,
@@ -523,6 +529,11 @@ class EpComm:
 
     def __init__(self, ctx: "Context", handle, world: int, rank: int):
         self.ctx, self.handle, self.world, self.rank = ctx, handle, world, rank
+
+    def abort(self):
+        """Abort the communicator (its in-flight exchanges end with an error)."""
+        if self.handle:
+            self.ctx.lib.har_cuda_ep_abort(self.handle)
 
     def free(self):
         if self.handle:
