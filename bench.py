@@ -879,43 +879,49 @@ def run_routed_decode(args, torch):
     peaks = load_peaks()
     hbm = peaks.get("hbm_gbs", 6650.0)
     out = {}
+    # the default path (every expert on the f32-grade tensor-core kernels), the
+    # opt-in f16-weight tensor-core variant and the CUDA-core GEMV path
+    paths = {"default": 0, "tc_f16w": har_cuda.MOE_TC_F16W, "gemv": har_cuda.MOE_FORCE_GEMV}
     for T in (1, 8, 64):
         x = torch.randn(T, H, device=dev, generator=g)
         y = torch.empty_like(x)
         ids = torch.empty((L, T, TOPK), dtype=torch.int32, device=dev)
         w = torch.empty((L, T, TOPK), dtype=torch.float32, device=dev)
-        step = lambda: ctx.routed_moe_stack(layers, routers, x, TOPK, ids, w, y,  # noqa: E731
-                                            har_cuda.MOE_ADD_RESIDUAL)
-        with torch.cuda.stream(stream):
-            for _ in range(max(3, args.warmup)):
+        row = {}
+        for pname, pf in paths.items():
+            step = lambda: ctx.routed_moe_stack(layers, routers, x, TOPK, ids, w, y,  # noqa: E731
+                                                har_cuda.MOE_ADD_RESIDUAL | pf)
+            with torch.cuda.stream(stream):
+                for _ in range(max(3, args.warmup)):
+                    step()
+            torch.cuda.synchronize()
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=stream):
                 step()
-        torch.cuda.synchronize()
-        gr = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(gr, stream=stream):
-            step()
-        ev0 = torch.cuda.Event(enable_timing=True)
-        ev1 = torch.cuda.Event(enable_timing=True)
-        n = max(3, min(args.steps, 50))
-        with torch.cuda.stream(stream):
-            gr.replay()
-            ev0.record(stream)
-            for _ in range(n):
+            ev0 = torch.cuda.Event(enable_timing=True)
+            ev1 = torch.cuda.Event(enable_timing=True)
+            n = max(3, min(args.steps, 50))
+            with torch.cuda.stream(stream):
                 gr.replay()
-            ev1.record(stream)
-        torch.cuda.synchronize()
-        try:  # the norm-free stack leaves f16 range from N(0,1) inputs (see run_ours)
-            ctx.synchronize()
-        except har_cuda.HarCudaError as e:
-            if e.status != har_cuda.ERR_DEVICE or "f16 range" not in str(e):
-                raise
-        ms = ev0.elapsed_time(ev1) / n
-        d = ids.cpu().numpy()
-        wbytes = sum((len(np.unique(d[l])) + 1) * EXPERT_BYTES for l in range(L))
-        out[f"T{T}"] = {"ms_per_step": round(ms, 4), "tokens_per_s": round(T / (ms * 1e-3), 1),
-                        "weight_gbs": round(wbytes / (ms * 1e-3) / 1e9, 1),
-                        "hbm_frac": round(wbytes / (ms * 1e-3) / 1e9 / hbm, 4)}
-        del gr
-    t1 = out["T1"]
+                ev0.record(stream)
+                for _ in range(n):
+                    gr.replay()
+                ev1.record(stream)
+            torch.cuda.synchronize()
+            try:  # the norm-free stack leaves f16 range from N(0,1) inputs (see run_ours)
+                ctx.synchronize()
+            except har_cuda.HarCudaError as e:
+                if e.status != har_cuda.ERR_DEVICE or "f16 range" not in str(e):
+                    raise
+            del gr
+            ms = ev0.elapsed_time(ev1) / n
+            d = ids.cpu().numpy()
+            wbytes = sum((len(np.unique(d[l])) + 1) * EXPERT_BYTES for l in range(L))
+            row[pname] = {"ms_per_step": round(ms, 4), "tokens_per_s": round(T / (ms * 1e-3), 1),
+                          "weight_gbs": round(wbytes / (ms * 1e-3) / 1e9, 1),
+                          "hbm_frac": round(wbytes / (ms * 1e-3) / 1e9 / hbm, 4)}
+        out[f"T{T}"] = row
+    t1 = out["T1"]["default"]
     return {"metric": "routed decode step, 48 Alice-shaped layers, device routing",
             "value": t1["tokens_per_s"], "unit": "tokens/s (T=1)", "n_gpus": 1,
             "ms_per_step": t1["ms_per_step"], "higher_is_better": True, "dtype": "f32 x, Q4_K W",

@@ -233,7 +233,7 @@ int32_t har_cuda_moe_ffn_host(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer
  * cannot take the synchronisation an allocation may imply.  Scratch comes from
  * a static device array of HAR_CUDA_NOALLOC_SCRATCH_BYTES held by every GPU
  * that loads the library until exit; calls needing more return
- * HAR_CUDA_ERR_GEOMETRY (T <= 148 tokens at E = 512, H = 2048, I = 512, k = 10
+ * HAR_CUDA_ERR_GEOMETRY (T <= 144 tokens at E = 512, H = 2048, I = 512, k = 10
  * with f32 activations, 276 with HAR_CUDA_MOE_ACT_Q8K).
  * The first call in each CUDA context looks up the array's address in that
  * context (make it before any stream capture); the address is cached per
