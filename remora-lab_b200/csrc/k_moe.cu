@@ -383,12 +383,12 @@ struct MoeScratch {
 // most experts with 1..16 tokens), the tensor-core kernels beat the CUDA-core
 // GEMV kernels even for single-token experts.  har_cuda_ctx_set_tc_min_tokens
 // overrides it per context, HAR_CUDA_TC_MIN_TOKENS in the environment per process.
-// The default for a single-token call (T = 1, batch-1 decode) is two tokens,
-// i.e. every expert on the CUDA-core GEMVs: measured on the routed 48-layer
-// stack, 3.24 ms per step on the f32 GEMV path against 3.42 ms on the
-// f32-grade tensor-core kernels (both meet HAR's verdict); from T = 2 on the
-// tensor cores win (T = 8: 7.8 against 14.1 ms, T = 64: 18.4 against 90.6).
+// A single-token call would be ~5% faster on the CUDA-core GEMVs (routed
+// 48-layer stack: 3.24 against 3.42 ms per step), but the default keeps every
+// call on one path so that a token's result does not depend on the batch it
+// came in, bit for bit (batched equals isolated, har-serve/src/moe.rs:301-314).
 static int tc_threshold(const har_cuda_ctx *ctx, uint32_t flags, int64_t T) {
+  (void)T;
   if (flags & HAR_CUDA_MOE_FORCE_TC) return 1;
   if (flags & HAR_CUDA_MOE_FORCE_GEMV) return INT_MAX;
   if (ctx->tc_min_tokens > 0) return ctx->tc_min_tokens;
@@ -397,8 +397,7 @@ static int tc_threshold(const har_cuda_ctx *ctx, uint32_t flags, int64_t T) {
     const int t = v ? atoi(v) : 0;
     return t > 0 ? t : 0;
   }();
-  if (thr > 0) return thr;
-  return T == 1 ? 2 : 1;
+  return thr > 0 ? thr : 1;
 }
 
 // Whether the layer's shapes fit the tensor-core kernels (H and I multiples
