@@ -72,6 +72,10 @@ def parse():
                     help="one JSON line for serving-style decode: the 48-layer stack with every "
                          "layer routed on the device (har_cuda_routed_moe_stack) at T = 1, 8, 64; "
                          "not the driver's bench line")
+    ap.add_argument("--rd-batches", default="1,8,64",
+                    help="--routed-decode: comma-separated tokens per step")
+    ap.add_argument("--rd-paths", default="default,tc_f16w,gemv,decode",
+                    help="--routed-decode: comma-separated paths to time")
     ap.add_argument("--layers", type=int, default=None,
                     help="override the layer count (small ncu captures only; the bench "
                          "line always uses the config's 48)")
@@ -881,14 +885,20 @@ def run_routed_decode(args, torch):
     out = {}
     # the default path (every expert on the f32-grade tensor-core kernels), the
     # opt-in f16-weight tensor-core variant and the CUDA-core GEMV path
-    paths = {"default": 0, "tc_f16w": har_cuda.MOE_TC_F16W, "gemv": har_cuda.MOE_FORCE_GEMV}
-    for T in (1, 8, 64):
+    # and the decode path (HAR_CUDA_MOE_DECODE, at most 8 tokens per call)
+    paths = {"default": 0, "tc_f16w": har_cuda.MOE_TC_F16W, "gemv": har_cuda.MOE_FORCE_GEMV,
+             "decode": har_cuda.MOE_DECODE}
+    want = set(args.rd_paths.split(","))
+    paths = {k: v for k, v in paths.items() if k in want}
+    for T in (int(b) for b in args.rd_batches.split(",")):
         x = torch.randn(T, H, device=dev, generator=g)
         y = torch.empty_like(x)
         ids = torch.empty((L, T, TOPK), dtype=torch.int32, device=dev)
         w = torch.empty((L, T, TOPK), dtype=torch.float32, device=dev)
         row = {}
         for pname, pf in paths.items():
+            if pf == har_cuda.MOE_DECODE and T > 8:
+                continue
             step = lambda: ctx.routed_moe_stack(layers, routers, x, TOPK, ids, w, y,  # noqa: E731
                                                 har_cuda.MOE_ADD_RESIDUAL | pf)
             with torch.cuda.stream(stream):
@@ -921,9 +931,10 @@ def run_routed_decode(args, torch):
                           "weight_gbs": round(wbytes / (ms * 1e-3) / 1e9, 1),
                           "hbm_frac": round(wbytes / (ms * 1e-3) / 1e9 / hbm, 4)}
         out[f"T{T}"] = row
-    t1 = out["T1"]["default"]
+    first_T, first_row = next(iter(out.items()))
+    first_path, t1 = next(iter(first_row.items()))
     return {"metric": "routed decode step, 48 Alice-shaped layers, device routing",
-            "value": t1["tokens_per_s"], "unit": "tokens/s (T=1)", "n_gpus": 1,
+            "value": t1["tokens_per_s"], "unit": f"tokens/s ({first_T}, {first_path} path)", "n_gpus": 1,
             "ms_per_step": t1["ms_per_step"], "higher_is_better": True, "dtype": "f32 x, Q4_K W",
             "data": "synthetic: N(0,0.02) Q4_K weights and f32 routers, N(0,1) tokens",
             "config": {"workload": "config 5 stack, har_cuda_routed_moe_stack in one CUDA graph",

@@ -63,6 +63,9 @@ extern "C" {
 #define HAR_CUDA_MOE_TC_F16W 0x20u     /* tensor-core experts round each dequantised weight
                                           to f16 (faster; max relative error ~4e-4, not
                                           HAR's 5e-5 RMS verdict, which the default meets) */
+#define HAR_CUDA_MOE_DECODE 0x40u      /* decode path for T <= 8 tokens: two launches per
+                                          layer, no grouping, f32 on CUDA cores (HAR's
+                                          verdict met); larger T returns GEOMETRY */
 
 typedef struct har_cuda_ctx har_cuda_ctx;
 typedef struct har_cuda_weights har_cuda_weights;

@@ -586,7 +586,12 @@ int32_t har::check_moe_args(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, 
   if ((flags & HAR_CUDA_MOE_ACT_Q8K) && (flags & HAR_CUDA_MOE_FORCE_TC))
     return set_error(ctx, HAR_CUDA_ERR_UNSUPPORTED,
                      "moe_ffn: the tensor-core path has no Q8_K activation mode");
-  if (flags & ~0x3Fu) return set_error(ctx, HAR_CUDA_ERR_ARG, "moe_ffn: unknown flag bits");
+  if (flags & ~0x7Fu) return set_error(ctx, HAR_CUDA_ERR_ARG, "moe_ffn: unknown flag bits");
+  if ((flags & HAR_CUDA_MOE_DECODE) &&
+      (flags & (HAR_CUDA_MOE_ACT_Q8K | HAR_CUDA_MOE_FORCE_TC | HAR_CUDA_MOE_TC_F16W | HAR_CUDA_MOE_EMPTY_SLOTS)))
+    return set_error(ctx, HAR_CUDA_ERR_ARG,
+                     "moe_ffn: HAR_CUDA_MOE_DECODE runs f32 activations on CUDA cores: not with ACT_Q8K, "
+                     "FORCE_TC, TC_F16W or EMPTY_SLOTS");
   return HAR_CUDA_OK;
 }
 

@@ -43,17 +43,11 @@ struct ActSmem<ACT_Q8K> {
   }
 };
 
-// Stage f32 activation rows (row pointers may be null for padding tokens).
-__device__ __forceinline__ void stage_f32(uint8_t *smem, const float *const *rows, int MT, int K) {
-  float *xs = reinterpret_cast<float *>(smem);
-  float *sums = xs + (size_t)MT * K;
-  const int nvec = K / 4;
-  for (int i = threadIdx.x; i < MT * nvec; i += blockDim.x) {
-    const int t = i / nvec, v = i - t * nvec;
-    float4 val = rows[t] ? reinterpret_cast<const float4 *>(rows[t])[v] : make_float4(0, 0, 0, 0);
-    reinterpret_cast<float4 *>(xs + (size_t)t * K)[v] = val;
-  }
-  __syncthreads();
+// Per-32-value sub-block sums of MT f32 rows already in shared memory
+// (xs[t][K] at the start of smem); ends with a CTA barrier.
+__device__ __forceinline__ void stage_f32_sums(uint8_t *smem, int MT, int K) {
+  const float *xs = reinterpret_cast<const float *>(smem);
+  float *sums = reinterpret_cast<float *>(smem) + (size_t)MT * K;
   const int nsub = K / 32;
   for (int i = threadIdx.x; i < MT * nsub; i += blockDim.x) {
     const int t = i / nsub, s = i - t * nsub;
@@ -64,6 +58,19 @@ __device__ __forceinline__ void stage_f32(uint8_t *smem, const float *const *row
     sums[(size_t)t * nsub + s] = acc;
   }
   __syncthreads();
+}
+
+// Stage f32 activation rows (row pointers may be null for padding tokens).
+__device__ __forceinline__ void stage_f32(uint8_t *smem, const float *const *rows, int MT, int K) {
+  float *xs = reinterpret_cast<float *>(smem);
+  const int nvec = K / 4;
+  for (int i = threadIdx.x; i < MT * nvec; i += blockDim.x) {
+    const int t = i / nvec, v = i - t * nvec;
+    float4 val = rows[t] ? reinterpret_cast<const float4 *>(rows[t])[v] : make_float4(0, 0, 0, 0);
+    reinterpret_cast<float4 *>(xs + (size_t)t * K)[v] = val;
+  }
+  __syncthreads();
+  stage_f32_sums(smem, MT, K);
 }
 
 // Stage packed Q8_K activation rows (292-byte blocks).
@@ -116,6 +123,30 @@ struct LaneAct<ACT_F32> {
     slo = sums[2 * chunk];
     shi = sums[2 * chunk + 1];
   }
+  // The chunk from a plain f32 row in shared memory (64 floats at src,
+  // 16-byte aligned), with the two sub-block sums taken in registers: a fixed
+  // pairwise tree, so the sums do not depend on the launch shape.
+  __device__ __forceinline__ void load_row(const float *src) {
+    const float4 *s4 = reinterpret_cast<const float4 *>(src);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 a = s4[i], b = s4[8 + i];
+      lo[4 * i] = a.x; lo[4 * i + 1] = a.y; lo[4 * i + 2] = a.z; lo[4 * i + 3] = a.w;
+      hi[4 * i] = b.x; hi[4 * i + 1] = b.y; hi[4 * i + 2] = b.z; hi[4 * i + 3] = b.w;
+    }
+    slo = tree_sum32(lo);
+    shi = tree_sum32(hi);
+  }
+  static __device__ __forceinline__ float tree_sum32(const float (&v)[32]) {
+    float t[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) t[i] = v[i] + v[i + 16];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) t[i] += t[i + 8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) t[i] += t[i + 4];
+    return (t[0] + t[2]) + (t[1] + t[3]);
+  }
 };
 
 template <>
@@ -151,6 +182,18 @@ __device__ __forceinline__ WChunk load_wchunk(const uint8_t *row, int chunk) {
   w.hdr = __ldg(reinterpret_cast<const uint4 *>(blk));
   w.q0 = __ldg(reinterpret_cast<const uint4 *>(blk + 16 + 32 * c));
   w.q1 = __ldg(reinterpret_cast<const uint4 *>(blk + 32 + 32 * c));
+  return w;
+}
+
+// The same chunk from a row staged in shared memory (plain loads: the
+// read-only global path must not see a shared address).
+__device__ __forceinline__ WChunk load_wchunk_s(const uint8_t *row, int chunk) {
+  const uint8_t *blk = row + (size_t)(chunk >> 2) * Q4K_BYTES;
+  const int c = chunk & 3;
+  WChunk w;
+  w.hdr = *reinterpret_cast<const uint4 *>(blk);
+  w.q0 = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * c);
+  w.q1 = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * c);
   return w;
 }
 

@@ -306,6 +306,11 @@ int32_t run_moe_ffn_in(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const
                        uint32_t flags, uint8_t *scratch);
 int32_t check_moe_args(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, int64_t T,
                        int32_t k, uint32_t flags);
+// The decode path (HAR_CUDA_MOE_DECODE, k_moe_decode.cu) on a scratch region.
+size_t moe_decode_scratch_bytes(const har_cuda_moe_layer *layer, int64_t T, int k);
+int32_t run_moe_decode(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const float *x,
+                       int64_t T, int k, const int32_t *ids, const float *weights, float *y,
+                       uint32_t flags, uint8_t *scratch);
 int32_t encode_tmap_2d(har_cuda_ctx *ctx, TmaDesc *out, const void *base, int elem_bytes,
                        uint64_t rows, uint64_t cols, uint64_t row_stride, uint32_t box_rows,
                        uint32_t box_cols, bool swizzle128);

@@ -98,16 +98,6 @@ __device__ __forceinline__ bool gs_wait(uint64_t *bar, uint32_t parity, volatile
   return false;
 }
 
-__device__ __forceinline__ WChunk load_wchunk_s(const uint8_t *row, int chunk) {
-  const uint8_t *blk = row + (size_t)(chunk >> 2) * Q4K_BYTES;
-  const int c = chunk & 3;
-  WChunk w;
-  w.hdr = *reinterpret_cast<const uint4 *>(blk);
-  w.q0 = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * c);
-  w.q1 = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * c);
-  return w;
-}
-
 template <int ACT, int LPR, int CPL, int CW>
 __global__ void __launch_bounds__(32 * (CW + 1), 1) q4k_gemv_stream_kernel(
     const uint8_t *__restrict__ W, int64_t N, int K, int64_t row_bytes, const uint8_t *__restrict__ act,

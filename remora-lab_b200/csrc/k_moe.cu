@@ -453,6 +453,7 @@ static MoeScratch moe_layout(const har_cuda_moe_layer *layer, int64_t T, int k, 
 
 size_t moe_scratch_bytes(const har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, int64_t T, int k,
                          uint32_t flags) {
+  if (flags & HAR_CUDA_MOE_DECODE) return moe_decode_scratch_bytes(layer, T, k);
   return moe_layout(layer, T, k, (flags & HAR_CUDA_MOE_ACT_Q8K) != 0,
                     tc_possible(ctx, layer, T, k, flags))
       .total;
@@ -471,6 +472,7 @@ int32_t run_moe_ffn(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const fl
 int32_t run_moe_ffn_in(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const float *x,
                        int64_t T, int k, const int32_t *ids, const float *weights, float *y,
                        uint32_t flags, uint8_t *S) {
+  if (flags & HAR_CUDA_MOE_DECODE) return run_moe_decode(ctx, layer, x, T, k, ids, weights, y, flags, S);
   if (((uintptr_t)x & 15u) || ((uintptr_t)y & 15u))
     return set_error(ctx, HAR_CUDA_ERR_ARG, "moe_ffn: x and y must be 16-byte aligned");
   const bool q8 = (flags & HAR_CUDA_MOE_ACT_Q8K) != 0;

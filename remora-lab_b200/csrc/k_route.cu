@@ -92,7 +92,125 @@ __device__ __forceinline__ void topk_warp(const float *l, int E, int k, float *p
   }
 }
 
-__global__ void __launch_bounds__(128) route_topk_kernel(const float *__restrict__ logits,
+// topk_warp with the token's values held in registers: lane l owns indices
+// l, l + 32, ... (EPL of them, E <= 32 * EPL).  The logits are read in one
+// burst, the exps are staged in p only for the sequential sum, and each of the
+// k rounds is an in-register tournament (lower index wins a tie, as the scan in
+// index order does) plus two warp reductions.  Same operations in the same
+// order as topk_warp, so the same bits.
+// One level of the in-register tournament (entries W apart), then the next.
+template <int EPL, int W>
+__device__ __forceinline__ void topk_tournament(uint32_t (&bk)[EPL], int (&bj)[EPL]) {
+  if constexpr (W < EPL) {
+#pragma unroll
+    for (int j = 0; j + W < EPL; j += 2 * W) {
+      const bool la = bk[j] < 0x80000000u, ra = bk[j + W] < 0x80000000u;
+      if (ra && (!la || bk[j + W] > bk[j])) {
+        bk[j] = bk[j + W];
+        bj[j] = bj[j + W];
+      }
+    }
+    topk_tournament<EPL, 2 * W>(bk, bj);
+  }
+}
+
+template <int EPL>
+__device__ __forceinline__ void topk_warp_regs(const float *l, int E, int k, float *p, int lane,
+                                               int32_t *ids, float *weights) {
+  float v[EPL];
+#pragma unroll
+  for (int j = 0; j < EPL; ++j) {
+    const int i = lane + 32 * j;
+    v[j] = i < E ? __ldcg(l + i) : -INFINITY;
+  }
+  float mx = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < EPL; ++j) mx = fmaxf(mx, v[j]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+#pragma unroll
+  for (int j = 0; j < EPL; ++j) {
+    const int i = lane + 32 * j;
+    v[j] = expf_ref(__fsub_rn(v[j], mx));
+    if (i < E) p[i] = v[j];
+  }
+  __syncwarp();
+  float den = 0.0f;
+  if (lane == 0) {  // exps.iter().sum(): one chain in index order
+    int i = 0;
+    if (E % 4 == 0) {
+      const float4 *p4 = reinterpret_cast<const float4 *>(p);
+#pragma unroll 8
+      for (; i < E; i += 4) {
+        const float4 q = p4[i >> 2];
+        den = __fadd_rn(den, q.x);
+        den = __fadd_rn(den, q.y);
+        den = __fadd_rn(den, q.z);
+        den = __fadd_rn(den, q.w);
+      }
+    }
+    for (; i < E; ++i) den = __fadd_rn(den, p[i]);
+    den = fmaxf(den, ROUTER_EPS);
+  }
+  den = __shfl_sync(0xffffffffu, den, 0);
+  // keys: the bits of p (>= +0, ordered like the values); taken entries and
+  // padding have the sign bit set
+  uint32_t key[EPL];
+#pragma unroll
+  for (int j = 0; j < EPL; ++j)
+    key[j] = lane + 32 * j < E ? __float_as_uint(__fdiv_rn(v[j], den)) : 0xffffffffu;
+  int sel_id = 0;
+  float sel_p = 0.0f;
+  for (int s = 0; s < k; ++s) {
+    // this lane's best available entry: a tournament over j, left (lower j,
+    // lower index) kept unless the right one is available and larger
+    uint32_t bk[EPL];
+    int bj[EPL];
+#pragma unroll
+    for (int j = 0; j < EPL; ++j) {
+      bk[j] = key[j];
+      bj[j] = j;
+    }
+    topk_tournament<EPL, 1>(bk, bj);
+    const bool avail = bk[0] < 0x80000000u;
+    const uint32_t bb = avail ? bk[0] : 0u;
+    const uint32_t bi = avail ? (uint32_t)(lane + 32 * bj[0]) : 0x7fffffffu;
+    const uint32_t mb = __reduce_max_sync(0xffffffffu, bb);
+    const uint32_t wi = __reduce_min_sync(0xffffffffu, bb == mb ? bi : 0x7fffffffu);
+    if (lane == s) {
+      sel_id = (int)wi;
+      sel_p = __uint_as_float(mb);
+    }
+    // mark the winner taken (branch-free: an indexed register write would
+    // put the keys in local memory)
+    const uint32_t hit = wi != 0x7fffffffu && lane == (int)(wi & 31u) ? 0x80000000u : 0u;
+    const int jw = (int)(wi >> 5);
+#pragma unroll
+    for (int j = 0; j < EPL; ++j) key[j] |= j == jw ? hit : 0u;
+  }
+  float tot = 0.0f;
+  for (int s = 0; s < k; ++s) tot = __fadd_rn(tot, __shfl_sync(0xffffffffu, sel_p, s));
+  tot = fmaxf(tot, ROUTER_EPS);
+  if (lane < k) {
+    ids[lane] = sel_id;
+    weights[lane] = __fdiv_rn(sel_p, tot);
+  }
+  __syncwarp();  // p is reused by the warp's next token
+}
+
+// One token's selection by one warp, in registers when E <= 1024.
+__device__ __forceinline__ void topk_token(const float *l, int E, int k, float *p, int lane, int32_t *ids,
+                                           float *weights) {
+  if (E <= 32) topk_warp_regs<1>(l, E, k, p, lane, ids, weights);
+  else if (E <= 64) topk_warp_regs<2>(l, E, k, p, lane, ids, weights);
+  else if (E <= 128) topk_warp_regs<4>(l, E, k, p, lane, ids, weights);
+  else if (E <= 256) topk_warp_regs<8>(l, E, k, p, lane, ids, weights);
+  else if (E <= 512) topk_warp_regs<16>(l, E, k, p, lane, ids, weights);
+  else if (E <= 1024) topk_warp_regs<32>(l, E, k, p, lane, ids, weights);
+  else topk_warp(l, E, k, p, lane, ids, weights);
+}
+
+__global__ void __launch_bounds__(128, 1) route_topk_kernel(const float *__restrict__ logits,
                                                          int64_t T, int E, int k,
                                                          int32_t *__restrict__ ids,
                                                          float *__restrict__ weights) {
@@ -100,7 +218,7 @@ __global__ void __launch_bounds__(128) route_topk_kernel(const float *__restrict
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t t = (int64_t)blockIdx.x * 4 + warp;
   if (t >= T) return;
-  topk_warp(logits + t * E, E, k, rsm + (size_t)warp * E, lane, ids + t * k, weights + t * k);
+  topk_token(logits + t * E, E, k, rsm + (size_t)warp * E, lane, ids + t * k, weights + t * k);
 }
 
 int32_t launch_route_topk(har_cuda_ctx *ctx, const float *logits, int64_t T, int E, int k,
@@ -485,89 +603,125 @@ __global__ void __launch_bounds__(RL_WARPS * 32) router_logits_pipe_kernel(
 }
 
 // router_logits_small_kernel: decode-sized batches (T <= RS_T).  The same
-// chains again, spread thin: one warp per CTA owns 8 experts x 4 tokens, lane
-// (expert e0 + lane/4, token lane%4), so E/8 CTAs share the router's reads.
-// A lone warp per SM has nothing to hide its latencies behind, so the kernel
-// keeps the instructions around each chain's dependent adds few: 128-wide
-// slices through a 6-deep cp.async ring, each lane copying one fixed 16-byte
-// column of all 12 staged rows (8 router rows, 4 token rows) from row pointers
-// computed once, and a fully unrolled pass over a full slice.
-constexpr int RS_E = 8, RS_T = 4, RS_ROWS = RS_E + RS_T, RS_KC = 128, RS_LD = RS_KC + 4, RS_S = 6;
+// chains again, spread thin: a CTA of RS_W warps owns RS_E experts x RS_T
+// tokens, lane (expert e0 + lane/4, token 4*warp + lane%4), so E/RS_E CTAs
+// share the router's reads and every chain of a token runs at once.  A chain
+// is H dependent adds long, so the kernel is built around keeping that chain
+// fed: RS_KC-wide slices of the RS_E router rows and the T token rows come
+// through an RS_S-deep cp.async ring, and each thread walks a slice in groups
+// of 16 values with the next group's shared-memory loads issued before the
+// current group's adds (register double buffering), so no add waits on a load.
+//
+// routed_moe's selection is fused in: the CTA that finishes last (all logits
+// written and fenced) runs the top-k, one token per warp at a time, then
+// re-arms the counter.
+constexpr int RS_E = 8, RS_TW = 4, RS_W = 4, RS_T = RS_TW * RS_W, RS_KC = 128, RS_LD = RS_KC + 4,
+              RS_S = 6, RS_G = 16;
 
-__global__ void __launch_bounds__(32) router_logits_small_kernel(
+// floats of one ring stage (RS_E router rows + the T token rows) and of the
+// whole dynamic shared memory (the ring, or E floats per warp for the top-k)
+__host__ __device__ inline int rs_stage_floats(int T) { return (RS_E + T) * RS_LD; }
+__host__ __device__ inline size_t rs_smem_bytes(int T, int E) {
+  const size_t ring = (size_t)RS_S * rs_stage_floats(T), topk = (size_t)RS_W * E;
+  return sizeof(float) * (ring > topk ? ring : topk);
+}
+
+__device__ __forceinline__ void rs_group_load(const float *wr, const float *xr, int c, float4 (&w)[RS_G / 4],
+                                              float4 (&v)[RS_G / 4]) {
+#pragma unroll
+  for (int i = 0; i < RS_G / 4; ++i) {
+    w[i] = *reinterpret_cast<const float4 *>(wr + c + 4 * i);
+    v[i] = *reinterpret_cast<const float4 *>(xr + c + 4 * i);
+  }
+}
+__device__ __forceinline__ float rs_group_chain(float s, const float4 (&w)[RS_G / 4], const float4 (&v)[RS_G / 4]) {
+#pragma unroll
+  for (int i = 0; i < RS_G / 4; ++i) {
+    s = __fadd_rn(s, __fmul_rn(w[i].x, v[i].x));
+    s = __fadd_rn(s, __fmul_rn(w[i].y, v[i].y));
+    s = __fadd_rn(s, __fmul_rn(w[i].z, v[i].z));
+    s = __fadd_rn(s, __fmul_rn(w[i].w, v[i].w));
+  }
+  return s;
+}
+
+__device__ __forceinline__ void rs_load_slice(float *st, const float *W, const float *x, int E, int H,
+                                              int e0, int nrows, int h0) {
+  for (int i = threadIdx.x; i < nrows * (RS_KC / 4); i += RS_W * 32) {
+    const int r = i / (RS_KC / 4), c = 4 * (i % (RS_KC / 4));
+    const bool ok = (r < RS_E ? e0 + r < E : true) && h0 + c < H;
+    const float *src = !ok ? W : r < RS_E ? W + (int64_t)(e0 + r) * H + h0 + c
+                                           : x + (int64_t)(r - RS_E) * H + h0 + c;
+    tc::cp_async16(st + r * RS_LD + c, src, ok ? 16u : 0u);
+  }
+}
+
+__global__ void __launch_bounds__(RS_W * 32, 1) router_logits_small_kernel(
     const float *__restrict__ W, const float *__restrict__ x, int64_t T, int E, int H,
     float *__restrict__ logits, int k, int32_t *__restrict__ ids, float *__restrict__ weights,
     int *counter) {
-  __shared__ __align__(16) float rss[RS_S][RS_ROWS * RS_LD];
-  const int lane = threadIdx.x, el = lane >> 2, tl = lane & 3;
+  extern __shared__ __align__(16) float rss[];
+  __shared__ int last_s;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int el = lane >> 2, tok = RS_TW * warp + (lane & 3);
   const int e0 = blockIdx.x * RS_E;
+  const int nt = (int)T, nrows = RS_E + nt, SF = rs_stage_floats(nt);
   const int nchunk = (H + RS_KC - 1) / RS_KC;
-  // this lane's column of every staged row, and which rows exist
-  const float *src[RS_ROWS];
-  uint32_t rows_ok = 0;
-#pragma unroll
-  for (int r = 0; r < RS_ROWS; ++r) {
-    const bool ok = r < RS_E ? e0 + r < E : (int64_t)(r - RS_E) < T;
-    src[r] = (r < RS_E ? W + (int64_t)(ok ? e0 + r : 0) * H
-                       : x + (int64_t)(ok ? r - RS_E : 0) * H) + 4 * lane;
-    rows_ok |= (ok ? 1u : 0u) << r;
-  }
-  auto load = [&](int ch) {
-    float *st = rss[ch % RS_S] + 4 * lane;
-    const int h = ch * RS_KC + 4 * lane;
-    const uint32_t ok = h < H ? rows_ok : 0u;
-#pragma unroll
-    for (int r = 0; r < RS_ROWS; ++r)
-      tc::cp_async16(st + r * RS_LD, (ok >> r) & 1u ? src[r] + ch * RS_KC : W,
-                     (ok >> r) & 1u ? 16u : 0u);
-  };
+  // slice `ch` into ring slot ch % RS_S: nrows rows x RS_KC / 4 16-byte
+  // columns over the CTA's threads; rows past E and columns past H are
+  // zero-filled and never read by the arithmetic
+  auto load = [=](int ch) { rs_load_slice(rss + (ch % RS_S) * SF, W, x, E, H, e0, nrows, ch * RS_KC); };
 #pragma unroll
   for (int ch = 0; ch < RS_S - 1; ++ch) {
     if (ch < nchunk) load(ch);
     tc::cp_async_commit();
   }
+  const bool active = tok < nt;  // a warp past T only helps load
   float s = 0.0f;
   for (int ch = 0; ch < nchunk; ++ch) {
     tc::cp_async_wait<RS_S - 2>();
-    __syncwarp();
+    __syncthreads();  // slice ch landed (everyone's copies); slice ch - 1 consumed
     if (ch + RS_S - 1 < nchunk) load(ch + RS_S - 1);
     tc::cp_async_commit();
-    const float *wr = rss[ch % RS_S] + el * RS_LD, *xr = rss[ch % RS_S] + (RS_E + tl) * RS_LD;
+    if (!active) continue;
+    const float *st = rss + (ch % RS_S) * SF;
+    const float *wr = st + el * RS_LD, *xr = st + (RS_E + tok) * RS_LD;
     const int kc = min(RS_KC, H - ch * RS_KC);
-    auto step = [&](int c) {
-      const float4 w = *reinterpret_cast<const float4 *>(wr + c);
-      const float4 v = *reinterpret_cast<const float4 *>(xr + c);
-      s = __fadd_rn(s, __fmul_rn(w.x, v.x));
-      s = __fadd_rn(s, __fmul_rn(w.y, v.y));
-      s = __fadd_rn(s, __fmul_rn(w.z, v.z));
-      s = __fadd_rn(s, __fmul_rn(w.w, v.w));
-    };
     if (kc == RS_KC) {
+      float4 wa[RS_G / 4], va[RS_G / 4], wb[RS_G / 4], vb[RS_G / 4];
+      rs_group_load(wr, xr, 0, wa, va);
 #pragma unroll
-      for (int c = 0; c < RS_KC; c += 4) step(c);
+      for (int g = 0; g < RS_KC / RS_G; g += 2) {
+        rs_group_load(wr, xr, (g + 1) * RS_G, wb, vb);
+        s = rs_group_chain(s, wa, va);
+        if (g + 2 < RS_KC / RS_G) rs_group_load(wr, xr, (g + 2) * RS_G, wa, va);
+        s = rs_group_chain(s, wb, vb);
+      }
     } else {
-      for (int c = 0; c < kc; c += 4) step(c);
+      for (int c = 0; c < kc; c += 4) {
+        const float4 w = *reinterpret_cast<const float4 *>(wr + c);
+        const float4 v = *reinterpret_cast<const float4 *>(xr + c);
+        s = __fadd_rn(s, __fmul_rn(w.x, v.x));
+        s = __fadd_rn(s, __fmul_rn(w.y, v.y));
+        s = __fadd_rn(s, __fmul_rn(w.z, v.z));
+        s = __fadd_rn(s, __fmul_rn(w.w, v.w));
+      }
     }
-    __syncwarp();  // the slot is refilled at the next iteration
   }
   tc::cp_async_wait_all();
-  if (e0 + el < E && tl < T) logits[(int64_t)tl * E + e0 + el] = s;
-  if (counter) {
-    // routed_moe's selection fused in: the CTA that finishes last (all logits
-    // written and fenced) runs the top-k of every token, then re-arms the counter
-    __threadfence();
-    __syncwarp();
-    int last = 0;
-    if (lane == 0) last = atomicAdd(counter, 1) == (int)gridDim.x - 1;
-    if (__shfl_sync(0xffffffffu, last, 0)) {
-      __threadfence();
-      float *p = &rss[0][0];  // the ring is idle: every copy has landed and been read
-      for (int t = 0; t < (int)T; ++t)
-        topk_warp(logits + (int64_t)t * E, E, k, p, lane, ids + (int64_t)t * k,
-                  weights + (int64_t)t * k);
-      if (lane == 0) *counter = 0;
-    }
-  }
+  if (active && e0 + el < E) logits[(int64_t)tok * E + e0 + el] = s;
+  if (!counter) return;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) last_s = atomicAdd(counter, 1) == (int)gridDim.x - 1;
+  __syncthreads();
+  if (!last_s) return;
+  __threadfence();
+  float *p = rss + (size_t)warp * E;  // the ring is idle: every copy landed and was read
+  for (int t = warp; t < nt; t += RS_W)
+    topk_token(logits + (int64_t)t * E, E, k, p, lane, ids + (int64_t)t * k, weights + (int64_t)t * k);
+  __syncthreads();
+  if (threadIdx.x == 0) *counter = 0;
 }
 
 // Router logits and top-k in one launch for decode batches; *done = false
@@ -577,10 +731,13 @@ int32_t launch_route_fused(har_cuda_ctx *ctx, const float *W, int E, int H, cons
                            bool *done) {
   *done = false;
   const bool vec = H % 4 == 0 && ((uintptr_t)W & 15u) == 0 && ((uintptr_t)x & 15u) == 0;
-  if (!vec || T > RS_T || T < 1 || (size_t)E > sizeof(float) * RS_S * RS_ROWS * RS_LD / 4)
-    return HAR_CUDA_OK;
+  if (!vec || T > RS_T || T < 1) return HAR_CUDA_OK;
+  const size_t smem = rs_smem_bytes((int)T, E);
+  if (smem > 227 * 1024) return HAR_CUDA_OK;
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(router_logits_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   prof_begin(ctx);
-  router_logits_small_kernel<<<(unsigned)((E + RS_E - 1) / RS_E), 32, 0, ctx->stream>>>(
+  router_logits_small_kernel<<<(unsigned)((E + RS_E - 1) / RS_E), RS_W * 32, smem, ctx->stream>>>(
       W, x, T, E, H, logits, k, ids, weights, ctx->d_status + 1);
   *done = true;
   return check_launch(ctx, "router_logits_small_kernel");
@@ -591,8 +748,11 @@ int32_t launch_router_logits(har_cuda_ctx *ctx, const float *W, int E, int H, co
   const dim3 grid((unsigned)((E + RL_E - 1) / RL_E), (unsigned)((T + RL_TT - 1) / RL_TT));
   const bool vec = H % 4 == 0 && ((uintptr_t)W & 15u) == 0 && ((uintptr_t)x & 15u) == 0;
   if (vec && T <= RS_T) {
+    const size_t smem = (size_t)RS_S * rs_stage_floats((int)T) * sizeof(float);
+    if (smem > 48 * 1024)
+      cudaFuncSetAttribute(router_logits_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     prof_begin(ctx);
-    router_logits_small_kernel<<<(unsigned)((E + RS_E - 1) / RS_E), 32, 0, ctx->stream>>>(
+    router_logits_small_kernel<<<(unsigned)((E + RS_E - 1) / RS_E), RS_W * 32, smem, ctx->stream>>>(
         W, x, T, E, H, logits, 0, nullptr, nullptr, nullptr);
     return check_launch(ctx, "router_logits_small_kernel");
   }

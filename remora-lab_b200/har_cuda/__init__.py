@@ -48,6 +48,7 @@ MOE_FORCE_GEMV = 0x4
 MOE_FORCE_TC = 0x8
 MOE_EMPTY_SLOTS = 0x10
 MOE_TC_F16W = 0x20
+MOE_DECODE = 0x40
 
 # Every symbol include/har_cuda.h declares (tests check the library exports them).
 EXPORTS = [

@@ -42,8 +42,10 @@ def _router(E, H, seed, dup=None):
 @pytest.mark.gpu
 @pytest.mark.parametrize("T,E,H", [(1, 512, 2048), (37, 100, 333), (256, 512, 2048),
                                    (70, 33, 64), (5, 8, 1),
-                                   # decode-sized batches (T <= 4), E not a multiple of 8
+                                   # decode-sized batches (T <= 16), E not a multiple of 8,
+                                   # H not a multiple of the 128-wide slice
                                    (2, 512, 2048), (4, 100, 512), (3, 7, 64),
+                                   (8, 512, 2048), (16, 100, 260), (11, 9, 4),
                                    # T > 512: four tokens per thread, a ragged last tile
                                    (600, 64, 256)])
 def test_router_logits_bit_exact(T, E, H):
@@ -66,7 +68,8 @@ def test_router_logits_bit_exact(T, E, H):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("T,E,H,k", [(1, 512, 2048, 10), (64, 512, 2048, 10), (33, 64, 512, 8),
-                                     (3, 32, 256, 32)])
+                                     (3, 32, 256, 32), (8, 512, 2048, 10), (16, 100, 260, 8),
+                                     (13, 64, 2048, 32)])
 def test_route_from_tokens_bit_exact(T, E, H, k):
     import torch
     from gpu_util import to_dev
