@@ -102,6 +102,21 @@ __device__ __forceinline__ void stage_q8k(uint8_t *smem, const uint8_t *const *r
   __syncthreads();
 }
 
+// 16-byte load from shared memory by its shared-window address: explicit, so
+// a staged row is never read through the generic path.  Volatile keeps it
+// after the barrier wait that publishes the row.
+__device__ __forceinline__ uint4 lds_u4(uint32_t saddr) {
+  uint4 r;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "r"(saddr));
+  return r;
+}
+__device__ __forceinline__ float4 lds_f4(uint32_t saddr) {
+  const uint4 r = lds_u4(saddr);
+  return make_float4(__uint_as_float(r.x), __uint_as_float(r.y), __uint_as_float(r.z), __uint_as_float(r.w));
+}
+
 // Per-lane activation registers for one chunk of one token.
 template <int ACT>
 struct LaneAct;
@@ -127,10 +142,10 @@ struct LaneAct<ACT_F32> {
   // 16-byte aligned), with the two sub-block sums taken in registers: a fixed
   // pairwise tree, so the sums do not depend on the launch shape.
   __device__ __forceinline__ void load_row(const float *src) {
-    const float4 *s4 = reinterpret_cast<const float4 *>(src);
+    const uint32_t sa = (uint32_t)__cvta_generic_to_shared(src);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const float4 a = s4[i], b = s4[8 + i];
+      const float4 a = lds_f4(sa + 16 * i), b = lds_f4(sa + 128 + 16 * i);
       lo[4 * i] = a.x; lo[4 * i + 1] = a.y; lo[4 * i + 2] = a.z; lo[4 * i + 3] = a.w;
       hi[4 * i] = b.x; hi[4 * i + 1] = b.y; hi[4 * i + 2] = b.z; hi[4 * i + 3] = b.w;
     }
@@ -188,12 +203,12 @@ __device__ __forceinline__ WChunk load_wchunk(const uint8_t *row, int chunk) {
 // The same chunk from a row staged in shared memory (plain loads: the
 // read-only global path must not see a shared address).
 __device__ __forceinline__ WChunk load_wchunk_s(const uint8_t *row, int chunk) {
-  const uint8_t *blk = row + (size_t)(chunk >> 2) * Q4K_BYTES;
-  const int c = chunk & 3;
+  const uint32_t blk = (uint32_t)__cvta_generic_to_shared(row) + (uint32_t)(chunk >> 2) * Q4K_BYTES;
+  const uint32_t c = (uint32_t)(chunk & 3);
   WChunk w;
-  w.hdr = *reinterpret_cast<const uint4 *>(blk);
-  w.q0 = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * c);
-  w.q1 = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * c);
+  w.hdr = lds_u4(blk);
+  w.q0 = lds_u4(blk + 16 + 32 * c);
+  w.q1 = lds_u4(blk + 32 + 32 * c);
   return w;
 }
 
@@ -231,6 +246,28 @@ __device__ __forceinline__ float chunk_dot(const WChunk &w, int chunk, const Lan
   }
   const ChunkScales s = chunk_scales(w.hdr, chunk & 3);
   return (s.d1 * slo - s.m1 * a.slo) + (s.d2 * shi - s.m2 * a.shi);
+}
+
+// chunk_dot for latency-bound callers (the decode kernels, a few warps per
+// SM): four accumulators per sub-block instead of one, so the dependent FMA
+// depth is 8 instead of 32; the four partial sums are added pairwise.  Same
+// terms, different association (within the f32 path's tolerance); a caller
+// uses one form throughout, so its results do not depend on the batch.
+__device__ __forceinline__ float chunk_dot_ilp(const WChunk &w, int chunk, const LaneAct<ACT_F32> &a) {
+  const uint32_t q[8] = {w.q0.x, w.q0.y, w.q0.z, w.q0.w, w.q1.x, w.q1.y, w.q1.z, w.q1.w};
+  float slo[4] = {0.0f, 0.0f, 0.0f, 0.0f}, shi[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint32_t lo = q[i] & 0x0F0F0F0Fu, hi = (q[i] >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      slo[j] = fmaf(u8_to_f32(lo, j), a.lo[4 * i + j], slo[j]);
+      shi[j] = fmaf(u8_to_f32(hi, j), a.hi[4 * i + j], shi[j]);
+    }
+  }
+  const float sl = (slo[0] + slo[1]) + (slo[2] + slo[3]), sh = (shi[0] + shi[1]) + (shi[2] + shi[3]);
+  const ChunkScales s = chunk_scales(w.hdr, chunk & 3);
+  return (s.d1 * sl - s.m1 * a.slo) + (s.d2 * sh - s.m2 * a.shi);
 }
 
 // Lanes per row, chunks per lane and tokens per pass for a given K.

@@ -118,9 +118,9 @@ __device__ const uint64_t EXP2_I32[32] = {
     0x3ffae89f995ad3adull, 0x3ffb7f76f2fb5e47ull, 0x3ffc199bdd85529cull, 0x3ffcb720dcef9069ull,
     0x3ffd5818dcfba487ull, 0x3ffdfc97337b9b5full, 0x3ffea4afa2a490daull, 0x3fff50765b6e4540ull};
 
+// Branch-free, so unrolled calls overlap: the two out-of-range cases are
+// selected at the end (the arithmetic on such x is discarded).
 __device__ __forceinline__ float expf_ref(float x) {
-  if (x < -0x1.9fe368p6f) return 0.0f;             // below log(2^-150): rounds to zero
-  if (x > 0x1.62e42ep6f) return __int_as_float(0x7f800000);  // above log(2^128): overflow
   const double inv = 0x1.71547652b82fep+0 * 32.0, shift = 0x1.8p+52;
   const double c0 = 0x1.c6af84b912394p-5 / 32768.0, c1 = 0x1.ebfce50fac4f3p-3 / 1024.0,
                c2 = 0x1.62e42ff0c52d6p-1 / 32.0;
@@ -136,7 +136,9 @@ __device__ __forceinline__ float expf_ref(float x) {
   const double r2 = __dmul_rn(r, r);
   double y = __fma_rn(c2, r, 1.0);
   y = __fma_rn(q, r2, y);
-  return __double2float_rn(__dmul_rn(y, s));
+  const float res = __double2float_rn(__dmul_rn(y, s));
+  return x < -0x1.9fe368p6f ? 0.0f                            // below log(2^-150): rounds to zero
+         : x > 0x1.62e42ep6f ? __int_as_float(0x7f800000) : res;  // above log(2^128): overflow
 }
 
 // sigmoid of har-native-qwen35moe.rs:207-214, with the reference's exp

@@ -31,11 +31,26 @@
 namespace har {
 
 constexpr int DECODE_MAX_T = 8;
-constexpr int DECODE_THREADS = 256;
+constexpr int DECODE_THREADS = 128;
 constexpr int DECODE_MAX_SLOTS = 33;  // k <= 32 routed slots + the shared one
-// rows per CTA: small blocks so that one token spreads over the SMs
-constexpr int DECODE_GU_ROWS = 32, DECODE_DOWN_ROWS = 16;
+// Rows per CTA.  A decode step's instructions are few and dependent, so the
+// kernels need many resident warps per SM to hide latency: small CTAs of
+// few rows (gate/up: 4 warps x 8 rows, several CTAs per SM; down: 8 hidden
+// rows, two CTAs per SM) rather than large blocks.
+constexpr int DECODE_GU_ROWS = 8, DECODE_DOWN_ROWS = 8;
 constexpr uint32_t DECODE_WAIT_LIMIT = 1u << 20;  // polls of a copy's barrier
+// Activation rows live in shared memory as 64-float chunks in slots of
+// DECODE_ACT_LD floats: lane c reads chunk c, and with 272-byte slots the
+// eight lanes of a quarter-warp reach eight different bank groups
+// (contiguous 256-byte chunks would put all eight on one).  The SwiGLU
+// activations are written to scratch in that padded layout, so the down
+// kernel copies them as they are; the token rows x are copied whole and
+// spread into the padded layout in shared memory (one bulk copy per chunk
+// would cost more: the copy engine takes tens of ns per request).
+constexpr int DECODE_ACT_LD = 68;
+__host__ __device__ inline size_t decode_act_row_bytes(int K) {
+  return (size_t)(K / 64) * DECODE_ACT_LD * sizeof(float);
+}
 
 struct DecodeArgs {
   const uint8_t *gate, *up, *down, *sh_gate, *sh_up, *sh_down;
@@ -51,7 +66,7 @@ struct DecodeArgs {
 };
 
 template <int LPR, int CPL>
-__global__ void __launch_bounds__(DECODE_THREADS) decode_gate_up_kernel(DecodeArgs p) {
+__global__ void __launch_bounds__(DECODE_THREADS, CPL == 1 ? 5 : 2) decode_gate_up_kernel(DecodeArgs p) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ uint64_t bar;
   __shared__ int skip;
@@ -64,8 +79,10 @@ __global__ void __launch_bounds__(DECODE_THREADS) decode_gate_up_kernel(DecodeAr
   const int r0 = blk * R, nr = min(p.I - r0, R);
   const int t = slot < n ? slot / p.k : slot - n;
   const float *xt = p.x + (int64_t)t * p.H;
-  float *xs = reinterpret_cast<float *>(smem);
-  uint8_t *wg_s = smem + 4 * (size_t)p.H, *wu_s = wg_s + (size_t)R * p.rb_h;
+  float *xraw = reinterpret_cast<float *>(smem);
+  float *xs = xraw + p.H;
+  uint8_t *wg_s = smem + ((4 * (size_t)p.H + decode_act_row_bytes(p.H) + 127) & ~(size_t)127);
+  uint8_t *wu_s = wg_s + (size_t)R * p.rb_h;
   if (threadIdx.x == 0) {
     const uint8_t *wg = p.sh_gate, *wu = p.sh_up;
     int bad = 0;
@@ -82,7 +99,7 @@ __global__ void __launch_bounds__(DECODE_THREADS) decode_gate_up_kernel(DecodeAr
       tc::mbar_init(&bar, 1);
       tc::fence_mbar_init();
       tc::mbar_expect_tx(&bar, xb + 2 * wb);
-      tc::bulk_g2s(xs, xt, xb, &bar);
+      tc::bulk_g2s(xraw, xt, xb, &bar);
       tc::bulk_g2s(wg_s, wg + (int64_t)r0 * p.rb_h, wb, &bar);
       tc::bulk_g2s(wu_s, wu + (int64_t)r0 * p.rb_h, wb, &bar);
     }
@@ -93,21 +110,23 @@ __global__ void __launch_bounds__(DECODE_THREADS) decode_gate_up_kernel(DecodeAr
     const float g = shared_gate_warp(p.gi, xt, p.H, lane);
     if (lane == 0) p.gsh[t] = g;
   }
-  if (!tc::mbar_wait(&bar, 0, DECODE_WAIT_LIMIT)) {
-    atomicOr(p.status, DEV_ERR_TIMEOUT);
-    return;
-  }
+  const bool landed = tc::mbar_wait(&bar, 0, DECODE_WAIT_LIMIT);
+  if (!landed && threadIdx.x == 0) atomicOr(p.status, DEV_ERR_TIMEOUT);
+  if (__syncthreads_or(!landed)) return;
+  for (int q = threadIdx.x; q < p.H / 4; q += DECODE_THREADS)  // x into the padded layout
+    reinterpret_cast<float4 *>(xs + DECODE_ACT_LD * (q >> 4))[q & 15] = reinterpret_cast<const float4 *>(xraw)[q];
+  __syncthreads();
   const int grp = lane / LPR, gl = lane % LPR;
   const int C = p.H / 64;
   LaneAct<ACT_F32> act[CPL];
 #pragma unroll
   for (int i = 0; i < CPL; ++i)
-    if (gl + LPR * i < C) act[i].load_row(xs + 64 * (gl + LPR * i));
+    if (gl + LPR * i < C) act[i].load_row(xs + DECODE_ACT_LD * (gl + LPR * i));
   // This warp's QN row passes of gate then up, one dot per iteration.  The
   // loop stays rolled on purpose: each launch runs once per layer on SMs whose
   // instruction caches hold other kernels, so one static copy of the chunk
   // dot fetched once beats unrolled copies that are each fetched from L2.
-  float *arow = p.a + (int64_t)slot * p.I + r0;
+  float *arow = p.a + (int64_t)slot * ((p.I / 64) * DECODE_ACT_LD);
   float g = 0.0f;
 #pragma unroll 1
   for (int it = 0; it < 2 * QN; ++it) {
@@ -117,24 +136,25 @@ __global__ void __launch_bounds__(DECODE_THREADS) decode_gate_up_kernel(DecodeAr
 #pragma unroll
     for (int i = 0; i < CPL; ++i) {
       const int ch = gl + LPR * i;
-      if (ch < C) v += chunk_dot(load_wchunk_s(row, ch), ch, act[i]);
+      if (ch < C) v += chunk_dot_ilp(load_wchunk_s(row, ch), ch, act[i]);
     }
     v = lane_group_sum<LPR>(v);
     if (!(it & 1)) {
       g = v;
     } else if (r < nr && gl == 0) {
-      arow[r] = __fmul_rn(g / (1.0f + expf(-g)), v);
+      const int ri = r0 + r;  // padded position of intermediate row ri
+      arow[DECODE_ACT_LD * (ri >> 6) + (ri & 63)] = __fmul_rn(g / (1.0f + expf(-g)), v);
     }
   }
 }
 
 // The down kernel runs one warp per slot, up to decode_down_warps(CPL) warps
-// (more slots wrap around); two chunks per lane need the registers of a
-// smaller CTA.
-__host__ __device__ constexpr int decode_down_warps(int cpl) { return cpl == 1 ? 16 : 8; }
+// (more slots wrap around), two CTAs per SM; two chunks per lane need the
+// registers of a smaller CTA.
+__host__ __device__ constexpr int decode_down_warps(int cpl) { return cpl == 1 ? 12 : 8; }
 
 template <int LPR, int CPL>
-__global__ void __launch_bounds__(decode_down_warps(CPL) * 32) decode_down_combine_kernel(DecodeArgs p,
+__global__ void __launch_bounds__(decode_down_warps(CPL) * 32, CPL == 1 ? 2 : 1) decode_down_combine_kernel(DecodeArgs p,
                                                                                           int rows_per_cta) {
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int RPW = 32 / LPR, QD = DECODE_DOWN_ROWS / RPW > 0 ? DECODE_DOWN_ROWS / RPW : 1;
@@ -149,35 +169,34 @@ __global__ void __launch_bounds__(decode_down_warps(CPL) * 32) decode_down_combi
   const int nw = (int)(blockDim.x >> 5), warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r0 = blk * R, nr = min(p.H - r0, R);
   float *as = reinterpret_cast<float *>(smem);
-  uint8_t *w_s = smem + 4 * (size_t)ns * p.I;
+  const int SLD = (p.I / 64) * DECODE_ACT_LD;  // floats per staged activation row
+  uint8_t *w_s = smem + (((size_t)ns * decode_act_row_bytes(p.I) + 127) & ~(size_t)127);
   if (threadIdx.x == 0) {
     tc::mbar_init(&bar, ns);
     tc::fence_mbar_init();
   }
   __syncthreads();
   if (threadIdx.x < ns) {
-    // slot j's activation row and its expert's down rows r0 .. r0 + nr - 1
+    // slot j's expert: its down rows r0 .. r0 + nr - 1; thread 0 also copies
+    // the token's activation rows (its k routed slots are contiguous)
     const int j = threadIdx.x;
     const uint8_t *wd = p.sh_down;
-    const float *arow = p.a + (int64_t)(n + t) * p.I;
     float wt = p.gi ? p.gsh[t] : 1.0f;
     bool ok = true;
     if (j < p.k) {
       const int s = t * p.k + j, e = p.ids[s];
       ok = e >= 0 && e < p.E;  // a bad id contributes nothing (gate/up reported it)
       wd = p.down + (int64_t)(ok ? e : 0) * p.ebytes_d;
-      arow = p.a + (int64_t)s * p.I;
       wt = p.weights[s];
     }
     ok_s[j] = ok;
     swt[j] = wt;
-    if (ok) {
-      const uint32_t ab = (uint32_t)(4 * p.I), wb = (uint32_t)(nr * p.rb_i);
-      tc::mbar_expect_tx(&bar, ab + wb);
-      tc::bulk_g2s(as + (size_t)j * p.I, arow, ab, &bar);
-      tc::bulk_g2s(w_s + (size_t)j * R * p.rb_i, wd + (int64_t)r0 * p.rb_i, wb, &bar);
-    } else {
-      tc::mbar_arrive(&bar);
+    const uint32_t rb = (uint32_t)(4 * SLD), wb = ok ? (uint32_t)(nr * p.rb_i) : 0u;
+    tc::mbar_expect_tx(&bar, wb + (j == 0 ? (uint32_t)ns * rb : 0u));
+    if (ok) tc::bulk_g2s(w_s + (size_t)j * R * p.rb_i, wd + (int64_t)r0 * p.rb_i, wb, &bar);
+    if (j == 0) {
+      tc::bulk_g2s(as, p.a + (int64_t)t * p.k * SLD, (uint32_t)p.k * rb, &bar);
+      if (p.has_shared) tc::bulk_g2s(as + (size_t)p.k * SLD, p.a + (int64_t)(n + t) * SLD, rb, &bar);
     }
   }
   const bool landed = tc::mbar_wait(&bar, 0, DECODE_WAIT_LIMIT);
@@ -190,7 +209,7 @@ __global__ void __launch_bounds__(decode_down_warps(CPL) * 32) decode_down_combi
     LaneAct<ACT_F32> act[CPL];
 #pragma unroll
     for (int i = 0; i < CPL; ++i)
-      if (gl + LPR * i < C) act[i].load_row(as + (size_t)j * p.I + 64 * (gl + LPR * i));
+      if (gl + LPR * i < C) act[i].load_row(as + (size_t)j * SLD + DECODE_ACT_LD * (gl + LPR * i));
 #pragma unroll 1
     for (int q = 0; q < QD; ++q) {  // rolled, as in the gate/up kernel
       const int r = q * RPW + grp;
@@ -199,7 +218,7 @@ __global__ void __launch_bounds__(decode_down_warps(CPL) * 32) decode_down_combi
 #pragma unroll
       for (int i = 0; i < CPL; ++i) {
         const int ch = gl + LPR * i;
-        if (ch < C) v += chunk_dot(load_wchunk_s(row, ch), ch, act[i]);
+        if (ch < C) v += chunk_dot_ilp(load_wchunk_s(row, ch), ch, act[i]);
       }
       v = lane_group_sum<LPR>(v);
       if (gl == 0 && r < nr) part[j][r] = v;
@@ -240,7 +259,7 @@ struct DownK {
 };
 
 size_t moe_decode_scratch_bytes(const har_cuda_moe_layer *layer, int64_t T, int k) {
-  const size_t a = 4 * (size_t)(T * k + T) * (size_t)layer->I;
+  const size_t a = (size_t)(T * k + T) * decode_act_row_bytes((int)layer->I);
   return ((a + 255) & ~(size_t)255) + 4 * (size_t)T + 256;
 }
 
@@ -281,7 +300,7 @@ int32_t run_moe_decode(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const
   p.weights = weights;
   p.ids = ids;
   p.gi = p.has_shared ? layer->sh_gate_inp : nullptr;
-  const size_t a_bytes = (4 * (size_t)(T * k + T) * (size_t)p.I + 255) & ~(size_t)255;
+  const size_t a_bytes = ((size_t)(T * k + T) * decode_act_row_bytes(p.I) + 255) & ~(size_t)255;
   p.a = reinterpret_cast<float *>(S);
   p.gsh = reinterpret_cast<float *>(S + a_bytes);
   p.y = y;
@@ -290,12 +309,15 @@ int32_t run_moe_decode(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const
   const int slots = (int)(T * k) + (p.has_shared ? (int)T : 0);
   const int ns = k + p.has_shared;
   constexpr size_t SMEM_MAX = 227 * 1024;
-  const size_t smem_gu = 4 * (size_t)p.H + 2 * (size_t)DECODE_GU_ROWS * p.rb_h;
+  const size_t smem_gu = ((4 * (size_t)p.H + decode_act_row_bytes(p.H) + 127) & ~(size_t)127) +
+                        2 * (size_t)DECODE_GU_ROWS * p.rb_h;
   if (smem_gu > SMEM_MAX)
     return set_error(ctx, HAR_CUDA_ERR_UNSUPPORTED, "moe_ffn: HAR_CUDA_MOE_DECODE: hidden size too large");
   // down rows per CTA: DECODE_DOWN_ROWS, halved until the slots' rows fit
   int rpc_d = DECODE_DOWN_ROWS;
-  auto smem_d = [&](int r) { return 4 * (size_t)ns * p.I + (size_t)ns * r * p.rb_i; };
+  auto smem_d = [&](int r) {
+    return (((size_t)ns * decode_act_row_bytes(p.I) + 127) & ~(size_t)127) + (size_t)ns * r * p.rb_i;
+  };
   while (rpc_d > 1 && smem_d(rpc_d) > SMEM_MAX) rpc_d /= 2;
   if (smem_d(rpc_d) > SMEM_MAX)
     return set_error(ctx, HAR_CUDA_ERR_GEOMETRY, "moe_ffn: HAR_CUDA_MOE_DECODE: (k + 1) x I too large");

@@ -210,6 +210,153 @@ __device__ __forceinline__ void topk_token(const float *l, int E, int k, float *
   else topk_warp(l, E, k, p, lane, ids, weights);
 }
 
+// One token's selection by a whole CTA of TK_W warps, for the latency of a
+// single token: thread th owns indices th, th + 32*TK_W, ... (EPT of them,
+// E <= 32*TK_W*EPT), so the exps and divisions are spread 4x thinner than in
+// topk_warp_regs.  Each warp takes its own k best (its entries in the same
+// (p desc, index asc) order), and the k best of the union are found by rank:
+// an entry's rank is the number of candidates ahead of it in that order.  The
+// global k best are all among their warps' k best, so the result is the
+// reference's.  p: E floats of shared memory.
+constexpr int TK_W = 4, TK_T = 32 * TK_W;
+
+struct TopkCtaSmem {
+  float red[TK_W + 1];
+  uint32_t ckey[TK_W * 32];
+  int32_t cidx[TK_W * 32];
+  int32_t out_id[32];
+  float out_p[32];
+};
+
+template <int EPT>
+__device__ __forceinline__ void topk_cta(const float *l, int E, int k, float *p, TopkCtaSmem &sm,
+                                         int32_t *ids, float *weights) {
+  const int th = threadIdx.x, warp = th >> 5, lane = th & 31;
+  float v[EPT];
+#pragma unroll
+  for (int j = 0; j < EPT; ++j) {
+    const int i = th + TK_T * j;
+    v[j] = i < E ? __ldcg(l + i) : -INFINITY;
+  }
+  float mx = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < EPT; ++j) mx = fmaxf(mx, v[j]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if (lane == 0) sm.red[warp] = mx;
+  __syncthreads();
+#pragma unroll
+  for (int w = 0; w < TK_W; ++w) mx = fmaxf(mx, sm.red[w]);
+#pragma unroll
+  for (int j = 0; j < EPT; ++j) {
+    const int i = th + TK_T * j;
+    v[j] = expf_ref(__fsub_rn(v[j], mx));
+    if (i < E) p[i] = v[j];
+  }
+  __syncthreads();
+  if (th == 0) {  // exps.iter().sum(): one chain in index order
+    float den = 0.0f;
+    int i = 0;
+    if (E % 4 == 0) {
+      const float4 *p4 = reinterpret_cast<const float4 *>(p);
+#pragma unroll 8
+      for (; i < E; i += 4) {
+        const float4 q = p4[i >> 2];
+        den = __fadd_rn(den, q.x);
+        den = __fadd_rn(den, q.y);
+        den = __fadd_rn(den, q.z);
+        den = __fadd_rn(den, q.w);
+      }
+    }
+    for (; i < E; ++i) den = __fadd_rn(den, p[i]);
+    sm.red[TK_W] = fmaxf(den, ROUTER_EPS);
+  }
+  __syncthreads();
+  const float den = sm.red[TK_W];
+  uint32_t key[EPT];
+#pragma unroll
+  for (int j = 0; j < EPT; ++j)
+    key[j] = th + TK_T * j < E ? __float_as_uint(__fdiv_rn(v[j], den)) : 0xffffffffu;
+  // this warp's k best, in order, to the candidate list
+  for (int s = 0; s < k; ++s) {
+    uint32_t bk[EPT];
+    int bj[EPT];
+#pragma unroll
+    for (int j = 0; j < EPT; ++j) {
+      bk[j] = key[j];
+      bj[j] = j;
+    }
+    topk_tournament<EPT, 1>(bk, bj);
+    const bool avail = bk[0] < 0x80000000u;
+    const uint32_t bb = avail ? bk[0] : 0u;
+    const uint32_t bi = avail ? (uint32_t)(th + TK_T * bj[0]) : 0x7fffffffu;
+    const uint32_t mb = __reduce_max_sync(0xffffffffu, bb);
+    const uint32_t wi = __reduce_min_sync(0xffffffffu, bb == mb ? bi : 0x7fffffffu);
+    if (lane == 0) {
+      sm.ckey[warp * k + s] = mb;
+      sm.cidx[warp * k + s] = (int32_t)wi;  // 0x7fffffff: nothing left in this warp
+    }
+    const uint32_t hit = wi != 0x7fffffffu && (int)((wi % TK_T) >> 5) == warp && lane == (int)(wi & 31u)
+                             ? 0x80000000u : 0u;
+    const int jw = (int)(wi / TK_T);
+#pragma unroll
+    for (int j = 0; j < EPT; ++j) key[j] |= j == jw ? hit : 0u;
+  }
+  if (th < k) {  // slots past the available entries, as the round-by-round scan leaves them
+    sm.out_id[th] = 0x7fffffff;
+    sm.out_p[th] = 0.0f;
+  }
+  __syncthreads();
+  const int nc = TK_W * k;
+  if (th < nc && sm.cidx[th] != 0x7fffffff) {
+    const uint32_t mk = sm.ckey[th];
+    const int32_t mi = sm.cidx[th];
+    int rank = 0;
+#pragma unroll 8
+    for (int c = 0; c < nc; ++c) {
+      const int32_t ci = sm.cidx[c];
+      const uint32_t ck = sm.ckey[c];
+      rank += ci != 0x7fffffff && (ck > mk || (ck == mk && ci < mi));
+    }
+    if (rank < k) {
+      sm.out_id[rank] = mi;
+      sm.out_p[rank] = __uint_as_float(mk);
+    }
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const float sel_p = lane < k ? sm.out_p[lane] : 0.0f;
+    float tot = 0.0f;
+    for (int s = 0; s < k; ++s) tot = __fadd_rn(tot, __shfl_sync(0xffffffffu, sel_p, s));
+    tot = fmaxf(tot, ROUTER_EPS);
+    if (lane < k) {
+      ids[lane] = sm.out_id[lane];
+      weights[lane] = __fdiv_rn(sel_p, tot);
+    }
+  }
+}
+
+// The CTA-wide selection for E <= 1024; false when E is larger.
+__device__ __forceinline__ bool topk_cta_token(const float *l, int E, int k, float *p, TopkCtaSmem &sm,
+                                               int32_t *ids, float *weights) {
+  if (E <= TK_T) topk_cta<1>(l, E, k, p, sm, ids, weights);
+  else if (E <= 2 * TK_T) topk_cta<2>(l, E, k, p, sm, ids, weights);
+  else if (E <= 4 * TK_T) topk_cta<4>(l, E, k, p, sm, ids, weights);
+  else if (E <= 8 * TK_T) topk_cta<8>(l, E, k, p, sm, ids, weights);
+  else return false;
+  return true;
+}
+
+// One CTA per token (small T: the tokens' selections run side by side).
+__global__ void __launch_bounds__(TK_T) route_topk_cta_kernel(const float *__restrict__ logits, int E, int k,
+                                                              int32_t *__restrict__ ids,
+                                                              float *__restrict__ weights) {
+  extern __shared__ __align__(16) float tks[];
+  __shared__ TopkCtaSmem sm;
+  const int64_t t = blockIdx.x;
+  topk_cta_token(logits + t * E, E, k, tks, sm, ids + t * k, weights + t * k);
+}
+
 __global__ void __launch_bounds__(128, 1) route_topk_kernel(const float *__restrict__ logits,
                                                          int64_t T, int E, int k,
                                                          int32_t *__restrict__ ids,
@@ -221,8 +368,17 @@ __global__ void __launch_bounds__(128, 1) route_topk_kernel(const float *__restr
   topk_token(logits + t * E, E, k, rsm + (size_t)warp * E, lane, ids + t * k, weights + t * k);
 }
 
+// tokens per call up to which each token gets a CTA of its own
+constexpr int64_t TK_CTA_MAX_T = 64;
+
 int32_t launch_route_topk(har_cuda_ctx *ctx, const float *logits, int64_t T, int E, int k,
                           int32_t *ids, float *weights) {
+  if (T <= TK_CTA_MAX_T && E <= 8 * TK_T) {
+    prof_begin(ctx);
+    route_topk_cta_kernel<<<(unsigned)T, TK_T, sizeof(float) * (size_t)E, ctx->stream>>>(logits, E, k, ids,
+                                                                                          weights);
+    return check_launch(ctx, "route_topk_cta_kernel");
+  }
   const size_t smem = (size_t)4 * E * sizeof(float);
   if (smem > 48 * 1024)
     cudaFuncSetAttribute(route_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -612,9 +768,10 @@ __global__ void __launch_bounds__(RL_WARPS * 32) router_logits_pipe_kernel(
 // of 16 values with the next group's shared-memory loads issued before the
 // current group's adds (register double buffering), so no add waits on a load.
 //
-// routed_moe's selection is fused in: the CTA that finishes last (all logits
-// written and fenced) runs the top-k, one token per warp at a time, then
-// re-arms the counter.
+// For a single token routed_moe's selection is fused in: the CTA that
+// finishes last (all logits written and fenced) runs the CTA-wide top-k, then
+// re-arms the counter.  Larger decode batches select in route_topk_cta_kernel,
+// one CTA per token.
 constexpr int RS_E = 8, RS_TW = 4, RS_W = 4, RS_T = RS_TW * RS_W, RS_KC = 128, RS_LD = RS_KC + 4,
               RS_S = 6, RS_G = 16;
 
@@ -622,7 +779,7 @@ constexpr int RS_E = 8, RS_TW = 4, RS_W = 4, RS_T = RS_TW * RS_W, RS_KC = 128, R
 // whole dynamic shared memory (the ring, or E floats per warp for the top-k)
 __host__ __device__ inline int rs_stage_floats(int T) { return (RS_E + T) * RS_LD; }
 __host__ __device__ inline size_t rs_smem_bytes(int T, int E) {
-  const size_t ring = (size_t)RS_S * rs_stage_floats(T), topk = (size_t)RS_W * E;
+  const size_t ring = (size_t)RS_S * rs_stage_floats(T), topk = (size_t)E;
   return sizeof(float) * (ring > topk ? ring : topk);
 }
 
@@ -662,6 +819,7 @@ __global__ void __launch_bounds__(RS_W * 32, 1) router_logits_small_kernel(
     int *counter) {
   extern __shared__ __align__(16) float rss[];
   __shared__ int last_s;
+  __shared__ TopkCtaSmem tk_sm;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int el = lane >> 2, tok = RS_TW * warp + (lane & 3);
   const int e0 = blockIdx.x * RS_E;
@@ -717,9 +875,103 @@ __global__ void __launch_bounds__(RS_W * 32, 1) router_logits_small_kernel(
   __syncthreads();
   if (!last_s) return;
   __threadfence();
-  float *p = rss + (size_t)warp * E;  // the ring is idle: every copy landed and was read
-  for (int t = warp; t < nt; t += RS_W)
-    topk_token(logits + (int64_t)t * E, E, k, p, lane, ids + (int64_t)t * k, weights + (int64_t)t * k);
+  // the ring is idle (every copy landed and was read): it holds the exps
+  topk_cta_token(logits, E, k, rss, tk_sm, ids, weights);
+  __syncthreads();
+  if (threadIdx.x == 0) *counter = 0;
+}
+
+// router_logits_staged_kernel: the same chains for decode batches whose rows
+// fit in shared memory whole ((RS_E + T) rows of H floats).  One warp issues
+// every row as RG_CH bulk copies at launch, each H-chunk completing on its own
+// mbarrier, so the copies overlap and the computing warps never stop for a
+// ring slot or a CTA barrier: each chain waits only for the chunk it reaches.
+// Rows are padded by 4 floats so lanes of different rows hit different banks.
+// The multiply stays next to its add: on B200 that measured faster (5.7
+// cycles per add) than forming a group's products ahead of its adds (6.8);
+// the bare chain of adds is 4.4.
+constexpr int RG_CH = 8;
+constexpr uint32_t RG_WAIT_LIMIT = 1u << 20;
+
+__host__ __device__ inline int rg_chunk(int H) { return ((H + RG_CH - 1) / RG_CH + 3) & ~3; }
+__host__ __device__ inline size_t rg_smem_bytes(int T, int H, int E) {
+  const size_t rows = (size_t)(RS_E + T) * (H + 4) * sizeof(float), topk = sizeof(float) * (size_t)E;
+  return rows > topk ? rows : topk;
+}
+
+__global__ void __launch_bounds__(RS_W * 32, 1) router_logits_staged_kernel(
+    const float *__restrict__ W, const float *__restrict__ x, int64_t T, int E, int H,
+    float *__restrict__ logits, int k, int32_t *__restrict__ ids, float *__restrict__ weights,
+    int *counter, int *status) {
+  extern __shared__ __align__(16) float rgs[];
+  __shared__ uint64_t full[RG_CH];
+  __shared__ int last_s;
+  __shared__ TopkCtaSmem tk_sm;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int el = lane >> 2, tok = RS_TW * warp + (lane & 3);
+  const int e0 = blockIdx.x * RS_E;
+  const int nt = (int)T, LD = H + 4, CH = rg_chunk(H);
+  const int ne = min(RS_E, E - e0), nrows = RS_E + nt;
+  if (threadIdx.x == 0) {
+    for (int c = 0; c < RG_CH; ++c) tc::mbar_init(full + c, 1);
+    tc::fence_mbar_init();
+  }
+  __syncthreads();
+  if (warp == RS_W - 1) {
+    // chunk-major, so the first chunks of every row are in flight first
+    if (lane == 0)
+      for (int c = 0; c < RG_CH; ++c) {
+        const int h0 = c * CH, n = max(0, min(CH, H - h0));
+        tc::mbar_expect_tx(full + c, (uint32_t)(4 * n * (ne + nt)));
+      }
+    __syncwarp();
+    for (int q = lane; q < RG_CH * nrows; q += 32) {
+      const int c = q / nrows, r = q - c * nrows;
+      const int h0 = c * CH, n = max(0, min(CH, H - h0));
+      if (n == 0 || (r < RS_E && r >= ne)) continue;
+      const float *src = r < RS_E ? W + (int64_t)(e0 + r) * H + h0 : x + (int64_t)(r - RS_E) * H + h0;
+      tc::bulk_g2s(rgs + (size_t)r * LD + h0, src, (uint32_t)(4 * n), full + c);
+    }
+  }
+  const bool active = tok < nt;
+  float s = 0.0f;
+  bool ok = true;
+  if (active) {
+    const float *wr = rgs + (size_t)el * LD, *xr = rgs + (size_t)(RS_E + tok) * LD;
+    for (int c = 0; c < RG_CH && ok; ++c) {
+      const int h0 = c * CH, h1 = min(H, h0 + CH);
+      if (h0 >= h1) break;
+      if (!tc::mbar_wait(full + c, 0, RG_WAIT_LIMIT)) {
+        ok = false;
+        break;
+      }
+#pragma unroll 4
+      for (int h = h0; h < h1; h += 4) {
+        const float4 w = *reinterpret_cast<const float4 *>(wr + h);
+        const float4 v = *reinterpret_cast<const float4 *>(xr + h);
+        s = __fadd_rn(s, __fmul_rn(w.x, v.x));
+        s = __fadd_rn(s, __fmul_rn(w.y, v.y));
+        s = __fadd_rn(s, __fmul_rn(w.z, v.z));
+        s = __fadd_rn(s, __fmul_rn(w.w, v.w));
+      }
+    }
+  }
+  // no thread leaves while a copy into this CTA's shared memory may be in flight
+  for (int c = 0; c < RG_CH; ++c)
+    if (!tc::mbar_wait(full + c, 0, RG_WAIT_LIMIT)) ok = false;
+  if (__syncthreads_or(!ok)) {
+    if (threadIdx.x == 0) atomicOr(status, DEV_ERR_TIMEOUT);
+    return;
+  }
+  if (active && el < ne) logits[(int64_t)tok * E + e0 + el] = s;
+  if (!counter) return;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) last_s = atomicAdd(counter, 1) == (int)gridDim.x - 1;
+  __syncthreads();
+  if (!last_s) return;
+  __threadfence();
+  topk_cta_token(logits, E, k, rgs, tk_sm, ids, weights);
   __syncthreads();
   if (threadIdx.x == 0) *counter = 0;
 }
@@ -731,7 +983,16 @@ int32_t launch_route_fused(har_cuda_ctx *ctx, const float *W, int E, int H, cons
                            bool *done) {
   *done = false;
   const bool vec = H % 4 == 0 && ((uintptr_t)W & 15u) == 0 && ((uintptr_t)x & 15u) == 0;
-  if (!vec || T > RS_T || T < 1) return HAR_CUDA_OK;
+  if (!vec || T != 1 || E > 8 * TK_T) return HAR_CUDA_OK;
+  const size_t gsm = rg_smem_bytes((int)T, H, E);
+  if (gsm <= 220 * 1024) {
+    cudaFuncSetAttribute(router_logits_staged_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gsm);
+    prof_begin(ctx);
+    router_logits_staged_kernel<<<(unsigned)((E + RS_E - 1) / RS_E), RS_W * 32, gsm, ctx->stream>>>(
+        W, x, T, E, H, logits, k, ids, weights, ctx->d_status + 1, ctx->d_status);
+    *done = true;
+    return check_launch(ctx, "router_logits_staged_kernel");
+  }
   const size_t smem = rs_smem_bytes((int)T, E);
   if (smem > 227 * 1024) return HAR_CUDA_OK;
   if (smem > 48 * 1024)
@@ -747,6 +1008,14 @@ int32_t launch_router_logits(har_cuda_ctx *ctx, const float *W, int E, int H, co
                              int64_t T, float *logits) {
   const dim3 grid((unsigned)((E + RL_E - 1) / RL_E), (unsigned)((T + RL_TT - 1) / RL_TT));
   const bool vec = H % 4 == 0 && ((uintptr_t)W & 15u) == 0 && ((uintptr_t)x & 15u) == 0;
+  if (vec && T <= RS_T && rg_smem_bytes((int)T, H, E) <= 220 * 1024) {
+    const size_t gsm = rg_smem_bytes((int)T, H, E);
+    cudaFuncSetAttribute(router_logits_staged_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gsm);
+    prof_begin(ctx);
+    router_logits_staged_kernel<<<(unsigned)((E + RS_E - 1) / RS_E), RS_W * 32, gsm, ctx->stream>>>(
+        W, x, T, E, H, logits, 0, nullptr, nullptr, nullptr, ctx->d_status);
+    return check_launch(ctx, "router_logits_staged_kernel");
+  }
   if (vec && T <= RS_T) {
     const size_t smem = (size_t)RS_S * rs_stage_floats((int)T) * sizeof(float);
     if (smem > 48 * 1024)
