@@ -141,6 +141,19 @@ __device__ __forceinline__ float expf_ref(float x) {
          : x > 0x1.62e42ep6f ? __int_as_float(0x7f800000) : res;  // above log(2^128): overflow
 }
 
+// Programmatic dependent launch.  A kernel launched with launch_pdl may start
+// while its predecessor in the stream is still running; pdl_wait blocks until
+// that predecessor has completed and its writes are visible.  The kernels that
+// use it read only constant data (weights) or data produced two or more
+// launches back before pdl_wait, write nothing before it, and call
+// pdl_launch_dependents only after it, so "two launches back" is always
+// complete by the time a dependent starts.  Both are no-ops in a kernel
+// launched normally.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // sigmoid of har-native-qwen35moe.rs:207-214, with the reference's exp
 __device__ __forceinline__ float sigmoid_f(float v) {
   if (v >= 0.0f) return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf_ref(-v)));
@@ -280,6 +293,23 @@ int32_t set_error(har_cuda_ctx *ctx, int32_t code, const std::string &msg);
 int32_t check_launch(har_cuda_ctx *ctx, const char *what);
 // Call immediately before a kernel launch; check_launch closes the record.
 void prof_begin(har_cuda_ctx *ctx);
+
+// Launch with programmatic stream serialization (see pdl_wait).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
 int32_t ensure_scratch(har_cuda_ctx *ctx, size_t bytes);
 
 // Kernel launchers (host functions defined in the kernel .cu files).

@@ -83,26 +83,32 @@ __global__ void __launch_bounds__(DECODE_THREADS, CPL == 1 ? 5 : 2) decode_gate_
   float *xs = xraw + p.H;
   uint8_t *wg_s = smem + ((4 * (size_t)p.H + decode_act_row_bytes(p.H) + 127) & ~(size_t)127);
   uint8_t *wu_s = wg_s + (size_t)R * p.rb_h;
+  const uint32_t wb = (uint32_t)(nr * p.rb_h), xb = (uint32_t)(4 * p.H);
   if (threadIdx.x == 0) {
-    const uint8_t *wg = p.sh_gate, *wu = p.sh_up;
+    tc::mbar_init(&bar, 1);
+    tc::fence_mbar_init();
+    if (slot >= n) {  // the shared expert's rows: constant, wanted before the predecessor ends
+      tc::mbar_expect_tx(&bar, xb + 2 * wb);
+      tc::bulk_g2s(wg_s, p.sh_gate + (int64_t)r0 * p.rb_h, wb, &bar);
+      tc::bulk_g2s(wu_s, p.sh_up + (int64_t)r0 * p.rb_h, wb, &bar);
+    }
+  }
+  pdl_wait();  // ids and x come from earlier launches
+  pdl_launch_dependents();
+  if (threadIdx.x == 0) {
     int bad = 0;
     if (slot < n) {
       const int e = p.ids[slot];
       bad = e < 0 || e >= p.E;
       if (bad && blk == 0) atomicOr(p.status, DEV_ERR_BOUNDS);
-      wg = p.gate + (int64_t)(bad ? 0 : e) * p.ebytes_gu;
-      wu = p.up + (int64_t)(bad ? 0 : e) * p.ebytes_gu;
+      if (!bad) {
+        tc::mbar_expect_tx(&bar, xb + 2 * wb);
+        tc::bulk_g2s(wg_s, p.gate + (int64_t)e * p.ebytes_gu + (int64_t)r0 * p.rb_h, wb, &bar);
+        tc::bulk_g2s(wu_s, p.up + (int64_t)e * p.ebytes_gu + (int64_t)r0 * p.rb_h, wb, &bar);
+      }
     }
     skip = bad;
-    if (!bad) {
-      const uint32_t wb = (uint32_t)(nr * p.rb_h), xb = (uint32_t)(4 * p.H);
-      tc::mbar_init(&bar, 1);
-      tc::fence_mbar_init();
-      tc::mbar_expect_tx(&bar, xb + 2 * wb);
-      tc::bulk_g2s(xraw, xt, xb, &bar);
-      tc::bulk_g2s(wg_s, wg + (int64_t)r0 * p.rb_h, wb, &bar);
-      tc::bulk_g2s(wu_s, wu + (int64_t)r0 * p.rb_h, wb, &bar);
-    }
+    if (!bad) tc::bulk_g2s(xraw, xt, xb, &bar);
   }
   __syncthreads();
   if (skip) return;  // an out-of-range expert id: the slot contributes nothing
@@ -176,27 +182,33 @@ __global__ void __launch_bounds__(decode_down_warps(CPL) * 32, CPL == 1 ? 2 : 1)
     tc::fence_mbar_init();
   }
   __syncthreads();
+  const uint32_t rb = (uint32_t)(4 * SLD);
   if (threadIdx.x < ns) {
-    // slot j's expert: its down rows r0 .. r0 + nr - 1; thread 0 also copies
-    // the token's activation rows (its k routed slots are contiguous)
+    // slot j's expert: its down rows r0 .. r0 + nr - 1.  The ids and weights
+    // come from two or more launches back, so these copies start before the
+    // gate/up launch has finished.
     const int j = threadIdx.x;
     const uint8_t *wd = p.sh_down;
-    float wt = p.gi ? p.gsh[t] : 1.0f;
     bool ok = true;
     if (j < p.k) {
       const int s = t * p.k + j, e = p.ids[s];
       ok = e >= 0 && e < p.E;  // a bad id contributes nothing (gate/up reported it)
       wd = p.down + (int64_t)(ok ? e : 0) * p.ebytes_d;
-      wt = p.weights[s];
+      swt[j] = p.weights[s];
     }
     ok_s[j] = ok;
-    swt[j] = wt;
-    const uint32_t rb = (uint32_t)(4 * SLD), wb = ok ? (uint32_t)(nr * p.rb_i) : 0u;
+    const uint32_t wb = ok ? (uint32_t)(nr * p.rb_i) : 0u;
     tc::mbar_expect_tx(&bar, wb + (j == 0 ? (uint32_t)ns * rb : 0u));
     if (ok) tc::bulk_g2s(w_s + (size_t)j * R * p.rb_i, wd + (int64_t)r0 * p.rb_i, wb, &bar);
-    if (j == 0) {
-      tc::bulk_g2s(as, p.a + (int64_t)t * p.k * SLD, (uint32_t)p.k * rb, &bar);
-      if (p.has_shared) tc::bulk_g2s(as + (size_t)p.k * SLD, p.a + (int64_t)(n + t) * SLD, rb, &bar);
+  }
+  pdl_wait();  // the activations and the shared gate are the gate/up launch's
+  pdl_launch_dependents();
+  if (threadIdx.x == 0) {
+    // the token's activation rows (its k routed slots are contiguous)
+    tc::bulk_g2s(as, p.a + (int64_t)t * p.k * SLD, (uint32_t)p.k * rb, &bar);
+    if (p.has_shared) {
+      tc::bulk_g2s(as + (size_t)p.k * SLD, p.a + (int64_t)(n + t) * SLD, rb, &bar);
+      swt[p.k] = p.gi ? p.gsh[t] : 1.0f;
     }
   }
   const bool landed = tc::mbar_wait(&bar, 0, DECODE_WAIT_LIMIT);
@@ -324,8 +336,8 @@ int32_t run_moe_decode(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const
   int32_t st = dispatch_shape<GateUpK>(ctx, p.H, [&](auto kern) -> int32_t {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_gu);
     prof_begin(ctx);
-    kern<<<(unsigned)(slots * ((p.I + DECODE_GU_ROWS - 1) / DECODE_GU_ROWS)), DECODE_THREADS, smem_gu,
-           ctx->stream>>>(p);
+    launch_pdl(kern, dim3((unsigned)(slots * ((p.I + DECODE_GU_ROWS - 1) / DECODE_GU_ROWS))),
+               dim3(DECODE_THREADS), smem_gu, ctx->stream, p);
     return check_launch(ctx, "decode_gate_up_kernel");
   });
   if (st) return st;
@@ -334,7 +346,8 @@ int32_t run_moe_decode(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     prof_begin(ctx);
     const int wmax = decode_down_warps(gemv_shape(p.I).CPL), warps = ns < wmax ? ns : wmax;
-    kern<<<(unsigned)(T * ((p.H + rpc_d - 1) / rpc_d)), 32 * warps, smem, ctx->stream>>>(p, rpc_d);
+    launch_pdl(kern, dim3((unsigned)(T * ((p.H + rpc_d - 1) / rpc_d))), dim3(32 * warps), smem, ctx->stream, p,
+               rpc_d);
     return check_launch(ctx, "decode_down_combine_kernel");
   });
 }

@@ -354,6 +354,8 @@ __global__ void __launch_bounds__(TK_T) route_topk_cta_kernel(const float *__res
   extern __shared__ __align__(16) float tks[];
   __shared__ TopkCtaSmem sm;
   const int64_t t = blockIdx.x;
+  pdl_wait();
+  pdl_launch_dependents();
   topk_cta_token(logits + t * E, E, k, tks, sm, ids + t * k, weights + t * k);
 }
 
@@ -375,8 +377,8 @@ int32_t launch_route_topk(har_cuda_ctx *ctx, const float *logits, int64_t T, int
                           int32_t *ids, float *weights) {
   if (T <= TK_CTA_MAX_T && E <= 8 * TK_T) {
     prof_begin(ctx);
-    route_topk_cta_kernel<<<(unsigned)T, TK_T, sizeof(float) * (size_t)E, ctx->stream>>>(logits, E, k, ids,
-                                                                                          weights);
+    launch_pdl(route_topk_cta_kernel, dim3((unsigned)T), dim3(TK_T), sizeof(float) * (size_t)E, ctx->stream,
+               logits, E, k, ids, weights);
     return check_launch(ctx, "route_topk_cta_kernel");
   }
   const size_t smem = (size_t)4 * E * sizeof(float);
@@ -917,22 +919,30 @@ __global__ void __launch_bounds__(RS_W * 32, 1) router_logits_staged_kernel(
     tc::fence_mbar_init();
   }
   __syncthreads();
+  // chunk-major, so the first chunks of every row are in flight first; the
+  // router rows (constant) go out before the predecessor has finished, the
+  // token rows after it
+  auto issue = [&](bool tokens) {
+    for (int q = lane; q < RG_CH * nrows; q += 32) {
+      const int c = q / nrows, r = q - c * nrows;
+      const int h0 = c * CH, n = max(0, min(CH, H - h0));
+      if (n == 0 || (r < RS_E && r >= ne) || (r >= RS_E) != tokens) continue;
+      const float *src = r < RS_E ? W + (int64_t)(e0 + r) * H + h0 : x + (int64_t)(r - RS_E) * H + h0;
+      tc::bulk_g2s(rgs + (size_t)r * LD + h0, src, (uint32_t)(4 * n), full + c);
+    }
+  };
   if (warp == RS_W - 1) {
-    // chunk-major, so the first chunks of every row are in flight first
     if (lane == 0)
       for (int c = 0; c < RG_CH; ++c) {
         const int h0 = c * CH, n = max(0, min(CH, H - h0));
         tc::mbar_expect_tx(full + c, (uint32_t)(4 * n * (ne + nt)));
       }
     __syncwarp();
-    for (int q = lane; q < RG_CH * nrows; q += 32) {
-      const int c = q / nrows, r = q - c * nrows;
-      const int h0 = c * CH, n = max(0, min(CH, H - h0));
-      if (n == 0 || (r < RS_E && r >= ne)) continue;
-      const float *src = r < RS_E ? W + (int64_t)(e0 + r) * H + h0 : x + (int64_t)(r - RS_E) * H + h0;
-      tc::bulk_g2s(rgs + (size_t)r * LD + h0, src, (uint32_t)(4 * n), full + c);
-    }
+    issue(false);
   }
+  pdl_wait();
+  pdl_launch_dependents();
+  if (warp == RS_W - 1) issue(true);
   const bool active = tok < nt;
   float s = 0.0f;
   bool ok = true;
@@ -988,8 +998,8 @@ int32_t launch_route_fused(har_cuda_ctx *ctx, const float *W, int E, int H, cons
   if (gsm <= 220 * 1024) {
     cudaFuncSetAttribute(router_logits_staged_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gsm);
     prof_begin(ctx);
-    router_logits_staged_kernel<<<(unsigned)((E + RS_E - 1) / RS_E), RS_W * 32, gsm, ctx->stream>>>(
-        W, x, T, E, H, logits, k, ids, weights, ctx->d_status + 1, ctx->d_status);
+    launch_pdl(router_logits_staged_kernel, dim3((unsigned)((E + RS_E - 1) / RS_E)), dim3(RS_W * 32), gsm,
+               ctx->stream, W, x, T, E, H, logits, k, ids, weights, ctx->d_status + 1, ctx->d_status);
     *done = true;
     return check_launch(ctx, "router_logits_staged_kernel");
   }
@@ -1012,8 +1022,9 @@ int32_t launch_router_logits(har_cuda_ctx *ctx, const float *W, int E, int H, co
     const size_t gsm = rg_smem_bytes((int)T, H, E);
     cudaFuncSetAttribute(router_logits_staged_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gsm);
     prof_begin(ctx);
-    router_logits_staged_kernel<<<(unsigned)((E + RS_E - 1) / RS_E), RS_W * 32, gsm, ctx->stream>>>(
-        W, x, T, E, H, logits, 0, nullptr, nullptr, nullptr, ctx->d_status);
+    launch_pdl(router_logits_staged_kernel, dim3((unsigned)((E + RS_E - 1) / RS_E)), dim3(RS_W * 32), gsm,
+               ctx->stream, W, x, T, E, H, logits, 0, (int32_t *)nullptr, (float *)nullptr, (int *)nullptr,
+               ctx->d_status);
     return check_launch(ctx, "router_logits_staged_kernel");
   }
   if (vec && T <= RS_T) {
