@@ -382,6 +382,73 @@ int32_t har_cuda_ep_moe_stack(har_cuda_ctx *ctx, har_cuda_ep *ep,
                               int64_t T, int32_t k, const int32_t *ids_dev,
                               const float *weights_dev, float *y_dev, uint32_t flags);
 
+/* ---- expert-slot residency (ExpertSlotTable, har/crates/har-vulkan/src/lib.rs:1233-1460) ---
+ * A bounded table of device slots, each holding one projection of one expert,
+ * for deployments whose experts do not all stay resident.  The rules are the
+ * reference's: a slot is Free, Uploading (reserve), Ready (mark_ready once the
+ * upload's event completed), InFlight (acquire_for_dispatch) and Ready again
+ * (release once the dispatch's event completed), or Free (evict, never while in
+ * flight); every transition takes the next value of a monotone epoch (the
+ * caller's LRU order, read back with snapshot).  Events are cudaEvent_t handles
+ * passed as void*, complete when cudaEventQuery reports so; an incomplete
+ * event is HAR_CUDA_ERR_ARG with the reference's message.  A table created
+ * with ctx == NULL has no storage (the state machine alone) and takes only
+ * NULL events, meaning "already complete".  To serve a MoE layer from slots,
+ * create one table per projection, keep an expert's three projections at the
+ * same slot index (identical operation sequences give identical indices), wrap
+ * each table's storage with har_cuda_weights_wrap_q4k(ctx, storage, count, N, K)
+ * and pass slot ids as the expert ids. */
+typedef struct har_cuda_slot_table har_cuda_slot_table;
+#define HAR_CUDA_PROJ_GATE 0u
+#define HAR_CUDA_PROJ_UP 1u
+#define HAR_CUDA_PROJ_DOWN 2u
+#define HAR_CUDA_SLOT_FREE 0
+#define HAR_CUDA_SLOT_UPLOADING 1
+#define HAR_CUDA_SLOT_READY 2
+#define HAR_CUDA_SLOT_IN_FLIGHT 3
+typedef struct {          /* ExpertSlotKey (lib.rs:1239-1244) */
+  uint32_t layer, expert_id, projection;  /* projection: HAR_CUDA_PROJ_* */
+  uint64_t generation;    /* 0 is reserved */
+} har_cuda_slot_key;
+typedef struct {          /* ExpertSlotSnapshot (lib.rs:1253-1260) */
+  uint32_t slot_id;
+  har_cuda_slot_key key;
+  int32_t state;          /* HAR_CUDA_SLOT_* */
+  uint64_t upload_epoch, last_use_epoch;
+  int32_t ready;
+} har_cuda_slot_snapshot;
+/* create_expert_slot_table (lib.rs:925-970): count x slot_bytes of device
+ * storage (none when ctx is NULL), every slot Free, epochs from 1. */
+int32_t har_cuda_slot_table_create(har_cuda_ctx *ctx, uint32_t slot_count, uint64_t slot_bytes,
+                                   har_cuda_slot_table **out);
+/* Waits for the context's stream, then frees the storage. */
+int32_t har_cuda_slot_table_free(har_cuda_slot_table *table);
+int32_t har_cuda_slot_table_storage(har_cuda_slot_table *table, void **dev, uint64_t *bytes);
+int32_t har_cuda_slot_table_last_error(const har_cuda_slot_table *table, char *buf, size_t len);
+/* reserve (lib.rs:1282-1314): the first Free slot takes the key. */
+int32_t har_cuda_slot_reserve(har_cuda_slot_table *table, const har_cuda_slot_key *key,
+                              uint32_t *slot_id);
+/* mark_upload_submitted (lib.rs:1315-1333), for a caller that moved the bytes. */
+int32_t har_cuda_slot_mark_upload_submitted(har_cuda_slot_table *table, uint32_t slot_id,
+                                            void *cuda_event);
+/* Copies bytes (<= slot_bytes) from host memory into the slot on the context's
+ * stream and records the table's event for it: mark_upload_submitted for the
+ * library's own upload. */
+int32_t har_cuda_slot_upload(har_cuda_slot_table *table, uint32_t slot_id, const void *host_src,
+                             uint64_t bytes);
+/* mark_ready (lib.rs:1334-1368); cuda_event NULL = the submitted upload's. */
+int32_t har_cuda_slot_mark_ready(har_cuda_slot_table *table, uint32_t slot_id, void *cuda_event);
+/* acquire_for_dispatch (lib.rs:1369-1394): Ready -> InFlight, the slot's record. */
+int32_t har_cuda_slot_acquire(har_cuda_slot_table *table, const har_cuda_slot_key *key,
+                              har_cuda_slot_snapshot *out);
+/* release_from_dispatch (lib.rs:1395-1419) */
+int32_t har_cuda_slot_release(har_cuda_slot_table *table, uint32_t slot_id, void *cuda_event);
+/* evict (lib.rs:1420-1450) */
+int32_t har_cuda_slot_evict(har_cuda_slot_table *table, uint32_t slot_id, void *cuda_event);
+/* snapshot (lib.rs:1451-1456): writes min(cap, count) records, *n = count. */
+int32_t har_cuda_slot_table_snapshot(har_cuda_slot_table *table, har_cuda_slot_snapshot *out,
+                                     uint32_t cap, uint32_t *n);
+
 /* ---- profiling (the role of TimestampQuery, har/crates/har-vulkan/src/lib.rs:2221-2257) ---
  * Between begin and end every kernel the context launches is bracketed by
  * CUDA events on its stream; end waits for the stream and returns up to cap

@@ -70,6 +70,10 @@ EXPORTS = [
     "har_cuda_ep_unique_id", "har_cuda_ep_create", "har_cuda_ep_free", "har_cuda_ep_moe_ffn",
     "har_cuda_ep_moe_stack", "har_cuda_ep_plan", "har_cuda_ep_combine",
     "har_cuda_ep_create_timeout", "har_cuda_ep_abort",
+    "har_cuda_slot_table_create", "har_cuda_slot_table_free", "har_cuda_slot_table_storage",
+    "har_cuda_slot_table_last_error", "har_cuda_slot_reserve", "har_cuda_slot_mark_upload_submitted",
+    "har_cuda_slot_upload", "har_cuda_slot_mark_ready", "har_cuda_slot_acquire",
+    "har_cuda_slot_release", "har_cuda_slot_evict", "har_cuda_slot_table_snapshot",
 ]
 
 
@@ -80,6 +84,29 @@ class HarCudaError(RuntimeError):
 
 
 _lib = None
+
+
+# expert-slot residency (har_cuda.h: HAR_CUDA_PROJ_*, HAR_CUDA_SLOT_*)
+PROJ_GATE, PROJ_UP, PROJ_DOWN = 0, 1, 2
+SLOT_FREE, SLOT_UPLOADING, SLOT_READY, SLOT_IN_FLIGHT = 0, 1, 2, 3
+
+
+class SlotKey(C.Structure):
+    """ExpertSlotKey (har/crates/har-vulkan/src/lib.rs:1239-1244)."""
+    _fields_ = [("layer", C.c_uint32), ("expert_id", C.c_uint32), ("projection", C.c_uint32),
+                ("generation", C.c_uint64)]
+
+
+class SlotSnapshot(C.Structure):
+    """ExpertSlotSnapshot (lib.rs:1253-1260)."""
+    _fields_ = [("slot_id", C.c_uint32), ("key", SlotKey), ("state", C.c_int32),
+                ("upload_epoch", C.c_uint64), ("last_use_epoch", C.c_uint64), ("ready", C.c_int32)]
+
+    def as_dict(self):
+        k = self.key
+        return {"slot_id": self.slot_id, "key": (k.layer, k.expert_id, k.projection, k.generation),
+                "state": self.state, "upload_epoch": self.upload_epoch,
+                "last_use_epoch": self.last_use_epoch, "ready": bool(self.ready)}
 
 
 def load_library() -> C.CDLL:
@@ -157,6 +184,18 @@ def load_library() -> C.CDLL:
         "har_cuda_profile_begin": (i32, [vp]),
         "har_cuda_moe_ffn_noalloc": (i32, [vp, vp, vp, i64, i32, vp, vp, vp, u32]),
         "har_cuda_profile_end": (i32, [vp, C.c_char_p, C.c_size_t, vp, i64, C.POINTER(C.c_int64)]),
+        "har_cuda_slot_table_create": (i32, [vp, u32, u64, pp]),
+        "har_cuda_slot_table_free": (i32, [vp]),
+        "har_cuda_slot_table_storage": (i32, [vp, pp, C.POINTER(u64)]),
+        "har_cuda_slot_table_last_error": (i32, [vp, C.c_char_p, C.c_size_t]),
+        "har_cuda_slot_reserve": (i32, [vp, C.POINTER(SlotKey), C.POINTER(u32)]),
+        "har_cuda_slot_mark_upload_submitted": (i32, [vp, u32, vp]),
+        "har_cuda_slot_upload": (i32, [vp, u32, vp, u64]),
+        "har_cuda_slot_mark_ready": (i32, [vp, u32, vp]),
+        "har_cuda_slot_acquire": (i32, [vp, C.POINTER(SlotKey), C.POINTER(SlotSnapshot)]),
+        "har_cuda_slot_release": (i32, [vp, u32, vp]),
+        "har_cuda_slot_evict": (i32, [vp, u32, vp]),
+        "har_cuda_slot_table_snapshot": (i32, [vp, C.POINTER(SlotSnapshot), u32, C.POINTER(u32)]),
     }
     for name, (res, args) in sigs.items():
         fn = getattr(L, name)
@@ -657,6 +696,177 @@ class MoeLayer:
             self.free()
         except Exception:
             pass
+
+
+def _event_ptr(event):
+    """A torch.cuda.Event (or a raw cudaEvent_t as int) as void*, None -> NULL."""
+    if event is None:
+        return None
+    return C.c_void_p(event.cuda_event if hasattr(event, "cuda_event") else int(event))
+
+
+class SlotTable:
+    """ExpertSlotTable (har/crates/har-vulkan/src/lib.rs:1233-1460) through the
+    C ABI: `slot_count` device slots of `slot_bytes` each (ctx None: the state
+    machine alone, no storage, events None).  Errors raise HarCudaError with the
+    reference's message."""
+
+    def __init__(self, ctx: "Context", slot_count: int, slot_bytes: int):
+        self.ctx = ctx
+        self.lib = ctx.lib if ctx is not None else load_library()
+        h = C.c_void_p()
+        st = self.lib.har_cuda_slot_table_create(ctx.handle if ctx is not None else None, slot_count,
+                                                 slot_bytes, C.byref(h))
+        if st:
+            raise HarCudaError(st, "slot table: create failed")
+        self.handle, self.slot_count, self.slot_bytes = h, slot_count, slot_bytes
+
+    def _check(self, st: int):
+        if st:
+            buf = C.create_string_buffer(512)
+            self.lib.har_cuda_slot_table_last_error(self.handle, buf, len(buf))
+            raise HarCudaError(st, buf.value.decode())
+
+    @staticmethod
+    def key(layer: int, expert: int, projection: int, generation: int = 1) -> SlotKey:
+        return SlotKey(layer, expert, projection, generation)
+
+    def storage(self):
+        """(device address, bytes) of the slots' storage (0 without a context)."""
+        p, n = C.c_void_p(), C.c_uint64()
+        self._check(self.lib.har_cuda_slot_table_storage(self.handle, C.byref(p), C.byref(n)))
+        return p.value or 0, n.value
+
+    def reserve(self, key: SlotKey) -> int:
+        sid = C.c_uint32()
+        self._check(self.lib.har_cuda_slot_reserve(self.handle, C.byref(key), C.byref(sid)))
+        return sid.value
+
+    def mark_upload_submitted(self, slot_id: int, event=None):
+        self._check(self.lib.har_cuda_slot_mark_upload_submitted(self.handle, slot_id, _event_ptr(event)))
+
+    def upload(self, slot_id: int, data: np.ndarray):
+        data = np.ascontiguousarray(data)
+        self._check(self.lib.har_cuda_slot_upload(self.handle, slot_id, _hptr(data), data.nbytes))
+        self._keep = data  # the copy is asynchronous: keep the source until the next upload
+
+    def mark_ready(self, slot_id: int, event=None):
+        self._check(self.lib.har_cuda_slot_mark_ready(self.handle, slot_id, _event_ptr(event)))
+
+    def acquire(self, key: SlotKey) -> dict:
+        out = SlotSnapshot()
+        self._check(self.lib.har_cuda_slot_acquire(self.handle, C.byref(key), C.byref(out)))
+        return out.as_dict()
+
+    def release(self, slot_id: int, event=None):
+        self._check(self.lib.har_cuda_slot_release(self.handle, slot_id, _event_ptr(event)))
+
+    def evict(self, slot_id: int, event=None):
+        self._check(self.lib.har_cuda_slot_evict(self.handle, slot_id, _event_ptr(event)))
+
+    def snapshot(self) -> list:
+        arr = (SlotSnapshot * self.slot_count)()
+        n = C.c_uint32()
+        self._check(self.lib.har_cuda_slot_table_snapshot(self.handle, arr, self.slot_count, C.byref(n)))
+        return [arr[i].as_dict() for i in range(n.value)]
+
+    def free(self):
+        if self.handle:
+            self.lib.har_cuda_slot_table_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+class SlottedMoeLayer:
+    """A MoE layer whose E experts live in host memory with at most n_slots of
+    them on the device: the host side of expert-slot residency (the role of
+    ExpertSlotTable in HAR's serving path).  One SlotTable per projection keeps
+    an expert's gate, up and down at the same slot index; the tables' storage
+    is wrapped as an n_slots-expert Q4_K layer, and a call maps its expert ids
+    to slot ids, so the kernels are the ordinary ones.  Missing experts evict
+    the least recently used slots the call does not need (epochs from the
+    tables' snapshots); slots are acquired for the dispatch and released once
+    its event has completed (at the next call)."""
+
+    def __init__(self, ctx: "Context", host_gate, host_up, host_down, E: int, H: int, I: int,
+                 n_slots: int, layer_id: int = 0, shared=None, sh_gate_inp=None):
+        self.ctx, self.E, self.H, self.I, self.n_slots, self.layer_id = ctx, E, H, I, n_slots, layer_id
+        pb = I * (H // QK_K) * Q4K_BLOCK_BYTES
+        assert H * (I // QK_K) * Q4K_BLOCK_BYTES == pb
+        self.host = [np.ascontiguousarray(h).reshape(E, pb) for h in (host_gate, host_up, host_down)]
+        self.tables = [SlotTable(ctx, n_slots, pb) for _ in range(3)]
+        views = []
+        for p, (N, K) in enumerate(((I, H), (I, H), (H, I))):
+            ptr, _ = self.tables[p].storage()
+            h = C.c_void_p()
+            ctx.check(ctx.lib.har_cuda_weights_wrap_q4k(ctx.handle, C.c_void_p(ptr), n_slots, N, K,
+                                                        C.byref(h)))
+            w = Q4KWeights(ctx, h, n_slots, N, K)
+            w.keepalive = self.tables[p]
+            views.append(w)
+        self.layer = ctx.moe_layer(views[0], views[1], views[2], shared, sh_gate_inp)
+        self.slot_of = {}       # expert -> slot
+        self.in_flight = []     # slots acquired for the last dispatch
+        self.event = None       # that dispatch's completion event
+        self.uploads = 0
+
+    def _settle(self):
+        """Release the previous dispatch's slots once its event has completed."""
+        if self.event is not None:
+            self.event.synchronize()
+            for sid in self.in_flight:
+                for t in self.tables:
+                    t.release(sid, self.event)
+            self.in_flight = []
+
+    def ffn(self, x, ids: np.ndarray, weights, y, flags: int = 0):
+        """moe_ffn for device x / weights / y and host expert ids [T][k]."""
+        import torch
+        ids = np.asarray(ids, np.int32)
+        need = list(dict.fromkeys(int(e) for e in ids.ravel()))
+        if len(need) > self.n_slots:
+            raise HarCudaError(ERR_GEOMETRY, "slotted layer: more distinct experts than slots")
+        self._settle()
+        fresh = []
+        for e in need:
+            if e in self.slot_of:
+                continue
+            snaps = self.tables[0].snapshot()
+            free = [s for s in snaps if s["state"] == SLOT_FREE]
+            if not free:
+                keep = {self.slot_of[n] for n in need if n in self.slot_of}
+                victims = [s for s in snaps if s["state"] == SLOT_READY and s["slot_id"] not in keep]
+                v = min(victims, key=lambda s: s["last_use_epoch"])
+                for t in self.tables:
+                    t.evict(v["slot_id"], self.event)
+                del self.slot_of[v["key"][1]]
+            sids = [t.reserve(SlotTable.key(self.layer_id, e, p)) for p, t in enumerate(self.tables)]
+            assert len(set(sids)) == 1, sids
+            for p, t in enumerate(self.tables):
+                t.upload(sids[0], self.host[p][e])
+            self.slot_of[e] = sids[0]
+            fresh.append(sids[0])
+            self.uploads += 1
+        if fresh:
+            self.ctx.synchronize()  # the uploads' events complete
+            for sid in fresh:
+                for t in self.tables:
+                    t.mark_ready(sid)
+        for e in need:
+            for p, t in enumerate(self.tables):
+                t.acquire(SlotTable.key(self.layer_id, e, p))
+        self.in_flight = [self.slot_of[e] for e in need]
+        remap = np.vectorize(self.slot_of.__getitem__, otypes=[np.int32])(ids) if ids.size else ids
+        sid_dev = torch.from_numpy(np.ascontiguousarray(remap, np.int32)).to(x.device)
+        self.ctx.moe_ffn(self.layer, x, sid_dev, weights, y, flags)
+        self.event = torch.cuda.Event()
+        self.event.record()
+        self._ids_keep = sid_dev
 
 
 # ---------------------------------------------------------------------------
