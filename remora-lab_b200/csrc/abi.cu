@@ -488,9 +488,13 @@ int32_t har_cuda_group_by_expert(har_cuda_ctx *ctx, const int32_t *ids_dev, int6
   if (T < 0 || k <= 0 || E <= 0 || E > 2048 || T * k > (int64_t)1 << 24)
     return set_error(ctx, HAR_CUDA_ERR_GEOMETRY, "group_by_expert: E <= 2048, T*k <= 2^24");
   HAR_TRY(use_device(ctx));
-  HAR_TRY(ensure_scratch(ctx, sizeof(int32_t) * (size_t)(T * k + 1)));
-  return launch_group(ctx, ids_dev, T, k, E, counts_dev, offsets_dev, order_dev,
-                      (int32_t *)ctx->scratch);
+  // scratch: inv[T*k], then the multi-CTA sort's segment counts (if any)
+  const size_t inv_words = ((size_t)(T * k) + 63) & ~(size_t)63;
+  const size_t gw = group_scratch_words(T * k, E);
+  HAR_TRY(ensure_scratch(ctx, sizeof(int32_t) * (inv_words + gw + 1)));
+  int32_t *inv = (int32_t *)ctx->scratch;
+  return launch_group(ctx, ids_dev, T, k, E, counts_dev, offsets_dev, order_dev, inv,
+                      gw ? inv + inv_words : nullptr);
 }
 
 int32_t har_cuda_moe_layer_create(har_cuda_ctx *ctx, const har_cuda_weights *gate,

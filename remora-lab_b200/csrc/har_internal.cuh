@@ -321,8 +321,10 @@ int32_t launch_q6k_gemv(har_cuda_ctx *ctx, const har_cuda_weights *w, int64_t ex
                         const float *x, int64_t M, float *y);
 int32_t launch_route_topk(har_cuda_ctx *ctx, const float *logits, int64_t T, int E, int k,
                           int32_t *ids, float *weights);
+// gcnt: group_scratch_words(T * k, E) words of scratch (may be null for one CTA)
 int32_t launch_group(har_cuda_ctx *ctx, const int32_t *ids, int64_t T, int k, int E,
-                     int32_t *counts, int32_t *offsets, int32_t *order, int32_t *inv);
+                     int32_t *counts, int32_t *offsets, int32_t *order, int32_t *inv, int32_t *gcnt);
+size_t group_scratch_words(int64_t n, int E);
 int32_t launch_router_logits(har_cuda_ctx *ctx, const float *W, int E, int H, const float *x,
                              int64_t T, float *logits);
 int32_t launch_route_fused(har_cuda_ctx *ctx, const float *W, int E, int H, const float *x,

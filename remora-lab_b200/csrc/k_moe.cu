@@ -33,7 +33,7 @@ size_t group_smem_bytes(int E);
 int32_t launch_group_full(har_cuda_ctx *ctx, const int32_t *ids, int64_t n, int E,
                           int32_t *counts, int32_t *offsets, int32_t *order, int32_t *inv,
                           int32_t *ne, int32_t *n_ne, int thr, int nt, int2 *tt_info,
-                          int32_t *n_tt, int shared_T, int allow_empty);
+                          int32_t *n_tt, int shared_T, int allow_empty, int32_t *gcnt);
 
 struct MoeDev {
   const uint8_t *gate, *up, *down, *sh_gate, *sh_up, *sh_down;
@@ -374,7 +374,7 @@ static size_t al256(size_t v) { return (v + 255) & ~(size_t)255; }
 // Scratch layout of one moe_ffn call (offsets in bytes, 256-byte aligned).
 struct MoeScratch {
   size_t o_counts, o_offsets, o_order, o_inv, o_ne, o_nne, o_xq, o_a, o_aq, o_y;
-  size_t o_ttinfo, o_ntt, o_x16, o_a16, o_xs16, o_as16, o_gsh, total;
+  size_t o_ttinfo, o_ntt, o_x16, o_a16, o_xs16, o_as16, o_gsh, o_gcnt, total;
 };
 
 // Experts with at least this many tokens take the tensor-core path
@@ -447,6 +447,8 @@ static MoeScratch moe_layout(const har_cuda_moe_layer *layer, int64_t T, int k, 
   s.o_xs16 = tc ? take(2 * (size_t)(2 * slots * (H / 16))) : 0;
   s.o_as16 = tc ? take(2 * (size_t)(2 * slots * (I / 16))) : 0;
   s.o_gsh = take(4 * (size_t)T);
+  const size_t gw = group_scratch_words(n, (int)E);  // the multi-CTA grouping's segment counts
+  s.o_gcnt = gw ? take(4 * gw) : 0;
   s.total = off;
   return s;
 }
@@ -538,7 +540,8 @@ int32_t run_moe_ffn_in(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const
                          (int32_t *)(S + o_order), (int32_t *)(S + o_inv), (int32_t *)(S + o_ne),
                          (int32_t *)(S + o_nne), thr, TC_NT, (int2 *)(S + L.o_ttinfo),
                          (int32_t *)(S + L.o_ntt), shared_tc ? (int)T : 0,
-                         (flags & HAR_CUDA_MOE_EMPTY_SLOTS) ? 1 : 0);
+                         (flags & HAR_CUDA_MOE_EMPTY_SLOTS) ? 1 : 0,
+                         L.o_gcnt ? (int32_t *)(S + L.o_gcnt) : nullptr);
   if (st) return st;
   // tensor-core path parameters (experts with >= thr tokens)
   TcParams tp{};

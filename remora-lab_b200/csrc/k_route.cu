@@ -391,35 +391,45 @@ int32_t launch_route_topk(har_cuda_ctx *ctx, const float *logits, int64_t T, int
 }
 
 // ---------------------------------------------------------------------------
-// group_kernel: stable counting sort of n = T*k entries by expert id.
+// Grouping: a stable counting sort of n = T*k entries by expert id
+// (MoEModel::forward_batch's groups, har/crates/har-serve/src/moe.rs:195-202).
 // Outputs counts[E], offsets[E+1], order[n] (entry at each grouped position),
 // inv[n] (grouped position of each entry) and, when ne != null, the list of
 // non-empty experts in expert order (ne[0..*n_ne)) below `thr` tokens, and
-// the token tiles of the experts at or above it (see the tail below).
-// Entries with an out-of-range id set DEV_ERR_BOUNDS in *status and are dropped;
-// with allow_empty, id -1 marks an empty slot and is dropped silently.
+// the token tiles of the experts at or above it (group_lists).  Entries with
+// an out-of-range id set DEV_ERR_BOUNDS in *status and are dropped; with
+// allow_empty, id -1 marks an empty slot and is dropped silently.
+//
+// Within a CTA of GROUP_WARPS warps each warp owns a contiguous run of
+// entries, counts them per expert with __match_any_sync (pass 1), and after a
+// scan places them (pass 2) — stable because runs, and entries within a run,
+// keep their order.  Up to GROUP_MC_MIN entries one CTA does everything
+// (group_kernel).  Above it the entries are cut into contiguous segments, one
+// CTA each: group_count_kernel counts a segment per expert, group_scan_kernel
+// (one CTA) turns the segments' counts into per-segment bases, the offsets and
+// the lists, and group_scatter_kernel recounts its segment per warp and
+// places it.  Measured on B200 in a CUDA graph: one CTA takes ~40 us for
+// 20,480 entries (the local layer of an 8-way expert-parallel step) and
+// ~21 us for 8,192; the three launches take ~10 and ~10 us (~13 us at 40,960).
 // ---------------------------------------------------------------------------
 constexpr int GROUP_WARPS = 16;
+constexpr int64_t GROUP_MC_MIN = 2048;  // entries above which the CTAs share the sort
+constexpr int GROUP_SEG = 1024;         // entries per segment (64 per warp)
+constexpr int GROUP_MAX_SEGS = 512;
 
-__global__ void __launch_bounds__(GROUP_WARPS * 32) group_kernel(
-    const int32_t *__restrict__ ids, int n, int E, int32_t *__restrict__ counts,
-    int32_t *__restrict__ offsets, int32_t *__restrict__ order, int32_t *__restrict__ inv,
-    int32_t *__restrict__ ne, int32_t *__restrict__ n_ne, int thr, int nt,
-    int2 *__restrict__ tt_info, int32_t *__restrict__ n_tt, int shared_T, int allow_empty,
-    int *status) {
-  extern __shared__ __align__(16) uint8_t gsm[];
-  int32_t *cnt = reinterpret_cast<int32_t *>(gsm);                       // [W][E]
-  int32_t *off = cnt + (size_t)GROUP_WARPS * E;                             // [E+1]
-  __shared__ int32_t warp_tot[GROUP_WARPS + 1];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int i = threadIdx.x; i < GROUP_WARPS * E; i += blockDim.x) cnt[i] = 0;
-  __syncthreads();
-  const int seg = (n + GROUP_WARPS - 1) / GROUP_WARPS;
-  const int s0 = min(n, warp * seg), s1 = min(n, s0 + seg);
+__host__ __device__ inline int group_segments(int64_t n) {
+  if (n <= GROUP_MC_MIN) return 1;
+  const int64_t s = (n + GROUP_SEG - 1) / GROUP_SEG;
+  return (int)(s < GROUP_MAX_SEGS ? s : GROUP_MAX_SEGS);
+}
+
+// Pass 1 for one warp: cnt[e] += entries of [s0, s1) with id e.  Ids are
+// loaded GB chunks of 32 at a time before the warp-synchronous updates, so one
+// load latency covers 32 * GB entries.  status != null reports bad ids.
+constexpr int GB = 8;
+__device__ __forceinline__ void group_count_run(const int32_t *ids, int s0, int s1, int E, int32_t *cnt,
+                                                int allow_empty, int *status, int lane) {
   const unsigned lt = (1u << lane) - 1u;
-  // pass 1: per-warp counts.  Ids are loaded GB chunks of 32 at a time before
-  // the warp-synchronous updates, so one load latency covers 32 * GB entries.
-  constexpr int GB = 8;
   for (int b0 = s0; b0 < s1; b0 += 32 * GB) {
     int ev[GB];
 #pragma unroll
@@ -432,31 +442,78 @@ __global__ void __launch_bounds__(GROUP_WARPS * 32) group_kernel(
       const int i = b0 + 32 * j + lane;
       int e = ev[j];
       if (i < s1 && (e < 0 || e >= E)) {
-        if (!(allow_empty && e == -1)) atomicOr(status, DEV_ERR_BOUNDS);
+        if (status && !(allow_empty && e == -1)) atomicOr(status, DEV_ERR_BOUNDS);
         e = -1;
       }
       const unsigned m = __match_any_sync(0xffffffffu, e);
-      if (e >= 0 && (m & lt) == 0) cnt[warp * E + e] += __popc(m);
+      if (e >= 0 && (m & lt) == 0) cnt[e] += __popc(m);
       __syncwarp();
     }
   }
-  __syncthreads();
-  // per-expert totals, then a block-wide exclusive scan in chunks of blockDim
+}
+
+// Pass 2 for one warp: entries of [s0, s1) to their positions; base[e] is
+// where this warp's next entry of expert e goes (advanced as it places).
+__device__ __forceinline__ void group_place_run(const int32_t *ids, int s0, int s1, int E, int32_t *base,
+                                                int32_t *order, int32_t *inv, int lane) {
+  const unsigned lt = (1u << lane) - 1u;
+  for (int b0 = s0; b0 < s1; b0 += 32 * GB) {
+    int ev[GB];
+#pragma unroll
+    for (int j = 0; j < GB; ++j) {
+      const int i = b0 + 32 * j + lane;
+      ev[j] = i < s1 ? ids[i] : -1;
+    }
+#pragma unroll
+    for (int j = 0; j < GB; ++j) {
+      const int i = b0 + 32 * j + lane;
+      int e = ev[j];
+      if (e < 0 || e >= E) e = -1;
+      const unsigned m = __match_any_sync(0xffffffffu, e);
+      int pos = 0;
+      if (e >= 0) pos = base[e] + __popc(m & lt);
+      __syncwarp();
+      if (e >= 0) {
+        order[pos] = i;
+        inv[i] = pos;
+        if ((m & lt) == 0) base[e] += __popc(m);
+      } else if (i < s1) {
+        inv[i] = -1;
+      }
+      __syncwarp();
+    }
+  }
+}
+
+// The run of warp w of GROUP_WARPS over [c0, c1).
+__device__ __forceinline__ void group_run(int c0, int c1, int w, int &s0, int &s1) {
+  const int seg = (c1 - c0 + GROUP_WARPS - 1) / GROUP_WARPS;
+  s0 = min(c1, c0 + w * seg);
+  s1 = min(c1, s0 + seg);
+}
+
+// Per-warp counts cnt[w][e] become each warp's base within expert e (plus
+// add[e] when given); tot[e] = the CTA's count of e.  Block-wide.
+__device__ __forceinline__ void group_warp_bases(int32_t *cnt, int E, const int32_t *add, int32_t *tot) {
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int run = add ? add[e] : 0;
+    for (int w = 0; w < GROUP_WARPS; ++w) {
+      const int c = cnt[w * E + e];
+      cnt[w * E + e] = run;
+      run += c;
+    }
+    if (tot) tot[e] = run - (add ? add[e] : 0);
+  }
+}
+
+// off[0..E] = exclusive scan of tot[0..E) (off[E] = the total), block-wide,
+// in chunks of blockDim; warp_tot holds GROUP_WARPS + 1 words of scratch.
+__device__ __forceinline__ void group_offsets(const int32_t *tot, int E, int32_t *off, int32_t *warp_tot) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int base = 0; base < E; base += blockDim.x) {
     const int e = base + threadIdx.x;
-    int tot = 0;
-    if (e < E) {
-      int run = 0;
-      for (int w = 0; w < GROUP_WARPS; ++w) {
-        const int c = cnt[w * E + e];
-        cnt[w * E + e] = run;  // becomes the warp's base within expert e
-        run += c;
-      }
-      tot = run;
-      counts[e] = tot;
-    }
-    // inclusive warp scan
-    int v = tot;
+    const int t = e < E ? tot[e] : 0;
+    int v = t;  // inclusive warp scan
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const int u = __shfl_up_sync(0xffffffffu, v, o);
@@ -474,136 +531,248 @@ __global__ void __launch_bounds__(GROUP_WARPS * 32) group_kernel(
       warp_tot[GROUP_WARPS] = r;
     }
     __syncthreads();
-    if (e < E) off[e] = warp_tot[warp] + v - tot;
+    if (e < E) off[e] = warp_tot[warp] + v - t;
     if (threadIdx.x == 0) off[min(E, base + (int)blockDim.x)] = warp_tot[GROUP_WARPS];
     __syncthreads();
   }
-  for (int e = threadIdx.x; e <= E; e += blockDim.x) offsets[e] = off[e];
-  // pass 2: positions (ids loaded in batches as in pass 1)
-  for (int b0 = s0; b0 < s1; b0 += 32 * GB) {
-    int ev[GB];
-#pragma unroll
-    for (int j = 0; j < GB; ++j) {
-      const int i = b0 + 32 * j + lane;
-      ev[j] = i < s1 ? ids[i] : -1;
-    }
-#pragma unroll
-    for (int j = 0; j < GB; ++j) {
-      const int i = b0 + 32 * j + lane;
-      int e = ev[j];
-      if (e < 0 || e >= E) e = -1;
-      const unsigned m = __match_any_sync(0xffffffffu, e);
-      int pos = 0;
-      if (e >= 0) pos = off[e] + cnt[warp * E + e] + __popc(m & lt);
-      __syncwarp();
-      if (e >= 0) {
-        order[pos] = i;
-        inv[i] = pos;
-        if ((m & lt) == 0) cnt[warp * E + e] += __popc(m);
-      } else if (i < s1) {
-        inv[i] = -1;
-      }
-      __syncwarp();
+}
+
+// Non-empty experts in expert order, split by token count: ne[] those below
+// `thr` (CUDA-core path); those at or above it (tensor-core path) are cut
+// into ceil(count/nt) token tiles, listed in expert order as
+// tt_info[j] = {expert | tokens << 16, first slot}.  When shared_T > 0 the
+// shared expert (index E, slots n .. n + shared_T) follows with
+// ceil(shared_T/nt) tiles.  *n_ne / *n_tt = the list lengths.  Each warp takes
+// chunks of 32 experts; a scan of the chunks' totals (in `scratch`, 2 words
+// per chunk) gives each chunk its offsets.  Block-wide; off[] in shared memory.
+__device__ __forceinline__ void group_lists(const int32_t *off, int E, int n, int thr, int nt,
+                                            int32_t *ne, int32_t *n_ne, int2 *tt_info, int32_t *n_tt,
+                                            int shared_T, int32_t *scratch, int32_t *warp_tot) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const unsigned lt = (1u << lane) - 1u;
+  const int nch = (E + 31) / 32;
+  int32_t *ch_small = scratch, *ch_tt = scratch + nch;
+  __syncthreads();
+  for (int c = warp; c < nch; c += GROUP_WARPS) {
+    const int e = c * 32 + lane;
+    const int ce = e < E ? off[e + 1] - off[e] : 0;
+    const bool small = ce > 0 && ce < thr;
+    const int tt = ce > 0 && ce >= thr ? (ce + nt - 1) / nt : 0;
+    const int ns = __popc(__ballot_sync(0xffffffffu, small));
+    const int ntt = __reduce_add_sync(0xffffffffu, (unsigned)tt);
+    if (lane == 0) {
+      ch_small[c] = ns;
+      ch_tt[c] = ntt;
     }
   }
-  // Non-empty experts in expert order, split by token count: ne[] those
-  // below `thr` (CUDA-core path); those at or above it (tensor-core path) are
-  // cut into ceil(count/nt) token tiles, listed in expert order as
-  // tt_info[j] = {expert | tokens << 16, first slot}.  When shared_T > 0 the
-  // shared expert (index E, slots n .. n + shared_T) follows with
-  // ceil(shared_T/nt) tiles.  *n_ne / *n_tt = the list lengths.  Each warp
-  // takes chunks of 32 experts; a scan of the chunks' totals (kept in the
-  // per-warp counters, free after pass 2) gives each chunk its offsets.
-  if (ne) {
-    const int nch = (E + 31) / 32;
-    int32_t *ch_small = cnt, *ch_tt = cnt + nch;
-    __syncthreads();  // pass 2 is done with cnt
-    for (int c = warp; c < nch; c += GROUP_WARPS) {
-      const int e = c * 32 + lane;
-      const int ce = e < E ? off[e + 1] - off[e] : 0;
-      const bool small = ce > 0 && ce < thr;
-      const int tt = ce > 0 && ce >= thr ? (ce + nt - 1) / nt : 0;
-      const int ns = __popc(__ballot_sync(0xffffffffu, small));
-      const int ntt = __reduce_add_sync(0xffffffffu, (unsigned)tt);
-      if (lane == 0) {
-        ch_small[c] = ns;
-        ch_tt[c] = ntt;
-      }
-    }
-    __syncthreads();
-    if (warp == 0) {  // exclusive scans over the chunks
-      int rs = 0, rt = 0;
-      for (int base = 0; base < nch; base += 32) {
-        const int c = base + lane;
-        const int a = c < nch ? ch_small[c] : 0, b = c < nch ? ch_tt[c] : 0;
-        int ia = a, ib = b;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const int ua = __shfl_up_sync(0xffffffffu, ia, o), ub = __shfl_up_sync(0xffffffffu, ib, o);
-          if (lane >= o) {
-            ia += ua;
-            ib += ub;
-          }
-        }
-        if (c < nch) {
-          ch_small[c] = rs + ia - a;
-          ch_tt[c] = rt + ib - b;
-        }
-        rs += __shfl_sync(0xffffffffu, ia, 31);
-        rt += __shfl_sync(0xffffffffu, ib, 31);
-      }
-      if (lane == 0) {
-        *n_ne = rs;
-        *n_tt = rt + (shared_T + nt - 1) / nt;
-        warp_tot[0] = rt;  // first tile of the shared expert
-      }
-    }
-    __syncthreads();
-    for (int c = warp; c < nch; c += GROUP_WARPS) {
-      const int e = c * 32 + lane;
-      const int ce = e < E ? off[e + 1] - off[e] : 0;
-      const bool small = ce > 0 && ce < thr;
-      const int tt = ce > 0 && ce >= thr ? (ce + nt - 1) / nt : 0;
-      const unsigned bm = __ballot_sync(0xffffffffu, small);
-      if (small) ne[ch_small[c] + __popc(bm & lt)] = e;
-      int incl = tt;
+  __syncthreads();
+  if (warp == 0) {  // exclusive scans over the chunks
+    int rs = 0, rt = 0;
+    for (int base = 0; base < nch; base += 32) {
+      const int c = base + lane;
+      const int a = c < nch ? ch_small[c] : 0, b = c < nch ? ch_tt[c] : 0;
+      int ia = a, ib = b;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
-        const int u = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += u;
+        const int ua = __shfl_up_sync(0xffffffffu, ia, o), ub = __shfl_up_sync(0xffffffffu, ib, o);
+        if (lane >= o) {
+          ia += ua;
+          ib += ub;
+        }
       }
-      for (int j = 0; j < tt; ++j)
-        tt_info[ch_tt[c] + incl - tt + j] = make_int2(e | (min(nt, ce - j * nt) << 16), off[e] + j * nt);
+      if (c < nch) {
+        ch_small[c] = rs + ia - a;
+        ch_tt[c] = rt + ib - b;
+      }
+      rs += __shfl_sync(0xffffffffu, ia, 31);
+      rt += __shfl_sync(0xffffffffu, ib, 31);
     }
-    const int run_tt = warp_tot[0];
-    for (int t0 = (int)threadIdx.x * nt; t0 < shared_T; t0 += (int)blockDim.x * nt)
-      tt_info[run_tt + t0 / nt] = make_int2(E | (min(nt, shared_T - t0) << 16), n + t0);
+    if (lane == 0) {
+      *n_ne = rs;
+      *n_tt = rt + (shared_T + nt - 1) / nt;
+      warp_tot[0] = rt;  // first tile of the shared expert
+    }
+  }
+  __syncthreads();
+  for (int c = warp; c < nch; c += GROUP_WARPS) {
+    const int e = c * 32 + lane;
+    const int ce = e < E ? off[e + 1] - off[e] : 0;
+    const bool small = ce > 0 && ce < thr;
+    const int tt = ce > 0 && ce >= thr ? (ce + nt - 1) / nt : 0;
+    const unsigned bm = __ballot_sync(0xffffffffu, small);
+    if (small) ne[ch_small[c] + __popc(bm & lt)] = e;
+    int incl = tt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int u = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += u;
+    }
+    for (int j = 0; j < tt; ++j)
+      tt_info[ch_tt[c] + incl - tt + j] = make_int2(e | (min(nt, ce - j * nt) << 16), off[e] + j * nt);
+  }
+  const int run_tt = warp_tot[0];
+  for (int t0 = (int)threadIdx.x * nt; t0 < shared_T; t0 += (int)blockDim.x * nt)
+    tt_info[run_tt + t0 / nt] = make_int2(E | (min(nt, shared_T - t0) << 16), n + t0);
+}
+
+// One CTA: the whole sort.
+__global__ void __launch_bounds__(GROUP_WARPS * 32) group_kernel(
+    const int32_t *__restrict__ ids, int n, int E, int32_t *__restrict__ counts,
+    int32_t *__restrict__ offsets, int32_t *__restrict__ order, int32_t *__restrict__ inv,
+    int32_t *__restrict__ ne, int32_t *__restrict__ n_ne, int thr, int nt,
+    int2 *__restrict__ tt_info, int32_t *__restrict__ n_tt, int shared_T, int allow_empty,
+    int *status) {
+  extern __shared__ __align__(16) uint8_t gsm[];
+  int32_t *cnt = reinterpret_cast<int32_t *>(gsm);  // [W][E]
+  int32_t *off = cnt + (size_t)GROUP_WARPS * E;      // [E+1]
+  int32_t *tot = off + E + 1;                         // [E]
+  __shared__ int32_t warp_tot[GROUP_WARPS + 1];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = threadIdx.x; i < GROUP_WARPS * E; i += blockDim.x) cnt[i] = 0;
+  __syncthreads();
+  int s0, s1;
+  group_run(0, n, warp, s0, s1);
+  group_count_run(ids, s0, s1, E, cnt + warp * E, allow_empty, status, lane);
+  __syncthreads();
+  group_warp_bases(cnt, E, nullptr, tot);
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) counts[e] = tot[e];
+  group_offsets(tot, E, off, warp_tot);
+  for (int e = threadIdx.x; e <= E; e += blockDim.x) offsets[e] = off[e];
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    const int o = off[e];
+    for (int w = 0; w < GROUP_WARPS; ++w) cnt[w * E + e] += o;
+  }
+  __syncthreads();
+  group_place_run(ids, s0, s1, E, cnt + warp * E, order, inv, lane);
+  if (ne) group_lists(off, E, n, thr, nt, ne, n_ne, tt_info, n_tt, shared_T, cnt, warp_tot);
+}
+
+// Several CTAs, 1 of 3: segment b's count of every expert, gcnt[b][e].
+__global__ void __launch_bounds__(GROUP_WARPS * 32) group_count_kernel(
+    const int32_t *__restrict__ ids, int n, int E, int seg, int32_t *__restrict__ gcnt, int allow_empty,
+    int *status) {
+  extern __shared__ __align__(16) uint8_t gsm[];
+  int32_t *cnt = reinterpret_cast<int32_t *>(gsm);  // [W][E]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = threadIdx.x; i < GROUP_WARPS * E; i += blockDim.x) cnt[i] = 0;
+  pdl_wait();  // the ids come from the previous launch
+  pdl_launch_dependents();
+  __syncthreads();
+  const int c0 = min(n, (int)blockIdx.x * seg), c1 = min(n, c0 + seg);
+  int s0, s1;
+  group_run(c0, c1, warp, s0, s1);
+  group_count_run(ids, s0, s1, E, cnt + warp * E, allow_empty, status, lane);
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int t = 0;
+    for (int w = 0; w < GROUP_WARPS; ++w) t += cnt[w * E + e];
+    gcnt[(size_t)blockIdx.x * E + e] = t;
   }
 }
 
+// 2 of 3 (one CTA): gcnt[b][e] becomes segment b's first position within
+// expert e; the counts, offsets and lists as in group_kernel.
+__global__ void __launch_bounds__(GROUP_WARPS * 32) group_scan_kernel(
+    int32_t *__restrict__ gcnt, int B, int n, int E, int32_t *__restrict__ counts,
+    int32_t *__restrict__ offsets, int32_t *__restrict__ ne, int32_t *__restrict__ n_ne, int thr, int nt,
+    int2 *__restrict__ tt_info, int32_t *__restrict__ n_tt, int shared_T) {
+  extern __shared__ __align__(16) uint8_t gsm[];
+  int32_t *off = reinterpret_cast<int32_t *>(gsm);  // [E+1]
+  int32_t *tot = off + E + 1;                        // [E]
+  int32_t *scratch = tot + E;                        // [2 * ceil(E/32)]
+  __shared__ int32_t warp_tot[GROUP_WARPS + 1];
+  pdl_wait();
+  pdl_launch_dependents();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int run = 0;
+    for (int b = 0; b < B; ++b) {
+      const int c = gcnt[(size_t)b * E + e];
+      gcnt[(size_t)b * E + e] = run;
+      run += c;
+    }
+    tot[e] = run;
+    counts[e] = run;
+  }
+  __syncthreads();
+  group_offsets(tot, E, off, warp_tot);
+  for (int e = threadIdx.x; e <= E; e += blockDim.x) offsets[e] = off[e];
+  if (ne) group_lists(off, E, n, thr, nt, ne, n_ne, tt_info, n_tt, shared_T, scratch, warp_tot);
+}
+
+// 3 of 3: segment b's entries to offsets[e] + gcnt[b][e] + their rank in it.
+__global__ void __launch_bounds__(GROUP_WARPS * 32) group_scatter_kernel(
+    const int32_t *__restrict__ ids, int n, int E, int seg, const int32_t *__restrict__ gcnt,
+    const int32_t *__restrict__ offsets, int32_t *__restrict__ order, int32_t *__restrict__ inv) {
+  extern __shared__ __align__(16) uint8_t gsm[];
+  int32_t *cnt = reinterpret_cast<int32_t *>(gsm);  // [W][E]
+  int32_t *add = cnt + (size_t)GROUP_WARPS * E;      // [E]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = threadIdx.x; i < GROUP_WARPS * E; i += blockDim.x) cnt[i] = 0;
+  pdl_wait();
+  pdl_launch_dependents();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) add[e] = offsets[e] + gcnt[(size_t)blockIdx.x * E + e];
+  __syncthreads();
+  const int c0 = min(n, (int)blockIdx.x * seg), c1 = min(n, c0 + seg);
+  int s0, s1;
+  group_run(c0, c1, warp, s0, s1);
+  group_count_run(ids, s0, s1, E, cnt + warp * E, 1, nullptr, lane);
+  __syncthreads();
+  group_warp_bases(cnt, E, add, nullptr);
+  __syncthreads();
+  group_place_run(ids, s0, s1, E, cnt + warp * E, order, inv, lane);
+}
+
 size_t group_smem_bytes(int E) {
-  return ((size_t)GROUP_WARPS * E + E + 1) * 4;
+  return ((size_t)GROUP_WARPS * E + 2 * (size_t)E + 1) * 4;
+}
+
+// Scratch words the multi-CTA sort needs beside the outputs (0: one CTA).
+size_t group_scratch_words(int64_t n, int E) {
+  const int B = group_segments(n);
+  return B > 1 ? (size_t)B * E : 0;
 }
 
 int32_t launch_group_full(har_cuda_ctx *ctx, const int32_t *ids, int64_t n, int E,
                           int32_t *counts, int32_t *offsets, int32_t *order, int32_t *inv,
                           int32_t *ne, int32_t *n_ne, int thr, int nt, int2 *tt_info,
-                          int32_t *n_tt, int shared_T, int allow_empty) {
+                          int32_t *n_tt, int shared_T, int allow_empty, int32_t *gcnt) {
   const size_t smem = group_smem_bytes(E);
-  if (smem > 48 * 1024)
-    cudaFuncSetAttribute(group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  const int B = group_segments(n);
+  if (B == 1 || !gcnt) {
+    if (smem > 48 * 1024)
+      cudaFuncSetAttribute(group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    prof_begin(ctx);
+    group_kernel<<<1, GROUP_WARPS * 32, smem, ctx->stream>>>(ids, (int)n, E, counts, offsets, order, inv,
+                                                             ne, n_ne, thr, nt, tt_info, n_tt, shared_T,
+                                                             allow_empty, ctx->d_status);
+    return check_launch(ctx, "group_kernel");
+  }
+  const int seg = (int)((n + B - 1) / B);
+  if (smem > 48 * 1024) {
+    cudaFuncSetAttribute(group_count_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(group_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(group_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  }
   prof_begin(ctx);
-  group_kernel<<<1, GROUP_WARPS * 32, smem, ctx->stream>>>(ids, (int)n, E, counts, offsets,
-                                                           order, inv, ne, n_ne, thr, nt,
-                                                           tt_info, n_tt, shared_T, allow_empty,
-                                                           ctx->d_status);
-  return check_launch(ctx, "group_kernel");
+  launch_pdl(group_count_kernel, dim3(B), dim3(GROUP_WARPS * 32), smem, ctx->stream, ids, (int)n, E, seg,
+             gcnt, allow_empty, ctx->d_status);
+  int32_t st = check_launch(ctx, "group_count_kernel");
+  if (st) return st;
+  prof_begin(ctx);
+  launch_pdl(group_scan_kernel, dim3(1), dim3(GROUP_WARPS * 32), smem, ctx->stream, gcnt, B, (int)n, E,
+             counts, offsets, ne, n_ne, thr, nt, tt_info, n_tt, shared_T);
+  if ((st = check_launch(ctx, "group_scan_kernel"))) return st;
+  prof_begin(ctx);
+  launch_pdl(group_scatter_kernel, dim3(B), dim3(GROUP_WARPS * 32), smem, ctx->stream, ids, (int)n, E, seg,
+             (const int32_t *)gcnt, (const int32_t *)offsets, order, inv);
+  return check_launch(ctx, "group_scatter_kernel");
 }
 
 int32_t launch_group(har_cuda_ctx *ctx, const int32_t *ids, int64_t T, int k, int E,
-                     int32_t *counts, int32_t *offsets, int32_t *order, int32_t *inv) {
+                     int32_t *counts, int32_t *offsets, int32_t *order, int32_t *inv, int32_t *gcnt) {
   return launch_group_full(ctx, ids, T * k, E, counts, offsets, order, inv, nullptr, nullptr, 0,
-                           1, nullptr, nullptr, 0, 0);
+                           1, nullptr, nullptr, 0, 0, gcnt);
 }
 
 // ---------------------------------------------------------------------------

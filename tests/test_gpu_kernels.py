@@ -170,7 +170,10 @@ def group(ctx, ids, E):
     return counts.cpu().numpy(), offsets.cpu().numpy(), order.cpu().numpy()
 
 
-@pytest.mark.parametrize("T,E,k", [(256, 512, 10), (4096, 512, 10), (1, 512, 10), (3, 2048, 1), (1000, 8, 8)])
+@pytest.mark.parametrize("T,E,k", [(256, 512, 10), (4096, 512, 10), (1, 512, 10), (3, 2048, 1), (1000, 8, 8),
+                                   # above 8192 entries the sort runs over several CTAs:
+                                   # a ragged last segment, the largest E, many segments
+                                   (2049, 64, 10), (1700, 2048, 10), (40000, 16, 2)])
 def test_group_by_expert_bit_exact(ctx, T, E, k):
     ids, _ = haro.zipf_routing(T + E, T, E, k)
     got = group(ctx, ids, E)
@@ -186,6 +189,16 @@ def test_group_rejects_out_of_range_ids(ctx):
         ctx.synchronize()
     assert e.value.status == har_cuda.ERR_DEVICE
     ctx.synchronize()  # the error word is cleared after it is reported
+
+
+def test_group_rejects_out_of_range_ids_across_ctas(ctx):
+    ids, _ = haro.zipf_routing(77, 2000, 64, 10)
+    ids[1500, 3] = 64
+    group(ctx, ids, 64)
+    with pytest.raises(har_cuda.HarCudaError) as e:
+        ctx.synchronize()
+    assert e.value.status == har_cuda.ERR_DEVICE
+    ctx.synchronize()
 
 
 def test_device_generator_matches_host_generator(ctx):
