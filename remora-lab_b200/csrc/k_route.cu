@@ -1062,6 +1062,7 @@ __global__ void __launch_bounds__(RS_W * 32, 1) router_logits_small_kernel(
 // cycles per add) than forming a group's products ahead of its adds (6.8);
 // the bare chain of adds is 4.4.
 constexpr int RG_CH = 8;
+constexpr int RG_FULL = 256;  // the chunk of H = 2048
 constexpr uint32_t RG_WAIT_LIMIT = 1u << 20;
 
 __host__ __device__ inline int rg_chunk(int H) { return ((H + RG_CH - 1) / RG_CH + 3) & ~3; }
@@ -1112,11 +1113,13 @@ __global__ void __launch_bounds__(RS_W * 32, 1) router_logits_staged_kernel(
   pdl_wait();
   pdl_launch_dependents();
   if (warp == RS_W - 1) issue(true);
-  const bool active = tok < nt;
+  // A warp with any token runs every lane's chain: lanes past T repeat the
+  // last token's (their results are dropped), so the warp runs converged.
+  const bool active = tok < nt, run = RS_TW * warp < nt;
   float s = 0.0f;
   bool ok = true;
-  if (active) {
-    const float *wr = rgs + (size_t)el * LD, *xr = rgs + (size_t)(RS_E + tok) * LD;
+  if (run) {
+    const float *wr = rgs + (size_t)el * LD, *xr = rgs + (size_t)(RS_E + min(tok, nt - 1)) * LD;
     for (int c = 0; c < RG_CH && ok; ++c) {
       const int h0 = c * CH, h1 = min(H, h0 + CH);
       if (h0 >= h1) break;
@@ -1124,14 +1127,20 @@ __global__ void __launch_bounds__(RS_W * 32, 1) router_logits_staged_kernel(
         ok = false;
         break;
       }
-#pragma unroll 4
-      for (int h = h0; h < h1; h += 4) {
+      auto step = [&](int h) {
         const float4 w = *reinterpret_cast<const float4 *>(wr + h);
         const float4 v = *reinterpret_cast<const float4 *>(xr + h);
         s = __fadd_rn(s, __fmul_rn(w.x, v.x));
         s = __fadd_rn(s, __fmul_rn(w.y, v.y));
         s = __fadd_rn(s, __fmul_rn(w.z, v.z));
         s = __fadd_rn(s, __fmul_rn(w.w, v.w));
+      };
+      if (h1 - h0 == RG_FULL) {  // the common chunk: a fixed trip count
+#pragma unroll 16
+        for (int h = 0; h < RG_FULL; h += 4) step(h0 + h);
+      } else {
+#pragma unroll 4
+        for (int h = h0; h < h1; h += 4) step(h);
       }
     }
   }
