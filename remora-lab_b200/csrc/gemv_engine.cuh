@@ -230,44 +230,38 @@ __device__ __forceinline__ float chunk_dot(const WChunk &w, int chunk, const Lan
   return (d * a.dx) * (float)i1 - (dmin * a.dx) * (float)i2;
 }
 
+// The f32 chunk dot: sum_q q*x per sub-block, then d1*sum(q*x) - m1*sum(x)
+// (q4k_dot's per-value (d1*q - m1)*x, reassociated; tolerance-checked).  Each
+// nibble becomes an exact f32 by a byte permute into the mantissa of 2^23 and
+// a subtraction of 2^23; values go through Blackwell's packed f32x2 add and
+// FMA two at a time, into four accumulators per sub-block (bytes 0-1 and 2-3
+// of each word as two pairs), added pairwise at the end.  Two instructions per
+// value instead of three, and a dependent FMA depth of 8: the decode GEMVs and
+// kernels are bound by instruction issue and latency.
+__device__ __forceinline__ float2 u8x2_to_f32(uint32_t v, int j) {
+  const float2 b = make_float2(__uint_as_float(__byte_perm(v, 0x4B000000u, 0x7440u | (uint32_t)j)),
+                               __uint_as_float(__byte_perm(v, 0x4B000000u, 0x7440u | (uint32_t)(j + 1))));
+  return __fadd2_rn(b, make_float2(-8388608.0f, -8388608.0f));
+}
 __device__ __forceinline__ float chunk_dot(const WChunk &w, int chunk, const LaneAct<ACT_F32> &a) {
   const uint32_t q[8] = {w.q0.x, w.q0.y, w.q0.z, w.q0.w, w.q1.x, w.q1.y, w.q1.z, w.q1.w};
-  float slo = 0.0f, shi = 0.0f;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    // the word's four low (high) nibbles, one per byte; each becomes an exact
-    // f32 by a byte permute into the mantissa of 2^23 and one subtraction
-    const uint32_t lo = q[i] & 0x0F0F0F0Fu, hi = (q[i] >> 4) & 0x0F0F0F0Fu;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      slo = fmaf(u8_to_f32(lo, j), a.lo[4 * i + j], slo);
-      shi = fmaf(u8_to_f32(hi, j), a.hi[4 * i + j], shi);
-    }
-  }
-  const ChunkScales s = chunk_scales(w.hdr, chunk & 3);
-  return (s.d1 * slo - s.m1 * a.slo) + (s.d2 * shi - s.m2 * a.shi);
-}
-
-// chunk_dot for latency-bound callers (the decode kernels, a few warps per
-// SM): four accumulators per sub-block instead of one, so the dependent FMA
-// depth is 8 instead of 32; the four partial sums are added pairwise.  Same
-// terms, different association (within the f32 path's tolerance); a caller
-// uses one form throughout, so its results do not depend on the batch.
-__device__ __forceinline__ float chunk_dot_ilp(const WChunk &w, int chunk, const LaneAct<ACT_F32> &a) {
-  const uint32_t q[8] = {w.q0.x, w.q0.y, w.q0.z, w.q0.w, w.q1.x, w.q1.y, w.q1.z, w.q1.w};
-  float slo[4] = {0.0f, 0.0f, 0.0f, 0.0f}, shi[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  float2 l01 = make_float2(0.0f, 0.0f), l23 = l01, h01 = l01, h23 = l01;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const uint32_t lo = q[i] & 0x0F0F0F0Fu, hi = (q[i] >> 4) & 0x0F0F0F0Fu;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      slo[j] = fmaf(u8_to_f32(lo, j), a.lo[4 * i + j], slo[j]);
-      shi[j] = fmaf(u8_to_f32(hi, j), a.hi[4 * i + j], shi[j]);
-    }
+    l01 = __ffma2_rn(u8x2_to_f32(lo, 0), make_float2(a.lo[4 * i], a.lo[4 * i + 1]), l01);
+    l23 = __ffma2_rn(u8x2_to_f32(lo, 2), make_float2(a.lo[4 * i + 2], a.lo[4 * i + 3]), l23);
+    h01 = __ffma2_rn(u8x2_to_f32(hi, 0), make_float2(a.hi[4 * i], a.hi[4 * i + 1]), h01);
+    h23 = __ffma2_rn(u8x2_to_f32(hi, 2), make_float2(a.hi[4 * i + 2], a.hi[4 * i + 3]), h23);
   }
-  const float sl = (slo[0] + slo[1]) + (slo[2] + slo[3]), sh = (shi[0] + shi[1]) + (shi[2] + shi[3]);
+  const float sl = (l01.x + l01.y) + (l23.x + l23.y), sh = (h01.x + h01.y) + (h23.x + h23.y);
   const ChunkScales s = chunk_scales(w.hdr, chunk & 3);
   return (s.d1 * sl - s.m1 * a.slo) + (s.d2 * sh - s.m2 * a.shi);
+}
+
+// The decode kernels' name for the same dot.
+__device__ __forceinline__ float chunk_dot_ilp(const WChunk &w, int chunk, const LaneAct<ACT_F32> &a) {
+  return chunk_dot(w, chunk, a);
 }
 
 // Lanes per row, chunks per lane and tokens per pass for a given K.

@@ -1123,7 +1123,8 @@ __global__ void __launch_bounds__(RS_W * 32, 1) router_logits_staged_kernel(
     for (int c = 0; c < RG_CH && ok; ++c) {
       const int h0 = c * CH, h1 = min(H, h0 + CH);
       if (h0 >= h1) break;
-      if (!tc::mbar_wait(full + c, 0, RG_WAIT_LIMIT)) {
+      // usually landed already: a non-suspending test first
+      if (!tc::mbar_test_wait(full + c, 0) && !tc::mbar_wait(full + c, 0, RG_WAIT_LIMIT)) {
         ok = false;
         break;
       }
