@@ -338,6 +338,10 @@ size_t moe_scratch_bytes(const har_cuda_ctx *ctx, const har_cuda_moe_layer *laye
 int32_t run_moe_ffn_in(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const float *x,
                        int64_t T, int k, const int32_t *ids, const float *weights, float *y,
                        uint32_t flags, uint8_t *scratch);
+// The same with the shared expert on tokens sh0 .. sh0 + shT - 1 only.
+int32_t run_moe_ffn_range(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const float *x,
+                          int64_t T, int k, const int32_t *ids, const float *weights, float *y,
+                          uint32_t flags, uint8_t *S, int64_t sh0, int64_t shT);
 int32_t check_moe_args(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, int64_t T,
                        int32_t k, uint32_t flags);
 // The decode path (HAR_CUDA_MOE_DECODE, k_moe_decode.cu) on a scratch region.

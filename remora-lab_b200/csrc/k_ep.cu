@@ -11,17 +11,19 @@
 //      (d, t) carries x[t] and t's k slots as d-local expert ids (-1 where the
 //      expert lives elsewhere) with their routing weights.  Every rank sends
 //      exactly T rows to every rank (rows without a local expert carry stale
-//      data and are skipped), so no count exchange or host sync is needed and
+//      data and are skipped, except the rows a rank sends itself, which its
+//      shared expert reads), so no count exchange or host sync is needed and
 //      the whole layer can be captured in a CUDA graph;
 //   2. one grouped NCCL send/recv round moves the rows (x, ids, weights);
 //   3. the expert pipeline runs on the G*T received rows with the rank's shard
-//      (empty slots allowed, no shared expert, no residual): each row's output
-//      is the partial sum over its slots that live here;
+//      (empty slots allowed, no residual): each row's output is the partial
+//      sum over its slots that live here.  The shared expert is the
+//      pipeline's shared expert for the rank's own T rows among them (rows
+//      rank*T ..), weighted by sigmoid(gate_inp . x): its token tiles join the
+//      routed experts' tensor-core launches;
 //   4. a second round returns the partial sums to the tokens' ranks;
-//   5. the shared expert runs on the rank's own T tokens as a one-expert layer
-//      weighted by sigmoid(gate_inp . x) (ep_gate_kernel), and
-//      ep_combine_kernel adds the residual, the shared output and the G
-//      partial sums in rank order.
+//   5. ep_combine_kernel adds the residual and the G partial sums in rank
+//      order (the rank's own partial holds the shared expert).
 // Results match the single-GPU layer up to f32 summation order (the routed
 // terms are summed per rank, then across ranks).
 #include <nccl.h>
@@ -89,7 +91,7 @@ __global__ void __launch_bounds__(128) ep_plan_kernel(const float *__restrict__ 
                                                       const float *__restrict__ w, int T, int k,
                                                       int E, int El, float *__restrict__ sx,
                                                       int32_t *__restrict__ sids,
-                                                      float *__restrict__ sw, int *status) {
+                                                      float *__restrict__ sw, int keep, int *status) {
   const int d = blockIdx.x / T, t = blockIdx.x % T;
   const int64_t row = (int64_t)d * T + t;
   __shared__ int any;
@@ -108,26 +110,10 @@ __global__ void __launch_bounds__(128) ep_plan_kernel(const float *__restrict__ 
     sw[row * k + j] = loc >= 0 ? w[(int64_t)t * k + j] : 0.0f;
   }
   __syncthreads();
-  if (!any) return;
+  if (!any && d != keep) return;  // rows to `keep` always carry x (its shared expert reads them)
   const float4 *src = reinterpret_cast<const float4 *>(x + (int64_t)t * H);
   float4 *dst = reinterpret_cast<float4 *>(sx + row * H);
   for (int i = threadIdx.x; i < H / 4; i += blockDim.x) dst[i] = src[i];
-}
-
-// g[t] = sigmoid(gate_inp . x[t]) (1 without a gate row) and ids0[t] = 0: the
-// shared expert as the only slot of a one-expert layer.  One warp per token,
-// the same dot as the single-GPU layer's gate (shared_gate_warp).
-__global__ void __launch_bounds__(256) ep_gate_kernel(const float *__restrict__ x, int H, int T,
-                                                      const float *__restrict__ gi,
-                                                      float *__restrict__ g,
-                                                      int32_t *__restrict__ ids0) {
-  const int t = blockIdx.x * 8 + (int)(threadIdx.x >> 5), lane = threadIdx.x & 31;
-  if (t >= T) return;
-  const float v = gi ? shared_gate_warp(gi, x + (int64_t)t * H, H, lane) : 1.0f;
-  if (lane == 0) {
-    g[t] = v;
-    ids0[t] = 0;
-  }
 }
 
 // y[t] = (x[t] with the residual flag) + shared[t] (when given) + sum_d back[d][t].
@@ -154,7 +140,7 @@ namespace {
 size_t al256(size_t v) { return (v + 255) & ~(size_t)255; }
 
 struct EpLayout {
-  size_t sx, sids, sw, rx, rids, rw, part, back, ysh, g, ids0, total;
+  size_t sx, sids, sw, rx, rids, rw, part, back, total;
 };
 
 EpLayout ep_layout(int G, int64_t T, int k, int64_t H) {
@@ -170,9 +156,6 @@ EpLayout ep_layout(int G, int64_t T, int k, int64_t H) {
   L.rw = take(4 * rows * k);
   L.part = take(4 * rows * H);
   L.back = take(4 * rows * H);
-  L.ysh = take(4 * (size_t)T * H);
-  L.g = take(4 * (size_t)T);
-  L.ids0 = take(4 * (size_t)T);
   L.total = off;
   return L;
 }
@@ -216,25 +199,42 @@ int32_t ep_layer(har_cuda_ctx *ctx, har_cuda_ep *ep, const har_cuda_moe_layer *l
   if (st) return st;
   const uint32_t mode0 = flags & (HAR_CUDA_MOE_ACT_Q8K | HAR_CUDA_MOE_FORCE_GEMV |
                                   HAR_CUDA_MOE_FORCE_TC | HAR_CUDA_MOE_TC_F16W);
-  // Both expert calls of the layer share the context's scratch arena: size it
-  // for the larger one before the first launch, so the arena never grows (a
-  // synchronising reallocation) between the two calls.
-  {
-    size_t need = moe_scratch_bytes(ctx, local, (int64_t)G * T, k, mode0 | HAR_CUDA_MOE_EMPTY_SLOTS);
-    if (shared) need = std::max(need, moe_scratch_bytes(ctx, shared, T, 1, mode0));
-    if ((st = ensure_scratch(ctx, need))) return st;
+  // The shared expert joins the rank's routed experts as the layer's shared
+  // expert, serving only the rank's own rows among the received ones (rows
+  // rank*T .. rank*T + T - 1: every rank sends its T rows to every rank, this
+  // one included), so one expert pipeline covers both: its token tiles share
+  // the tensor-core launches with the routed tiles.
+  har_cuda_moe_layer comb;
+  const har_cuda_moe_layer *lay = local;
+  if (shared) {
+    comb.gate = local->gate;
+    comb.up = local->up;
+    comb.down = local->down;
+    comb.sh_gate = shared->gate;
+    comb.sh_up = shared->up;
+    comb.sh_down = shared->down;
+    comb.sh_gate_inp = gate_inp;
+    comb.E = local->E;
+    comb.H = local->H;
+    comb.I = local->I;
+    comb.tc_maps = local->tc_maps && shared->tc_maps;
+    comb.map_gate = local->map_gate;
+    comb.map_up = local->map_up;
+    comb.map_down = local->map_down;
+    comb.map_sh_gate = shared->map_gate;
+    comb.map_sh_up = shared->map_up;
+    comb.map_sh_down = shared->map_down;
+    lay = &comb;
   }
+  const uint32_t lmode = mode0 | HAR_CUDA_MOE_EMPTY_SLOTS;
+  if ((st = ensure_scratch(ctx, moe_scratch_bytes(ctx, lay, (int64_t)G * T, k, lmode)))) return st;
   uint8_t *B = (uint8_t *)ep->buf;
   float *sx = (float *)(B + L.sx), *sw = (float *)(B + L.sw), *rx = (float *)(B + L.rx);
   float *rw = (float *)(B + L.rw), *part = (float *)(B + L.part), *back = (float *)(B + L.back);
-  float *ysh = (float *)(B + L.ysh), *g = (float *)(B + L.g);
   int32_t *sids = (int32_t *)(B + L.sids), *rids = (int32_t *)(B + L.rids);
-  int32_t *ids0 = (int32_t *)(B + L.ids0);
-  const uint32_t mode = mode0;
   // Compute runs on ctx->stream, the exchanges on ep->cs; events order them:
-  // plan -> dispatch -> local experts -> return -> combine, with the shared
-  // expert (it needs only this rank's x) computing while the dispatch moves
-  // rows.  The same order holds under CUDA-graph capture (fork and join).
+  // plan -> dispatch -> experts -> return -> combine.  The same order holds
+  // under CUDA-graph capture (fork and join).
   auto join = [&](cudaStream_t from, cudaStream_t to, cudaEvent_t e) -> int32_t {
     if (cudaEventRecord(e, from) != cudaSuccess || cudaStreamWaitEvent(to, e, 0) != cudaSuccess)
       return set_error(ctx, HAR_CUDA_ERR_CUDA, "ep: stream ordering failed");
@@ -243,7 +243,8 @@ int32_t ep_layer(har_cuda_ctx *ctx, har_cuda_ep *ep, const har_cuda_moe_layer *l
   // 1. plan
   prof_begin(ctx);
   ep_plan_kernel<<<(unsigned)(G * T), 128, 0, ctx->stream>>>(x, (int)H, ids, w, (int)T, k, E, El,
-                                                            sx, sids, sw, ctx->d_status);
+                                                            sx, sids, sw, shared ? ep->rank : -1,
+                                                            ctx->d_status);
   if ((st = check_launch(ctx, "ep_plan_kernel"))) return st;
   if ((st = join(ctx->stream, ep->cs, ep->ev[0]))) return st;
   // 2. dispatch (exchange stream)
@@ -255,23 +256,15 @@ int32_t ep_layer(har_cuda_ctx *ctx, har_cuda_ep *ep, const har_cuda_moe_layer *l
   r = ncclGroupEnd();
   if (st) return st;
   if ((st = nccl_settle(ctx, &ep->comm, r, "ep dispatch", ep->op_timeout_ms))) return st;
-  // 3. the shared expert on the rank's tokens, meanwhile
-  if (shared) {
-    prof_begin(ctx);
-    ep_gate_kernel<<<(unsigned)((T + 7) / 8), 256, 0, ctx->stream>>>(x, (int)H, (int)T, gate_inp, g,
-                                                                     ids0);
-    if ((st = check_launch(ctx, "ep_gate_kernel"))) return st;
-    if ((st = run_moe_ffn(ctx, shared, x, T, 1, ids0, g, ysh, mode))) return st;
-  } else if (cudaMemsetAsync(ysh, 0, 4 * (size_t)T * H, ctx->stream) != cudaSuccess) {
-    return set_error(ctx, HAR_CUDA_ERR_CUDA, "ep: memset failed");
-  }
-  // 4. the rank's experts on the received rows: partial sums per row
+  // 3. the rank's experts on the received rows (partial sums per row), with
+  // the shared expert on the rank's own rows
   if ((st = join(ep->cs, ctx->stream, ep->ev[1]))) return st;
-  if ((st = run_moe_ffn(ctx, local, rx, (int64_t)G * T, k, rids, rw, part,
-                        mode | HAR_CUDA_MOE_EMPTY_SLOTS)))
+  if ((st = run_moe_ffn_range(ctx, lay, rx, (int64_t)G * T, k, rids, rw, part, lmode,
+                              (uint8_t *)ctx->scratch, shared ? (int64_t)ep->rank * T : 0,
+                              shared ? T : 0)))
     return st;
   if ((st = join(ctx->stream, ep->cs, ep->ev[2]))) return st;
-  // 5. return the partial sums (exchange stream)
+  // 4. return the partial sums (exchange stream)
   r = ncclGroupStart();
   if (r != ncclSuccess) return nccl_error(ctx, "ncclGroupStart", r);
   st = ep_all_to_all(ctx, ep, part, back, (size_t)T * H, ncclFloat32, 4);
@@ -279,10 +272,10 @@ int32_t ep_layer(har_cuda_ctx *ctx, har_cuda_ep *ep, const har_cuda_moe_layer *l
   if (st) return st;
   if ((st = nccl_settle(ctx, &ep->comm, r, "ep return", ep->op_timeout_ms))) return st;
   if ((st = join(ep->cs, ctx->stream, ep->ev[3]))) return st;
-  // 6. residual + shared + partials in rank order
+  // 5. residual + partials in rank order (this rank's holds the shared expert)
   prof_begin(ctx);
   ep_combine_kernel<<<(unsigned)T, 256, 0, ctx->stream>>>(
-      x, (int)H, (int)T, G, ysh, back, (flags & HAR_CUDA_MOE_ADD_RESIDUAL) ? 1 : 0, y);
+      x, (int)H, (int)T, G, nullptr, back, (flags & HAR_CUDA_MOE_ADD_RESIDUAL) ? 1 : 0, y);
   return check_launch(ctx, "ep_combine_kernel");
 }
 
@@ -432,7 +425,7 @@ int32_t har_cuda_ep_plan(har_cuda_ctx *ctx, const float *x_dev, int64_t H, int64
   prof_begin(ctx);
   ep_plan_kernel<<<(unsigned)(world * T), 128, 0, ctx->stream>>>(x_dev, (int)H, ids_dev, weights_dev,
                                                                 (int)T, k, E, E / world, sx_dev,
-                                                                sids_dev, sw_dev, ctx->d_status);
+                                                                sids_dev, sw_dev, -1, ctx->d_status);
   return check_launch(ctx, "ep_plan_kernel");
 }
 

@@ -42,6 +42,7 @@ struct MoeDev {
   int64_t xrow, arow;           // activation row bytes (f32 or Q8_K) for H and I
   int E, H, I, T, k, n;
   int has_shared;   // the layer has a shared expert (combine adds it)
+  int sh0, shT;     // it serves tokens sh0 .. sh0 + shT - 1 (slots n .. n + shT - 1)
   int gemv_shared;  // the shared expert runs on the CUDA-core path
   const int32_t *counts, *offsets, *order, *inv, *ne, *n_ne;
   const uint8_t *xact;  // x rows (f32) or their Q8_K image
@@ -54,10 +55,11 @@ struct MoeDev {
 // gsh[t] = sigmoid(gi . x[t]), one warp per token: the shared expert's gate,
 // computed before any kernel of the layer writes y (which may alias x).
 __global__ void __launch_bounds__(256) shared_gate_kernel(const float *__restrict__ gi,
-                                                          const float *__restrict__ x, int H, int T,
-                                                          float *__restrict__ gsh) {
-  const int t = blockIdx.x * 8 + (int)(threadIdx.x >> 5), lane = threadIdx.x & 31;
-  if (t >= T) return;
+                                                          const float *__restrict__ x, int H, int t0,
+                                                          int count, float *__restrict__ gsh) {
+  const int j = blockIdx.x * 8 + (int)(threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (j >= count) return;
+  const int t = t0 + j;
   const float g = shared_gate_warp(gi, x + (int64_t)t * H, H, lane);
   if (lane == 0) gsh[t] = g;
 }
@@ -74,7 +76,7 @@ __device__ __forceinline__ void group_info(const MoeDev &p, int gi, int nne, int
     base = p.offsets[g];
   } else {
     g = p.E;  // shared expert
-    cnt = p.T;
+    cnt = p.shT;
     base = p.n;
   }
 }
@@ -89,7 +91,7 @@ __device__ __forceinline__ void token_table(const MoeDev &p, int g, int cnt, int
     if (idx < cnt) {
       int s, tok;
       if (g == p.E) {
-        tok = idx;
+        tok = p.sh0 + idx;
         s = p.n + idx;
       } else {
         tok = p.order[base + idx] / p.k;
@@ -291,8 +293,8 @@ __global__ void __launch_bounds__(COMB_T) moe_combine_kernel(MoeDev p, const flo
       acc.w = __fadd_rn(acc.w, __fmul_rn(wv[j], v[j].w));
     }
   }
-  if (p.has_shared) {
-    const float4 v = yb4[(int64_t)(p.n + t) * H4 + h];
+  if (p.has_shared && t >= p.sh0 && t < p.sh0 + p.shT) {
+    const float4 v = yb4[(int64_t)(p.n + t - p.sh0) * H4 + h];
     acc.x = __fadd_rn(acc.x, __fmul_rn(g, v.x));
     acc.y = __fadd_rn(acc.y, __fmul_rn(g, v.y));
     acc.z = __fadd_rn(acc.z, __fmul_rn(g, v.z));
@@ -474,7 +476,23 @@ int32_t run_moe_ffn(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const fl
 int32_t run_moe_ffn_in(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const float *x,
                        int64_t T, int k, const int32_t *ids, const float *weights, float *y,
                        uint32_t flags, uint8_t *S) {
-  if (flags & HAR_CUDA_MOE_DECODE) return run_moe_decode(ctx, layer, x, T, k, ids, weights, y, flags, S);
+  return run_moe_ffn_range(ctx, layer, x, T, k, ids, weights, y, flags, S, 0, T);
+}
+
+// The same with the shared expert serving only tokens sh0 .. sh0 + shT - 1 of
+// the call (the expert-parallel local layer: the shared expert runs on the
+// rank's own rows among the received ones); the other tokens get the routed
+// sum alone.
+int32_t run_moe_ffn_range(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const float *x,
+                          int64_t T, int k, const int32_t *ids, const float *weights, float *y,
+                          uint32_t flags, uint8_t *S, int64_t sh0, int64_t shT) {
+  if (flags & HAR_CUDA_MOE_DECODE) {
+    if (sh0 != 0 || shT != T)
+      return set_error(ctx, HAR_CUDA_ERR_UNSUPPORTED, "moe_ffn: the decode path serves the shared expert on every token");
+    return run_moe_decode(ctx, layer, x, T, k, ids, weights, y, flags, S);
+  }
+  if (sh0 < 0 || shT < 0 || sh0 + shT > T)
+    return set_error(ctx, HAR_CUDA_ERR_ARG, "moe_ffn: shared-expert token range outside the call");
   if (((uintptr_t)x & 15u) || ((uintptr_t)y & 15u))
     return set_error(ctx, HAR_CUDA_ERR_ARG, "moe_ffn: x and y must be 16-byte aligned");
   const bool q8 = (flags & HAR_CUDA_MOE_ACT_Q8K) != 0;
@@ -485,7 +503,7 @@ int32_t run_moe_ffn_in(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const
   const bool tc = tc_possible(ctx, layer, T, k, flags);
   const bool f16w = (flags & HAR_CUDA_MOE_TC_F16W) != 0;  // the f16-weight tensor-core variant
   const int thr = tc ? tc_threshold(ctx, flags, T) : INT_MAX;
-  const bool shared_tc = has_sh && tc && T >= thr;
+  const bool shared_tc = has_sh && tc && shT >= thr;
   if (tc && ((H % TC_M) || (I % TC_M) || (H % TC_KS) || (I % TC_KS)))
     return set_error(ctx, HAR_CUDA_ERR_UNSUPPORTED,
                      "moe_ffn: the tensor-core path needs H and I multiples of 128");
@@ -511,8 +529,10 @@ int32_t run_moe_ffn_in(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const
   p.T = (int)T;
   p.k = k;
   p.n = (int)n;
-  p.has_shared = has_sh;
-  p.gemv_shared = has_sh && !shared_tc;
+  p.has_shared = has_sh && shT > 0;
+  p.sh0 = (int)sh0;
+  p.shT = (int)shT;
+  p.gemv_shared = has_sh && shT > 0 && !shared_tc;
   p.counts = (const int32_t *)(S + o_counts);
   p.offsets = (const int32_t *)(S + o_offsets);
   p.order = (const int32_t *)(S + o_order);
@@ -539,7 +559,7 @@ int32_t run_moe_ffn_in(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const
   st = launch_group_full(ctx, ids, n, E, (int32_t *)(S + o_counts), (int32_t *)(S + o_offsets),
                          (int32_t *)(S + o_order), (int32_t *)(S + o_inv), (int32_t *)(S + o_ne),
                          (int32_t *)(S + o_nne), thr, TC_NT, (int2 *)(S + L.o_ttinfo),
-                         (int32_t *)(S + L.o_ntt), shared_tc ? (int)T : 0,
+                         (int32_t *)(S + L.o_ntt), shared_tc ? (int)shT : 0,
                          (flags & HAR_CUDA_MOE_EMPTY_SLOTS) ? 1 : 0,
                          L.o_gcnt ? (int32_t *)(S + L.o_gcnt) : nullptr);
   if (st) return st;
@@ -590,25 +610,25 @@ int32_t run_moe_ffn_in(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const
         return st;
     }
     if ((st = launch_gather_f16(ctx, x, H, p.order, ids, p.counts, p.offsets + E, thr, (int)n, k,
-                                (int)T, tp.shared_tc, (__half *)(S + L.o_x16), (__half *)(S + L.o_xs16),
+                                (int)sh0, (int)shT, tp.shared_tc, (__half *)(S + L.o_x16), (__half *)(S + L.o_xs16),
                                 tp.shared_tc ? layer->sh_gate_inp : nullptr, (float *)(S + L.o_gsh))))
       return st;
   }
-  if (gate_row && !(tc && shared_tc)) {
+  if (gate_row && shT > 0 && !(tc && shared_tc)) {
     prof_begin(ctx);
-    shared_gate_kernel<<<(unsigned)((T + 7) / 8), 256, 0, ctx->stream>>>(layer->sh_gate_inp, x, H, (int)T,
-                                                                        (float *)(S + L.o_gsh));
+    shared_gate_kernel<<<(unsigned)((shT + 7) / 8), 256, 0, ctx->stream>>>(layer->sh_gate_inp, x, H, (int)sh0,
+                                                                          (int)shT, (float *)(S + L.o_gsh));
     if ((st = check_launch(ctx, "shared_gate_kernel"))) return st;
   }
   // upper bound of tensor-core token tiles: each big expert has >= thr tokens
   const int64_t max_tc_tt =
-      tc ? std::min<int64_t>(E, n / std::max(thr, 1)) + n / TC_NT + 2 + (shared_tc ? T / TC_NT + 1 : 0) : 0;
+      tc ? std::min<int64_t>(E, n / std::max(thr, 1)) + n / TC_NT + 2 + (shared_tc ? shT / TC_NT + 1 : 0) : 0;
   if (q8 && (st = launch_q8k_quantize(ctx, x, T, H, S + o_xq))) return st;
-  const int max_groups = (int)std::min<int64_t>(E, n) + has_sh;
+  const int max_groups = (int)std::min<int64_t>(E, n) + p.has_shared;
   const int grid_cap = ctx->num_sms * 4;
   // the CUDA-core kernels have work unless every non-empty expert (threshold 1)
   // and the shared expert take the tensor-core path
-  const bool gemv_work = !tc || thr > 1 || (has_sh && !shared_tc);
+  const bool gemv_work = !tc || thr > 1 || p.gemv_shared;
   if (gemv_work) {
     const int rpt = rows_per_tile_gu(H), ntg = (I + rpt - 1) / rpt;
     const int grid = std::max(1, std::min(grid_cap, max_groups * ntg));
@@ -630,7 +650,7 @@ int32_t run_moe_ffn_in(har_cuda_ctx *ctx, const har_cuda_moe_layer *layer, const
               : launch_moe_tc(ctx, gmaps, g, 2, (int)std::min<int64_t>(INT_MAX, max_tc_tt * (I / TC_M)));
     if (st) return st;
   }
-  if (q8 && (st = launch_q8k_quantize(ctx, p.a, n + (has_sh ? T : 0), I, S + o_aq))) return st;
+  if (q8 && (st = launch_q8k_quantize(ctx, p.a, n + (p.has_shared ? shT : 0), I, S + o_aq))) return st;
   if (gemv_work) {
     const int rpt = rows_per_tile_d(I), ntg = (H + rpt - 1) / rpt;
     const int grid = std::max(1, std::min(grid_cap, max_groups * ntg));

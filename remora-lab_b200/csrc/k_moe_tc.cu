@@ -554,23 +554,23 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
 // xg[2 slot] = hi = f16(x[token of slot]) and xg[2 slot + 1] = f16(x - hi),
 // K order (0, 2, 1, 3) inside each group of four (the weight operand's order),
 // for every slot whose expert runs on the tensor-core path: routed slot s holds entry order[s] (token order[s] / k,
-// expert ids[order[s]]); slot n + t is the shared expert's row of token t.
+// expert ids[order[s]]); slot n + j is the shared expert's row of token sh0 + j (j < shT).
 // Rows 2 slot and 2 slot + 1 of xs16 [2 slots][H/16] get the f16 hi and lo of
 // the slot's 32-value sub-block sums, each twice: the min-term operand.
 // Slots of CUDA-core experts are skipped.  One warp per slot, GATHER_WARPS
 // slots per block: the slot's index chain (order -> ids -> counts) of several
-// slots is in flight at once.  The warp of shared slot n + t also writes the
+// slots is in flight at once.  The warp of a shared slot also writes the
 // shared expert's gate gsh[t] = sigmoid(gi . x[t]) when gi is given.
 constexpr int GATHER_WARPS = 8;
 
 __global__ void __launch_bounds__(GATHER_WARPS * 32) gather_f16_kernel(
     const float *__restrict__ x, int H, const int32_t *__restrict__ order,
     const int32_t *__restrict__ ids, const int32_t *__restrict__ counts,
-    const int32_t *__restrict__ n_valid, int thr, int n, int k, int T, int shared_tc,
+    const int32_t *__restrict__ n_valid, int thr, int n, int k, int sh0, int shT, int shared_tc,
     __half *__restrict__ xg, __half *__restrict__ xs16, const float *__restrict__ gi,
     float *__restrict__ gsh, int *status) {
   const int slot = blockIdx.x * GATHER_WARPS + (int)(threadIdx.x >> 5), lane = threadIdx.x & 31;
-  if (slot >= n + T) return;
+  if (slot >= n + shT) return;
   int tok;
   if (slot < n) {
     // grouped positions past the valid entries (those with an out-of-range
@@ -581,7 +581,7 @@ __global__ void __launch_bounds__(GATHER_WARPS * 32) gather_f16_kernel(
     tok = entry / k;
   } else {
     if (!shared_tc) return;
-    tok = slot - n;
+    tok = sh0 + (slot - n);
   }
   const float4 *src = reinterpret_cast<const float4 *>(x + (int64_t)tok * H);
   uint2 *dhi = reinterpret_cast<uint2 *>(xg + 2 * (int64_t)slot * H);
@@ -620,13 +620,14 @@ __global__ void __launch_bounds__(GATHER_WARPS * 32) gather_f16_kernel(
 
 int32_t launch_gather_f16(har_cuda_ctx *ctx, const float *x, int H, const int32_t *order,
                           const int32_t *ids, const int32_t *counts, const int32_t *n_valid,
-                          int thr, int n, int k, int T, int shared_tc, __half *xg, __half *xs16,
-                          const float *gi, float *gsh) {
+                          int thr, int n, int k, int sh0, int shT, int shared_tc, __half *xg,
+                          __half *xs16, const float *gi, float *gsh) {
   int *status = ctx->d_status;
   prof_begin(ctx);
-  const unsigned grid = (unsigned)((n + T + GATHER_WARPS - 1) / GATHER_WARPS);
+  const unsigned grid = (unsigned)((n + shT + GATHER_WARPS - 1) / GATHER_WARPS);
   gather_f16_kernel<<<grid, GATHER_WARPS * 32, 0, ctx->stream>>>(x, H, order, ids, counts, n_valid, thr,
-                                                                n, k, T, shared_tc, xg, xs16, gi, gsh, status);
+                                                                n, k, sh0, shT, shared_tc, xg, xs16, gi, gsh,
+                                                                status);
   return check_launch(ctx, "gather_f16_kernel");
 }
 

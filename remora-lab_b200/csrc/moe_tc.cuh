@@ -70,7 +70,7 @@ int32_t launch_moe_tc_f16w(har_cuda_ctx *ctx, const TcMaps &maps, const TcParams
 // n_valid = the number of grouped entries (offsets[E]); later routed slots are empty.
 int32_t launch_gather_f16(har_cuda_ctx *ctx, const float *x, int H, const int32_t *order,
                           const int32_t *ids, const int32_t *counts, const int32_t *n_valid,
-                          int thr, int n, int k, int T, int shared_tc, __half *xg, __half *xs16,
+                          int thr, int n, int k, int sh0, int shT, int shared_tc, __half *xg, __half *xs16,
                           const float *gi, float *gsh);
 
 }  // namespace har
