@@ -435,24 +435,26 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_tc_kernel(const __grid_cons
           if (NA == 2) dm1 = __ldg(reinterpret_cast<const uint32_t *>(hp1 + (int64_t)(b + 1) * Q4K_BYTES));
         }
         for (int u = 0; ok && u < nq; ++u)
-          ok = tc_wait_warp(acc_full + q0 + u, (par >> (q0 + u)) & 1u, abort_s, lane, 128);
+          ok = tc_wait_warp(acc_full + q0 + u, (par >> (q0 + u)) & 1u, abort_s, lane, 32);
         if (!ok) break;
         tc::tc_fence_after();
         const uint32_t dcol = tmem + lane_addr + (uint32_t)(q0 * 64) + (uint32_t)(32 * h);
+        const float sb0 = tc_unit_scale(cd0).s, sb1 = NA == 2 ? tc_unit_scale(cd1).s : 0.0f;
 #pragma unroll
-        for (int m = 0; m < NA; ++m) {
-          const float sb = tc_unit_scale(m == 0 ? cd0 : cd1).s;
+        for (int c4 = 0; c4 < 4; ++c4) {
+          if (4 * c4 >= nmine) break;  // warp-uniform
+          // tokens 4c4 .. 4c4+3 (hi, lo) of every matrix: one TMEM round trip per group
+          uint32_t v[NA][8];
 #pragma unroll
-          for (int c4 = 0; c4 < 4; ++c4) {
-            if (4 * c4 >= nmine) break;  // warp-uniform
-            uint32_t v[8];
-            tc::tmem_ld8(dcol + (uint32_t)(m * bw + 8 * c4), v);  // tokens 4c4 .. 4c4+3: hi, lo
-            tc::tmem_wait_ld();
+          for (int m = 0; m < NA; ++m) tc::tmem_ld8(dcol + (uint32_t)(m * bw + 8 * c4), v[m]);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int m = 0; m < NA; ++m)
 #pragma unroll
             for (int c = 0; c < 4; ++c)
-              acc[m][4 * c4 + c] =
-                  fmaf(sb, __uint_as_float(v[2 * c]) + __uint_as_float(v[2 * c + 1]), acc[m][4 * c4 + c]);
-          }
+              acc[m][4 * c4 + c] = fmaf(m == 0 ? sb0 : sb1,
+                                        __uint_as_float(v[m][2 * c]) + __uint_as_float(v[m][2 * c + 1]),
+                                        acc[m][4 * c4 + c]);
         }
         tc::tc_fence_before();
         __syncwarp();
