@@ -315,18 +315,28 @@ int32_t har_cuda_gguf_read_f32(har_cuda_ctx *ctx, har_cuda_gguf *g, const char *
 int32_t har_cuda_moe_layer_from_gguf(har_cuda_ctx *ctx, har_cuda_gguf *g, int32_t layer,
                                      har_cuda_moe_layer **out);
 
-/* ---- expert parallelism over the GPUs of one box (NCCL over NVLink) ----------------------
+/* ---- expert parallelism over the GPUs of one box (NVLink peer memory, NCCL) --------------
  * No counterpart in the reference, which runs every expert on one CPU
  * (compose_moe_route, har-native-qwen35moe.rs:979-1048): this is the router-to-
  * expert dispatch of a sharded deployment.  Rank r of G holds the routed experts
  * [r*E/G, (r+1)*E/G) of every layer as a `local` layer (no shared expert) and the
  * shared expert as a one-expert `shared` layer (replicated on every rank), plus
  * the shared expert's gate row.  Per layer: token rows go to the ranks holding
- * their experts (one grouped NCCL send/recv round), each rank runs its experts,
- * partial sums come back (a second round), and the tokens' rank adds residual,
- * shared expert and partial sums.  Results equal har_cuda_moe_ffn on the
- * unsharded layer up to f32 summation order.  All ranks call collectively with
- * the same T, k and flags (ADD_RESIDUAL, ACT_Q8K, FORCE_*). */
+ * their experts, each rank runs its experts, partial sums come back, and the
+ * tokens' rank adds residual, shared expert and partial sums.  Results equal
+ * har_cuda_moe_ffn on the unsharded layer up to f32 summation order.  All
+ * ranks call collectively with the same T, k and flags (ADD_RESIDUAL,
+ * ACT_Q8K, FORCE_*).
+ * The rows move through peer memory by default: every rank's exchange window
+ * is mapped into the other ranks by CUDA IPC on the first call (collective;
+ * again when a call needs a larger window, and that call must not be under
+ * graph capture), and each rank pulls over NVLink the token rows that have an
+ * expert of its own and the partial sums of its own tokens, synchronised by
+ * epoch flags whose waits give up after the communicator's timeout (the next
+ * har_cuda_synchronize then returns HAR_CUDA_ERR_TIMEOUT, and the
+ * communicator should be aborted).
+ * When any rank cannot map every window (ranks sharing a GPU, no peer access)
+ * all ranks use two grouped NCCL send/recv rounds instead. */
 /* The two device steps of the exchange on their own, without a communicator:
  * for callers that move the rows with their own transport, and for checking
  * the plan and the combine on one GPU.
@@ -367,7 +377,17 @@ int32_t har_cuda_ep_create_timeout(har_cuda_ctx *ctx, const uint8_t *unique_id, 
  * whose peer is gone); later EP calls on it return HAR_CUDA_ERR_NOT_INIT.  The
  * handle still needs har_cuda_ep_free. */
 int32_t har_cuda_ep_abort(har_cuda_ep *ep);
+/* Collective when windows were mapped (every rank calls it): unmaps the peers'
+ * windows, then frees this rank's after a barrier over the communicator
+ * (without one — aborted, or a rank gone — the window stays allocated). */
 int32_t har_cuda_ep_free(har_cuda_ep *ep);
+/* Choose the transport of later calls: on != 0 peer memory where every rank
+ * can map every window (the default), 0 the NCCL rounds.  Call it with the
+ * same value on every rank. */
+int32_t har_cuda_ep_set_p2p(har_cuda_ep *ep, int32_t on);
+/* The transport of the last call: 1 peer memory, 0 NCCL (chosen, or not yet
+ * set up), -1 NCCL because some rank could not map the windows. */
+int32_t har_cuda_ep_exchange_mode(const har_cuda_ep *ep);
 /* One layer; ids are global expert ids [T][k] of this rank's T tokens. */
 int32_t har_cuda_ep_moe_ffn(har_cuda_ctx *ctx, har_cuda_ep *ep, const har_cuda_moe_layer *local,
                             const har_cuda_moe_layer *shared, const float *gate_inp_dev,

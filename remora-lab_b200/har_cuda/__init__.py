@@ -69,7 +69,8 @@ EXPORTS = [
     "har_cuda_profile_end", "har_cuda_moe_ffn_noalloc", "har_cuda_ctx_set_tc_min_tokens",
     "har_cuda_ep_unique_id", "har_cuda_ep_create", "har_cuda_ep_free", "har_cuda_ep_moe_ffn",
     "har_cuda_ep_moe_stack", "har_cuda_ep_plan", "har_cuda_ep_combine",
-    "har_cuda_ep_create_timeout", "har_cuda_ep_abort",
+    "har_cuda_ep_create_timeout", "har_cuda_ep_abort", "har_cuda_ep_set_p2p",
+    "har_cuda_ep_exchange_mode",
     "har_cuda_slot_table_create", "har_cuda_slot_table_free", "har_cuda_slot_table_storage",
     "har_cuda_slot_table_last_error", "har_cuda_slot_reserve", "har_cuda_slot_mark_upload_submitted",
     "har_cuda_slot_upload", "har_cuda_slot_mark_ready", "har_cuda_slot_acquire",
@@ -139,6 +140,8 @@ def load_library() -> C.CDLL:
         "har_cuda_ep_free": (i32, [vp]),
         "har_cuda_ep_create_timeout": (i32, [vp, vp, C.c_size_t, i32, i32, i64, pp]),
         "har_cuda_ep_abort": (i32, [vp]),
+        "har_cuda_ep_set_p2p": (i32, [vp, i32]),
+        "har_cuda_ep_exchange_mode": (i32, [vp]),
         "har_cuda_ep_moe_ffn": (i32, [vp, vp, vp, vp, vp, vp, i64, i32, vp, vp, vp, u32]),
         "har_cuda_ep_moe_stack": (i32, [vp, vp, vp, vp, vp, i32, vp, i64, i32, vp, vp, vp, u32]),
         "har_cuda_ep_plan": (i32, [vp, vp, i64, i64, i32, vp, vp, i32, i32, vp, vp, vp]),
@@ -564,11 +567,23 @@ def expert_range(E: int, world: int, rank: int):
 
 
 class EpComm:
-    """An expert-parallel NCCL communicator (one per rank and context); free it
-    explicitly, on every rank, after the last collective call."""
+    """An expert-parallel communicator (one per rank and context): NCCL, plus
+    the peer-memory windows mapped on first use; free it explicitly, on every
+    rank, after the last collective call (the free is collective too)."""
 
     def __init__(self, ctx: "Context", handle, world: int, rank: int):
         self.ctx, self.handle, self.world, self.rank = ctx, handle, world, rank
+
+    def set_p2p(self, on: bool):
+        """Peer-memory exchange (default) or the NCCL rounds; same value on every rank."""
+        st = self.ctx.lib.har_cuda_ep_set_p2p(self.handle, 1 if on else 0)
+        if st != 0:
+            raise HarCudaError(st, "ep_set_p2p failed")
+
+    @property
+    def exchange_mode(self) -> int:
+        """1 peer memory, 0 NCCL (chosen or not yet set up), -1 NCCL (windows unmappable)."""
+        return int(self.ctx.lib.har_cuda_ep_exchange_mode(self.handle))
 
     def abort(self):
         """Abort the communicator (its in-flight exchanges end with an error)."""
