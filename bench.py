@@ -9,8 +9,8 @@ per layer; residual add between layers (y = x + moe(x), as execute_layer_cpu).
 A step is one pass of the 256 tokens through all 48 layers.  With N GPUs
 (torchrun) each rank has its own 256 tokens and holds 512/N experts of every
 layer (expert parallelism: token rows go to the experts' GPUs and partial sums
-come back, pulled over NVLink from the ranks' IPC-mapped windows, or over
-NCCL with --ep-nccl); the job's tokens grow with N ("scaling": "weak").
+come back over NCCL, or pulled over NVLink from the ranks' IPC-mapped windows
+with --ep-p2p); the job's tokens grow with N ("scaling": "weak").
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                   [--config 1..5] [--act f32|q8k]
@@ -67,9 +67,9 @@ def parse():
     ap.add_argument("--tc-f16w", action="store_true",
                     help="run the opt-in f16-weight tensor-core variant (HAR_CUDA_MOE_TC_F16W) "
                          "as the timed path")
-    ap.add_argument("--ep-nccl", action="store_true",
-                    help="with N > 1: move the expert-parallel rows with NCCL send/recv instead "
-                         "of peer memory")
+    ap.add_argument("--ep-p2p", action="store_true",
+                    help="with N > 1: move the expert-parallel rows through peer memory (CUDA IPC "
+                         "windows over NVLink) instead of NCCL send/recv")
     ap.add_argument("--profile-only", action="store_true",
                     help="run warm-up + a few steps only (for ncu launch lists)")
     ap.add_argument("--routed-decode", action="store_true",
@@ -334,14 +334,14 @@ def run_ours(args, torch):
     ep = None
     if world > 1:
         # expert parallelism: this rank's expert shard; rows exchanged through
-        # peer memory (or NCCL with --ep-nccl)
+        # NCCL (or peer memory with --ep-p2p)
         locals_, shareds, gates, keep, x, ids, w, distinct, local_distinct = build_ep_stack(
             ctx, torch, args.config, rank, world)
         box = [har_cuda.ep_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(box, src=0)
         ep = ctx.ep_create(box[0], world, rank, timeout_ms=60000)
-        if args.ep_nccl:
-            ep.set_p2p(False)
+        if args.ep_p2p:
+            ep.set_p2p(True)
         L = len(locals_)
     else:
         layers, keep, x, ids, w, distinct = build_stack(ctx, torch, args.config, rank, args.layers)

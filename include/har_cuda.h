@@ -327,8 +327,10 @@ int32_t har_cuda_moe_layer_from_gguf(har_cuda_ctx *ctx, har_cuda_gguf *g, int32_
  * har_cuda_moe_ffn on the unsharded layer up to f32 summation order.  All
  * ranks call collectively with the same T, k and flags (ADD_RESIDUAL,
  * ACT_Q8K, FORCE_*).
- * The rows move through peer memory by default: every rank's exchange window
- * is mapped into the other ranks by CUDA IPC on the first call (collective;
+ * By default the rows move in two grouped NCCL send/recv rounds.  With
+ * har_cuda_ep_set_p2p(ep, 1) they move through peer memory instead: every
+ * rank's exchange window is mapped into the other ranks by CUDA IPC on the
+ * first call (collective;
  * again when a call needs a larger window, and that call must not be under
  * graph capture), and each rank pulls over NVLink the token rows that have an
  * expert of its own and the partial sums of its own tokens, synchronised by
@@ -336,7 +338,7 @@ int32_t har_cuda_moe_layer_from_gguf(har_cuda_ctx *ctx, har_cuda_gguf *g, int32_
  * har_cuda_synchronize then returns HAR_CUDA_ERR_TIMEOUT, and the
  * communicator should be aborted).
  * When any rank cannot map every window (ranks sharing a GPU, no peer access)
- * all ranks use two grouped NCCL send/recv rounds instead. */
+ * all ranks keep the NCCL rounds. */
 /* The two device steps of the exchange on their own, without a communicator:
  * for callers that move the rows with their own transport, and for checking
  * the plan and the combine on one GPU.
@@ -382,7 +384,7 @@ int32_t har_cuda_ep_abort(har_cuda_ep *ep);
  * (without one — aborted, or a rank gone — the window stays allocated). */
 int32_t har_cuda_ep_free(har_cuda_ep *ep);
 /* Choose the transport of later calls: on != 0 peer memory where every rank
- * can map every window (the default), 0 the NCCL rounds.  Call it with the
+ * can map every window, 0 the NCCL rounds (the default).  Call it with the
  * same value on every rank. */
 int32_t har_cuda_ep_set_p2p(har_cuda_ep *ep, int32_t on);
 /* The transport of the last call: 1 peer memory, 0 NCCL (chosen, or not yet

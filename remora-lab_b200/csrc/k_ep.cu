@@ -51,7 +51,7 @@ struct har_cuda_ep {
   // Peer-memory exchange: every rank's window (flags, staged token rows, the
   // partial sums it computes) is mapped into every other rank's address space
   // by CUDA IPC, and the rows move by loads over NVLink instead of NCCL.
-  int p2p = 1;          // requested (har_cuda_ep_set_p2p); the windows are set up on first use
+  int p2p = 0;          // requested (har_cuda_ep_set_p2p, opt-in); the windows are set up on first use
   int p2p_state = 0;    // 0 not set up, 1 mapped on every rank, -1 some rank could not (NCCL only)
   void *win = nullptr;  // this rank's window
   size_t win_bytes = 0;

@@ -575,7 +575,7 @@ class EpComm:
         self.ctx, self.handle, self.world, self.rank = ctx, handle, world, rank
 
     def set_p2p(self, on: bool):
-        """Peer-memory exchange (default) or the NCCL rounds; same value on every rank."""
+        """Peer-memory exchange (opt-in) or the NCCL rounds (default); same value on every rank."""
         st = self.ctx.lib.har_cuda_ep_set_p2p(self.handle, 1 if on else 0)
         if st != 0:
             raise HarCudaError(st, "ep_set_p2p failed")

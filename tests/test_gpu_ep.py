@@ -1,9 +1,9 @@
 """Expert parallelism on two GPUs of one box (har_cuda_ep_moe_ffn / _stack).
 
 Each rank holds half of the routed experts and the shared expert; its tokens
-go to the experts' ranks and their partial sums come back, through peer
-memory (the default: windows mapped by CUDA IPC, rows pulled over NVLink) or
-the NCCL rounds.  Per rank, the result must equal the unsharded layer run on
+go to the experts' ranks and their partial sums come back, through the NCCL
+rounds (the default) or peer memory (windows mapped by CUDA IPC, rows pulled
+over NVLink).  Per rank, the result must equal the unsharded layer run on
 that GPU alone (har_cuda_moe_ffn / _moe_stack) up to f32 summation order, and
 the two transports must agree exactly (the same rows reach the same expert
 launches; the peer path only leaves out the zero partial sums).  Runs as two
@@ -100,8 +100,7 @@ def worker(rank, world, port, q):
             err = float(np.abs(a - b).max() / np.abs(b).max())
             errs.append(err)
             assert err < 1e-5, (flags, "stack", err)
-        mode = ep.exchange_mode
-        assert mode in (1, -1), mode  # peer memory, or NCCL where the windows cannot be mapped
+        assert ep.exchange_mode == 0
         # the two transports on the same stack, both twice (windows and flags reused)
         outs = {}
         for p2p in (False, True, False, True):
@@ -111,6 +110,8 @@ def worker(rank, world, port, q):
             torch.cuda.synchronize()
             ctx.synchronize()
             outs.setdefault(p2p, []).append(yo.cpu().numpy())
+        mode = ep.exchange_mode
+        assert mode in (1, -1), mode  # peer memory, or NCCL where the windows cannot be mapped
         for p2p, ys_ in outs.items():
             assert np.array_equal(ys_[0], ys_[1]), ("repeat", p2p)
         assert np.array_equal(outs[False][0], outs[True][0]), "peer memory and NCCL differ"

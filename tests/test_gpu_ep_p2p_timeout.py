@@ -45,6 +45,7 @@ def worker(rank, world, port, q):
         box = [har_cuda.ep_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(box, src=0)
         ep = ctx.ep_create(box[0], world, rank, timeout_ms=TIMEOUT_MS)
+        ep.set_p2p(True)
         lo, hi = har_cuda.expert_range(E, world, rank)
         El = hi - lo
 
