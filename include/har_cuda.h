@@ -107,11 +107,13 @@ int32_t har_cuda_weights_wrap_q4k(har_cuda_ctx *ctx, const void *dev_bytes, int6
                                   int64_t N, int64_t K, har_cuda_weights **out);
 /* Any supported GGML block type: the type ids HAR's GGUF reader matches
  * (har/crates/har-demo/src/bin/har-native-qwen35moe.rs:37-41), rows of
- * K/256 super-blocks (Q4_K 144 B, Q6_K 210 B; row_bytes_for_type, :176-199),
- * laid out [E][N][K/256] like the GGUF expert tensors.  Each entry point
- * accepts only the type it computes on (HAR_CUDA_ERR_UNSUPPORTED otherwise):
- * Q4_K for the Q4_K GEMV and the MoE layers, Q6_K for har_cuda_q6k_gemv. */
+ * K/256 super-blocks (Q4_K 144 B, Q6_K 210 B; row_bytes_for_type, :176-199;
+ * Q3_K 110 B, har/crates/har-model/src/lib.rs:591), laid out [E][N][K/256]
+ * like the GGUF expert tensors.  Each entry point accepts only the type it
+ * computes on (HAR_CUDA_ERR_UNSUPPORTED otherwise): Q4_K for the Q4_K GEMV and
+ * the MoE layers, Q6_K for har_cuda_q6k_gemv, Q3_K for har_cuda_q3k_gemv. */
 #define HAR_CUDA_GGML_F32 0
+#define HAR_CUDA_GGML_Q3_K 11
 #define HAR_CUDA_GGML_Q4_K 12
 #define HAR_CUDA_GGML_Q6_K 14
 int32_t har_cuda_weights_upload(har_cuda_ctx *ctx, int32_t ggml_type, const void *host_bytes,
@@ -146,6 +148,16 @@ int32_t har_cuda_q4k_gemv(har_cuda_ctx *ctx, const har_cuda_weights *w, int64_t 
  * as NativeQwen35Moe::matvec reaches it for Q6_K tensors
  * (har/crates/har-demo/src/bin/har-native-qwen35moe.rs:551-556,583-624). */
 int32_t har_cuda_q6k_gemv(har_cuda_ctx *ctx, const har_cuda_weights *w, int64_t expert,
+                          const float *x_dev, int64_t M, float *y_dev);
+
+/* ---- Q3_K GEMV --------------------------------------------------------------
+ * y[m][n] = sum_k W_e[n][k] * x[m][k] for Q3_K weights and f32 activations
+ * x_dev [M][K] (16-byte aligned); y_dev f32 [M][N].  The reference records
+ * Q3_K's geometry only (GGML type 11, 110 B per 256 values,
+ * har/crates/har-model/src/lib.rs:591) and no arithmetic; the block layout is
+ * GGUF's: hmask[32] (high bits), qs[64] (2-bit planes), 12 bytes of packed
+ * 6-bit sub-block scales (offset 32), f16 d. */
+int32_t har_cuda_q3k_gemv(har_cuda_ctx *ctx, const har_cuda_weights *w, int64_t expert,
                           const float *x_dev, int64_t M, float *y_dev);
 
 /* ---- router top-k ---------------------------------------------------------

@@ -261,6 +261,51 @@ float haro_dot_quant_row_q6k(const uint8_t *row, const float *input, int64_t k) 
     return sum;
 }
 
+/* ---- Q3_K (f3; parity unpinned: the reference holds only the geometry,
+ * har/crates/har-model/src/lib.rs:591; the layout restated is GGUF's, as
+ * ggml's k-quants define it) ------------------------------------------------ */
+
+/* 16 six-bit scales in 12 bytes: the low four bits of scale s sit in byte
+ * s (s < 8, low nibble) or byte s - 8 (high nibble); its top two bits in
+ * byte 8 + s % 4 at bit 2 * (s / 4). */
+int haro_q3k_scale(const uint8_t *sc, int s) {
+    const int low = s < 8 ? (sc[s] & 0x0f) : (sc[s - 8] >> 4);
+    const int high = (sc[8 + (s & 3)] >> (2 * (s >> 2))) & 3;
+    return low | (high << 4);
+}
+
+void haro_q3k_dequant_block(const uint8_t *block, float out[256]) {
+    const uint8_t *hmask = block, *qs = block + 32, *sc = block + 96;
+    const float d = haro_half_to_f32((uint16_t)(block[108] | (block[109] << 8)));
+    for (int n = 0; n < 2; ++n)
+        for (int j = 0; j < 4; ++j)
+            for (int l = 0; l < 32; ++l) {
+                const int s = 8 * n + 2 * j + l / 16;
+                const float dl = d * (float)(haro_q3k_scale(sc, s) - 32);
+                const int q2 = (qs[32 * n + l] >> (2 * j)) & 3;
+                const int hi = (hmask[l] >> (4 * n + j)) & 1;
+                out[128 * n + 32 * j + l] = dl * (float)(q2 - (hi ? 0 : 4));
+            }
+}
+
+float haro_q3k_dot(const uint8_t *block, const float *input) {
+    float w[256];
+    haro_q3k_dequant_block(block, w);
+    float sum = 0.0f;
+    for (int i = 0; i < 256; ++i) sum += w[i] * input[i];
+    return sum;
+}
+
+void haro_q3k_matvec(const uint8_t *w, int64_t rows, int64_t k, const float *x, float *out) {
+    const int64_t rb = k / HARO_QK_K * HARO_Q3K_BLOCK_BYTES;
+    for (int64_t r = 0; r < rows; ++r) {
+        float sum = 0.0f;
+        for (int64_t b = 0; b < k / HARO_QK_K; ++b)
+            sum += haro_q3k_dot(w + r * rb + b * HARO_Q3K_BLOCK_BYTES, x + b * HARO_QK_K);
+        out[r] = sum;
+    }
+}
+
 /* matvec over a Q6_K tensor's rows (har-native-qwen35moe.rs:561-624 with
  * dot_row's Q6_K arm, :551-556): out[r] = dot_quant_row(row r, x). */
 void haro_q6k_matvec(const uint8_t *w, int64_t rows, int64_t k, const float *x, float *out) {

@@ -34,6 +34,7 @@ extern "C" {
 #define HARO_Q4K_BLOCK_BYTES 144
 #define HARO_Q8K_BLOCK_BYTES 292
 #define HARO_Q6K_BLOCK_BYTES 210
+#define HARO_Q3K_BLOCK_BYTES 110
 #define HARO_ROUTER_EPS 1.0e-9f
 
 /* ---- a1: binary16 -> f32 ------------------------------------------------ */
@@ -75,6 +76,23 @@ float haro_q6k_dot(const uint8_t *block, const float *x);
 float haro_dot_quant_row_q6k(const uint8_t *row, const float *x, int64_t k);
 /* rows x k Q6_K tensor times x (the per-row dot above for every row) */
 void haro_q6k_matvec(const uint8_t *w, int64_t rows, int64_t k, const float *x, float *out);
+
+/* ---- f3: Q3_K (parity unpinned) ------------------------------------------
+ * The reference holds only Q3_K's geometry (GGML type 11, 110 bytes per 256
+ * values: har/crates/har-model/src/lib.rs:591,
+ * benchmarks/local-bench/crates/lb-model/src/lib.rs:84) and no arithmetic;
+ * this restates the GGUF block layout as ggml publishes it (block_q3_K and its
+ * row dequantisation, ggml's k-quants, the format GGUF files carry): hmask[32]
+ * @0, qs[64] @32, 12 bytes of packed 6-bit scales @96, f16 d @108.  Value
+ * i = 128n + 32j + l (n < 2, j < 4, l < 32) is
+ *   d * (scale[8n + 2j + l/16] - 32) * (((qs[32n + l] >> 2j) & 3) - 4 * !(hmask[l] >> (4n + j) & 1)).
+ * No reference vectors exist to pin it: checked against hand-built blocks. */
+/* The 6-bit scale of sub-block s (0..15) from the 12 packed bytes. */
+int haro_q3k_scale(const uint8_t *scales12, int s);
+void haro_q3k_dequant_block(const uint8_t *block, float out[256]);
+/* sum over the block of (d * (scale - 32)) * q * x, in index order, in f32. */
+float haro_q3k_dot(const uint8_t *block, const float *input);
+void haro_q3k_matvec(const uint8_t *w, int64_t rows, int64_t k, const float *x, float *out);
 /* har/crates/har-demo/src/bin/har-native-qwen35moe.rs:154-163 */
 float haro_dot_f32_row(const float *row, const float *x, int64_t k);
 

@@ -60,6 +60,10 @@ def lib():
         "haro_router_logits": (None, [_f32p, _i64, _i64, _f32p, _f32p]),
         "haro_q6k_dot": (C.c_float, [_u8p, _f32p]),
         "haro_q6k_matvec": (None, [_u8p, _i64, _i64, _f32p, _f32p]),
+        "haro_q3k_scale": (C.c_int, [_u8p, C.c_int]),
+        "haro_q3k_dequant_block": (None, [_u8p, _f32p]),
+        "haro_q3k_dot": (C.c_float, [_u8p, _f32p]),
+        "haro_q3k_matvec": (None, [_u8p, _i64, _i64, _f32p, _f32p]),
         "haro_group_by_expert": (None, [_i64, C.c_int, C.c_int, _i32p, _i32p, _i32p, _i32p]),
         "haro_q8k_quantize": (None, [_f32p, _i64, _u8p]),
         "haro_q8k_dot_row": (C.c_float, [_u8p, _u8p, _i64]),
@@ -208,6 +212,44 @@ def random_q6k(seed: int, rows: int, K: int, d_lo: float = 1e-3, d_hi: float = 4
     d = rng.uniform(d_lo, d_hi, size=nb).astype(np.float16).view(np.uint8).reshape(nb, 2)
     b[:, 208:210] = d
     return b.reshape(rows, (K // QK_K) * Q6K_BLOCK_BYTES)
+
+
+# ---- Q3_K (parity unpinned: the reference holds only the geometry,
+# har/crates/har-model/src/lib.rs:591; the GGUF layout as ggml defines it) ----
+Q3K_BLOCK_BYTES = 110
+
+
+def q3k_scale(scales12: np.ndarray, s: int) -> int:
+    return int(lib().haro_q3k_scale(np.ascontiguousarray(scales12, np.uint8), s))
+
+
+def q3k_dequant_block(block: np.ndarray) -> np.ndarray:
+    out = np.empty(256, np.float32)
+    lib().haro_q3k_dequant_block(np.ascontiguousarray(block, np.uint8), out)
+    return out
+
+
+def q3k_matvec(w: np.ndarray, rows: int, K: int, x: np.ndarray) -> np.ndarray:
+    """Q3_K rows [rows][K/256*110] times every row of x [M][K] -> [M][rows]."""
+    w = np.ascontiguousarray(w, np.uint8).reshape(-1)
+    x = np.ascontiguousarray(x, np.float32).reshape(-1, K)
+    out = np.empty((x.shape[0], rows), np.float32)
+    for m in range(x.shape[0]):
+        row = np.empty(rows, np.float32)
+        lib().haro_q3k_matvec(w, rows, K, np.ascontiguousarray(x[m]), row)
+        out[m] = row
+    return out
+
+
+def random_q3k(seed: int, rows: int, K: int, d_lo: float = 1e-3, d_hi: float = 4e-3) -> np.ndarray:
+    """Seeded Q3_K test tensor [rows][K/256*110]: uniform random bits and
+    scales, d a random finite f16 in [d_lo, d_hi) (any other bytes decode)."""
+    rng = np.random.default_rng(seed)
+    nb = rows * (K // QK_K)
+    b = rng.integers(0, 256, size=(nb, Q3K_BLOCK_BYTES), dtype=np.uint8)
+    d = rng.uniform(d_lo, d_hi, size=nb).astype(np.float16).view(np.uint8).reshape(nb, 2)
+    b[:, 108:110] = d
+    return b.reshape(rows, (K // QK_K) * Q3K_BLOCK_BYTES)
 
 
 def router_logits(gate_inp: np.ndarray, x: np.ndarray) -> np.ndarray:

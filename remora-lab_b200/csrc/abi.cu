@@ -300,9 +300,10 @@ static int32_t make_weights(har_cuda_ctx *ctx, int32_t type, int64_t E, int64_t 
                             har_cuda_weights **out) {
   if (!ctx || !out) return HAR_CUDA_ERR_ARG;
   *out = nullptr;
-  if (type != GGML_Q4_K && type != GGML_Q6_K)
+  if (!ggml_block_bytes(type))
     return set_error(ctx, HAR_CUDA_ERR_UNSUPPORTED,
-                     "weights: GGML type " + std::to_string(type) + " (supported: 12 Q4_K, 14 Q6_K)");
+                     "weights: GGML type " + std::to_string(type) +
+                         " (supported: 11 Q3_K, 12 Q4_K, 14 Q6_K)");
   if (E <= 0 || N <= 0 || K <= 0)
     return set_error(ctx, HAR_CUDA_ERR_GEOMETRY, "weights: E, N and K must be positive");
   if (K % QK != 0)
@@ -313,7 +314,7 @@ static int32_t make_weights(har_cuda_ctx *ctx, int32_t type, int64_t E, int64_t 
   w->N = N;
   w->K = K;
   w->type = type;
-  w->row_bytes = K / QK * (type == GGML_Q6_K ? Q6K_BYTES : Q4K_BYTES);
+  w->row_bytes = K / QK * ggml_block_bytes(type);
   w->expert_bytes = w->row_bytes * N;
   w->device = ctx->device;
   *out = w;
@@ -411,6 +412,23 @@ int32_t har_cuda_q4k_gemv(har_cuda_ctx *ctx, const har_cuda_weights *w, int64_t 
   if (M == 0) return HAR_CUDA_OK;
   HAR_TRY(use_device(ctx));
   return launch_gemv(ctx, w, expert, x_dev, act_kind, M, y_dev);
+}
+
+int32_t har_cuda_q3k_gemv(har_cuda_ctx *ctx, const har_cuda_weights *w, int64_t expert,
+                          const float *x_dev, int64_t M, float *y_dev) {
+  if (!ctx) return HAR_CUDA_ERR_ARG;
+  HAR_TRY(check_weights(ctx, w, "q3k_gemv: weights", GGML_Q3_K));
+  if (!x_dev || !y_dev) return set_error(ctx, HAR_CUDA_ERR_ARG, "q3k_gemv: null pointer");
+  if (expert < 0 || expert >= w->E)
+    return set_error(ctx, HAR_CUDA_ERR_ARG, "q3k_gemv: expert " + std::to_string(expert) +
+                                                " out of range [0, " + std::to_string(w->E) + ")");
+  if (M < 0 || M > ((int64_t)1 << 19))
+    return set_error(ctx, HAR_CUDA_ERR_GEOMETRY, "q3k_gemv: need 0 <= M <= 2^19");
+  if (((uintptr_t)x_dev & 15u) || ((uintptr_t)y_dev & 3u))
+    return set_error(ctx, HAR_CUDA_ERR_ARG, "q3k_gemv: x must be 16-byte aligned, y 4-byte");
+  if (M == 0) return HAR_CUDA_OK;
+  HAR_TRY(use_device(ctx));
+  return launch_q3k_gemv(ctx, w, expert, x_dev, M, y_dev);
 }
 
 int32_t har_cuda_q6k_gemv(har_cuda_ctx *ctx, const har_cuda_weights *w, int64_t expert,

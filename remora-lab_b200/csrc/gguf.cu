@@ -337,10 +337,10 @@ int32_t gguf_load_weights(har_cuda_ctx *ctx, har_cuda_gguf *g, const char *name,
                           har_cuda_weights **out) {
   const har_cuda_gguf::Tensor *t = find_tensor(g, name);
   if (!t) return set_error(ctx, HAR_CUDA_ERR_ARG, std::string("gguf: no tensor ") + (name ? name : "(null)"));
-  if (t->type != GGML_Q4_K && t->type != GGML_Q6_K)
+  if (!ggml_block_bytes((int)t->type))
     return set_error(ctx, HAR_CUDA_ERR_UNSUPPORTED,
                      "gguf: tensor " + t->name + " has GGML type " + std::to_string(t->type) +
-                         " (loadable: 12 Q4_K, 14 Q6_K)");
+                         " (loadable: 11 Q3_K, 12 Q4_K, 14 Q6_K)");
   if (t->dims.size() != 2 && t->dims.size() != 3)
     return set_error(ctx, HAR_CUDA_ERR_GEOMETRY, "gguf: tensor " + t->name + " is not 2-D or 3-D");
   const int64_t K = (int64_t)t->dims[0], N = (int64_t)t->dims[1];
@@ -348,8 +348,7 @@ int32_t gguf_load_weights(har_cuda_ctx *ctx, har_cuda_gguf *g, const char *name,
   if (K <= 0 || N <= 0 || E <= 0 || K % QK != 0)
     return set_error(ctx, HAR_CUDA_ERR_GEOMETRY,
                      "gguf: tensor " + t->name + " has K not a positive multiple of 256");
-  const uint64_t bytes = (uint64_t)E * (uint64_t)N * (uint64_t)(K / QK) *
-                         (t->type == GGML_Q6_K ? Q6K_BYTES : Q4K_BYTES);
+  const uint64_t bytes = (uint64_t)E * (uint64_t)N * (uint64_t)(K / QK) * (uint64_t)ggml_block_bytes((int)t->type);
   if (t->payload != bytes)
     return set_error(ctx, HAR_CUDA_ERR_GEOMETRY, "gguf: tensor " + t->name + " payload mismatch");
   const uint64_t at = g->data_offset + t->offset;
@@ -374,7 +373,7 @@ int32_t gguf_load_weights(har_cuda_ctx *ctx, har_cuda_gguf *g, const char *name,
   w->E = E;
   w->N = N;
   w->K = K;
-  w->row_bytes = K / QK * (t->type == GGML_Q6_K ? Q6K_BYTES : Q4K_BYTES);
+  w->row_bytes = K / QK * ggml_block_bytes((int)t->type);
   w->expert_bytes = w->row_bytes * N;
   w->device = ctx->device;
   *out = w;

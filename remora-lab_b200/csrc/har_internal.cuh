@@ -18,9 +18,15 @@ namespace har {
 constexpr int QK = 256;           // values per super-block
 constexpr int Q4K_BYTES = 144;    // bytes per Q4_K super-block
 constexpr int Q6K_BYTES = 210;    // bytes per Q6_K super-block
+constexpr int Q3K_BYTES = 110;    // bytes per Q3_K super-block
 // GGML tensor type ids (the ids HAR's GGUF reader matches,
-// har/crates/har-demo/src/bin/har-native-qwen35moe.rs:37-41)
-constexpr int GGML_F32 = 0, GGML_Q4_K = 12, GGML_Q6_K = 14;
+// har/crates/har-demo/src/bin/har-native-qwen35moe.rs:37-41; Q3_K's from
+// har/crates/har-model/src/lib.rs:591)
+constexpr int GGML_F32 = 0, GGML_Q3_K = 11, GGML_Q4_K = 12, GGML_Q6_K = 14;
+// bytes per 256-value super-block of the block types the weights accept (0 = other)
+inline int ggml_block_bytes(int type) {
+  return type == GGML_Q4_K ? Q4K_BYTES : type == GGML_Q6_K ? Q6K_BYTES : type == GGML_Q3_K ? Q3K_BYTES : 0;
+}
 constexpr int Q8K_BYTES = 292;    // bytes per Q8_K block
 constexpr float ROUTER_EPS = 1.0e-9f;
 
@@ -317,6 +323,8 @@ int32_t launch_q8k_quantize(har_cuda_ctx *ctx, const float *x, int64_t M, int64_
                             uint8_t *out);
 int32_t launch_gemv(har_cuda_ctx *ctx, const har_cuda_weights *w, int64_t expert,
                     const void *x, int act_kind, int64_t M, float *y);
+int32_t launch_q3k_gemv(har_cuda_ctx *ctx, const har_cuda_weights *w, int64_t expert,
+                        const float *x, int64_t M, float *y);
 int32_t launch_q6k_gemv(har_cuda_ctx *ctx, const har_cuda_weights *w, int64_t expert,
                         const float *x, int64_t M, float *y);
 int32_t launch_route_topk(har_cuda_ctx *ctx, const float *logits, int64_t T, int E, int k,

@@ -32,6 +32,7 @@
 #include <chrono>
 #include <thread>
 #include <climits>
+#include <cstdio>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -529,7 +530,26 @@ int32_t ep_p2p_setup(har_cuda_ctx *ctx, har_cuda_ep *ep, size_t bytes) {
     for (int d = 0; d < G; ++d) {
       if (d == ep->rank) {
         ep->peer[d] = ep->win;
-      } else if (cudaIpcOpenMemHandle(&ep->peer[d], all[d].h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+        continue;
+      }
+      // peer access to rank d's GPU checked and enabled here, so that a pair
+      // without it (or a device out of peer connections) keeps every rank on
+      // NCCL instead of failing at the first load
+      char bus[32];
+      snprintf(bus, sizeof bus, "%04x:%02x:%02x.0", all[d].domain, all[d].bus, all[d].dev);
+      int pdev = -1, can = 0;
+      if (cudaDeviceGetByPCIBusId(&pdev, bus) != cudaSuccess ||
+          cudaDeviceCanAccessPeer(&can, ctx->device, pdev) != cudaSuccess || !can) {
+        mapped = 0;
+        continue;
+      }
+      const cudaError_t pe = cudaDeviceEnablePeerAccess(pdev, 0);
+      if (pe != cudaSuccess && pe != cudaErrorPeerAccessAlreadyEnabled) {
+        mapped = 0;
+        continue;
+      }
+      cudaGetLastError();
+      if (cudaIpcOpenMemHandle(&ep->peer[d], all[d].h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
         ep->peer[d] = nullptr;
         mapped = 0;
       }

@@ -29,9 +29,10 @@ QK_K = 256
 Q4K_BLOCK_BYTES = 144
 Q8K_BLOCK_BYTES = 292
 Q6K_BLOCK_BYTES = 210
+Q3K_BLOCK_BYTES = 110
 # GGML tensor type ids (har/crates/har-demo/src/bin/har-native-qwen35moe.rs:37-41)
-GGML_F32, GGML_Q4_K, GGML_Q6_K = 0, 12, 14
-BLOCK_BYTES = {GGML_Q4_K: Q4K_BLOCK_BYTES, GGML_Q6_K: Q6K_BLOCK_BYTES}
+GGML_F32, GGML_Q3_K, GGML_Q4_K, GGML_Q6_K = 0, 11, 12, 14
+BLOCK_BYTES = {GGML_Q4_K: Q4K_BLOCK_BYTES, GGML_Q6_K: Q6K_BLOCK_BYTES, GGML_Q3_K: Q3K_BLOCK_BYTES}
 
 OK = 0
 CUDA_STREAM_LEGACY = 0x1  # cudaStreamLegacy: the legacy default stream's handle value
@@ -57,7 +58,7 @@ EXPORTS = [
     "har_cuda_gguf_header", "har_cuda_gguf_tensor_info", "har_cuda_gguf_find",
     "har_cuda_gguf_meta_u64", "har_cuda_gguf_meta_string", "har_cuda_weights_from_gguf",
     "har_cuda_gguf_read_f32", "har_cuda_moe_layer_from_gguf",
-    "har_cuda_weights_upload", "har_cuda_weights_wrap", "har_cuda_q6k_gemv",
+    "har_cuda_weights_upload", "har_cuda_weights_wrap", "har_cuda_q6k_gemv", "har_cuda_q3k_gemv",
     "har_cuda_router_logits", "har_cuda_route", "har_cuda_routed_moe",
     "har_cuda_abi_version", "har_cuda_ctx_create", "har_cuda_ctx_destroy", "har_cuda_last_error",
     "har_cuda_ctx_set_stream", "har_cuda_synchronize", "har_cuda_launch_count",
@@ -154,6 +155,7 @@ def load_library() -> C.CDLL:
         "har_cuda_weights_upload": (i32, [vp, i32, vp, i64, i64, i64, pp]),
         "har_cuda_weights_wrap": (i32, [vp, i32, vp, i64, i64, i64, pp]),
         "har_cuda_q6k_gemv": (i32, [vp, vp, i64, vp, i64, vp]),
+        "har_cuda_q3k_gemv": (i32, [vp, vp, i64, vp, i64, vp]),
         "har_cuda_gguf_open": (i32, [C.c_char_p, C.c_char_p, C.c_size_t, pp]),
         "har_cuda_gguf_close": (i32, [vp]),
         "har_cuda_gguf_last_error": (i32, [vp, C.c_char_p, C.c_size_t]),
@@ -361,6 +363,12 @@ class Context:
         ml = MoeLayer(self, h, None, E, H, I)
         ml.shared = g.find(f"blk.{layer}.ffn_gate_shexp.weight") >= 0
         return ml
+
+    def q3k_gemv(self, w: "Q4KWeights", expert: int, x, M: int, y):
+        """y [M][N] = W_e x for Q3_K weights and f32 activations x [M][K]."""
+        self.check(self.lib.har_cuda_q3k_gemv(self.handle, w.handle, expert, _dptr(x), M,
+                                              _dptr(y)))
+        return y
 
     def q6k_gemv(self, w: "Q4KWeights", expert: int, x, M: int, y):
         """y [M][N] = W_e x for Q6_K weights and f32 activations x [M][K]."""
