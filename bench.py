@@ -791,28 +791,47 @@ def run_gemv_roofline(args, torch):
         keep.append(t)
         q6.append(ctx.wrap(har_cuda.GGML_Q6_K, t, 1, n6, K))
     y6 = torch.empty((1, n6), dtype=torch.float32, device=dev)
-    with torch.cuda.stream(stream):
-        for j in range(per):
-            ctx.q6k_gemv(q6[j % 2], 0, x, 1, y6)
-    torch.cuda.synchronize()
-    g6 = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g6, stream=stream):
-        for j in range(per):
-            ctx.q6k_gemv(q6[j % 2], 0, x, 1, y6)
-    with torch.cuda.stream(stream):
-        for _ in range(max(3, args.warmup)):
-            g6.replay()
-    torch.cuda.synchronize()
+
+    def time_alternating(gemv, mats):
+        """ms per GEMV: `per` launches alternating over mats, in a CUDA graph."""
+        with torch.cuda.stream(stream):
+            for j in range(per):
+                gemv(mats[j % 2], 0, x, 1, y6)
+        torch.cuda.synchronize()
+        gx = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gx, stream=stream):
+            for j in range(per):
+                gemv(mats[j % 2], 0, x, 1, y6)
+        with torch.cuda.stream(stream):
+            for _ in range(max(3, args.warmup)):
+                gx.replay()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(args.steps):
+                gx.replay()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / (args.steps * per)
+
+    ms6 = time_alternating(ctx.q6k_gemv, q6)
+    gbs6 = q6bytes / (ms6 * 1e-3) / 1e9
+    # Q3_K (the routed gate/up type of the real Alice model): two 65536 x 4096
+    # Q3_K matrices (115 MB each) of random bits and scales, d = 2^-8.
+    q3bytes = n6 * (K // 256) * 110
+    q3 = []
+    for i in range(2):
+        t = torch.randint(0, 256, (q3bytes,), dtype=torch.uint8, device=dev,
+                          generator=torch.Generator(dev).manual_seed(9500 + i))
+        t.view(-1, 110)[:, 108:110] = torch.tensor([0x00, 0x1C], dtype=torch.uint8, device=dev)
+        keep.append(t)
+        q3.append(ctx.wrap(har_cuda.GGML_Q3_K, t, 1, n6, K))
+    ms3 = time_alternating(ctx.q3k_gemv, q3)
+    gbs3 = q3bytes / (ms3 * 1e-3) / 1e9
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        ev0.record(stream)
-        for _ in range(args.steps):
-            g6.replay()
-        ev1.record(stream)
-    torch.cuda.synchronize()
-    ms6 = ev0.elapsed_time(ev1) / (args.steps * per)
-    gbs6 = q6bytes / (ms6 * 1e-3) / 1e9
     # The router on the device (har_cuda_router_logits / har_cuda_route) at the
     # Alice shape, E = 512, H = 2048, k = 10: per call, CUDA-graph replays of
     # 20 calls, at the decode and batch sizes it serves.
@@ -866,6 +885,9 @@ def run_gemv_roofline(args, torch):
         "router": dict(router, E=E_r, H=H_r, k=k_r),
         "q6k_f32_65536": {"kernel": "q6k_gemv_stream_kernel", "weight_gbs": round(gbs6, 1),
                           "frac": round(gbs6 / hbm, 4), "ms_per_gemv": round(ms6, 5),
+                          "rows": n6, "K": K},
+        "q3k_f32_65536": {"kernel": "q3k_gemv_kernel", "weight_gbs": round(gbs3, 1),
+                          "frac": round(gbs3 / hbm, 4), "ms_per_gemv": round(ms3, 5),
                           "rows": n6, "K": K},
         "clocks": q["clocks"],
     }
