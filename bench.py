@@ -886,7 +886,7 @@ def run_gemv_roofline(args, torch):
         "q6k_f32_65536": {"kernel": "q6k_gemv_stream_kernel", "weight_gbs": round(gbs6, 1),
                           "frac": round(gbs6 / hbm, 4), "ms_per_gemv": round(ms6, 5),
                           "rows": n6, "K": K},
-        "q3k_f32_65536": {"kernel": "q3k_gemv_kernel", "weight_gbs": round(gbs3, 1),
+        "q3k_f32_65536": {"kernel": "q3k_gemv_smem_kernel", "weight_gbs": round(gbs3, 1),
                           "frac": round(gbs3 / hbm, 4), "ms_per_gemv": round(ms3, 5),
                           "rows": n6, "K": K},
         "clocks": q["clocks"],

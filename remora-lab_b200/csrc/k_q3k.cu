@@ -25,6 +25,7 @@
 #include <algorithm>
 
 #include "har_internal.cuh"
+#include "tc_ptx.cuh"
 
 namespace har {
 
@@ -153,6 +154,117 @@ __global__ void __launch_bounds__(Q3K_WARPS * 32) q3k_gemv_kernel(
   }
 }
 
+// ---------------------------------------------------------------------------
+// q3k_gemv_smem_kernel: the same lane split with each warp's rows staged in
+// shared memory.  Global loads of 16-bit fields from 2-byte-aligned 110-byte
+// blocks spread one warp instruction over several sectors; here each warp
+// copies whole rows (row bytes a multiple of 16) with 16-byte cp.async,
+// double-buffered — the next row is in flight while the current one is
+// computed — and the lanes read their fields from shared memory.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t q3_lds_u16(const uint8_t *p) {
+  return *reinterpret_cast<const unsigned short *>(p);
+}
+
+template <int MT>
+__global__ void __launch_bounds__(Q3K_WARPS * 32) q3k_gemv_smem_kernel(
+    const uint8_t *__restrict__ W, int64_t N, int K, const float *__restrict__ x, int64_t M,
+    float *__restrict__ y) {
+  extern __shared__ __align__(16) uint8_t q3s[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const Q3Lane L = q3_lane(lane);
+  const int nb = K / QK;
+  const int rb = nb * Q3K_BYTES;  // a multiple of 16 (the launcher checks)
+  uint8_t *const base = q3s + (size_t)warp * 2 * rb;  // this warp's two row buffers
+  const int64_t m0 = (int64_t)blockIdx.y * MT;
+  const int mt = (int)min((int64_t)MT, M - m0);
+  const float *xm = x + m0 * K;
+  const int64_t stride = (int64_t)gridDim.x * Q3K_WARPS;
+  auto issue = [&](int64_t row, uint8_t *dst) {  // one commit group per row (empty past the end)
+    if (row < N) {
+      const uint8_t *src = W + row * (int64_t)rb;
+      for (int i = lane; i < rb / 16; i += 32) tc::cp_async16(dst + 16 * i, src + 16 * i, 16u);
+    }
+    tc::cp_async_commit();
+  };
+  int64_t row = (int64_t)blockIdx.x * Q3K_WARPS + warp;
+  issue(row, base);
+  for (int cur = 0; row < N; row += stride, cur ^= 1) {
+    issue(row + stride, base + (cur ^ 1) * rb);
+    tc::cp_async_wait<1>();  // this lane's copies of the current row
+    __syncwarp();            // ... and every other lane's
+    const uint8_t *r = base + cur * rb;
+    float acc[MT];
+#pragma unroll
+    for (int m = 0; m < MT; ++m) acc[m] = 0.0f;
+    for (int b = 0; b < nb; ++b) {
+      const uint8_t *blk = r + b * Q3K_BYTES;
+      const uint32_t qs = q3_lds_u16(blk + L.qs_off) | (q3_lds_u16(blk + L.qs_off + 2) << 16);
+      const uint32_t hm = q3_lds_u16(blk + L.hm_off) | (q3_lds_u16(blk + L.hm_off + 2) << 16);
+      const uint32_t sb = (uint32_t)blk[L.lo0] | ((uint32_t)blk[L.lo1] << 8) |
+                          ((uint32_t)blk[L.hi0] << 16) | ((uint32_t)blk[L.hi1] << 24);
+      const float d = f16_bits_to_f32(q3_lds_u16(blk + 108));
+      uint32_t c0, c1;
+      q3_codes(qs, hm, L, c0, c1);
+      const float2 s = q3_scales(sb, L);
+      float q0[4], q1[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        q0[i] = q3_value(c0, i);
+        q1[i] = q3_value(c1, i);
+      }
+      const float *xb = xm + (int64_t)b * QK + L.x_off;
+#pragma unroll
+      for (int m = 0; m < MT; ++m) {
+        if (m < mt) {
+          const float4 xa = __ldg(reinterpret_cast<const float4 *>(xb + (int64_t)m * K));
+          const float4 xc = __ldg(reinterpret_cast<const float4 *>(xb + (int64_t)m * K + 32));
+          float p0 = q0[0] * xa.x;
+          p0 = fmaf(q0[1], xa.y, p0);
+          p0 = fmaf(q0[2], xa.z, p0);
+          p0 = fmaf(q0[3], xa.w, p0);
+          float p1 = q1[0] * xc.x;
+          p1 = fmaf(q1[1], xc.y, p1);
+          p1 = fmaf(q1[2], xc.z, p1);
+          p1 = fmaf(q1[3], xc.w, p1);
+          acc[m] = fmaf(d, fmaf(s.x, p0, s.y * p1), acc[m]);
+        }
+      }
+    }
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      float v = acc[m];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (lane == 0 && m < mt) y[(m0 + m) * N + row] = v;
+    }
+    __syncwarp();  // every lane is done with this buffer before the next issue refills it
+  }
+  tc::cp_async_wait<0>();
+}
+
+// Shared memory of the staged kernel (two rows per warp), or 0 when the
+// shape does not suit it (row bytes not a multiple of 16, too long a row,
+// an unaligned base).
+static size_t q3k_smem_bytes(int K, const uint8_t *W) {
+  const size_t rb = (size_t)(K / QK) * Q3K_BYTES;
+  if (rb % 16 || ((uintptr_t)W & 15u)) return 0;
+  const size_t bytes = 2 * Q3K_WARPS * rb;
+  return bytes <= 200 * 1024 ? bytes : 0;
+}
+
+template <int MT>
+static void launch_q3k_smem(har_cuda_ctx *ctx, const uint8_t *W, int64_t N, int K, const float *x,
+                            int64_t M, float *y, size_t smem) {
+  cudaFuncSetAttribute(q3k_gemv_smem_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  const int64_t tiles = (M + MT - 1) / MT;
+  int64_t gx = (N + Q3K_WARPS - 1) / Q3K_WARPS;
+  const int64_t cap = std::max<int64_t>(1, (int64_t)ctx->num_sms * 8 / tiles);
+  if (gx > cap) gx = cap;
+  q3k_gemv_smem_kernel<MT><<<dim3((unsigned)gx, (unsigned)tiles), Q3K_WARPS * 32, smem, ctx->stream>>>(
+      W, N, K, x, M, y);
+}
+
 template <int MT>
 static void launch_q3k_mt(har_cuda_ctx *ctx, const uint8_t *W, int64_t N, int K, const float *x,
                           int64_t M, float *y) {
@@ -169,6 +281,18 @@ int32_t launch_q3k_gemv(har_cuda_ctx *ctx, const har_cuda_weights *w, int64_t ex
   const uint8_t *W = w->dev + expert * w->expert_bytes;
   const int K = (int)w->K;
   prof_begin(ctx);
+  const size_t smem = q3k_smem_bytes(K, W);
+  if (smem) {
+    if (M == 1)
+      launch_q3k_smem<1>(ctx, W, w->N, K, x, M, y, smem);
+    else if (M == 2)
+      launch_q3k_smem<2>(ctx, W, w->N, K, x, M, y, smem);
+    else if (M <= 4)
+      launch_q3k_smem<4>(ctx, W, w->N, K, x, M, y, smem);
+    else
+      launch_q3k_smem<8>(ctx, W, w->N, K, x, M, y, smem);
+    return check_launch(ctx, "q3k_gemv_smem_kernel");
+  }
   if (M == 1)
     launch_q3k_mt<1>(ctx, W, w->N, K, x, M, y);
   else if (M == 2)
