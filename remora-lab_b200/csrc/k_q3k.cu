@@ -161,6 +161,13 @@ __global__ void __launch_bounds__(Q3K_WARPS * 32) q3k_gemv_kernel(
 // copies whole rows (row bytes a multiple of 16) with 16-byte cp.async,
 // double-buffered — the next row is in flight while the current one is
 // computed — and the lanes read their fields from shared memory.
+// Lane split: half-warp hw takes block b + hw of each pair of blocks; lane
+// (n, a) of a half owns positions l = 4a..4a+3 of half n in all four planes
+// (16 values): one qs word, one hmask word, the four sub-block scales of
+// those positions (low nibbles in bytes a/4 + 2j, top bits in bytes
+// 8 + a/4 and 10 + a/4), so each value costs fewer shared-memory loads than
+// the 8-value split.  Codes become exact f32 by a byte permute into the
+// mantissa of 2^23; the offset and the products run as packed f32x2.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t q3_lds_u16(const uint8_t *p) {
   return *reinterpret_cast<const unsigned short *>(p);
@@ -172,10 +179,11 @@ __global__ void __launch_bounds__(Q3K_WARPS * 32) q3k_gemv_smem_kernel(
     float *__restrict__ y) {
   extern __shared__ __align__(16) uint8_t q3s[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const Q3Lane L = q3_lane(lane);
   const int nb = K / QK;
   const int rb = nb * Q3K_BYTES;  // a multiple of 16 (the launcher checks)
   uint8_t *const base = q3s + (size_t)warp * 2 * rb;  // this warp's two row buffers
+  const int hw = lane >> 4, n = (lane >> 3) & 1, a = lane & 7, c = a >> 2;
+  const int qs_off = 32 + 32 * n + 4 * a, hm_off = 4 * a, x_off = 128 * n + 4 * a;
   const int64_t m0 = (int64_t)blockIdx.y * MT;
   const int mt = (int)min((int64_t)MT, M - m0);
   const float *xm = x + m0 * K;
@@ -197,37 +205,41 @@ __global__ void __launch_bounds__(Q3K_WARPS * 32) q3k_gemv_smem_kernel(
     float acc[MT];
 #pragma unroll
     for (int m = 0; m < MT; ++m) acc[m] = 0.0f;
-    for (int b = 0; b < nb; ++b) {
+#pragma unroll 2
+    for (int b = hw; b < nb; b += 2) {  // nb is even here (rows are a multiple of 16 bytes)
       const uint8_t *blk = r + b * Q3K_BYTES;
-      const uint32_t qs = q3_lds_u16(blk + L.qs_off) | (q3_lds_u16(blk + L.qs_off + 2) << 16);
-      const uint32_t hm = q3_lds_u16(blk + L.hm_off) | (q3_lds_u16(blk + L.hm_off + 2) << 16);
-      const uint32_t sb = (uint32_t)blk[L.lo0] | ((uint32_t)blk[L.lo1] << 8) |
-                          ((uint32_t)blk[L.hi0] << 16) | ((uint32_t)blk[L.hi1] << 24);
+      const uint32_t qs = q3_lds_u16(blk + qs_off) | (q3_lds_u16(blk + qs_off + 2) << 16);
+      const uint32_t hm = q3_lds_u16(blk + hm_off) | (q3_lds_u16(blk + hm_off + 2) << 16);
+      const uint32_t top0 = blk[96 + 8 + c], top1 = blk[96 + 10 + c];
       const float d = f16_bits_to_f32(q3_lds_u16(blk + 108));
-      uint32_t c0, c1;
-      q3_codes(qs, hm, L, c0, c1);
-      const float2 s = q3_scales(sb, L);
-      float q0[4], q1[4];
+      float2 q[4][2];  // plane j: positions (0, 1), (2, 3) as code - 4
+      float sc[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        q0[i] = q3_value(c0, i);
-        q1[i] = q3_value(c1, i);
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t low = blk[96 + c + 2 * j];
+        const uint32_t top = (j & 1) ? top1 : top0;
+        sc[j] = (float)((int)(((low >> (4 * n)) & 15u) | (((top >> (4 * n + 2 * (j >> 1))) & 3u) << 4)) - 32);
+        const uint32_t code = ((qs >> (2 * j)) & 0x03030303u) | (((hm >> (4 * n + j)) & 0x01010101u) << 2);
+        const float2 lo = make_float2(__uint_as_float(__byte_perm(code, 0x4B000000u, 0x7440u)),
+                                      __uint_as_float(__byte_perm(code, 0x4B000000u, 0x7441u)));
+        const float2 hi = make_float2(__uint_as_float(__byte_perm(code, 0x4B000000u, 0x7442u)),
+                                      __uint_as_float(__byte_perm(code, 0x4B000000u, 0x7443u)));
+        q[j][0] = __fadd2_rn(lo, make_float2(-8388612.0f, -8388612.0f));
+        q[j][1] = __fadd2_rn(hi, make_float2(-8388612.0f, -8388612.0f));
       }
-      const float *xb = xm + (int64_t)b * QK + L.x_off;
+      const float *xb = xm + (int64_t)b * QK + x_off;
 #pragma unroll
       for (int m = 0; m < MT; ++m) {
         if (m < mt) {
-          const float4 xa = __ldg(reinterpret_cast<const float4 *>(xb + (int64_t)m * K));
-          const float4 xc = __ldg(reinterpret_cast<const float4 *>(xb + (int64_t)m * K + 32));
-          float p0 = q0[0] * xa.x;
-          p0 = fmaf(q0[1], xa.y, p0);
-          p0 = fmaf(q0[2], xa.z, p0);
-          p0 = fmaf(q0[3], xa.w, p0);
-          float p1 = q1[0] * xc.x;
-          p1 = fmaf(q1[1], xc.y, p1);
-          p1 = fmaf(q1[2], xc.z, p1);
-          p1 = fmaf(q1[3], xc.w, p1);
-          acc[m] = fmaf(d, fmaf(s.x, p0, s.y * p1), acc[m]);
+          float sum = 0.0f;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float4 xv = __ldg(reinterpret_cast<const float4 *>(xb + (int64_t)m * K + 32 * j));
+            float2 p = __fmul2_rn(q[j][0], make_float2(xv.x, xv.y));
+            p = __ffma2_rn(q[j][1], make_float2(xv.z, xv.w), p);
+            sum = fmaf(sc[j], p.x + p.y, sum);
+          }
+          acc[m] = fmaf(d, sum, acc[m]);
         }
       }
     }
