@@ -340,7 +340,7 @@ class Context:
 
     # ---- GGUF ---------------------------------------------------------------
     def weights_from_gguf(self, g: "Gguf", name: str) -> "Q4KWeights":
-        """Upload a Q4_K/Q6_K tensor of a GGUF file into the device layout."""
+        """Upload a Q3_K/Q4_K/Q6_K tensor of a GGUF file into the device layout."""
         h = C.c_void_p()
         self.check(self.lib.har_cuda_weights_from_gguf(self.handle, g.handle, name.encode(),
                                                        C.byref(h)))

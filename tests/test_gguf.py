@@ -1,6 +1,6 @@
 """GGUF expert loader (include/har_cuda.h har_cuda_gguf_*): the directory
 parse against files written to the format (host-only, no GPU), its error
-handling, and on the GPU the upload of expert, shared-expert, router and Q6_K
+handling, and on the GPU the upload of expert, shared-expert, router, Q6_K and Q3_K
 tensors checked through the kernels against the oracle.
 
 The parse follows GgufReader::inspect (har/crates/har-model/src/lib.rs:126-399);
@@ -15,7 +15,7 @@ import har_cuda
 import haro
 from gguf_writer import (ARRAY, BOOL, F32, I64, STRING, U32, U64, write_gguf)
 
-GT_F32, GT_Q4K, GT_Q6K = 0, 12, 14
+GT_F32, GT_Q3K, GT_Q4K, GT_Q6K = 0, 11, 12, 14
 
 
 def _meta(extra=()):
@@ -177,7 +177,7 @@ def test_moe_model_from_gguf_routes_and_matches_oracle(tmp_path):
 
 
 @pytest.mark.gpu
-def test_weights_from_gguf_q4k_q6k_and_f32(tmp_path):
+def test_weights_from_gguf_q4k_q6k_q3k_and_f32(tmp_path):
     import torch
     from _common import assert_close
 
@@ -185,11 +185,13 @@ def test_weights_from_gguf_q4k_q6k_and_f32(tmp_path):
     E, N, K = 3, 40, 512
     q4 = haro.gen_q4k(901, E * N, K)
     q6 = haro.random_q6k(902, N, K)
+    q3 = haro.random_q3k(905, N, K)
     f = haro.normal_f32(903, 0, 5 * 7)
     p = tmp_path / "w.gguf"
     write_gguf(p, [], [("a.weight", [K, N, E], GT_Q4K, q4),
                        ("b.weight", [K, N], GT_Q6K, q6),
-                       ("c.weight", [7, 5], GT_F32, f)])
+                       ("c.weight", [7, 5], GT_F32, f),
+                       ("d.weight", [K, N], GT_Q3K, q3)])
     g = har_cuda.Gguf(str(p))
     w4 = ctx.weights_from_gguf(g, "a.weight")
     w6 = ctx.weights_from_gguf(g, "b.weight")
@@ -205,6 +207,12 @@ def test_weights_from_gguf_q4k_q6k_and_f32(tmp_path):
     ctx.q6k_gemv(w6, 0, xd, 2, y)
     torch.cuda.synchronize()
     assert_close(y.cpu().numpy(), haro.q6k_matvec(q6, N, K, x), what="gguf q6k")
+    w3 = ctx.weights_from_gguf(g, "d.weight")
+    assert (w3.E, w3.N, w3.K, w3.ggml_type) == (1, N, K, GT_Q3K)
+    ctx.q3k_gemv(w3, 0, xd, 2, y)
+    torch.cuda.synchronize()
+    assert_close(y.cpu().numpy(), haro.q3k_matvec(q3, N, K, x), what="gguf q3k")
+    w3.free()
     fd = torch.empty(35, dtype=torch.float32, device="cuda")
     ctx.gguf_read_f32(g, "c.weight", fd)
     torch.cuda.synchronize()
